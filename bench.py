@@ -1,0 +1,384 @@
+"""Benchmark of the B200 MoE block (BASELINE.json metric: MoE-layer tokens/s
+and HBM GB/s or tensor-pipe % of peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill] [--impl ours|reference]
+
+Workloads (synthetic, seeded, GPT-OSS-120B MoE layout: E=128, H=I=2880, top-4):
+  decode   config 1: T=256 tokens per GPU (headline), plus a sweep over T=1,8,64,256
+  prefill  config 2: T=4096 tokens, router biased to a Zipf(1.1) expert popularity
+
+A step is one MoE-layer forward (router -> dispatch -> MXFP4 SwiGLU experts ->
+combine) over the step's tokens with the weights resident in HBM.  With N>1
+(one process per GPU under torchrun) every rank runs the same per-GPU
+workload on its own layer replica (weak scaling; the layer needs no
+collective when tokens are split by rank).  Timing: W untimed warm-up steps,
+then K steps bracketed by a barrier and cuda synchronize, CUDA events on the
+launching stream, max over ranks.  The weights (1.7 GB per layer) exceed the
+126 MB L2, so each step streams them from HBM; for T <= 8 (52-380 MB of
+weights touched) a 256 MB buffer is written between timed steps to flush L2.
+
+``--impl reference`` times the reference algorithm on the host CPU (the numpy
+restatement in oracle/, used only here and in tests) on the same layer,
+rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+GPT_OSS_E, GPT_OSS_H, GPT_OSS_I, TOP_K = 128, 2880, 2880, 4
+BYTES_PER_EXPERT = (2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H // 32 + 2 * GPT_OSS_I * 2) + (
+    GPT_OSS_H * GPT_OSS_I // 2 + GPT_OSS_H * GPT_OSS_I // 32 + GPT_OSS_H * 2
+)  # 13,236,480
+GATE_UP_BYTES_PER_EXPERT = 2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H // 32 + 2 * GPT_OSS_I * 2  # 8,824,320
+FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H)  # 199,065,600
+
+
+def peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(use_gpu: bool = True):
+    """One process per GPU under torchrun (RANK/LOCAL_RANK/WORLD_SIZE); NCCL for the GPU arm, gloo for the CPU arm."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if use_gpu:
+        torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        if use_gpu:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def make_layer(workload: str, seed: int, device):
+    from kcapw_klcquant_b200 import MoeLayer
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    zipf = 1.1 if workload == "prefill" else None
+    layer = syn.make_layer(syn.GPT_OSS_120B, seed=seed, zipf=zipf, device=device)
+    return MoeLayer.from_tensors(0, layer, device, top_k=TOP_K)
+
+
+def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None, world: int):
+    """Per-step device times (ms) of ``fn`` with CUDA events on the current stream."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush.add_(1)
+        ev[i][0].record(stream)
+        fn()
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+def unique_experts(ml, x) -> int:
+    _, rb = ml.forward(x, precision="bf16")
+    return int(torch.unique(rb.indices).numel())
+
+
+def cpu_baseline_sample(layer: dict[str, torch.Tensor], x_host: torch.Tensor, n_tokens: int) -> dict:
+    """Time the CPU restatement of the reference (oracle/) on the first tokens, dense experts cached.
+
+    ``layer`` holds the checkpoint-named tensors on the CPU.  Mirrors the
+    reference's warm decode path: one route() per token (bf16 logits, top-k,
+    softmax, per-expert GEMVs with the dequantized experts already cached,
+    bf16 combine).
+    """
+    import numpy as np
+
+    from oracle import moe_oracle as orc
+
+    p = "model.layers.0.mlp"
+    bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    xs = bits(x_host[:n_tokens])
+    rw, rbias = bits(layer[f"{p}.router.weight"]), bits(layer[f"{p}.router.bias"])
+    lg = orc.router_logits_bits(xs, rw, rbias)
+    idx, _ = orc.select_topk(orc.bf16_bits_to_f32(lg), TOP_K)
+    ex = orc.DenseExperts(*(layer[f"{p}.experts.{n}"].cpu().numpy() for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "down_proj_blocks", "down_proj_scales")))
+    for e in np.unique(idx):  # warm the dequantized-expert cache (the reference's warm path)
+        ex.get(int(e))
+    gub, dnb = bits(layer[f"{p}.experts.gate_up_proj_bias"]), bits(layer[f"{p}.experts.down_proj_bias"])
+    t0 = time.perf_counter()
+    for t in range(n_tokens):  # one token at a time, as route() does
+        lgt = orc.router_logits_bits(xs[t : t + 1], rw, rbias)
+        it, st = orc.select_topk(orc.bf16_bits_to_f32(lgt), TOP_K)
+        orc.moe_layer(xs[t : t + 1], it, orc.softmax_weights_bits(st), ex, gub, dnb, "bf16")
+    dt = time.perf_counter() - t0
+    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_tokens} tokens of the same layer, one token per route() call, experts pre-dequantized (warm cache), numpy with all host threads"}
+
+
+def run_reference(args, world, rank):
+    """Reference arm: the reference algorithm (CPU restatement) on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    T = args.tokens
+    zipf = 1.1 if args.workload == "prefill" else None
+    layer = syn.make_layer(syn.GPT_OSS_120B, seed=args.seed, zipf=zipf, device="cpu")
+    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed, device="cpu")
+    n = 4
+    vals, r = [], {}
+    for i in range(args.warmup + args.steps):
+        r = cpu_baseline_sample(layer, x, n)
+        if i >= args.warmup:
+            vals.append(r["value"])
+    v = statistics.median(vals)
+    out = {
+        "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": n / v * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"config {'1' if args.workload == 'decode' else '2'}: {args.workload} MoE layer, T={T}, E=128, H=I=2880, top-4",
+                   "cpu_sample_tokens": n},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port", "sample": r["sample"]},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+
+
+def run_ours(args, world, rank, local):
+    from kcapw_klcquant_b200 import _lib
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    device = torch.device("cuda", local)
+    T = args.tokens
+    ml = make_layer(args.workload, args.seed, device)
+    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed + rank, device=device)
+    pk = peaks()
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device) if T <= 8 else None
+    out = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16, device=device)
+    fwd = lambda: ml.forward(x, precision=args.precision, out=out, path=args.path)  # noqa: E731
+
+    U = unique_experts(ml, x)
+    with ClockSampler(local) as clk:
+        times = time_steps(fwd, args.steps, args.warmup, flush, world)
+    ms = max_over_ranks(sum(times) / len(times), world)
+    tokens_per_s = world * T / (ms / 1e3)
+
+    # stage breakdown (same workload, separate pass)
+    _lib.stage_timing(True)
+    stage = {}
+    for _ in range(3):
+        if flush is not None:
+            flush.add_(1)
+        fwd()
+        stage = _lib.stage_times()
+    _lib.stage_timing(False)
+    # end-to-end through the public API with host buffers
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e():
+        x_dev.copy_(x_host, non_blocking=True)
+        y, _ = ml.forward(x_dev, precision=args.precision, out=out, path=args.path)
+        y_host.copy_(y, non_blocking=True)
+
+    et = time_steps(e2e, args.steps, args.warmup, flush, world)
+    e2e_ms = max_over_ranks(sum(et) / len(et), world)
+
+    # roofline of the dominant kernel (gate_up GEMM for decode)
+    decode = args.workload == "decode"
+    if decode:
+        gu_ms = stage.get("gate_up", float("nan"))
+        bytes_gu = U * GATE_UP_BYTES_PER_EXPERT + T * TOP_K * GPT_OSS_H * 2
+        achieved = bytes_gu / (gu_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "kernel": "gate_up GEMM (MXFP4 dequant + SwiGLU epilogue)", "achieved": achieved, "peak": pk["hbm_gbs"],
+                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"],
+                "algorithmic_bytes": bytes_gu, "unique_experts": U}
+        layer_bytes = U * BYTES_PER_EXPERT + GPT_OSS_E * GPT_OSS_H * 2 + GPT_OSS_E * 2 + T * GPT_OSS_H * 4
+        layer_roof = {"bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9, "frac": layer_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"]}
+    else:
+        gu_ms = stage.get("gate_up", float("nan"))
+        flops_gu = 2 * T * TOP_K * GPT_OSS_H * 2 * GPT_OSS_I
+        achieved = flops_gu / (gu_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": "gate_up GEMM", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / pk["bf16_tflops"], "traffic": None, "peak_source": pk["source"], "algorithmic_flops": flops_gu}
+        layer_roof = {"flops": T * FLOPS_PER_TOKEN, "achieved_tflops": T * FLOPS_PER_TOKEN / (ms / 1e3) / 1e12}
+
+    result = {
+        "metric": "moe_layer_tokens_per_s",
+        "value": tokens_per_s,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded GPT-OSS-120B MXFP4 MoE layer, bf16 N(0,1) activations)",
+        "config": {
+            "workload": f"config {'1' if decode else '2'}: {args.workload} MoE layer, T={T} tokens per GPU, E=128, H=I=2880, top-4"
+                        + (", Zipf(1.1) router bias" if not decode else ""),
+            "precision": args.precision, "expert_path": args.path, "l2": "L2 flushed between steps" if flush is not None else "weights (>=1.4 GB) exceed L2",
+            "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
+        },
+        "roofline": roof,
+        "layer_roofline": layer_roof,
+        "stages_ms": stage,
+        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * GPT_OSS_H * 2, "d2h_bytes_per_step": T * GPT_OSS_H * 2},
+        "gpu_launches": 7 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if decode and args.sweep and world == 1:
+        sweep = {}
+        for t in (1, 8, 64, 256):
+            xs = syn.make_hidden(t, GPT_OSS_H, seed=args.seed + t, device=device)
+            ob = torch.empty((t, GPT_OSS_H), dtype=torch.bfloat16, device=device)
+            u = unique_experts(ml, xs)
+            tt = time_steps(lambda: ml.forward(xs, precision=args.precision, out=ob, path=args.path), max(args.steps, 5), args.warmup, flush if t <= 8 else None, 1)
+            m = sum(tt) / len(tt)
+            b = u * BYTES_PER_EXPERT + GPT_OSS_E * GPT_OSS_H * 2 + GPT_OSS_E * 2 + t * GPT_OSS_H * 4
+            sweep[str(t)] = {"tokens_per_s": t / (m / 1e3), "ms": m, "unique_experts": u, "layer_gbs": b / (m / 1e3) / 1e9,
+                             "layer_frac_hbm": b / (m / 1e3) / 1e9 / pk["hbm_gbs"]}
+        result["decode_sweep"] = sweep
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        p = ml.packed
+        layer_cpu = {
+            "model.layers.0.mlp.router.weight": ml.router_weight.cpu(), "model.layers.0.mlp.router.bias": ml.router_bias.cpu(),
+            "model.layers.0.mlp.experts.gate_up_proj_bias": ml.gate_up_bias.cpu(), "model.layers.0.mlp.experts.down_proj_bias": ml.down_bias.cpu(),
+            "model.layers.0.mlp.experts.gate_up_proj_blocks": p.gu_blocks.cpu(), "model.layers.0.mlp.experts.gate_up_proj_scales": p.gu_scales.cpu(),
+            "model.layers.0.mlp.experts.down_proj_blocks": p.dn_blocks.cpu(), "model.layers.0.mlp.experts.down_proj_scales": p.dn_scales.cpu(),
+        }
+        result["cpu_baseline"] = cpu_baseline_sample(layer_cpu, x.cpu(), 4)
+    if rank == 0:
+        print(json.dumps(result))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
+    ap.add_argument("--path", choices=["auto", "simt", "tc"], default="auto")
+    ap.add_argument("--seed", type=int, default=1)
+    ap.add_argument("--sweep", action="store_true", default=True)
+    ap.add_argument("--no-sweep", dest="sweep", action="store_false")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.tokens is None:
+        args.tokens = 256 if args.workload == "decode" else 4096
+    world, rank, local = dist_setup(use_gpu=args.impl != "reference")
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

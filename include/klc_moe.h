@@ -1,0 +1,224 @@
+/*
+ * klc_moe.h — C ABI of the B200-native KLCquant MoE block (libklcmoe.so).
+ *
+ * Every entry point takes plain device pointers, 64-bit sizes and a CUDA
+ * stream passed as `void*` (NULL = legacy default stream), returns an `int`
+ * status (KLC_OK = 0) and never aborts, throws or frees caller memory.
+ * `klc_last_error()` gives a thread-local message for the last failure on the
+ * calling thread.  Device tensors are row-major and contiguous unless a
+ * stride argument says otherwise.  bf16 values travel as uint16_t bit
+ * patterns.
+ *
+ * Reference interfaces replaced (KLCquant, a Python/PyTorch package):
+ *   klc_mxfp4_dequant        <- dequantize_mxfp4_matrix        mxfp4_expert.py:357-379
+ *   klc_router_topk          <- StreamedMoERouter.route, router part
+ *                               (F.linear + topk + softmax)     streamed_moe_router.py:269-284
+ *   klc_moe_permute          <- (no counterpart: the reference loops one token
+ *                               and one expert at a time,       streamed_moe_router.py:499)
+ *   klc_moe_experts          <- _execute_mxfp4_experts expert math (gate_up GEMM,
+ *                               bias, _apply_gate, down GEMM)   streamed_moe_router.py:483-511,524-529
+ *   klc_moe_combine          <- weighted bf16 combine           streamed_moe_router.py:497,512-513
+ *   klc_moe_bias_only        <- execute_experts=False path      streamed_moe_router.py:317-329
+ *   klc_moe_forward          <- StreamedMoERouter.route as a whole, batched over tokens
+ *   klc_rms_norm             <- rms_norm                        streamed_attention.py:27-28
+ *   klc_runtime_dequant      <- RuntimeDequantizer.dequantize   runtime_dequantizer.py:30-52
+ *                               (unpack_lowbit adaptive_quantizer.py:183-213,
+ *                                reconstruct_pruned tensor_pruner.py:62-69)
+ */
+#ifndef KLC_MOE_H
+#define KLC_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------- */
+enum klc_status {
+  KLC_OK = 0,
+  KLC_ERR_INVALID = 1,        /* bad pointer, shape or enum value            */
+  KLC_ERR_UNSUPPORTED = 2,    /* valid request this build does not handle    */
+  KLC_ERR_WORKSPACE = 3,      /* caller workspace smaller than required      */
+  KLC_ERR_CUDA = 4,           /* a CUDA runtime / driver call failed         */
+  KLC_ERR_DEVICE_TIMEOUT = 5, /* a bounded device-side wait gave up          */
+  KLC_ERR_DEVICE_FAULT = 6,   /* a device-side check recorded a bad index    */
+  KLC_ERR_NCCL = 7            /* a collective failed                         */
+};
+
+/* ---- dtype enum ------------------------------------------------------ */
+enum klc_dtype { KLC_BF16 = 0, KLC_F16 = 1, KLC_F32 = 2 };
+
+/* ---- expert math precision (the reference's matmul_precision) ----------
+ * KLC_PREC_FP32: gu = x @ Wgu + b in fp32, out = gated @ Wd + b in fp32
+ *                (streamed_moe_router.py:505,511).
+ * KLC_PREC_BF16: both products rounded to bf16 before the fp32 bias add
+ *                (streamed_moe_router.py:502-503,507-509).                 */
+enum klc_precision { KLC_PREC_FP32 = 0, KLC_PREC_BF16 = 1 };
+
+/* ---- expert kernel selection ------------------------------------------ */
+enum klc_expert_path {
+  KLC_PATH_AUTO = 0, /* tcgen05 grouped GEMM when available, else SIMT       */
+  KLC_PATH_SIMT = 1, /* CUDA-core dequant + FMA kernels                      */
+  KLC_PATH_TC = 2    /* tcgen05/TMEM grouped GEMM, dequant into TMEM         */
+};
+
+int klc_version(void);
+const char* klc_last_error(void);
+/* Expert paths built into this library: bit 0 = KLC_PATH_SIMT,
+ * bit 1 = KLC_PATH_TC (tcgen05). */
+int klc_capabilities(int* flags);
+/* Number of SMs of the current device (for host-side planning). */
+int klc_device_sm_count(int* out_sms);
+
+/* ---- MXFP4 dequant ---------------------------------------------------- *
+ * Replaces dequantize_mxfp4_matrix(blocks, scales, dtype)
+ * (mxfp4_expert.py:357-379).  blocks uint8 [out_dim, groups, 16], scales uint8
+ * [out_dim, groups]; writes out [groups*32, out_dim] (the transposed [in, out]
+ * matrix) in `out_dtype`.  Bit-exact: FP4[nibble] * 2^(scale-127) rounded
+ * once to the target type, low nibble = even K index.                     */
+int klc_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t out_dim, int64_t groups,
+                      void* out, int out_dtype, void* stream);
+
+/* One-time re-layout of E8M0 scales [E, rows, groups] -> [E, groups, rows]
+ * (the layout the expert kernels read).  No counterpart in the reference,
+ * which stores scales as [E, rows, groups] (checkpoint layout).           */
+int klc_mxfp4_transpose_scales(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups,
+                               uint8_t* scales_t, void* stream);
+
+/* ---- router ------------------------------------------------------------ *
+ * Replaces the router part of StreamedMoERouter.route
+ * (streamed_moe_router.py:269-284): logits = bf16(x @ W^T + b) with fp32
+ * accumulation; selection = top-k of (logits + adjust) by value, ties to the
+ * lower expert index; weights = softmax over the selected fp32 scores,
+ * rounded to bf16.  x bf16 [T,H], w bf16 [E,H], b bf16 [E]; adjust fp32 [E]
+ * or NULL (the host-built locality bias vector); out_idx int32 [T,k];
+ * out_w bf16 [T,k]; out_logits bf16 [T,E] or NULL.  Requires k <= 8, E <= 1024. */
+int klc_router_topk(const uint16_t* x, int64_t tokens, int64_t hidden, const uint16_t* w, const uint16_t* b,
+                    int64_t experts, int k, const float* adjust, int32_t* out_idx, uint16_t* out_w,
+                    uint16_t* out_logits, void* stream);
+
+/* Selection + softmax on given fp32 scores [T, E] (the locality path: the
+ * host applies the reference's bias / guard policy, streamed_moe_router.py:
+ * 331-394, to logits read back from klc_router_topk).  keep_order != 0:
+ * the row holds exactly k scores in the wanted order (E == k) and only the
+ * softmax is computed; out_idx may then be NULL.                          */
+int klc_select_softmax(const float* scores, int64_t tokens, int64_t experts, int k, int keep_order, int32_t* out_idx,
+                       uint16_t* out_w, void* stream);
+
+/* ---- full layer workspace ---------------------------------------------- */
+typedef struct klc_moe_dims {
+  int64_t tokens;       /* T                                    */
+  int64_t hidden;       /* H (multiple of 64)                   */
+  int64_t intermediate; /* I (multiple of 64)                   */
+  int64_t experts;      /* E experts held by this call          */
+  int32_t top_k;        /* k                                    */
+  int32_t path;         /* enum klc_expert_path                 */
+} klc_moe_dims;
+
+/* Bytes of device workspace klc_moe_forward / klc_moe_experts need. */
+int klc_moe_workspace_size(const klc_moe_dims* dims, size_t* out_bytes);
+
+/* Packed expert weights of one layer, all device pointers.
+ * gu_blocks  uint8 [E, 2I, H/32, 16]   gate_up_proj_blocks (checkpoint layout)
+ * gu_scales_t uint8 [E, H/32, 2I]      gate_up_proj_scales re-laid by klc_mxfp4_transpose_scales
+ * gu_bias    bf16 [E, 2I]
+ * dn_blocks  uint8 [E, H, I/32, 16]    down_proj_blocks
+ * dn_scales_t uint8 [E, I/32, H]
+ * dn_bias    bf16 [E, H]
+ * router_w   bf16 [E, H], router_b bf16 [E]                               */
+typedef struct klc_moe_weights {
+  const uint8_t* gu_blocks;
+  const uint8_t* gu_scales_t;
+  const uint16_t* gu_bias;
+  const uint8_t* dn_blocks;
+  const uint8_t* dn_scales_t;
+  const uint16_t* dn_bias;
+  const uint16_t* router_w;
+  const uint16_t* router_b;
+  float swiglu_limit; /* 7.0   (streamed_moe_router.py:242) */
+  float alpha;        /* 1.702 (streamed_moe_router.py:248) */
+} klc_moe_weights;
+
+/* Expert execution + combine for given routing (idx, weights), the body of
+ * _execute_mxfp4_experts (streamed_moe_router.py:483-522) batched over T
+ * tokens: permute/gather, gate_up GEMM + bias + clamped SwiGLU, down GEMM +
+ * bias, bf16 combine in selection order.  x bf16 [T,H]; idx int32 [T,k]
+ * (values in [0,E)); w bf16 [T,k]; y bf16 [T,H].  norms fp32 [T,k,2] or NULL
+ * receives (||gated||, ||out||) per pair (the expert_logs of :514-521).
+ * residual: if non-NULL, y = residual + moe_out (bf16 add).               */
+int klc_moe_experts(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x, const int32_t* idx,
+                    const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Router + experts + combine in one call (StreamedMoERouter.route batched).
+ * out_idx/out_w receive the routing (int32 [T,k], bf16 [T,k]); out_logits
+ * bf16 [T,E] or NULL; adjust fp32 [E] or NULL.                            */
+int klc_moe_forward(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x, const float* adjust,
+                    int precision, uint16_t* y, int32_t* out_idx, uint16_t* out_w, uint16_t* out_logits,
+                    float* norms, const uint16_t* residual, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Weighted combine of expert output rows back to tokens
+ * (streamed_moe_router.py:497,512-513): for each token t, in slot order s,
+ * out[t] = bf16(out[t] + bf16(y_rows[pair_pos[t*k+s]] * w[t,s])), starting
+ * from zero (or from residual[t] added at the end when residual != NULL).
+ * y_rows bf16 [*, H]; pair_pos int32 [T*k]; w bf16 [T,k]; out bf16 [T,H]. */
+int klc_moe_combine(const uint16_t* y_rows, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,
+                    int64_t hidden, const uint16_t* residual, uint16_t* out, void* stream);
+
+/* execute_experts=False path (streamed_moe_router.py:317-329):
+ * y[t] = sum_s bf16(bias[idx[t,s]] * w[t,s]) accumulated in fp32, rounded once. */
+int klc_moe_bias_only(const uint16_t* dn_bias, int64_t tokens, int64_t hidden, int k, const int32_t* idx,
+                      const uint16_t* w, uint16_t* y, void* stream);
+
+/* Stable counting-sort permutation of (token, slot) pairs by expert.
+ * idx int32 [T,k]; writes pair_pos int32 [T*k] (padded row of each pair),
+ * counts int32 [E], offsets int32 [E+1] (each group padded to `pad` rows)
+ * and rows int32 [rows_cap] (pair id per padded row, -1 in padding).
+ * rows_cap >= T*k + E*(pad-1).  Uses `workspace` (klc_moe_workspace_size). */
+int klc_moe_permute(const int32_t* idx, int64_t tokens, int k, int64_t experts, int pad, int32_t* pair_pos,
+                    int32_t* counts, int32_t* offsets, int32_t* rows, int64_t rows_cap, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Per-stage timing of the layer entry points on the calling host thread.
+ * klc_stage_timing(1) makes klc_moe_forward / klc_moe_experts record a CUDA
+ * event on their stream at each stage boundary; klc_stage_times then
+ * synchronises on those events and writes the milliseconds of the last call
+ * for [router, permute+gather, gate_up GEMM, down GEMM, combine] (-1 where
+ * the stage did not run), and the number of stages measured to *n_out.    */
+int klc_stage_timing(int enable);
+int klc_stage_times(float* ms, int max_stages, int* n_out);
+
+/* Read back the device status word at the start of a workspace used by
+ * klc_moe_experts / klc_moe_forward / klc_moe_permute (synchronises
+ * `stream`).  Returns KLC_OK, or the device-side error a kernel recorded
+ * (KLC_ERR_DEVICE_FAULT for an out-of-range expert index,
+ * KLC_ERR_DEVICE_TIMEOUT for a bounded wait that gave up); code/where/detail
+ * may be NULL.                                                             */
+int klc_workspace_status(const void* workspace, int* code, int* where, int* detail, void* stream);
+
+/* RMSNorm (streamed_attention.py:27-28): y = bf16(bf16(x * bf16(rsqrt(mean(x^2)+eps))) * w). */
+int klc_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int64_t hidden, float eps, uint16_t* y,
+                 void* stream);
+
+/* ---- runtime dequantizer (RuntimeDequantizer.dequantize) ---------------
+ * Replaces runtime_dequantizer.py:30-52 (with unpack_lowbit,
+ * adaptive_quantizer.py:183-213, and reconstruct_pruned,
+ * tensor_pruner.py:62-69).  Writes `numel` elements of `out_dtype`:
+ *   mode 0 ("fp16"):   out = data                  data_dtype bf16/f16/f32
+ *   mode 1 (packed q1-q4, bits 1..4): out = unpack_lowbit(data) * scale[0];
+ *                      data uint8, `count` bytes
+ *   mode 2 (unpacked q8/q16, bits 8 or 16): out = int(data) * scale[0]
+ *   mode 3 ("pruned"): out = 0, then out[index[j]] = data[j] for j < count;
+ *                      data_dtype bf16/f16/f32, index int64
+ * Products are formed in fp32 and rounded once to out_dtype, as the
+ * reference's q.float() * scale.float() then .to(dtype).                  */
+int klc_runtime_dequant(int mode, const void* data, int data_dtype, const float* scale, const int64_t* index,
+                        int64_t count, int bits, int64_t numel, void* out, int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLC_MOE_H */

@@ -1,0 +1,53 @@
+// Status / error plumbing of the C ABI.
+#include <cstdio>
+#include <string>
+
+#include "klc_common.cuh"
+
+namespace klc {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return KLC_OK;
+  g_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return KLC_ERR_CUDA;
+}
+
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n;
+}
+
+}  // namespace klc
+
+extern "C" int klc_version(void) { return 1; }
+
+extern "C" const char* klc_last_error(void) { return klc::g_last_error.c_str(); }
+
+namespace klc {
+bool tc_path_supported(int64_t hidden, int64_t inter);
+}
+
+extern "C" int klc_capabilities(int* flags) {
+  if (flags == nullptr) return klc::fail(KLC_ERR_INVALID, "klc_capabilities: null output");
+  *flags = 1 | (klc::tc_path_supported(2880, 2880) ? 2 : 0);
+  return KLC_OK;
+}
+
+extern "C" int klc_device_sm_count(int* out_sms) {
+  if (out_sms == nullptr) return klc::fail(KLC_ERR_INVALID, "klc_device_sm_count: null output");
+  int dev = 0;
+  KLC_CUDA(cudaGetDevice(&dev));
+  KLC_CUDA(cudaDeviceGetAttribute(out_sms, cudaDevAttrMultiProcessorCount, dev));
+  return KLC_OK;
+}

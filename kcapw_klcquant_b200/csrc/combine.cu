@@ -1,0 +1,156 @@
+// Un-permute + weighted combine, the bias-only MoE path and RMSNorm.
+//
+// Combine restates streamed_moe_router.py:497,512-513 exactly:
+//   output = zeros_like(hidden)                       (bf16)
+//   for each selected expert, in top-k order:
+//       output += out.to(bf16) * w                    (bf16 product, bf16 sum)
+// so the result is bit-identical to the reference's for identical expert
+// outputs.  One CTA per token; each thread owns 8 hidden elements and
+// gathers them (16-byte loads) from the k permuted rows of the token.
+// Memory-bound: k*H*2 bytes read + H*2 written per token.
+#include "permute.cuh"
+
+namespace klc {
+
+namespace {
+
+__global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ pair_pos,
+                               const uint16_t* __restrict__ w, int k, int64_t hidden,
+                               const uint16_t* __restrict__ residual, uint16_t* __restrict__ out,
+                               const float* __restrict__ normsq, float* __restrict__ norms) {
+  const int64_t t = blockIdx.x;
+  const int chunks = int(hidden / 8);
+  if (norms != nullptr && threadIdx.x < 2 * k) {
+    const int64_t q = t * k * 2 + threadIdx.x;
+    norms[q] = sqrtf(normsq[q]);
+  }
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int s = 0; s < k; ++s) {
+      const int pos = pair_pos[t * k + s];
+      if (pos < 0) continue;  // pair dropped by the permute's index check (recorded in the status word)
+      const float ws = bf16_to_f32(w[t * k + s]);
+      const uint4 v = reinterpret_cast<const uint4*>(y + int64_t(pos) * hidden)[c];
+      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
+        acc[2 * j] = round_bf16(acc[2 * j] + round_bf16(lo * ws));
+        acc[2 * j + 1] = round_bf16(acc[2 * j + 1] + round_bf16(hi * ws));
+      }
+    }
+    if (residual != nullptr) {
+      const uint4 r = reinterpret_cast<const uint4*>(residual + t * hidden)[c];
+      const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = round_bf16(__uint_as_float(rr[j] << 16) + acc[2 * j]);
+        acc[2 * j + 1] = round_bf16(__uint_as_float(rr[j] & 0xffff0000u) + acc[2 * j + 1]);
+      }
+    }
+    uint4 o;
+    o.x = uint32_t(f32_to_bf16(acc[0])) | (uint32_t(f32_to_bf16(acc[1])) << 16);
+    o.y = uint32_t(f32_to_bf16(acc[2])) | (uint32_t(f32_to_bf16(acc[3])) << 16);
+    o.z = uint32_t(f32_to_bf16(acc[4])) | (uint32_t(f32_to_bf16(acc[5])) << 16);
+    o.w = uint32_t(f32_to_bf16(acc[6])) | (uint32_t(f32_to_bf16(acc[7])) << 16);
+    reinterpret_cast<uint4*>(out + t * hidden)[c] = o;
+  }
+}
+
+// execute_experts=False (streamed_moe_router.py:317-329):
+//   contribution = sum(down_bias[experts].to(bf16) * weights[:, None], dim=0)
+// products rounded to bf16, the k-term sum accumulated in fp32, rounded once.
+__global__ void bias_only_kernel(const uint16_t* __restrict__ bias, int64_t hidden, int k,
+                                 const int32_t* __restrict__ idx, const uint16_t* __restrict__ w,
+                                 uint16_t* __restrict__ y) {
+  const int64_t t = blockIdx.x;
+  for (int64_t h = threadIdx.x; h < hidden; h += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < k; ++s) {
+      const int e = idx[t * k + s];
+      acc += round_bf16(bf16_to_f32(bias[int64_t(e) * hidden + h]) * bf16_to_f32(w[t * k + s]));
+    }
+    y[t * hidden + h] = f32_to_bf16(acc);
+  }
+}
+
+// rms_norm (streamed_attention.py:27-28):
+//   x * rsqrt(mean(x.float()^2) + eps).to(bf16) * weight   (bf16 products)
+__global__ void rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wt, int64_t hidden,
+                                float eps, uint16_t* __restrict__ y) {
+  __shared__ float red[32];
+  const int64_t r = blockIdx.x;
+  const uint16_t* xr = x + r * hidden;
+  float ss = 0.f;
+  for (int64_t h = threadIdx.x; h < hidden; h += blockDim.x) {
+    const float v = bf16_to_f32(xr[h]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  if (warp == 0) {
+    float v = (lane < int(blockDim.x >> 5)) ? red[lane] : 0.f;
+    v = warp_sum(v);
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float mean = red[0] / float(hidden);
+  const float inv = round_bf16(1.0f / sqrtf(mean + eps));
+  for (int64_t h = threadIdx.x; h < hidden; h += blockDim.x) {
+    const float v = round_bf16(bf16_to_f32(xr[h]) * inv);
+    y[r * hidden + h] = f32_to_bf16(v * bf16_to_f32(wt[h]));
+  }
+}
+
+}  // namespace
+
+int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,
+                   int64_t hidden, const uint16_t* residual, uint16_t* out, const float* normsq, float* norms,
+                   cudaStream_t stream) {
+  if (tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(tokens <= 0x7fffffff, "combine: too many tokens");
+  int64_t threads = (hidden / 8 + 31) / 32 * 32;
+  threads = threads < 64 ? 64 : (threads > 256 ? 256 : threads);
+  combine_kernel<<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq, norms);
+  KLC_LAUNCH_CHECK("combine launch");
+  return KLC_OK;
+}
+
+}  // namespace klc
+
+extern "C" int klc_moe_bias_only(const uint16_t* dn_bias, int64_t tokens, int64_t hidden, int k, const int32_t* idx,
+                                 const uint16_t* w, uint16_t* y, void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(tokens >= 0 && hidden > 0 && k >= 1, "klc_moe_bias_only: bad sizes");
+  if (tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(dn_bias && idx && w && y, "klc_moe_bias_only: null pointer");
+  KLC_CHECK_ARG(tokens <= 0x7fffffff, "klc_moe_bias_only: too many tokens");
+  bias_only_kernel<<<unsigned(tokens), 256, 0, as_stream(stream)>>>(dn_bias, hidden, k, idx, w, y);
+  KLC_LAUNCH_CHECK("klc_moe_bias_only launch");
+  return KLC_OK;
+}
+
+extern "C" int klc_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int64_t hidden, float eps,
+                            uint16_t* y, void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(rows >= 0 && hidden > 0, "klc_rms_norm: bad sizes");
+  if (rows == 0) return KLC_OK;
+  KLC_CHECK_ARG(x && w && y, "klc_rms_norm: null pointer");
+  KLC_CHECK_ARG(rows <= 0x7fffffff, "klc_rms_norm: too many rows");
+  rms_norm_kernel<<<unsigned(rows), 256, 0, as_stream(stream)>>>(x, w, hidden, eps, y);
+  KLC_LAUNCH_CHECK("klc_rms_norm launch");
+  return KLC_OK;
+}
+
+extern "C" int klc_moe_combine(const uint16_t* y_rows, const int32_t* pair_pos, const uint16_t* w, int64_t tokens,
+                               int k, int64_t hidden, const uint16_t* residual, uint16_t* out, void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(tokens >= 0 && k >= 1 && hidden > 0 && hidden % 8 == 0, "klc_moe_combine: bad sizes");
+  if (tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(y_rows && pair_pos && w && out, "klc_moe_combine: null pointer");
+  return launch_combine(y_rows, pair_pos, w, tokens, k, hidden, residual, out, nullptr, nullptr, as_stream(stream));
+}

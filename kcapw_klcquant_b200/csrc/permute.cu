@@ -1,0 +1,182 @@
+// Token dispatch: stable counting-sort of (token, slot) pairs by expert into
+// contiguous, padded row groups, fused with the gather of each pair's
+// activation row.
+//
+// The reference has no dispatch step: route() handles one token and loops
+// over its k experts (streamed_moe_router.py:499).  Batched execution needs
+// the pairs of each expert contiguous; the order inside a group is
+// token-major, slot-minor (a stable sort of the flat expert ids), so results
+// are deterministic and independent of the grid size.
+//
+// Three launches, each a pass over the int32 index array (HBM/L2-bound, a
+// few microseconds at the benchmark sizes):
+//   1. per-chunk expert histograms (1024 pairs per CTA, shared-memory atomics)
+//   2. one CTA: per-expert prefix over chunks, padded group offsets, and the
+//      list of row-blocks (<= block_n rows of one expert) the GEMMs iterate
+//   3. per chunk: stable rank of each pair among equal experts (warp
+//      match_any + per-warp counts), scatter of rows/pair_pos, and the copy of
+//      x[token] into its padded row (optionally in the tensor-core K order).
+#include "klc_common.cuh"
+#include "permute.cuh"
+
+namespace klc {
+
+namespace {
+
+constexpr int kChunk = 1024;
+
+__global__ void __launch_bounds__(kChunk)
+    hist_kernel(const int32_t* __restrict__ idx, int64_t pairs, int experts, int32_t* __restrict__ chunk_hist) {
+  extern __shared__ int32_t hist[];
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const int64_t p = int64_t(blockIdx.x) * kChunk + threadIdx.x;
+  if (p < pairs) {
+    const int e = idx[p];
+    if (e >= 0 && e < experts) atomicAdd(&hist[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < experts; e += blockDim.x) chunk_hist[int64_t(blockIdx.x) * experts + e] = hist[e];
+}
+
+// exclusive scan over a 1024-thread block; returns the block total in *total
+__device__ int block_exclusive_scan(int v, int* tmp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) tmp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = (lane < int(blockDim.x >> 5)) ? tmp[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    tmp[lane] = wi - w;  // exclusive warp prefix
+    if (lane == 31) tmp[32] = wi;
+  }
+  __syncthreads();
+  const int r = tmp[warp] + incl - v;
+  *total = tmp[32];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(1024)
+    scan_kernel(int32_t* __restrict__ chunk_hist, int nchunks, int experts, int pad, int block_n,
+                int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
+                int4* __restrict__ rowblocks, DeviceStatus* st) {
+  __shared__ int tmp[33];
+  const int e = threadIdx.x;
+  int cnt = 0;
+  if (e < experts) {
+    for (int c = 0; c < nchunks; ++c) {
+      const int h = chunk_hist[int64_t(c) * experts + e];
+      chunk_hist[int64_t(c) * experts + e] = cnt;
+      cnt += h;
+    }
+    counts[e] = cnt;
+  }
+  const int padded = (e < experts) ? (cnt + pad - 1) / pad * pad : 0;
+  int total = 0;
+  const int off = block_exclusive_scan(padded, tmp, &total);
+  if (e < experts) {
+    offsets[e] = off;
+    for (int c = 0; c < nchunks; ++c) chunk_hist[int64_t(c) * experts + e] += off;
+    for (int j = cnt; j < padded; ++j) rows[off + j] = -1;
+  }
+  if (e == 0) offsets[experts] = total;
+  const int nb = (e < experts) ? (cnt + block_n - 1) / block_n : 0;
+  int nblocks = 0;
+  const int base = block_exclusive_scan(nb, tmp, &nblocks);
+  for (int j = 0; j < nb; ++j) {
+    const int r0 = j * block_n;
+    rowblocks[base + j] = make_int4(e, off + r0, min(block_n, cnt - r0), 0);
+  }
+  if (e == 0) st->rowblocks = nblocks;
+}
+
+__global__ void __launch_bounds__(kChunk)
+    scatter_gather_kernel(const int32_t* __restrict__ idx, int64_t pairs, int k, int experts,
+                          const int32_t* __restrict__ chunk_base, int32_t* __restrict__ rows,
+                          int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x, int64_t hidden,
+                          uint16_t* __restrict__ xp, int perm_k, DeviceStatus* st) {
+  extern __shared__ int32_t sm[];
+  int32_t* warp_cnt = sm;                      // [32][experts]
+  int32_t* s_pos = sm + 32 * experts;          // [kChunk]
+  int32_t* s_tok = s_pos + kChunk;             // [kChunk]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < 32 * experts; i += blockDim.x) warp_cnt[i] = 0;
+  const int64_t p = int64_t(blockIdx.x) * kChunk + threadIdx.x;
+  int e = -1;
+  if (p < pairs) {
+    e = idx[p];
+    if (e < 0 || e >= experts) {
+      record_fault(st, KLC_ERR_DEVICE_FAULT, 1, e);
+      e = -1;
+    }
+  }
+  __syncthreads();
+  const unsigned same = __match_any_sync(0xffffffffu, e);
+  const int rank = __popc(same & ((1u << lane) - 1u));
+  if (e >= 0 && rank == 0) warp_cnt[warp * experts + e] = __popc(same);
+  __syncthreads();
+  for (int ex = threadIdx.x; ex < experts; ex += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = warp_cnt[w * experts + ex];
+      warp_cnt[w * experts + ex] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  int pos = -1;
+  if (e >= 0) {
+    pos = chunk_base[int64_t(blockIdx.x) * experts + e] + warp_cnt[warp * experts + e] + rank;
+    rows[pos] = int32_t(p);
+  }
+  if (p < pairs) pair_pos[p] = pos;
+  s_pos[threadIdx.x] = pos;
+  s_tok[threadIdx.x] = (p < pairs) ? int32_t(p / k) : -1;
+  __syncthreads();
+  if (xp == nullptr) return;
+  const int chunks = int(hidden / 8);
+  for (int i = warp; i < kChunk; i += 32) {
+    const int dst = s_pos[i];
+    if (dst < 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(s_tok[i]) * hidden);
+    uint4* out = reinterpret_cast<uint4*>(xp + int64_t(dst) * hidden);
+    for (int c = lane; c < chunks; c += 32) {
+      uint4 v = src[c];
+      out[c] = perm_k ? perm8_bf16(v) : v;
+    }
+  }
+}
+
+}  // namespace
+
+int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
+  const int64_t pairs = a.tokens * a.k;
+  if (pairs == 0) return KLC_OK;
+  const int nchunks = int((pairs + kChunk - 1) / kChunk);
+  const int E = int(a.experts);
+  hist_kernel<<<nchunks, kChunk, E * sizeof(int32_t), stream>>>(a.idx, pairs, E, a.chunk_hist);
+  KLC_LAUNCH_CHECK("permute hist launch");
+  scan_kernel<<<1, 1024, 0, stream>>>(a.chunk_hist, nchunks, E, a.pad, a.block_n, a.counts, a.offsets, a.rows,
+                                      a.rowblocks, a.status);
+  KLC_LAUNCH_CHECK("permute scan launch");
+  const size_t smem = (size_t(32) * E + 2 * kChunk) * sizeof(int32_t);
+  KLC_CUDA(cudaFuncSetAttribute(scatter_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  scatter_gather_kernel<<<nchunks, kChunk, smem, stream>>>(a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos,
+                                                          a.x, a.hidden, a.xp, a.perm_k, a.status);
+  KLC_LAUNCH_CHECK("permute scatter launch");
+  return KLC_OK;
+}
+
+}  // namespace klc

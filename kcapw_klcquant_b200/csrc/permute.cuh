@@ -1,0 +1,82 @@
+// Internal interfaces shared by the MoE-layer kernels of libklcmoe.
+#pragma once
+
+#include "klc_common.cuh"
+
+namespace klc {
+
+// ---------------------------------------------------------------------------
+// permute
+// ---------------------------------------------------------------------------
+struct PermuteArgs {
+  const int32_t* idx;  // [T, k]
+  int64_t tokens;
+  int k;
+  int64_t experts;
+  int pad;             // rows of each expert group padded to a multiple of this
+  int block_n;         // max rows per row-block
+  int32_t* counts;     // [E]
+  int32_t* offsets;    // [E+1]
+  int32_t* rows;       // [rows_cap]   padded row -> pair id (-1 = padding)
+  int32_t* pair_pos;   // [T*k]        pair id -> padded row
+  int32_t* chunk_hist; // [nchunks*E]  scratch
+  int4* rowblocks;     // [max_rowblocks] (expert, first row, rows, 0)
+  DeviceStatus* status;
+  const uint16_t* x;   // [T, H] or null (no gather)
+  int64_t hidden;
+  uint16_t* xp;        // [rows_cap, H] or null
+  int perm_k;          // 1: write rows in the tensor-core K order
+};
+
+int launch_permute(const PermuteArgs& a, cudaStream_t stream);
+
+int launch_router(const uint16_t* x, int64_t tokens, int64_t hidden, const uint16_t* w, const uint16_t* b,
+                  int64_t experts, int k, const float* adjust, int32_t* out_idx, uint16_t* out_w,
+                  uint16_t* out_logits, cudaStream_t stream);
+
+// ---------------------------------------------------------------------------
+// workspace layout (all offsets 256-byte aligned, status word first)
+// ---------------------------------------------------------------------------
+struct WorkspaceLayout {
+  int64_t pairs, rows_cap, max_rowblocks, nchunks;
+  int pad, block_n;
+  size_t status, counts, offsets, chunk_hist, rows, pair_pos, rowblocks, normsq, xp, gated, y, idx, w, total;
+};
+
+WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffers);
+
+// ---------------------------------------------------------------------------
+// expert kernels
+// ---------------------------------------------------------------------------
+struct ExpertArgs {
+  const klc_moe_weights* wts;
+  int64_t hidden, inter, experts;
+  int k;
+  int precision;
+  const int4* rowblocks;
+  int max_rowblocks;
+  const int32_t* rows;
+  const DeviceStatus* status;  // rowblocks count lives here
+  DeviceStatus* status_rw;
+  const uint16_t* xp;          // [rows_cap, H]
+  void* gated;                 // [rows_cap, I] fp32 (SIMT) or bf16 (TC)
+  uint16_t* y;                 // [rows_cap, H]
+  float* normsq;               // [pairs, 2] or null
+  int64_t rows_cap;
+};
+
+int launch_experts_simt(const ExpertArgs& a, cudaStream_t stream);
+int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream);
+bool tc_path_supported(int64_t hidden, int64_t inter);
+
+// ---------------------------------------------------------------------------
+// optional per-stage CUDA-event timing (klc_stage_timing / klc_stage_times)
+// ---------------------------------------------------------------------------
+enum Stage { kStageStart = 0, kStageRouted = 1, kStagePermuted = 2, kStageGateUp = 3, kStageDown = 4, kStageCombined = 5, kStageCount = 6 };
+void stage_mark(int stage, cudaStream_t stream);
+
+int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,
+                   int64_t hidden, const uint16_t* residual, uint16_t* out, const float* normsq, float* norms,
+                   cudaStream_t stream);
+
+}  // namespace klc

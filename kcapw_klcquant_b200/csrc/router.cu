@@ -1,0 +1,213 @@
+// Fused router: logits GEMV/GEMM + top-k + softmax over the selected experts.
+//
+// Replaces streamed_moe_router.py:269-284 (F.linear in bf16, topk of the
+// fp32 logits, softmax of the selected fp32 scores cast to bf16).
+//
+// One CTA handles kTok tokens.  The tokens' activations sit in shared memory
+// (bf16), each warp streams router rows (E x H bf16, L2-resident after the
+// first CTA) with 16-byte loads and accumulates kTok dot products in fp32;
+// a butterfly reduction finishes each dot product, the bias is added in fp32
+// and the logit is rounded once to bf16.  Then one warp per token runs k
+// rounds of a warp-wide arg-max (value descending, lower index on ties) and a
+// k-way softmax.
+#include "klc_common.cuh"
+
+namespace klc {
+
+namespace {
+
+constexpr int kTok = 8;       // tokens per CTA
+constexpr int kWarps = 8;     // warps per CTA
+constexpr int kMaxK = 8;
+
+// k rounds of a warp-wide arg-max over `row` (value descending, lower index
+// on ties), then softmax over the k selected fp32 scores (max-subtracted,
+// summed in selection order), each weight rounded once to bf16.  With
+// keep_order the row already holds exactly k scores in the wanted order.
+__device__ void select_softmax_warp(const float* row, int experts, int k, bool keep_order, int32_t* out_idx,
+                                    uint16_t* out_w) {
+  const int lane = threadIdx.x & 31;
+  float sel_v[kMaxK];
+  int sel_i[kMaxK];
+  for (int r = 0; r < k; ++r) {
+    if (keep_order) {
+      sel_v[r] = row[r];
+      sel_i[r] = r;
+      continue;
+    }
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int e = lane; e < experts; e += 32) {
+      bool taken = false;
+      for (int q = 0; q < r; ++q) taken |= (sel_i[q] == e);
+      const float v = row[e];
+      // -inf is still selectable; NaN compares false and is only taken when nothing else is left
+      if (!taken && (v > bv || (v == bv && e < bi))) {
+        bv = v;
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (bi == 0x7fffffff) {
+      for (int e = 0; e < experts; ++e) {
+        bool taken = false;
+        for (int q = 0; q < r; ++q) taken |= (sel_i[q] == e);
+        if (!taken) {
+          bi = e;
+          bv = row[e];
+          break;
+        }
+      }
+    }
+    sel_v[r] = bv;
+    sel_i[r] = bi;
+  }
+  if (lane == 0) {
+    float m = sel_v[0];
+    for (int r = 1; r < k; ++r) m = fmaxf(m, sel_v[r]);
+    float ex[kMaxK];
+    float sum = 0.f;
+    for (int r = 0; r < k; ++r) {
+      ex[r] = expf(sel_v[r] - m);
+      sum += ex[r];
+    }
+    for (int r = 0; r < k; ++r) {
+      if (!keep_order) out_idx[r] = sel_i[r];
+      out_w[r] = f32_to_bf16(ex[r] / sum);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kWarps * 32)
+    router_kernel(const uint16_t* __restrict__ x, int64_t tokens, int64_t hidden, const uint16_t* __restrict__ w,
+                  const uint16_t* __restrict__ b, int experts, int k, const float* __restrict__ adjust,
+                  int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem);                                      // [kTok][hidden]
+  float* logit_s = reinterpret_cast<float*>(smem + size_t(kTok) * hidden * 2);          // [kTok][experts]
+  const int64_t t0 = int64_t(blockIdx.x) * kTok;
+  const int ntok = int(tokens - t0 < kTok ? tokens - t0 : kTok);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  // stage activations (16-byte chunks); rows past the end are zero
+  const int chunks_per_row = int(hidden / 8);
+  for (int i = threadIdx.x; i < kTok * chunks_per_row; i += blockDim.x) {
+    const int r = i / chunks_per_row, c = i % chunks_per_row;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < ntok) v = *reinterpret_cast<const uint4*>(x + (t0 + r) * hidden + c * 8);
+    reinterpret_cast<uint4*>(xs + size_t(r) * hidden)[c] = v;
+  }
+  __syncthreads();
+
+  for (int e = warp; e < experts; e += kWarps) {
+    float acc[kTok];
+#pragma unroll
+    for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
+    const uint16_t* wr = w + int64_t(e) * hidden;
+    for (int c = lane; c < chunks_per_row; c += 32) {
+      const uint4 wv = ldg_nc_v4(wr + c * 8);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      float wf[8];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        wf[2 * j] = __uint_as_float(ww[j] << 16);
+        wf[2 * j + 1] = __uint_as_float(ww[j] & 0xffff0000u);
+      }
+#pragma unroll
+      for (int t = 0; t < kTok; ++t) {
+        const uint4 xv = reinterpret_cast<const uint4*>(xs + size_t(t) * hidden)[c];
+        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[t] = fmaf(wf[2 * j], __uint_as_float(xx[j] << 16), acc[t]);
+          acc[t] = fmaf(wf[2 * j + 1], __uint_as_float(xx[j] & 0xffff0000u), acc[t]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < kTok; ++t) acc[t] = warp_sum(acc[t]);
+    if (lane == 0) {
+      const float bias = bf16_to_f32(b[e]);
+      for (int t = 0; t < ntok; ++t) {
+        const uint16_t lb = f32_to_bf16(acc[t] + bias);
+        logit_s[t * experts + e] = bf16_to_f32(lb);
+        if (out_logits) out_logits[(t0 + t) * experts + e] = lb;
+      }
+    }
+  }
+  __syncthreads();
+
+  // top-k + softmax: one warp per token
+  for (int t = warp; t < ntok; t += kWarps) {
+    float* row = logit_s + t * experts;
+    if (adjust) {
+      for (int e = lane; e < experts; e += 32) row[e] += adjust[e];
+    }
+    __syncwarp();
+    select_softmax_warp(row, experts, k, false, out_idx + (t0 + t) * k, out_w + (t0 + t) * k);
+  }
+}
+
+__global__ void select_kernel(const float* __restrict__ scores, int64_t tokens, int experts, int k, int keep_order,
+                              int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  (void)lane;
+  select_softmax_warp(scores + t * experts, experts, k, keep_order != 0, out_idx + t * k, out_w + t * k);
+}
+
+}  // namespace
+
+int launch_router(const uint16_t* x, int64_t tokens, int64_t hidden, const uint16_t* w, const uint16_t* b,
+                  int64_t experts, int k, const float* adjust, int32_t* out_idx, uint16_t* out_w,
+                  uint16_t* out_logits, cudaStream_t stream) {
+  KLC_CHECK_ARG(tokens >= 0 && hidden > 0 && experts > 0, "klc_router_topk: bad sizes");
+  KLC_CHECK_ARG(hidden % 8 == 0, "klc_router_topk: hidden must be a multiple of 8");
+  KLC_CHECK_ARG(k >= 1 && k <= kMaxK && k <= experts, "klc_router_topk: need 1 <= k <= min(8, experts)");
+  KLC_CHECK_ARG(experts <= 1024, "klc_router_topk: at most 1024 experts");
+  if (tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(x && w && b && out_idx && out_w, "klc_router_topk: null pointer");
+  KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
+                "klc_router_topk: x and w must be 16-byte aligned");
+  const size_t smem = size_t(kTok) * hidden * 2 + size_t(kTok) * experts * 4;
+  KLC_CHECK_ARG(smem <= 200 * 1024, "klc_router_topk: hidden size too large for one CTA tile");
+  KLC_CUDA(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const int64_t grid = (tokens + kTok - 1) / kTok;
+  KLC_CHECK_ARG(grid <= 0x7fffffff, "klc_router_topk: too many tokens");
+  router_kernel<<<unsigned(grid), kWarps * 32, smem, stream>>>(x, tokens, hidden, w, b, int(experts), k, adjust,
+                                                               out_idx, out_w, out_logits);
+  KLC_LAUNCH_CHECK("klc_router_topk launch");
+  return KLC_OK;
+}
+
+}  // namespace klc
+
+extern "C" int klc_select_softmax(const float* scores, int64_t tokens, int64_t experts, int k, int keep_order,
+                                  int32_t* out_idx, uint16_t* out_w, void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(tokens >= 0 && experts >= 1 && k >= 1 && k <= 8 && k <= experts, "klc_select_softmax: bad sizes");
+  KLC_CHECK_ARG(!keep_order || experts == k, "klc_select_softmax: keep_order needs experts == k");
+  if (tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(scores && out_w && (keep_order || out_idx), "klc_select_softmax: null pointer");
+  const int64_t blocks = (tokens + 7) / 8;
+  KLC_CHECK_ARG(blocks <= 0x7fffffff, "klc_select_softmax: too many tokens");
+  select_kernel<<<unsigned(blocks), 256, 0, as_stream(stream)>>>(scores, tokens, int(experts), k, keep_order, out_idx, out_w);
+  KLC_LAUNCH_CHECK("klc_select_softmax launch");
+  return KLC_OK;
+}
+
+extern "C" int klc_router_topk(const uint16_t* x, int64_t tokens, int64_t hidden, const uint16_t* w,
+                               const uint16_t* b, int64_t experts, int k, const float* adjust, int32_t* out_idx,
+                               uint16_t* out_w, uint16_t* out_logits, void* stream) {
+  return klc::launch_router(x, tokens, hidden, w, b, experts, k, adjust, out_idx, out_w, out_logits,
+                            klc::as_stream(stream));
+}

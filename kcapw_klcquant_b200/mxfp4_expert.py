@@ -1,0 +1,378 @@
+"""MXFP4 expert weights on the device: drop-in for klcquant's mxfp4_expert module.
+
+Mirrors the public surface of the reference module (klcquant mxfp4_expert.py):
+
+* ``FP4_VALUES`` (:17-34)
+* ``dequantize_mxfp4_matrix(blocks, scales, dtype)`` (:357-379), computed by
+  the ``klc_mxfp4_dequant`` CUDA kernel (bit-exact, same ValueError on shape
+  mismatch);
+* ``ExpertCacheStats`` (:37-65) and ``Mxfp4ExpertStore`` (:382-531) with the
+  same constructor and methods.
+
+Design difference (B200-first): the reference materialises one dense bf16
+[in, out] matrix per (layer, expert, projection) on a cache miss (safetensors
+read, pinned H2D copy, device sync, dequant).  Here a layer's packed MXFP4
+tensors (13.2 MB per expert instead of 49.8 MB dense bf16) are loaded to HBM
+once and stay resident; the expert kernels dequantize on the fly.  The dense
+``load_expert_matrix`` API is kept for callers that want it and goes through
+the same dequant kernel with a byte-bounded cache whose statistics keep the
+reference's field names.
+"""
+from __future__ import annotations
+
+import json
+import threading
+import time
+from collections import OrderedDict
+from dataclasses import dataclass, field
+from pathlib import Path
+
+import torch
+
+from . import _lib
+
+FP4_VALUES = [+0.0, +0.5, +1.0, +1.5, +2.0, +3.0, +4.0, +6.0, -0.0, -0.5, -1.0, -1.5, -2.0, -3.0, -4.0, -6.0]
+
+
+def dequantize_mxfp4_matrix(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtype = torch.float16) -> torch.Tensor:
+    """Dequantize one GPT-OSS MXFP4 expert matrix on the GPU.
+
+    ``blocks`` uint8 [out_dim, groups, 16] (two E2M1 values per byte, low
+    nibble first), ``scales`` uint8 [out_dim, groups] (E8M0).  Returns the
+    [in_dim, out_dim] matrix (in_dim = groups * 32) in ``dtype``, bit-identical
+    to the reference's ``dequantize_mxfp4_matrix`` (mxfp4_expert.py:357-379).
+    """
+    if blocks.shape[:-1] != scales.shape:
+        raise ValueError(f"MXFP4 block/scale shape mismatch: {blocks.shape=} {scales.shape=}")
+    if dtype not in _lib.DTYPE_CODE:
+        raise ValueError(f"unsupported output dtype {dtype}")
+    if blocks.dim() != 3 or blocks.shape[-1] != 16:
+        raise ValueError(f"MXFP4 blocks must be [out_dim, groups, 16], got {tuple(blocks.shape)}")
+    blocks = blocks.to(torch.uint8).contiguous()
+    scales = scales.to(torch.uint8).contiguous()
+    _lib.require_cuda(blocks, scales)
+    out_dim, groups, _ = blocks.shape
+    out = torch.empty((groups * 32, out_dim), dtype=dtype, device=blocks.device)
+    with torch.cuda.device(blocks.device):
+        _lib.check(
+            _lib.lib().klc_mxfp4_dequant(
+                blocks.data_ptr(), scales.data_ptr(), out_dim, groups, out.data_ptr(), _lib.DTYPE_CODE[dtype], _lib.stream_ptr()
+            )
+        )
+    return out
+
+
+def transpose_scales(scales: torch.Tensor) -> torch.Tensor:
+    """E8M0 scales [E, rows, groups] -> [E, groups, rows] (the expert kernels' layout)."""
+    scales = scales.to(torch.uint8).contiguous()
+    _lib.require_cuda(scales)
+    E, rows, groups = scales.shape
+    out = torch.empty((E, groups, rows), dtype=torch.uint8, device=scales.device)
+    with torch.cuda.device(scales.device):
+        _lib.check(_lib.lib().klc_mxfp4_transpose_scales(scales.data_ptr(), E, rows, groups, out.data_ptr(), _lib.stream_ptr()))
+    return out
+
+
+@dataclass
+class PackedLayer:
+    """One layer's expert weights resident on the device (packed MXFP4)."""
+
+    gu_blocks: torch.Tensor    # uint8 [E, 2I, H/32, 16]
+    gu_scales_t: torch.Tensor  # uint8 [E, H/32, 2I]
+    dn_blocks: torch.Tensor    # uint8 [E, H, I/32, 16]
+    dn_scales_t: torch.Tensor  # uint8 [E, I/32, H]
+    gu_scales: torch.Tensor | None = None  # original [E, 2I, H/32] (kept for load_expert_matrix)
+    dn_scales: torch.Tensor | None = None
+
+    @property
+    def experts(self) -> int:
+        return int(self.gu_blocks.shape[0])
+
+    @property
+    def hidden(self) -> int:
+        return int(self.gu_blocks.shape[2]) * 32
+
+    @property
+    def intermediate(self) -> int:
+        return int(self.dn_blocks.shape[2]) * 32
+
+    @property
+    def nbytes(self) -> int:
+        return sum(t.numel() for t in (self.gu_blocks, self.gu_scales_t, self.dn_blocks, self.dn_scales_t))
+
+    @classmethod
+    def from_checkpoint_tensors(
+        cls, gu_blocks: torch.Tensor, gu_scales: torch.Tensor, dn_blocks: torch.Tensor, dn_scales: torch.Tensor, device: torch.device
+    ) -> "PackedLayer":
+        def dev(t):
+            return t.to(device=device, dtype=torch.uint8, non_blocking=True).contiguous()
+
+        gb, gs, db, ds = dev(gu_blocks), dev(gu_scales), dev(dn_blocks), dev(dn_scales)
+        E, two_i, g_h, _ = gb.shape
+        if gs.shape != (E, two_i, g_h) or db.shape[0] != E or ds.shape != db.shape[:3]:
+            raise ValueError(f"inconsistent MXFP4 layer shapes {gb.shape} {gs.shape} {db.shape} {ds.shape}")
+        if db.shape[1] != g_h * 32 or db.shape[2] * 64 != two_i:
+            raise ValueError("down_proj must be [E, H, I/32, 16] with gate_up [E, 2I, H/32, 16]")
+        return cls(gb, transpose_scales(gs), db, transpose_scales(ds), gs, ds)
+
+
+@dataclass
+class ExpertCacheStats:
+    """Same fields as the reference's ExpertCacheStats (mxfp4_expert.py:37-65)."""
+
+    hits: int = 0
+    misses: int = 0
+    evictions: int = 0
+    loaded_bytes: int = 0
+    dequantized_bytes: int = 0
+    hit_bytes: int = 0
+    miss_loaded_bytes: int = 0
+    pinned_hits: int = 0
+    lifetime_accesses: int = 0
+    materializations: int = 0
+    materialization_time_s: float = 0.0
+    transfer_time_s: float = 0.0
+    dequant_time_s: float = 0.0
+    blocked_on_prefetch_s: float = 0.0
+    futures_waited: int = 0
+    prefetch_submitted: int = 0
+    prefetch_completed: int = 0
+    prefetch_failed: int = 0
+    prefetch_used: int = 0
+    prefetch_skipped_resident: int = 0
+    prefetch_skipped_pending: int = 0
+    protected_eviction_skips: int = 0
+
+    @property
+    def hit_rate(self) -> float:
+        total = self.hits + self.misses
+        return self.hits / total if total else 0.0
+
+
+class DenseMatrixCache:
+    """Byte-bounded LRU of dense dequantized matrices, keyed (layer, expert, proj).
+
+    Only ``load_expert_matrix`` uses it; the fused expert kernels read packed
+    weights directly and never touch it.  Pinned keys are never evicted.
+    """
+
+    def __init__(self, max_bytes: int) -> None:
+        self.max_bytes = int(max_bytes)
+        self.items: OrderedDict[tuple[int, int, str], torch.Tensor] = OrderedDict()
+        self.pinned: set[tuple[int, int, str]] = set()
+        self.current_bytes = 0
+        self.stats = ExpertCacheStats()
+        self.lock = threading.RLock()
+
+    def get(self, key):
+        with self.lock:
+            self.stats.lifetime_accesses += 1
+            v = self.items.get(key)
+            if v is None:
+                self.stats.misses += 1
+                return None
+            self.items.move_to_end(key)
+            self.stats.hits += 1
+            self.stats.hit_bytes += v.numel() * v.element_size()
+            if key in self.pinned:
+                self.stats.pinned_hits += 1
+            return v
+
+    def put(self, key, value: torch.Tensor) -> None:
+        nbytes = value.numel() * value.element_size()
+        self.stats.dequantized_bytes += nbytes
+        if self.max_bytes <= 0:
+            return
+        with self.lock:
+            old = self.items.pop(key, None)
+            if old is not None:
+                self.current_bytes -= old.numel() * old.element_size()
+            self.items[key] = value
+            self.current_bytes += nbytes
+            for victim in list(self.items):
+                if self.current_bytes <= self.max_bytes:
+                    break
+                if victim in self.pinned or victim == key:
+                    continue
+                t = self.items.pop(victim)
+                self.current_bytes -= t.numel() * t.element_size()
+                self.stats.evictions += 1
+
+    def contains(self, key) -> bool:
+        with self.lock:
+            return key in self.items
+
+    def to_json(self) -> dict:
+        s = self.stats
+        return {
+            "hits": s.hits,
+            "misses": s.misses,
+            "hit_rate": s.hit_rate,
+            "pinned_hits": s.pinned_hits,
+            "evictions": s.evictions,
+            "resident_bytes": self.current_bytes,
+            "resident_mb": round(self.current_bytes / 2**20, 6),
+            "resident_items": len(self.items),
+            "pinned_items": len(self.pinned),
+            "loaded_bytes": s.loaded_bytes,
+            "loaded_mb": round(s.loaded_bytes / 2**20, 6),
+            "dequantized_bytes": s.dequantized_bytes,
+            "dequantized_mb": round(s.dequantized_bytes / 2**20, 6),
+            "hit_bytes": s.hit_bytes,
+            "materializations": s.materializations,
+            "materialization_time_s": round(s.materialization_time_s, 6),
+            "transfer_time_s": round(s.transfer_time_s, 6),
+            "dequant_time_s": round(s.dequant_time_s, 6),
+        }
+
+
+def _read_weight_map(support_dir: Path) -> dict[str, str]:
+    index = support_dir / "model.safetensors.index.json"
+    return json.loads(index.read_text())["weight_map"]
+
+
+class Mxfp4ExpertStore:
+    """Device-resident MXFP4 expert store with the reference's constructor and methods.
+
+    ``layer(layer_idx)`` returns the packed :class:`PackedLayer` the fused
+    kernels consume; it is loaded from the checkpoint (reference safetensors
+    layout, ``model.layers.{L}.mlp.experts.{gate_up_proj,down_proj}_{blocks,scales}``)
+    on first use, for all experts of the layer at once.
+    """
+
+    def __init__(
+        self,
+        model_dir: str | Path | None,
+        support_dir: str | Path | None,
+        device: torch.device | str,
+        dtype: torch.dtype = torch.float16,
+        cache_bytes: int = 0,
+        quant_loader=None,
+        async_prefetch: bool = False,
+        max_prefetch_workers: int = 1,
+        layer_count: int = 0,
+        layer_aware_cache: bool = False,
+        adaptive_layer_quota: bool = False,
+        adaptive_layer_quota_strength: float = 1.5,
+        default_protect_window: int = 64,
+    ) -> None:
+        self.model_dir = Path(model_dir) if model_dir is not None else None
+        self.support_dir = Path(support_dir) if support_dir is not None else None
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("Mxfp4ExpertStore keeps experts in GPU memory; pass a CUDA device")
+        self.dtype = dtype
+        self.quant_loader = quant_loader
+        self.async_prefetch = async_prefetch
+        self.default_protect_window = max(int(default_protect_window), 1)
+        self.cache = DenseMatrixCache(cache_bytes)
+        self.weight_map = _read_weight_map(self.support_dir) if self.support_dir is not None else {}
+        self.layers: dict[int, PackedLayer] = {}
+        self.protected: dict[int, set[int]] = {}
+        self._lock = threading.RLock()
+
+    # -- construction from in-memory tensors (synthetic layers, benchmarks) --
+    @classmethod
+    def from_layers(cls, layers: dict[int, dict[str, torch.Tensor]], device: torch.device | str, dtype: torch.dtype = torch.bfloat16) -> "Mxfp4ExpertStore":
+        store = cls(None, None, device, dtype=dtype)
+        for layer_idx, tensors in layers.items():
+            store.add_layer(layer_idx, tensors)
+        return store
+
+    def add_layer(self, layer_idx: int, tensors: dict[str, torch.Tensor]) -> PackedLayer:
+        p = f"model.layers.{layer_idx}.mlp.experts"
+        packed = PackedLayer.from_checkpoint_tensors(
+            tensors[f"{p}.gate_up_proj_blocks"], tensors[f"{p}.gate_up_proj_scales"],
+            tensors[f"{p}.down_proj_blocks"], tensors[f"{p}.down_proj_scales"], self.device,
+        )
+        with self._lock:
+            self.layers[int(layer_idx)] = packed
+        return packed
+
+    # -- packed access used by the fused path --
+    def layer(self, layer_idx: int) -> PackedLayer:
+        with self._lock:
+            packed = self.layers.get(int(layer_idx))
+        if packed is not None:
+            return packed
+        start = time.perf_counter()
+        names = {k: f"model.layers.{layer_idx}.mlp.experts.{k}" for k in ("gate_up_proj_blocks", "gate_up_proj_scales", "down_proj_blocks", "down_proj_scales")}
+        loaded = {k: self._load_tensor(n) for k, n in names.items()}
+        nbytes = sum(t.numel() for t in loaded.values())
+        self.cache.stats.loaded_bytes += nbytes
+        self.cache.stats.miss_loaded_bytes += nbytes
+        t0 = time.perf_counter()
+        packed = PackedLayer.from_checkpoint_tensors(
+            loaded["gate_up_proj_blocks"], loaded["gate_up_proj_scales"], loaded["down_proj_blocks"], loaded["down_proj_scales"], self.device
+        )
+        self.cache.stats.transfer_time_s += time.perf_counter() - t0
+        self.cache.stats.materialization_time_s += time.perf_counter() - start
+        with self._lock:
+            self.layers[int(layer_idx)] = packed
+        return packed
+
+    def _load_tensor(self, name: str) -> torch.Tensor:
+        if self.quant_loader is not None and name in self.quant_loader.tensor_index:
+            full, meta = self.quant_loader.load_tensor(name, dtype=self.dtype)
+            if meta.dtype == "torch.uint8":
+                return torch.clamp(torch.round(full.float()), 0, 255).to(torch.uint8)
+            return full
+        if self.model_dir is None:
+            raise KeyError(f"{name}: layer not added and no checkpoint directory")
+        from safetensors import safe_open
+
+        shard = self.weight_map[name]
+        with safe_open(str(self.model_dir / shard), framework="pt", device="cpu") as handle:
+            return handle.get_tensor(name)
+
+    # -- reference API --
+    def load_expert_matrix(self, layer_idx: int, expert_idx: int, proj: str) -> torch.Tensor:
+        key = (int(layer_idx), int(expert_idx), proj)
+        cached = self.cache.get(key)
+        if cached is not None:
+            return cached
+        packed = self.layer(layer_idx)
+        start = time.perf_counter()
+        if proj == "gate_up_proj":
+            blocks, scales = packed.gu_blocks[expert_idx], packed.gu_scales[expert_idx]
+        elif proj == "down_proj":
+            blocks, scales = packed.dn_blocks[expert_idx], packed.dn_scales[expert_idx]
+        else:
+            raise KeyError(proj)
+        matrix = dequantize_mxfp4_matrix(blocks, scales, self.dtype)
+        self.cache.stats.dequant_time_s += time.perf_counter() - start
+        self.cache.stats.materializations += 1
+        self.cache.put(key, matrix)
+        return matrix
+
+    def protect_experts(self, layer_idx: int, expert_ids: list[int], protect_window: int | None = None) -> None:
+        with self._lock:
+            self.protected.setdefault(int(layer_idx), set()).update(int(e) for e in expert_ids)
+
+    def prefetch_experts(self, layer_idx: int, expert_ids: list[int], protect_window: int | None = None) -> None:
+        """Packed weights of a layer are resident once loaded; prefetch loads the layer."""
+        if not expert_ids:
+            return
+        if int(layer_idx) in self.layers:
+            self.cache.stats.prefetch_skipped_resident += len(expert_ids)
+            return
+        self.cache.stats.prefetch_submitted += 1
+        self.layer(layer_idx)
+        self.cache.stats.prefetch_completed += 1
+
+    def resident_experts(self, layer_idx: int) -> set[int]:
+        """Experts whose weights are in device memory (all of a loaded layer)."""
+        packed = self.layers.get(int(layer_idx))
+        return set(range(packed.experts)) if packed is not None else set()
+
+    def pin_experts(self, keys: list[tuple[int, int, str]]) -> None:
+        for layer_idx, expert_idx, proj in keys:
+            self.load_expert_matrix(layer_idx, expert_idx, proj)
+            self.cache.pinned.add((int(layer_idx), int(expert_idx), proj))
+
+    def to_json(self) -> dict:
+        payload = self.cache.to_json()
+        payload["pending_prefetches"] = 0
+        payload["packed_layers"] = sorted(self.layers)
+        payload["packed_resident_bytes"] = sum(p.nbytes for p in self.layers.values())
+        return payload

@@ -240,14 +240,15 @@ def expert_forward(
     x = bf16_bits_to_f32(x_bits)
     bgu = bf16_bits_to_f32(b_gate_up_bits)
     bd = bf16_bits_to_f32(b_down_bits)
+    # fp32 GEMV/GEMM with fp32 accumulation (BLAS), as the reference's torch CPU matmuls
     if precision == "bf16":
-        gu = round_bf16(x.astype(np.float64) @ w_gate_up.astype(np.float64)) + bgu
+        gu = round_bf16(x @ w_gate_up) + bgu
         gated = apply_gate(gu, limit, alpha)
-        out = round_bf16(round_bf16(gated).astype(np.float64) @ w_down.astype(np.float64)) + bd
+        out = round_bf16(round_bf16(gated) @ w_down) + bd
     else:
-        gu = (x.astype(np.float64) @ w_gate_up.astype(np.float64)).astype(np.float32) + bgu
+        gu = (x @ w_gate_up) + bgu
         gated = apply_gate(gu, limit, alpha)
-        out = (gated.astype(np.float64) @ w_down.astype(np.float64)).astype(np.float32) + bd
+        out = (gated @ w_down) + bd
     return gu.astype(np.float32), gated, out.astype(np.float32)
 
 

@@ -1,0 +1,92 @@
+"""CPU-side checks of the C ABI: the library loads, exports every declared
+symbol, and validates arguments on the host before touching a GPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from kcapw_klcquant_b200 import _lib
+from tests.conftest import REPO
+
+HEADER = REPO / "include" / "klc_moe.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(klc_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    names = declared_functions()
+    assert len(names) >= 15, names
+    for n in names:
+        assert hasattr(L, n), f"libklcmoe.so does not export {n}"
+    assert L.klc_version() >= 1
+
+
+def test_python_signatures_cover_header():
+    names = set(declared_functions())
+    assert names - {"klc_last_error"} <= set(_lib.SIGNATURES), names - set(_lib.SIGNATURES)
+
+
+def _status_and_msg(st):
+    return st, _lib.lib().klc_last_error().decode()
+
+
+def test_host_validation_without_gpu():
+    L = _lib.lib()
+    st, msg = _status_and_msg(L.klc_mxfp4_dequant(None, None, -1, 3, None, 0, None))
+    assert st == _lib.KLC_ERR_INVALID and "negative" in msg
+    st, msg = _status_and_msg(L.klc_mxfp4_dequant(None, None, 0, 0, None, 0, None))
+    assert st == _lib.KLC_OK  # empty matrix is a no-op
+    st, msg = _status_and_msg(L.klc_router_topk(None, 4, 2880, None, None, 128, 9, None, None, None, None, None))
+    assert st == _lib.KLC_ERR_INVALID and "k" in msg
+    st, msg = _status_and_msg(L.klc_runtime_dequant(7, None, 0, None, None, 0, 4, 10, None, 0, None))
+    assert st == _lib.KLC_ERR_INVALID
+    st, msg = _status_and_msg(L.klc_runtime_dequant(1, None, 0, None, None, 0, 4, 10, ctypes.c_void_p(16), 0, None))
+    assert st == _lib.KLC_ERR_INVALID and "scale" in msg
+
+
+def test_check_maps_invalid_to_value_error():
+    L = _lib.lib()
+    with pytest.raises(ValueError):
+        _lib.check(L.klc_mxfp4_dequant(None, None, -1, 3, None, 0, None))
+
+
+@pytest.mark.parametrize("path", ["simt", "tc", "auto"])
+def test_workspace_size_grows_with_tokens(path):
+    L = _lib.lib()
+    sizes = []
+    for T in (1, 8, 256, 4096):
+        d = _lib.KlcDims(T, 2880, 2880, 128, 4, _lib.PATH_CODE[path])
+        n = ctypes.c_size_t(0)
+        _lib.check(L.klc_moe_workspace_size(ctypes.byref(d), ctypes.byref(n)))
+        sizes.append(n.value)
+    assert sizes == sorted(sizes) and sizes[0] > 0
+    # the permuted activations, intermediate and expert outputs dominate: ~T*k rows
+    assert sizes[-1] > 4096 * 4 * 2880 * 2 * 3
+
+
+def test_workspace_rejects_bad_dims():
+    L = _lib.lib()
+    n = ctypes.c_size_t(0)
+    for d in (
+        _lib.KlcDims(8, 2880, 2880, 128, 9, 0),   # k > 8
+        _lib.KlcDims(8, 2881, 2880, 128, 4, 0),   # hidden not a multiple of 64
+        _lib.KlcDims(8, 2880, 2880, 0, 4, 0),     # no experts
+        _lib.KlcDims(-1, 2880, 2880, 128, 4, 0),  # negative tokens
+        _lib.KlcDims(8, 2880, 2880, 128, 4, 5),   # unknown path
+    ):
+        assert L.klc_moe_workspace_size(ctypes.byref(d), ctypes.byref(n)) == _lib.KLC_ERR_INVALID
+
+
+def test_experts_reject_small_workspace():
+    L = _lib.lib()
+    d = _lib.KlcDims(8, 128, 128, 8, 2, 1)
+    w = _lib.KlcWeights(16, 16, 16, 16, 16, 16, 16, 16, 7.0, 1.702)
+    st = L.klc_moe_experts(ctypes.byref(d), ctypes.byref(w), 16, 16, 16, 0, 16, None, None, 256, 64, None)
+    assert st == _lib.KLC_ERR_WORKSPACE
