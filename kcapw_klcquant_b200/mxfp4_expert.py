@@ -273,8 +273,9 @@ class Mxfp4ExpertStore:
 
     # -- construction from in-memory tensors (synthetic layers, benchmarks) --
     @classmethod
-    def from_layers(cls, layers: dict[int, dict[str, torch.Tensor]], device: torch.device | str, dtype: torch.dtype = torch.bfloat16) -> "Mxfp4ExpertStore":
-        store = cls(None, None, device, dtype=dtype)
+    def from_layers(cls, layers: dict[int, dict[str, torch.Tensor]], device: torch.device | str, dtype: torch.dtype = torch.bfloat16,
+                    cache_bytes: int = 0) -> "Mxfp4ExpertStore":
+        store = cls(None, None, device, dtype=dtype, cache_bytes=cache_bytes)
         for layer_idx, tensors in layers.items():
             store.add_layer(layer_idx, tensors)
         return store

@@ -201,8 +201,9 @@ def test_experts_replay_vs_reference(case_cache, name, precision, path):
     ml.check_device_status()
     m = parity.assert_output_close(bits_of(y), fx[f"out_{precision}"], f"{name}/{precision}/{path}")
     if path == "simt":
-        # fp32 CUDA-core math: within a few bf16 ulps of the reference everywhere
-        assert parity.ulp_distance_bf16(bits_of(y), fx[f"out_{precision}"]).max() <= 8, m
+        # fp32 CUDA-core math: only the summation order differs from the
+        # reference, so almost every output is bit-identical
+        assert m["bit_equal_frac"] >= 0.99, m
     np.testing.assert_allclose(norms.cpu().numpy(), fx[f"norms_{precision}"], rtol=5e-3 if path == "tc" else 1e-4)
 
 
@@ -214,8 +215,13 @@ def test_forward_end_to_end(case_cache, name, path):
     y, rb = ml.forward(x.to(DEV), precision="bf16", return_logits=True, path=path)
     ml.check_device_status()
     got_logits = bits_of(rb.logits)
-    same = np.all(got_logits == fx["logits"], axis=1) & np.all(np.sort(rb.indices.cpu().numpy(), 1) == np.sort(fx["experts_bf16"], 1), axis=1)
-    assert same.mean() >= 0.9
+    got_idx = rb.indices.cpu().numpy()
+    parity.check_selection(got_logits, got_idx, dims.top_k)
+    equal_logits = np.all(got_logits == fx["logits"], axis=1)
+    parity.same_selection_modulo_ties(fx["logits"][equal_logits], fx["experts_bf16"][equal_logits], got_idx[equal_logits], dims.top_k)
+    same = equal_logits & np.all(np.sort(got_idx, 1) == np.sort(fx["experts_bf16"], 1), axis=1)
+    if not name.startswith("tie"):  # exact ties may legitimately pick another member of the tied class
+        assert same.mean() >= 0.9
     parity.assert_output_close(bits_of(y)[same], fx["out_bf16"][same], f"{name}/{path}")
 
 
@@ -263,7 +269,7 @@ def test_store_load_expert_matrix_matches_dequant(case_cache):
     from kcapw_klcquant_b200 import Mxfp4ExpertStore
 
     fx, dims, layer, x, ml = load(case_cache, "mini_e16_h256_t32")
-    store = Mxfp4ExpertStore.from_layers({0: layer}, DEV, dtype=torch.bfloat16)
+    store = Mxfp4ExpertStore.from_layers({0: layer}, DEV, dtype=torch.bfloat16, cache_bytes=1 << 30)
     m = store.load_expert_matrix(0, 3, "gate_up_proj")
     ref = orc.dequantize_mxfp4_bits(cases.bits(layer["model.layers.0.mlp.experts.gate_up_proj_blocks"][3]),
                                     cases.bits(layer["model.layers.0.mlp.experts.gate_up_proj_scales"][3]), "bf16")
