@@ -152,6 +152,24 @@ int klc_moe_experts(const klc_moe_dims* dims, const klc_moe_weights* wts, const 
                     const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of klc_moe_experts (no counterpart in the
+ * reference).  For callers that cannot allocate device memory themselves --
+ * e.g. a host runtime reaching this library through an FFI without a CUDA
+ * allocator, or an application whose device memory belongs to another pool.
+ * Same arguments as klc_moe_experts minus the workspace; the scratch is a
+ * static 16 MiB device array inside the library (held by every GPU that
+ * loads it until the process exits; klc_moe_noalloc_scratch_bytes reports
+ * the size).  Always runs the CUDA-core expert kernels.  A batch whose
+ * scratch would exceed the array is rejected with KLC_ERR_INVALID.  The first
+ * call on a device looks up the array's address (cudaGetSymbolAddress): make
+ * it before any stream capture on that device.  All calls on a device share
+ * the array, so calls that overlap on the GPU race: serialise them.  Calls no
+ * cudaMalloc/cudaFree or allocating library routine.                       */
+int klc_moe_experts_noalloc(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x, const int32_t* idx,
+                            const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
+                            void* stream);
+int klc_moe_noalloc_scratch_bytes(size_t* out_bytes);
+
 /* Router + experts + combine in one call (StreamedMoERouter.route batched).
  * out_idx/out_w receive the routing (int32 [T,k], bf16 [T,k]); out_logits
  * bf16 [T,E] or NULL; adjust fp32 [E] or NULL.                            */
