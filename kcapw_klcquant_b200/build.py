@@ -66,7 +66,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     objs = [BUILD / (s.stem + ".o") for s in sources]
     if todo or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
-        cmd = [exe, *ARCH, "-shared", "-o", str(tmp), *map(str, objs), "-lcuda"]
+        cmd = [exe, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

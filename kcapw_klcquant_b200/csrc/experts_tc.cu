@@ -1,12 +1,620 @@
-// tcgen05 grouped expert GEMM (placeholder until the tensor-core path lands).
+// Tensor-core grouped expert GEMMs for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Both expert GEMMs of the reference's _execute_mxfp4_experts
+// (streamed_moe_router.py:500-511) for every (expert, row-block) of the
+// permuted tokens, with the bias and the clamped SwiGLU (:524-529) fused
+// into the epilogue.  "Swap-AB" orientation: the weights are the MMA's A
+// operand (M = 128 output features of one expert), the tokens of a
+// row-block are B (N = up to 256 rows), K is the reduction (H for gate_up,
+// I for down).  One persistent CTA per SM walks the (row-block, m-tile)
+// work list.
+//
+// Per CTA, warp-specialised:
+//   warp 0      TMA producer: packed E2M1 nibbles (128 rows x 32 B, 32B
+//               swizzle) + E8M0 scales (2 groups x 128 rows) into an A ring,
+//               token rows (n x 64 bf16, 128B swizzle) into a B ring
+//   warp 1      TMEM allocator and MMA issuer (one thread):
+//               tcgen05.mma.cta_group::1.kind::f16, A from TMEM, B from smem
+//   warps 4-11  two dequant warpgroups (alternating K-steps): one thread per
+//               weight row converts 64 E2M1 values x 2^(s-127) to exact bf16
+//               and writes them straight into a TMEM A stage (tcgen05.st) --
+//               the dequantized weights never touch shared memory
+//   warps 12-15 epilogue: tcgen05.ld of the fp32 accumulators, bias,
+//               SwiGLU (gate_up) or bias (down), bf16 stores
+// Inside every 8-element K chunk the dequant emits the order
+// {0,4,1,5,2,6,3,7} (cheapest bit extraction); the activation rows are
+// written in the same order by the permute/gather and by the gate_up
+// epilogue, so the dot products are unchanged.
+//
+// Every mbarrier wait is bounded by %globaltimer: after kWaitNs the waiting
+// role records KLC_ERR_DEVICE_TIMEOUT in the workspace status word, raises a
+// CTA-wide abort flag, and all roles drain (TMA and MMA completion are
+// awaited, again bounded) before the TMEM is freed and the CTA exits.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "permute.cuh"
 
 namespace klc {
 
-bool tc_path_supported(int64_t, int64_t) { return false; }
+namespace {
 
-int launch_experts_tc(const ExpertArgs&, cudaStream_t) {
-  return fail(KLC_ERR_UNSUPPORTED, "tensor-core expert path not built");
+constexpr int kThreads = 512;
+constexpr int kBM = 128;        // weight rows per tile (MMA M)
+constexpr int kBK = 64;         // K per stage (one 128-byte swizzle atom of bf16)
+constexpr int kNA = 8;          // A ring depth (nibbles + scales)
+constexpr int kNT = 4;          // TMEM A stages
+constexpr int kAColsPerStage = kBK / 2;  // 32-bit TMEM columns per A stage
+constexpr int kNibBytes = kBM * kBK / 2;     // 4096
+constexpr int kScaleBytes = kBM * kBK / 32;  // 256
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+struct Ctl {
+  volatile int* abort;
+  DeviceStatus* status;
+};
+
+// Bounded wait for the completion of phase `parity` of a barrier.  Returns
+// false when the CTA is aborting (this wait timed out or another did).
+__device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31) == 0) {
+      if (*c.abort) return false;
+      if (globaltimer() - t0 > kWaitNs) {
+        *c.abort = 1;
+        record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
+        return false;
+      }
+      __nanosleep(32);
+    }
+  }
+}
+
+// Drain-time wait: bounded, ignores the abort flag.
+__device__ __noinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitNs) return;
+    __nanosleep(64);
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accum));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), leading offset unused (1), descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
+         (uint64_t(2) << 61);
+}
+
+// kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both
+// K-major, M = 128, N = n.
+__device__ __forceinline__ uint32_t make_idesc(int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
+}
+
+// Four bf16x2 words (8 consecutive E2M1 values of a 32-bit nibble word, in
+// the {0,4,1,5,2,6,3,7} order) scaled by 2^(s-127), exact.  The nibble bits
+// are placed as a bf16 of value FP4 * 2^-126 (sign -> bit 15, e2m1 -> bits
+// 8:6) and rescaled by bf16 multiplies with exact powers of two.
+__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t f1, uint32_t f2, bool two, uint32_t* out) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t u = w >> (4 * q);
+    uint32_t r = ((u << 6) & 0x01C001C0u) | ((u << 12) & 0x80008000u);
+    r = bf16x2_mul(r, f1);
+    if (two) r = bf16x2_mul(r, f2);
+    out[q] = r;
+  }
+}
+
+struct TcParams {
+  int n_out;          // weight rows of one expert (2I or H)
+  int k_in;           // reduction length (H or I)
+  int ksteps;         // k_in / kBK
+  int n_mtiles;       // ceil(n_out / 128)
+  const int4* rowblocks;
+  DeviceStatus* status;
+  const int32_t* rows;
+  const uint16_t* bias;  // [E, n_out]
+  uint16_t* out;         // phase 1: [rows_cap, n_out/2] (K-order permuted); phase 2: [rows_cap, n_out]
+  int out_ld;
+  float* normsq;
+  int precision;
+  float limit, alpha;
+};
+
+template <int PHASE, int BN, int NB>
+struct Smem {
+  static constexpr int kND = (BN <= 128) ? 2 : 1;
+  static constexpr int kBStage = BN * kBK * 2;
+  static constexpr int kNib = 0;
+  static constexpr int kScl = kNib + kNA * kNibBytes;
+  static constexpr int kB = kScl + kNA * kScaleBytes;  // 1024-aligned (8*4096 + 8*256 = 34816)
+  static constexpr int kBar = kB + NB * kBStage;
+  static constexpr int kNumBars = 2 * kNA + 2 * NB + 2 * kNT + 2 * kND + 1;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBytes = kMisc + 16;
+};
+
+template <int PHASE, int BN, int NB>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_s,
+                     const __grid_constant__ CUtensorMap map_b, TcParams p) {
+  using S = Smem<PHASE, BN, NB>;
+  constexpr int ND = S::kND;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // TMA destinations and swizzled operand tiles need 1024-byte alignment
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBar);
+  const uint32_t bar0 = smem_u32(bars);
+  auto afull = [&](int s) { return bar0 + 8u * s; };
+  auto aempty = [&](int s) { return bar0 + 8u * (kNA + s); };
+  auto bfull = [&](int s) { return bar0 + 8u * (2 * kNA + s); };
+  auto bempty = [&](int s) { return bar0 + 8u * (2 * kNA + NB + s); };
+  auto tfull = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + s); };
+  auto tempty = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + kNT + s); };
+  auto dfull = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + s); };
+  auto dempty = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + ND + s); };
+  const uint32_t mma_done = bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + 2 * ND);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + S::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kMisc + 4);
+  const Ctl ctl{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kNA; ++s) {
+      mbar_init(afull(s), 1);
+      mbar_init(aempty(s), 4);
+    }
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(bfull(s), 1);
+      mbar_init(bempty(s), 1);
+    }
+    for (int s = 0; s < kNT; ++s) {
+      mbar_init(tfull(s), 4);
+      mbar_init(tempty(s), 1);
+    }
+    for (int s = 0; s < ND; ++s) {
+      mbar_init(dfull(s), 1);
+      mbar_init(dempty(s), 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_holder)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int nrb = p.status->rowblocks;
+  const int total = nrb * p.n_mtiles;
+  const int ks_n = p.ksteps;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int last_a[kNA], last_b[NB];  // latest iteration that loaded each stage (-1: never)
+      for (int s = 0; s < kNA; ++s) last_a[s] = -1;
+      for (int s = 0; s < NB; ++s) last_b[s] = -1;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int mt = item % p.n_mtiles;
+        const int npad = (rb.z + 15) & ~15;
+        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+          const int sa = it % kNA, sb = it % NB;
+          if (!(ok = wait_bar(aempty(sa), ((it / kNA) & 1) ^ 1, ctl, 10))) break;
+          mbar_arrive_expect_tx(afull(sa), kNibBytes + kScaleBytes);
+          tma_load_3d(smem_u32(smem + S::kNib + sa * kNibBytes), &map_a, ks * (kBK / 2), mt * kBM, rb.x, afull(sa));
+          tma_load_3d(smem_u32(smem + S::kScl + sa * kScaleBytes), &map_s, mt * kBM, ks * (kBK / 32), rb.x, afull(sa));
+          last_a[sa] = int(it);
+          if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
+          mbar_arrive_expect_tx(bfull(sb), uint32_t(npad) * kBK * 2);
+          for (int j = 0; j < npad; j += 16)
+            tma_load_2d(smem_u32(smem + S::kB + sb * S::kBStage + j * kBK * 2), &map_b, ks * kBK, rb.y + j, bfull(sb));
+          last_b[sb] = int(it);
+        }
+      }
+      if (!ok) {
+        // aborting: wait (bounded) until no bulk copy still writes shared memory
+        for (int s = 0; s < kNA; ++s)
+          if (last_a[s] >= 0) drain_wait(afull(s), (uint32_t(last_a[s]) / kNA) & 1);
+        for (int s = 0; s < NB; ++s)
+          if (last_b[s] >= 0) drain_wait(bfull(s), (uint32_t(last_b[s]) / NB) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, ic = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int npad = (rb.z + 15) & ~15;
+        const uint32_t idesc = make_idesc(npad);
+        const int d = ic % ND;
+        const uint32_t d_tmem = tmem + uint32_t(kNT * kAColsPerStage + d * BN);
+        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
+        tc_fence_after();
+        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+          const int st = it % kNT, sb = it % NB;
+          if (!(ok = wait_bar(tfull(st), (it / kNT) & 1, ctl, 21))) break;
+          if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
+          tc_fence_after();
+          const uint32_t a_tmem = tmem + uint32_t(st * kAColsPerStage);
+          const uint64_t bdesc = sw128_desc(smem_u32(smem + S::kB + sb * S::kBStage));
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc + uint64_t(kk * 2), idesc, (ks | kk) != 0);
+          tc_commit(tempty(st));
+          tc_commit(bempty(sb));
+        }
+        if (ok) tc_commit(dfull(d));
+      }
+      tc_commit(mma_done);
+      drain_wait(mma_done, 0);
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------ dequant
+    const int wg = (warp - 4) >> 2;  // 0 or 1: alternate K-steps
+    const int q = warp & 3;          // TMEM lane quarter
+    const int m = q * 32 + lane;     // weight row within the tile
+    const int sw = (m >> 2) & 1;     // 32-byte swizzle of the nibble tile
+    uint32_t it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+      for (int ks = 0; ks < ks_n; ++ks, ++it) {
+        if (int(it & 1) != wg) continue;
+        const int sa = it % kNA, st = it % kNT;
+        // every lane waits (acquire), the decision is made warp-uniform so the
+        // .sync.aligned tcgen05 instructions below never run divergent
+        ok = wait_bar(afull(sa), (it / kNA) & 1, ctl, 30);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        ok = wait_bar(tempty(st), ((it / kNT) & 1) ^ 1, ctl, 31);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        tc_fence_after();
+        const unsigned char* nib = smem + S::kNib + sa * kNibBytes + m * 32;
+        const unsigned char* scl = smem + S::kScl + sa * kScaleBytes;
+        const uint4 c0 = *reinterpret_cast<const uint4*>(nib + ((0 ^ sw) << 4));
+        const uint4 c1 = *reinterpret_cast<const uint4*>(nib + ((1 ^ sw) << 4));
+        const uint32_t s0 = scl[m], s1 = scl[kBM + m];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(aempty(sa));
+        uint32_t v[32];
+        {
+          const uint32_t lo0 = s0 < 128u ? s0 : 128u, lo1 = s1 < 128u ? s1 : 128u;
+          const uint32_t f1a = ((lo0 + 126u) << 7) * 0x10001u, f1b = ((lo1 + 126u) << 7) * 0x10001u;
+          const uint32_t f2a = ((s0 > 128u ? s0 - 1u : 127u) << 7) * 0x10001u;
+          const uint32_t f2b = ((s1 > 128u ? s1 - 1u : 127u) << 7) * 0x10001u;
+          const bool ta = s0 > 128u, tb = s1 > 128u;
+          dequant_word(c0.x, f1a, f2a, ta, v + 0);
+          dequant_word(c0.y, f1a, f2a, ta, v + 4);
+          dequant_word(c0.z, f1a, f2a, ta, v + 8);
+          dequant_word(c0.w, f1a, f2a, ta, v + 12);
+          dequant_word(c1.x, f1b, f2b, tb, v + 16);
+          dequant_word(c1.y, f1b, f2b, tb, v + 20);
+          dequant_word(c1.z, f1b, f2b, tb, v + 24);
+          dequant_word(c1.w, f1b, f2b, tb, v + 28);
+        }
+        tmem_st32(tmem + (uint32_t(q * 32) << 16) + uint32_t(st * kAColsPerStage), v);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tfull(st));
+      }
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int m = q * 32 + lane;
+    uint32_t ic = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+      const int4 rb = p.rowblocks[item / p.n_mtiles];
+      const int mt = item % p.n_mtiles;
+      const int e = rb.x, r0 = rb.y, nrows = rb.z;
+      const int npad = (nrows + 15) & ~15;
+      const int d = ic % ND;
+      ok = wait_bar(dfull(d), (ic / ND) & 1, ctl, 40);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      const int j = mt * kBM + m;  // output feature
+      const bool jok = j < p.n_out;
+      const float bias = jok ? bf16_to_f32(p.bias[int64_t(e) * p.n_out + j]) : 0.f;
+      const uint32_t dcol = tmem + (uint32_t(q * 32) << 16) + uint32_t(kNT * kAColsPerStage + d * BN);
+      for (int c0 = 0; c0 < npad; c0 += 16) {
+        uint32_t raw[16];
+        tmem_ld16(dcol + uint32_t(c0), raw);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int n = c0 + c;
+          float v = __uint_as_float(raw[c]);
+          if (p.precision == KLC_PREC_BF16) v = round_bf16(v);
+          v += bias;
+          const bool nok = n < nrows;
+          if (PHASE == 1) {
+            const float up_raw = __shfl_xor_sync(0xffffffffu, v, 1);
+            float g2 = 0.f;
+            if ((lane & 1) == 0 && jok && nok) {
+              const float gate = fminf(v, p.limit);
+              const float up = fminf(fmaxf(up_raw, -p.limit), p.limit);
+              const float glu = gate * (1.0f / (1.0f + expf(-(gate * p.alpha))));
+              const float gated = (up + 1.0f) * glu;
+              const uint16_t gb = f32_to_bf16(gated);
+              const int i = j >> 1;
+              const int pos = (i & ~7) | (((i & 3) << 1) | ((i >> 2) & 1));  // element i%8 -> slot {0,2,4,6,1,3,5,7}
+              p.out[int64_t(r0 + n) * p.out_ld + pos] = gb;
+              const float gr = bf16_to_f32(gb);
+              g2 = (p.precision == KLC_PREC_BF16) ? gr * gr : gated * gated;
+            }
+            if (p.normsq != nullptr) {
+              g2 = warp_sum(g2);
+              if (lane == 0 && nok) atomicAdd(&p.normsq[int64_t(p.rows[r0 + n]) * 2 + 0], g2);
+            }
+          } else {
+            float o2 = 0.f;
+            if (jok && nok) {
+              p.out[int64_t(r0 + n) * p.out_ld + j] = f32_to_bf16(v);
+              o2 = v * v;
+            }
+            if (p.normsq != nullptr) {
+              o2 = warp_sum(o2);
+              if (lane == 0 && nok) atomicAdd(&p.normsq[int64_t(p.rows[r0 + n]) * 2 + 1], o2);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dempty(d));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_fn(EncodeTiledFn* out) {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (fn == nullptr) return fail(KLC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  *out = fn;
+  return KLC_OK;
+}
+
+int make_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = nullptr;
+  int st = encode_fn(&fn);
+  if (st != KLC_OK) return st;
+  cuuint64_t gd[3], gs[2];
+  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+  const CUresult r = fn(map, type, cuuint32_t(rank), const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KLC_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(r)));
+  return KLC_OK;
+}
+
+template <int PHASE, int BN, int NB>
+int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16_t* act, int64_t rows_cap, int experts,
+                    const TcParams& p, int max_rowblocks, cudaStream_t stream) {
+  using S = Smem<PHASE, BN, NB>;
+  CUtensorMap ma, ms, mb;
+  const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out), G = K / 32;
+  {
+    const uint64_t dims[3] = {K / 2, N, uint64_t(experts)};
+    const uint64_t strides[2] = {K / 2, N * K / 2};
+    const uint32_t box[3] = {kBK / 2, kBM, 1};
+    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B);
+    if (st != KLC_OK) return st;
+  }
+  {
+    const uint64_t dims[3] = {N, G, uint64_t(experts)};
+    const uint64_t strides[2] = {N, G * N};
+    const uint32_t box[3] = {kBM, kBK / 32, 1};
+    int st = make_map(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, scales_t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != KLC_OK) return st;
+  }
+  {
+    const uint64_t dims[2] = {K, uint64_t(rows_cap)};
+    const uint64_t strides[1] = {K * 2};
+    const uint32_t box[2] = {kBK, 16};
+    int st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, act, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  // >= 116 KB of shared memory keeps one CTA (and one 512-column TMEM allocation) per SM
+  const int smem = (S::kBytes + 1024 > 118 * 1024) ? S::kBytes + 1024 : 118 * 1024;
+  KLC_CUDA(cudaFuncSetAttribute(tc_expert_kernel<PHASE, BN, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
+  const int grid = int(items < sm_count() ? items : sm_count());
+  if (grid <= 0) return KLC_OK;
+  tc_expert_kernel<PHASE, BN, NB><<<grid, kThreads, smem, stream>>>(ma, ms, mb, p);
+  KLC_LAUNCH_CHECK("tcgen05 expert launch");
+  return KLC_OK;
+}
+
+template <int BN, int NB>
+int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
+  const klc_moe_weights& w = *a.wts;
+  TcParams p1{};
+  p1.n_out = int(2 * a.inter);
+  p1.k_in = int(a.hidden);
+  p1.ksteps = int(a.hidden / kBK);
+  p1.n_mtiles = (p1.n_out + kBM - 1) / kBM;
+  p1.rowblocks = a.rowblocks;
+  p1.status = a.status_rw;
+  p1.rows = a.rows;
+  p1.bias = w.gu_bias;
+  p1.out = static_cast<uint16_t*>(a.gated);
+  p1.out_ld = int(a.inter);
+  p1.normsq = a.normsq;
+  p1.precision = a.precision;
+  p1.limit = w.swiglu_limit;
+  p1.alpha = w.alpha;
+  int st = launch_tc_phase<1, BN, NB>(w.gu_blocks, w.gu_scales_t, a.xp, a.rows_cap, int(a.experts), p1, a.max_rowblocks, stream);
+  if (st != KLC_OK) return st;
+  stage_mark(kStageGateUp, stream);
+  TcParams p2 = p1;
+  p2.n_out = int(a.hidden);
+  p2.k_in = int(a.inter);
+  p2.ksteps = int(a.inter / kBK);
+  p2.n_mtiles = (p2.n_out + kBM - 1) / kBM;
+  p2.bias = w.dn_bias;
+  p2.out = a.y;
+  p2.out_ld = int(a.hidden);
+  st = launch_tc_phase<2, BN, NB>(w.dn_blocks, w.dn_scales_t, static_cast<const uint16_t*>(a.gated), a.rows_cap,
+                                  int(a.experts), p2, a.max_rowblocks, stream);
+  stage_mark(kStageDown, stream);
+  return st;
+}
+
+}  // namespace
+
+bool tc_path_supported(int64_t hidden, int64_t inter) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return true;  // no device: report the build's capability
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return true;
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0 && hidden % kBK == 0 && inter % kBK == 0;
+}
+
+int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
+  KLC_CHECK_ARG(a.hidden % kBK == 0 && a.inter % kBK == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
+  KLC_CHECK_ARG(a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
+  // block_n (the max rows of a row-block) decides the N tile and the B ring depth
+  switch (a.block_n) {
+    case 64: return launch_tc_both<64, 8>(a, stream);
+    case 128: return launch_tc_both<128, 6>(a, stream);
+    case 256: return launch_tc_both<256, 4>(a, stream);
+    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 64, 128 or 256");
+  }
 }
 
 }  // namespace klc

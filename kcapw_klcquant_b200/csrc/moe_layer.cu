@@ -153,6 +153,7 @@ int run_experts(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_
   ea.y = reinterpret_cast<uint16_t*>(ws + L.y);
   ea.normsq = normsq;
   ea.rows_cap = L.rows_cap;
+  ea.block_n = L.block_n;
   st = tc ? launch_experts_tc(ea, stream) : launch_experts_simt(ea, stream);
   if (st != KLC_OK) return st;
   st = launch_combine(ea.y, pa.pair_pos, w, d.tokens, d.top_k, d.hidden, residual, y, normsq, norms, stream);

@@ -63,6 +63,7 @@ struct ExpertArgs {
   uint16_t* y;                 // [rows_cap, H]
   float* normsq;               // [pairs, 2] or null
   int64_t rows_cap;
+  int block_n;                 // max rows per row-block
 };
 
 int launch_experts_simt(const ExpertArgs& a, cudaStream_t stream);
