@@ -26,7 +26,7 @@
 // written in the same order by the permute/gather and by the gate_up
 // epilogue, so the dot products are unchanged.
 //
-// Every mbarrier wait is bounded by %globaltimer: after kWaitNs the waiting
+// Every mbarrier wait is bounded (SM cycle counter): after kWaitCycles the waiting
 // role records KLC_ERR_DEVICE_TIMEOUT in the workspace status word, raises a
 // CTA-wide abort flag, and all roles drain (TMA and MMA completion are
 // awaited, again bounded) before the TMEM is freed and the CTA exits.
@@ -42,13 +42,16 @@ namespace {
 
 constexpr int kThreads = 512;
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
-constexpr int kBK = 64;         // K per stage (one 128-byte swizzle atom of bf16)
-constexpr int kNA = 8;          // A ring depth (nibbles + scales)
+constexpr int kAtom = 64;       // K per 128-byte swizzle atom of bf16
+constexpr int kKA = 2;          // atoms per pipeline stage
+constexpr int kBK = kAtom * kKA;  // K per stage (128)
+constexpr int kNA = 6;          // A ring depth (nibbles + scales)
 constexpr int kNT = 4;          // TMEM A stages
-constexpr int kAColsPerStage = kBK / 2;  // 32-bit TMEM columns per A stage
-constexpr int kNibBytes = kBM * kBK / 2;     // 4096
-constexpr int kScaleBytes = kBM * kBK / 32;  // 256
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s
+constexpr int kAColsPerStage = kBK / 2;  // 32-bit TMEM columns per A stage (64)
+constexpr int kNibBytes = kBM * kBK / 2;     // 8192
+constexpr int kScaleBytes = kBM * kBK / 32;  // 512
+constexpr uint64_t kWaitNs = 2000000000ull;      // drain bound: 2 s of %globaltimer
+constexpr long long kWaitCycles = 4000000000ll;  // wait bound: 4e9 SM cycles (2 s at 2 GHz)
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -94,19 +97,50 @@ struct Ctl {
 
 // Bounded wait for the completion of phase `parity` of a barrier.  Returns
 // false when the CTA is aborting (this wait timed out or another did).
-__device__ __noinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  // slow path: the SM cycle counter is cheap to read (the global timer is
+  // not); the bound is checked every 64 polls and is a few seconds at any clock
+  const long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 31) == 0) {
+    if ((i & 63) == 0) {
       if (*c.abort) return false;
-      if (globaltimer() - t0 > kWaitNs) {
+      if (clock64() - t0 > kWaitCycles) {
         *c.abort = 1;
         record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
         return false;
       }
-      __nanosleep(32);
+    }
+  }
+}
+
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Spinning variant for the single MMA-issuing thread: non-suspending polls,
+// so it observes a completed phase with the least latency.
+__device__ __forceinline__ bool spin_bar(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 255) == 0) {
+      if (*c.abort) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        *c.abort = 1;
+        record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
+        return false;
+      }
     }
   }
 }
@@ -160,6 +194,22 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&v)[64]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,"
+      "%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,"
+      "%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]), "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]), "r"(v[36]),
+      "r"(v[37]), "r"(v[38]), "r"(v[39]), "r"(v[40]), "r"(v[41]), "r"(v[42]), "r"(v[43]), "r"(v[44]), "r"(v[45]),
+      "r"(v[46]), "r"(v[47]), "r"(v[48]), "r"(v[49]), "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]),
+      "r"(v[55]), "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -191,25 +241,43 @@ __device__ __forceinline__ uint32_t make_idesc(int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(kBM >> 4) << 24);
 }
 
-// Four bf16x2 words (8 consecutive E2M1 values of a 32-bit nibble word, in
-// the {0,4,1,5,2,6,3,7} order) scaled by 2^(s-127), exact.  The nibble bits
-// are placed as a bf16 of value FP4 * 2^-126 (sign -> bit 15, e2m1 -> bits
-// 8:6) and rescaled by bf16 multiplies with exact powers of two.
-__device__ __forceinline__ void dequant_word(uint32_t w, uint32_t f1, uint32_t f2, bool two, uint32_t* out) {
+// One 16-byte MXFP4 group (32 E2M1 values, one E8M0 scale s) -> 16 bf16x2
+// words, exact.  Each pair word holds nibbles (q, q+4) of a 32-bit nibble
+// word, i.e. the K order {0,4,1,5,2,6,3,7} inside every 8 values.  The two
+// nibbles are isolated with one AND and spread with one integer multiply
+// (the two shifted copies do not overlap, so the multiply is a shift-OR) to
+// a bf16 pair of value FP4 * 2^-126 (sign -> bit 15, e2m1 -> bits 8:6); a
+// second AND drops the stray copies.  bf16 multiplies by exact powers of two
+// then apply 2^(s-1) (split in two factors above s = 128 so no factor
+// overflows).  Per 8 values: 9 ALU-pipe ops (1 shift, 8 AND) and 8 FMA-pipe
+// ops (4 IMAD, 4 HMUL2).
+__device__ __forceinline__ void dequant_group(uint4 c, uint32_t s, uint32_t* out) {
+  const uint32_t lo = s < 128u ? s : 128u;
+  const uint32_t f1 = ((lo + 126u) << 7) * 0x10001u;                   // 2^(min(s,128)-1)
+  const bool two = s > 128u;
+  const uint32_t f2 = ((two ? s - 1u : 127u) << 7) * 0x10001u;          // 2^(s-128)
+  const uint32_t words[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const uint32_t u = w >> (4 * q);
-    uint32_t r = ((u << 6) & 0x01C001C0u) | ((u << 12) & 0x80008000u);
-    r = bf16x2_mul(r, f1);
-    if (two) r = bf16x2_mul(r, f2);
-    out[q] = r;
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t w = words[j], wh = w >> 8;
+    uint32_t r[4];
+    r[0] = ((w & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;   // nibbles 0, 4
+    r[1] = ((w & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;   // nibbles 1, 5
+    r[2] = ((wh & 0x000F000Fu) * 0x1040u) & 0x81C081C0u;  // nibbles 2, 6
+    r[3] = ((wh & 0x00F000F0u) * 0x0104u) & 0x81C081C0u;  // nibbles 3, 7
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t v = bf16x2_mul(r[q], f1);
+      if (two) v = bf16x2_mul(v, f2);
+      out[4 * j + q] = v;
+    }
   }
 }
 
 struct TcParams {
   int n_out;          // weight rows of one expert (2I or H)
   int k_in;           // reduction length (H or I)
-  int ksteps;         // k_in / kBK
+  int ksteps;         // ceil(k_in / kBK); the tail of the last stage is zero-filled by TMA
   int n_mtiles;       // ceil(n_out / 128)
   const int4* rowblocks;
   DeviceStatus* status;
@@ -225,10 +293,11 @@ struct TcParams {
 template <int PHASE, int BN, int NB>
 struct Smem {
   static constexpr int kND = (BN <= 128) ? 2 : 1;
-  static constexpr int kBStage = BN * kBK * 2;
+  static constexpr int kBAtom = BN * kAtom * 2;   // one 64-wide K atom of BN token rows
+  static constexpr int kBStage = kKA * kBAtom;
   static constexpr int kNib = 0;
   static constexpr int kScl = kNib + kNA * kNibBytes;
-  static constexpr int kB = kScl + kNA * kScaleBytes;  // 1024-aligned (8*4096 + 8*256 = 34816)
+  static constexpr int kB = (kScl + kNA * kScaleBytes + 1023) / 1024 * 1024;
   static constexpr int kBar = kB + NB * kBStage;
   static constexpr int kNumBars = 2 * kNA + 2 * NB + 2 * kNT + 2 * kND + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
@@ -241,13 +310,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap map_b, TcParams p) {
   using S = Smem<PHASE, BN, NB>;
   constexpr int ND = S::kND;
+  static_assert(kNT * kAColsPerStage + ND * BN <= 512, "TMEM budget");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // TMA destinations and swizzled operand tiles need 1024-byte alignment
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::kBar);
-  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t bar0 = smem_u32(smem + S::kBar);
   auto afull = [&](int s) { return bar0 + 8u * s; };
   auto aempty = [&](int s) { return bar0 + 8u * (kNA + s); };
   auto bfull = [&](int s) { return bar0 + 8u * (2 * kNA + s); };
@@ -315,8 +384,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           last_a[sa] = int(it);
           if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
           mbar_arrive_expect_tx(bfull(sb), uint32_t(npad) * kBK * 2);
-          for (int j = 0; j < npad; j += 16)
-            tma_load_2d(smem_u32(smem + S::kB + sb * S::kBStage + j * kBK * 2), &map_b, ks * kBK, rb.y + j, bfull(sb));
+#pragma unroll
+          for (int a = 0; a < kKA; ++a)
+            for (int j = 0; j < npad; j += 16)
+              tma_load_2d(smem_u32(smem + S::kB + sb * S::kBStage + a * S::kBAtom + j * kAtom * 2), &map_b,
+                          ks * kBK + a * kAtom, rb.y + j, bfull(sb));
           last_b[sb] = int(it);
         }
       }
@@ -339,18 +411,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t idesc = make_idesc(npad);
         const int d = ic % ND;
         const uint32_t d_tmem = tmem + uint32_t(kNT * kAColsPerStage + d * BN);
-        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
+        if (!(ok = spin_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
         tc_fence_after();
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
           const int st = it % kNT, sb = it % NB;
-          if (!(ok = wait_bar(tfull(st), (it / kNT) & 1, ctl, 21))) break;
-          if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
+          if (!(ok = spin_bar(tfull(st), (it / kNT) & 1, ctl, 21))) break;
+          if (!(ok = spin_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
           tc_fence_after();
           const uint32_t a_tmem = tmem + uint32_t(st * kAColsPerStage);
-          const uint64_t bdesc = sw128_desc(smem_u32(smem + S::kB + sb * S::kBStage));
+          const uint32_t b_base = smem_u32(smem + S::kB + sb * S::kBStage);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc + uint64_t(kk * 2), idesc, (ks | kk) != 0);
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t bdesc = sw128_desc(b_base + uint32_t((kk >> 2) * S::kBAtom + (kk & 3) * 32));
+            tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (ks | kk) != 0);
+          }
           tc_commit(tempty(st));
           tc_commit(bempty(sb));
         }
@@ -364,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wg = (warp - 4) >> 2;  // 0 or 1: alternate K-steps
     const int q = warp & 3;          // TMEM lane quarter
     const int m = q * 32 + lane;     // weight row within the tile
-    const int sw = (m >> 2) & 1;     // 32-byte swizzle of the nibble tile
+    const int sw = (m >> 1) & 3;     // 64-byte swizzle of the nibble tile
     uint32_t it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
@@ -375,33 +449,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         // .sync.aligned tcgen05 instructions below never run divergent
         ok = wait_bar(afull(sa), (it / kNA) & 1, ctl, 30);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        const unsigned char* nib = smem + S::kNib + sa * kNibBytes + m * (kBK / 2);
+        const unsigned char* scl = smem + S::kScl + sa * kScaleBytes;
+        uint4 c[4];
+        uint32_t sc[4];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          c[g] = *reinterpret_cast<const uint4*>(nib + ((g ^ sw) << 4));
+          sc[g] = scl[g * kBM + m];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(aempty(sa));
+        uint32_t v[64];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) dequant_group(c[g], sc[g], v + 16 * g);
         ok = wait_bar(tempty(st), ((it / kNT) & 1) ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         tc_fence_after();
-        const unsigned char* nib = smem + S::kNib + sa * kNibBytes + m * 32;
-        const unsigned char* scl = smem + S::kScl + sa * kScaleBytes;
-        const uint4 c0 = *reinterpret_cast<const uint4*>(nib + ((0 ^ sw) << 4));
-        const uint4 c1 = *reinterpret_cast<const uint4*>(nib + ((1 ^ sw) << 4));
-        const uint32_t s0 = scl[m], s1 = scl[kBM + m];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(aempty(sa));
-        uint32_t v[32];
-        {
-          const uint32_t lo0 = s0 < 128u ? s0 : 128u, lo1 = s1 < 128u ? s1 : 128u;
-          const uint32_t f1a = ((lo0 + 126u) << 7) * 0x10001u, f1b = ((lo1 + 126u) << 7) * 0x10001u;
-          const uint32_t f2a = ((s0 > 128u ? s0 - 1u : 127u) << 7) * 0x10001u;
-          const uint32_t f2b = ((s1 > 128u ? s1 - 1u : 127u) << 7) * 0x10001u;
-          const bool ta = s0 > 128u, tb = s1 > 128u;
-          dequant_word(c0.x, f1a, f2a, ta, v + 0);
-          dequant_word(c0.y, f1a, f2a, ta, v + 4);
-          dequant_word(c0.z, f1a, f2a, ta, v + 8);
-          dequant_word(c0.w, f1a, f2a, ta, v + 12);
-          dequant_word(c1.x, f1b, f2b, tb, v + 16);
-          dequant_word(c1.y, f1b, f2b, tb, v + 20);
-          dequant_word(c1.z, f1b, f2b, tb, v + 24);
-          dequant_word(c1.w, f1b, f2b, tb, v + 28);
-        }
-        tmem_st32(tmem + (uint32_t(q * 32) << 16) + uint32_t(st * kAColsPerStage), v);
+        tmem_st64(tmem + (uint32_t(q * 32) << 16) + uint32_t(st * kAColsPerStage), v);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -420,21 +485,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = rb.x, r0 = rb.y, nrows = rb.z;
       const int npad = (nrows + 15) & ~15;
       const int d = ic % ND;
-      ok = wait_bar(dfull(d), (ic / ND) & 1, ctl, 40);
-      if (!(ok = __all_sync(0xffffffffu, ok))) break;
-      tc_fence_after();
       const int j = mt * kBM + m;  // output feature
       const bool jok = j < p.n_out;
       const float bias = jok ? bf16_to_f32(p.bias[int64_t(e) * p.n_out + j]) : 0.f;
+      ok = wait_bar(dfull(d), (ic / ND) & 1, ctl, 40);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
       const uint32_t dcol = tmem + (uint32_t(q * 32) << 16) + uint32_t(kNT * kAColsPerStage + d * BN);
       for (int c0 = 0; c0 < npad; c0 += 16) {
         uint32_t raw[16];
         tmem_ld16(dcol + uint32_t(c0), raw);
         tmem_wait_ld();
+        if (c0 + 16 >= npad) {
+          // last accumulator columns read: hand the buffer back to the MMA warp early
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dempty(d));
+        }
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int n = c0 + c;
-          float v = __uint_as_float(raw[c]);
+        for (int cc = 0; cc < 16; ++cc) {
+          const int n = c0 + cc;
+          float v = __uint_as_float(raw[cc]);
           if (p.precision == KLC_PREC_BF16) v = round_bf16(v);
           v += bias;
           const bool nok = n < nrows;
@@ -470,9 +541,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dempty(d));
     }
   }
 
@@ -492,12 +560,12 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 int encode_fn(EncodeTiledFn* out) {
   static std::once_flag once;
   static EncodeTiledFn fn = nullptr;
-  static cudaError_t err = cudaSuccess;
   std::call_once(once, [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q{};
-    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
-    if (err == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
   });
   if (fn == nullptr) return fail(KLC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   *out = fn;
@@ -529,13 +597,15 @@ int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16
   CUtensorMap ma, ms, mb;
   const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out), G = K / 32;
   {
+    // packed nibbles [E][N][K/2] bytes; box = 128 rows x 64 bytes (128 values), 64-byte swizzle
     const uint64_t dims[3] = {K / 2, N, uint64_t(experts)};
     const uint64_t strides[2] = {K / 2, N * K / 2};
     const uint32_t box[3] = {kBK / 2, kBM, 1};
-    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_32B);
+    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
     if (st != KLC_OK) return st;
   }
   {
+    // scales [E][G][N] bytes; box = 4 groups x 128 rows
     const uint64_t dims[3] = {N, G, uint64_t(experts)};
     const uint64_t strides[2] = {N, G * N};
     const uint32_t box[3] = {kBM, kBK / 32, 1};
@@ -543,9 +613,10 @@ int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16
     if (st != KLC_OK) return st;
   }
   {
+    // token rows [rows_cap][K] bf16; box = 16 rows x one 64-wide atom, 128-byte swizzle
     const uint64_t dims[2] = {K, uint64_t(rows_cap)};
     const uint64_t strides[1] = {K * 2};
-    const uint32_t box[2] = {kBK, 16};
+    const uint32_t box[2] = {kAtom, 16};
     int st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, act, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != KLC_OK) return st;
   }
@@ -566,7 +637,7 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   TcParams p1{};
   p1.n_out = int(2 * a.inter);
   p1.k_in = int(a.hidden);
-  p1.ksteps = int(a.hidden / kBK);
+  p1.ksteps = int((a.hidden + kBK - 1) / kBK);
   p1.n_mtiles = (p1.n_out + kBM - 1) / kBM;
   p1.rowblocks = a.rowblocks;
   p1.status = a.status_rw;
@@ -584,7 +655,7 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   TcParams p2 = p1;
   p2.n_out = int(a.hidden);
   p2.k_in = int(a.inter);
-  p2.ksteps = int(a.inter / kBK);
+  p2.ksteps = int((a.inter + kBK - 1) / kBK);
   p2.n_mtiles = (p2.n_out + kBM - 1) / kBM;
   p2.bias = w.dn_bias;
   p2.out = a.y;
@@ -599,20 +670,21 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
 
 bool tc_path_supported(int64_t hidden, int64_t inter) {
   int dev = 0, major = 0, minor = 0;
+  if (hidden % kAtom != 0 || inter % kAtom != 0) return false;
   if (cudaGetDevice(&dev) != cudaSuccess) return true;  // no device: report the build's capability
   if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return true;
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
-  return major == 10 && minor == 0 && hidden % kBK == 0 && inter % kBK == 0;
+  return major == 10 && minor == 0;
 }
 
 int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
-  KLC_CHECK_ARG(a.hidden % kBK == 0 && a.inter % kBK == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
+  KLC_CHECK_ARG(a.hidden % kAtom == 0 && a.inter % kAtom == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
   KLC_CHECK_ARG(a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
   // block_n (the max rows of a row-block) decides the N tile and the B ring depth
   switch (a.block_n) {
-    case 64: return launch_tc_both<64, 8>(a, stream);
-    case 128: return launch_tc_both<128, 6>(a, stream);
-    case 256: return launch_tc_both<256, 4>(a, stream);
+    case 64: return launch_tc_both<64, 4>(a, stream);
+    case 128: return launch_tc_both<128, 4>(a, stream);
+    case 256: return launch_tc_both<256, 2>(a, stream);
     default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 64, 128 or 256");
   }
 }
