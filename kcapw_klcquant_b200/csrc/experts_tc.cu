@@ -45,7 +45,6 @@ constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kAtom = 64;       // K per 128-byte swizzle atom of bf16
 constexpr int kKA = 2;          // atoms per pipeline stage
 constexpr int kBK = kAtom * kKA;  // K per stage (128)
-constexpr int kNA = 6;          // A ring depth (nibbles + scales)
 constexpr int kNT = 4;          // TMEM A stages
 constexpr int kAColsPerStage = kBK / 2;  // 32-bit TMEM columns per A stage (64)
 constexpr int kNibBytes = kBM * kBK / 2;     // 8192
@@ -290,27 +289,35 @@ struct TcParams {
   float limit, alpha;
 };
 
-template <int PHASE, int BN, int NB>
+// DUAL: two MMA pipelines (even / odd K-stages of a tile, separate fp32
+// accumulators summed by the epilogue), so one issuer's commit / fence / wait
+// overhead overlaps the other's MMAs.  Needs two BN-column accumulators per
+// tile, so it is used for BN <= 128.
+template <int PHASE, int BN, int NB, bool DUAL>
 struct Smem {
-  static constexpr int kND = (BN <= 128) ? 2 : 1;
+  // A ring depth (packed weights + scales, 8.5 KB per stage): as deep as the
+  // shared memory left next to the B ring allows
+  static constexpr int kNA = (BN <= 64) ? 12 : 8;
+  static constexpr int kNP = DUAL ? 2 : 1;                       // MMA pipelines
+  static constexpr int kND = (DUAL ? (BN <= 64 ? 2 : 1) : 1);    // accumulator sets in flight
   static constexpr int kBAtom = BN * kAtom * 2;   // one 64-wide K atom of BN token rows
   static constexpr int kBStage = kKA * kBAtom;
-  static constexpr int kNib = 0;
+  static constexpr int kNib = 0;  // A ring: kNA x 8 KB nibbles
   static constexpr int kScl = kNib + kNA * kNibBytes;
   static constexpr int kB = (kScl + kNA * kScaleBytes + 1023) / 1024 * 1024;
   static constexpr int kBar = kB + NB * kBStage;
-  static constexpr int kNumBars = 2 * kNA + 2 * NB + 2 * kNT + 2 * kND + 1;
+  static constexpr int kNumBars = 2 * kNA + 2 * NB + 2 * kNT + kNP * kND + kND + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
 };
 
-template <int PHASE, int BN, int NB>
+template <int PHASE, int BN, int NB, bool DUAL>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_s,
                      const __grid_constant__ CUtensorMap map_b, TcParams p) {
-  using S = Smem<PHASE, BN, NB>;
-  constexpr int ND = S::kND;
-  static_assert(kNT * kAColsPerStage + ND * BN <= 512, "TMEM budget");
+  using S = Smem<PHASE, BN, NB, DUAL>;
+  constexpr int ND = S::kND, NP = S::kNP, kNA = S::kNA;
+  static_assert(kNT * kAColsPerStage + ND * NP * BN <= 512, "TMEM budget");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // TMA destinations and swizzled operand tiles need 1024-byte alignment
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -323,9 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bempty = [&](int s) { return bar0 + 8u * (2 * kNA + NB + s); };
   auto tfull = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + s); };
   auto tempty = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + kNT + s); };
-  auto dfull = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + s); };
-  auto dempty = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + ND + s); };
-  const uint32_t mma_done = bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + 2 * ND);
+  auto dfull = [&](int pp, int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + pp * ND + s); };
+  auto dempty = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + NP * ND + s); };
+  const uint32_t mma_done = bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + NP * ND + ND);
+  // accumulator of pipeline pp for accumulator set d
+  auto dcol = [&](int pp, int d) { return uint32_t(kNT * kAColsPerStage + (d * NP + pp) * BN); };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + S::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kMisc + 4);
   const Ctl ctl{abort_flag, p.status};
@@ -344,10 +353,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(tempty(s), 1);
     }
     for (int s = 0; s < ND; ++s) {
-      mbar_init(dfull(s), 1);
+      for (int pp = 0; pp < NP; ++pp) mbar_init(dfull(pp, s), 1);
       mbar_init(dempty(s), 4);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(mma_done, NP);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -364,24 +373,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ks_n = p.ksteps;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ A producer (weights)
     if (lane == 0) {
       uint32_t it = 0;
-      int last_a[kNA], last_b[NB];  // latest iteration that loaded each stage (-1: never)
-      for (int s = 0; s < kNA; ++s) last_a[s] = -1;
-      for (int s = 0; s < NB; ++s) last_b[s] = -1;
+      int last[kNA];  // latest iteration that loaded each stage (-1: never)
+      for (int s = 0; s < kNA; ++s) last[s] = -1;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
         const int mt = item % p.n_mtiles;
-        const int npad = (rb.z + 15) & ~15;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
-          const int sa = it % kNA, sb = it % NB;
+          const int sa = it % kNA;
           if (!(ok = wait_bar(aempty(sa), ((it / kNA) & 1) ^ 1, ctl, 10))) break;
           mbar_arrive_expect_tx(afull(sa), kNibBytes + kScaleBytes);
           tma_load_3d(smem_u32(smem + S::kNib + sa * kNibBytes), &map_a, ks * (kBK / 2), mt * kBM, rb.x, afull(sa));
           tma_load_3d(smem_u32(smem + S::kScl + sa * kScaleBytes), &map_s, mt * kBM, ks * (kBK / 32), rb.x, afull(sa));
-          last_a[sa] = int(it);
+          last[sa] = int(it);
+        }
+      }
+      if (!ok)  // aborting: wait (bounded) until no bulk copy still writes shared memory
+        for (int s = 0; s < kNA; ++s)
+          if (last[s] >= 0) drain_wait(afull(s), (uint32_t(last[s]) / kNA) & 1);
+    }
+  } else if (warp == 3) {
+    // ------------------------------------------------------------ B producer (token rows)
+    if (lane == 0) {
+      uint32_t it = 0;
+      int last[NB];
+      for (int s = 0; s < NB; ++s) last[s] = -1;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int npad = (rb.z + 15) & ~15;
+        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+          const int sb = it % NB;
           if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
           mbar_arrive_expect_tx(bfull(sb), uint32_t(npad) * kBK * 2);
 #pragma unroll
@@ -389,20 +414,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < npad; j += 16)
               tma_load_2d(smem_u32(smem + S::kB + sb * S::kBStage + a * S::kBAtom + j * kAtom * 2), &map_b,
                           ks * kBK + a * kAtom, rb.y + j, bfull(sb));
-          last_b[sb] = int(it);
+          last[sb] = int(it);
         }
       }
-      if (!ok) {
-        // aborting: wait (bounded) until no bulk copy still writes shared memory
-        for (int s = 0; s < kNA; ++s)
-          if (last_a[s] >= 0) drain_wait(afull(s), (uint32_t(last_a[s]) / kNA) & 1);
+      if (!ok)
         for (int s = 0; s < NB; ++s)
-          if (last_b[s] >= 0) drain_wait(bfull(s), (uint32_t(last_b[s]) / NB) & 1);
-      }
+          if (last[s] >= 0) drain_wait(bfull(s), (uint32_t(last[s]) / NB) & 1);
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 1 || (DUAL && warp == 2)) {
+    // ------------------------------------------------------------ MMA issuers
+    const int pp = warp - 1;  // pipeline: K-stages with it % NP == pp
     if (lane == 0) {
+      const bool half_last = ((p.k_in / kAtom) % kKA) != 0;  // last stage holds one valid atom
       uint32_t it = 0, ic = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
@@ -410,25 +433,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int npad = (rb.z + 15) & ~15;
         const uint32_t idesc = make_idesc(npad);
         const int d = ic % ND;
-        const uint32_t d_tmem = tmem + uint32_t(kNT * kAColsPerStage + d * BN);
+        const uint32_t d_tmem = tmem + dcol(pp, d);
         if (!(ok = spin_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
         tc_fence_after();
+        bool first = true;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+          if (NP > 1 && int(it % NP) != pp) continue;
           const int st = it % kNT, sb = it % NB;
           if (!(ok = spin_bar(tfull(st), (it / kNT) & 1, ctl, 21))) break;
           if (!(ok = spin_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
           tc_fence_after();
           const uint32_t a_tmem = tmem + uint32_t(st * kAColsPerStage);
           const uint32_t b_base = smem_u32(smem + S::kB + sb * S::kBStage);
+          const int kk_n = (half_last && ks == ks_n - 1) ? kBK / 32 : kBK / 16;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t bdesc = sw128_desc(b_base + uint32_t((kk >> 2) * S::kBAtom + (kk & 3) * 32));
-            tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (ks | kk) != 0);
+            if (kk < kk_n) {
+              const uint64_t bdesc = sw128_desc(b_base + uint32_t((kk >> 2) * S::kBAtom + (kk & 3) * 32));
+              tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
+            }
           }
+          first = false;
           tc_commit(tempty(st));
           tc_commit(bempty(sb));
         }
-        if (ok) tc_commit(dfull(d));
+        if (ok) tc_commit(dfull(pp, d));
       }
       tc_commit(mma_done);
       drain_wait(mma_done, 0);
@@ -488,14 +517,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int j = mt * kBM + m;  // output feature
       const bool jok = j < p.n_out;
       const float bias = jok ? bf16_to_f32(p.bias[int64_t(e) * p.n_out + j]) : 0.f;
-      ok = wait_bar(dfull(d), (ic / ND) & 1, ctl, 40);
+      ok = wait_bar(dfull(0, d), (ic / ND) & 1, ctl, 40);
+      if (NP > 1 && ok) ok = wait_bar(dfull(NP - 1, d), (ic / ND) & 1, ctl, 41);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
-      const uint32_t dcol = tmem + (uint32_t(q * 32) << 16) + uint32_t(kNT * kAColsPerStage + d * BN);
+      const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
       for (int c0 = 0; c0 < npad; c0 += 16) {
         uint32_t raw[16];
-        tmem_ld16(dcol + uint32_t(c0), raw);
-        tmem_wait_ld();
+        tmem_ld16(lane_base + dcol(0, d) + uint32_t(c0), raw);
+        if (NP > 1) {
+          uint32_t raw2[16];
+          tmem_ld16(lane_base + dcol(NP - 1, d) + uint32_t(c0), raw2);
+          tmem_wait_ld();
+#pragma unroll
+          for (int cc = 0; cc < 16; ++cc) raw[cc] = __float_as_uint(__uint_as_float(raw[cc]) + __uint_as_float(raw2[cc]));
+        } else {
+          tmem_wait_ld();
+        }
         if (c0 + 16 >= npad) {
           // last accumulator columns read: hand the buffer back to the MMA warp early
           tc_fence_before();
@@ -590,10 +628,10 @@ int make_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* b
   return KLC_OK;
 }
 
-template <int PHASE, int BN, int NB>
+template <int PHASE, int BN, int NB, bool DUAL>
 int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16_t* act, int64_t rows_cap, int experts,
                     const TcParams& p, int max_rowblocks, cudaStream_t stream) {
-  using S = Smem<PHASE, BN, NB>;
+  using S = Smem<PHASE, BN, NB, DUAL>;
   CUtensorMap ma, ms, mb;
   const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out), G = K / 32;
   {
@@ -622,13 +660,22 @@ int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16
   }
   // >= 116 KB of shared memory keeps one CTA (and one 512-column TMEM allocation) per SM
   const int smem = (S::kBytes + 1024 > 118 * 1024) ? S::kBytes + 1024 : 118 * 1024;
-  KLC_CUDA(cudaFuncSetAttribute(tc_expert_kernel<PHASE, BN, NB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  KLC_CUDA(cudaFuncSetAttribute(tc_expert_kernel<PHASE, BN, NB, DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
   const int grid = int(items < sm_count() ? items : sm_count());
   if (grid <= 0) return KLC_OK;
-  tc_expert_kernel<PHASE, BN, NB><<<grid, kThreads, smem, stream>>>(ma, ms, mb, p);
+  tc_expert_kernel<PHASE, BN, NB, DUAL><<<grid, kThreads, smem, stream>>>(ma, ms, mb, p);
   KLC_LAUNCH_CHECK("tcgen05 expert launch");
   return KLC_OK;
+}
+
+// DUAL pipelines need at least two K-stages per tile (K > 128)
+template <int PHASE, int BN, int NB>
+int launch_tc_phase_any(const uint8_t* blocks, const uint8_t* scales_t, const uint16_t* act, int64_t rows_cap,
+                        int experts, const TcParams& p, int max_rowblocks, cudaStream_t stream) {
+  if (BN <= 128 && p.ksteps >= 2)
+    return launch_tc_phase<PHASE, BN, NB, (BN <= 128)>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
+  return launch_tc_phase<PHASE, BN, NB, false>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
 }
 
 template <int BN, int NB>
@@ -649,7 +696,7 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   p1.precision = a.precision;
   p1.limit = w.swiglu_limit;
   p1.alpha = w.alpha;
-  int st = launch_tc_phase<1, BN, NB>(w.gu_blocks, w.gu_scales_t, a.xp, a.rows_cap, int(a.experts), p1, a.max_rowblocks, stream);
+  int st = launch_tc_phase_any<1, BN, NB>(w.gu_blocks, w.gu_scales_t, a.xp, a.rows_cap, int(a.experts), p1, a.max_rowblocks, stream);
   if (st != KLC_OK) return st;
   stage_mark(kStageGateUp, stream);
   TcParams p2 = p1;
@@ -660,7 +707,7 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   p2.bias = w.dn_bias;
   p2.out = a.y;
   p2.out_ld = int(a.hidden);
-  st = launch_tc_phase<2, BN, NB>(w.dn_blocks, w.dn_scales_t, static_cast<const uint16_t*>(a.gated), a.rows_cap,
+  st = launch_tc_phase_any<2, BN, NB>(w.dn_blocks, w.dn_scales_t, static_cast<const uint16_t*>(a.gated), a.rows_cap,
                                   int(a.experts), p2, a.max_rowblocks, stream);
   stage_mark(kStageDown, stream);
   return st;
