@@ -40,12 +40,14 @@ namespace klc {
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kDqWGs = 4;                       // dequant warpgroups (one TMEM A stage each)
+constexpr int kEpiWarp0 = 4 + 4 * kDqWGs;       // first epilogue warp (20)
+constexpr int kThreads = (kEpiWarp0 + 4) * 32;  // 768
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kAtom = 64;       // K per 128-byte swizzle atom of bf16
 constexpr int kKA = 2;          // atoms per pipeline stage
 constexpr int kBK = kAtom * kKA;  // K per stage (128)
-constexpr int kNT = 4;          // TMEM A stages
+constexpr int kNT = kDqWGs;     // TMEM A stages
 constexpr int kAColsPerStage = kBK / 2;  // 32-bit TMEM columns per A stage (64)
 constexpr int kNibBytes = kBM * kBK / 2;     // 8192
 constexpr int kScaleBytes = kBM * kBK / 32;  // 512
@@ -250,11 +252,11 @@ __device__ __forceinline__ uint32_t make_idesc(int n) {
 // then apply 2^(s-1) (split in two factors above s = 128 so no factor
 // overflows).  Per 8 values: 9 ALU-pipe ops (1 shift, 8 AND) and 8 FMA-pipe
 // ops (4 IMAD, 4 HMUL2).
+template <bool kTwo>
 __device__ __forceinline__ void dequant_group(uint4 c, uint32_t s, uint32_t* out) {
   const uint32_t lo = s < 128u ? s : 128u;
   const uint32_t f1 = ((lo + 126u) << 7) * 0x10001u;                   // 2^(min(s,128)-1)
-  const bool two = s > 128u;
-  const uint32_t f2 = ((two ? s - 1u : 127u) << 7) * 0x10001u;          // 2^(s-128)
+  const uint32_t f2 = ((s > 128u ? s - 1u : 127u) << 7) * 0x10001u;     // 2^(s-128), or 1
   const uint32_t words[4] = {c.x, c.y, c.z, c.w};
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -267,7 +269,7 @@ __device__ __forceinline__ void dequant_group(uint4 c, uint32_t s, uint32_t* out
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       uint32_t v = bf16x2_mul(r[q], f1);
-      if (two) v = bf16x2_mul(v, f2);
+      if (kTwo) v = bf16x2_mul(v, f2);
       out[4 * j + q] = v;
     }
   }
@@ -434,14 +436,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t idesc = make_idesc(npad);
         const int d = ic % ND;
         const uint32_t d_tmem = tmem + dcol(pp, d);
-        if (!(ok = spin_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
+        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
         tc_fence_after();
         bool first = true;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
           if (NP > 1 && int(it % NP) != pp) continue;
           const int st = it % kNT, sb = it % NB;
-          if (!(ok = spin_bar(tfull(st), (it / kNT) & 1, ctl, 21))) break;
-          if (!(ok = spin_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
+          if (!(ok = wait_bar(tfull(st), (it / kNT) & 1, ctl, 21))) break;
+          if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
           tc_fence_after();
           const uint32_t a_tmem = tmem + uint32_t(st * kAColsPerStage);
           const uint32_t b_base = smem_u32(smem + S::kB + sb * S::kBStage);
@@ -462,18 +464,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(mma_done);
       drain_wait(mma_done, 0);
     }
-  } else if (warp >= 4 && warp < 12) {
+  } else if (warp >= 4 && warp < kEpiWarp0) {
     // ------------------------------------------------------------ dequant
-    const int wg = (warp - 4) >> 2;  // 0 or 1: alternate K-steps
+    const int wg = (warp - 4) >> 2;  // K-stages with it % kDqWGs == wg, TMEM A stage wg
     const int q = warp & 3;          // TMEM lane quarter
     const int m = q * 32 + lane;     // weight row within the tile
     const int sw = (m >> 1) & 3;     // 64-byte swizzle of the nibble tile
+    const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(wg * kAColsPerStage);
     uint32_t it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
       for (int ks = 0; ks < ks_n; ++ks, ++it) {
-        if (int(it & 1) != wg) continue;
-        const int sa = it % kNA, st = it % kNT;
+        if (int(it % kDqWGs) != wg) continue;
+        const int sa = it % kNA;
         // every lane waits (acquire), the decision is made warp-uniform so the
         // .sync.aligned tcgen05 instructions below never run divergent
         ok = wait_bar(afull(sa), (it / kNA) & 1, ctl, 30);
@@ -489,20 +492,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(aempty(sa));
-        uint32_t v[64];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) dequant_group(c[g], sc[g], v + 16 * g);
-        ok = wait_bar(tempty(st), ((it / kNT) & 1) ^ 1, ctl, 31);
+        // scales above 128 need a second power-of-two factor; decided per warp
+        const bool two = __any_sync(0xffffffffu, (sc[0] | sc[1] | sc[2] | sc[3]) > 128u);
+        ok = wait_bar(tempty(wg), ((it / kNT) & 1) ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         tc_fence_after();
-        tmem_st64(tmem + (uint32_t(q * 32) << 16) + uint32_t(st * kAColsPerStage), v);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {  // two halves of 32 columns keep the register footprint small
+          uint32_t v[32];
+          if (two) {
+            dequant_group<true>(c[2 * h], sc[2 * h], v);
+            dequant_group<true>(c[2 * h + 1], sc[2 * h + 1], v + 16);
+          } else {
+            dequant_group<false>(c[2 * h], sc[2 * h], v);
+            dequant_group<false>(c[2 * h + 1], sc[2 * h + 1], v + 16);
+          }
+          tmem_st32(tbase + uint32_t(h * 32), v);
+        }
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(tfull(st));
+        if (lane == 0) mbar_arrive(tfull(wg));
       }
     }
-  } else if (warp >= 12) {
+  } else if (warp >= kEpiWarp0) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
     const int m = q * 32 + lane;
