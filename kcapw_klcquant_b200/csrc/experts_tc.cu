@@ -40,17 +40,11 @@ namespace klc {
 
 namespace {
 
-constexpr int kDqWGs = 4;                       // dequant warpgroups (one TMEM A stage each)
+constexpr int kDqWGs = 4;                       // dequant warpgroups (warps 4..19)
 constexpr int kEpiWarp0 = 4 + 4 * kDqWGs;       // first epilogue warp (20)
 constexpr int kThreads = (kEpiWarp0 + 4) * 32;  // 768
-constexpr int kBM = 128;        // weight rows per tile (MMA M)
-constexpr int kAtom = 64;       // K per 128-byte swizzle atom of bf16
-constexpr int kKA = 2;          // atoms per pipeline stage
-constexpr int kBK = kAtom * kKA;  // K per stage (128)
-constexpr int kNT = kDqWGs;     // TMEM A stages
-constexpr int kAColsPerStage = kBK / 2;  // 32-bit TMEM columns per A stage (64)
-constexpr int kNibBytes = kBM * kBK / 2;     // 8192
-constexpr int kScaleBytes = kBM * kBK / 32;  // 512
+constexpr int kBM = 128;                        // weight rows per tile (MMA M)
+constexpr int kAtom = 64;                       // K per 128-byte swizzle atom of bf16
 constexpr uint64_t kWaitNs = 2000000000ull;      // drain bound: 2 s of %globaltimer
 constexpr long long kWaitCycles = 4000000000ll;  // wait bound: 4e9 SM cycles (2 s at 2 GHz)
 
@@ -278,7 +272,7 @@ __device__ __forceinline__ void dequant_group(uint4 c, uint32_t s, uint32_t* out
 struct TcParams {
   int n_out;          // weight rows of one expert (2I or H)
   int k_in;           // reduction length (H or I)
-  int ksteps;         // ceil(k_in / kBK); the tail of the last stage is zero-filled by TMA
+  int ksteps;         // ceil(k_in / stage K); the tail of the last stage is zero-filled by TMA
   int n_mtiles;       // ceil(n_out / 128)
   const int4* rowblocks;
   DeviceStatus* status;
@@ -291,58 +285,69 @@ struct TcParams {
   float limit, alpha;
 };
 
-// DUAL: two MMA pipelines (even / odd K-stages of a tile, separate fp32
-// accumulators summed by the epilogue), so one issuer's commit / fence / wait
-// overhead overlaps the other's MMAs.  Needs two BN-column accumulators per
-// tile, so it is used for BN <= 128.
-template <int PHASE, int BN, int NB, bool DUAL>
-struct Smem {
-  // A ring depth (packed weights + scales, 8.5 KB per stage): as deep as the
-  // shared memory left next to the B ring allows
-  static constexpr int kNA = (BN <= 64) ? 12 : 8;
-  static constexpr int kNP = DUAL ? 2 : 1;                       // MMA pipelines
-  static constexpr int kND = (DUAL ? (BN <= 64 ? 2 : 1) : 1);    // accumulator sets in flight
-  static constexpr int kBAtom = BN * kAtom * 2;   // one 64-wide K atom of BN token rows
-  static constexpr int kBStage = kKA * kBAtom;
-  static constexpr int kNib = 0;  // A ring: kNA x 8 KB nibbles
-  static constexpr int kScl = kNib + kNA * kNibBytes;
-  static constexpr int kB = (kScl + kNA * kScaleBytes + 1023) / 1024 * 1024;
-  static constexpr int kBar = kB + NB * kBStage;
-  static constexpr int kNumBars = 2 * kNA + 2 * NB + 2 * kNT + kNP * kND + kND + 1;
-  static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kBytes = kMisc + 16;
+// Tile / pipeline configuration.
+//   BN    max token rows of a tile (MMA N <= BN)
+//   NB    token (B) ring depth
+//   DUAL  two MMA pipelines (even / odd K-stages into separate fp32
+//         accumulators summed by the epilogue), so one issuer's commit /
+//         fence / wait overhead overlaps the other's MMAs
+//   KA    64-wide K atoms per stage (16 * KA MMAs per stage)
+//   NT    TMEM A stages (KA * 32 columns each), one per active dequant warpgroup
+//   NA    weight (A) ring depth
+//   ND    accumulator sets in flight (epilogue of one tile overlaps the next)
+template <int BN_, int NB_, bool DUAL_, int KA_, int NT_, int NA_, int ND_>
+struct Cfg {
+  static constexpr int BN = BN_, NB = NB_, KA = KA_, NT = NT_, NA = NA_, ND = ND_;
+  static constexpr bool DUAL = DUAL_;
+  static constexpr int NP = DUAL ? 2 : 1;
+  static constexpr int BK = kAtom * KA;         // K per stage
+  static constexpr int ACOLS = BK / 2;          // TMEM columns per A stage
+  static constexpr int NIB = kBM * BK / 2;      // nibble bytes per stage
+  static constexpr int SCL = kBM * BK / 32;     // scale bytes per stage
+  static constexpr int GROUPS = BK / 32;        // scale groups per stage
+  static constexpr int BATOM = BN * kAtom * 2;  // bytes of one K atom of BN token rows
+  static constexpr int BSTAGE = KA * BATOM;
+  // shared memory layout
+  static constexpr int OFF_NIB = 0;
+  static constexpr int OFF_SCL = OFF_NIB + NA * NIB;
+  static constexpr int OFF_B = (OFF_SCL + NA * SCL + 1023) / 1024 * 1024;
+  static constexpr int OFF_BAR = OFF_B + NB * BSTAGE;
+  static constexpr int NUM_BARS = 2 * NA + 2 * NB + 2 * NT + NP * ND + ND + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static_assert(NT * ACOLS + ND * NP * BN <= 512, "TMEM budget");
+  static_assert(NT <= kDqWGs, "one dequant warpgroup per TMEM A stage");
+  static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
 };
 
-template <int PHASE, int BN, int NB, bool DUAL>
+template <int PHASE, class C>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_s,
                      const __grid_constant__ CUtensorMap map_b, TcParams p) {
-  using S = Smem<PHASE, BN, NB, DUAL>;
-  constexpr int ND = S::kND, NP = S::kNP, kNA = S::kNA;
-  static_assert(kNT * kAColsPerStage + ND * NP * BN <= 512, "TMEM budget");
+  constexpr int NA = C::NA, NB = C::NB, NT = C::NT, ND = C::ND, NP = C::NP, KA = C::KA, BN = C::BN;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // TMA destinations and swizzled operand tiles need 1024-byte alignment
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const uint32_t bar0 = smem_u32(smem + S::kBar);
+  const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
   auto afull = [&](int s) { return bar0 + 8u * s; };
-  auto aempty = [&](int s) { return bar0 + 8u * (kNA + s); };
-  auto bfull = [&](int s) { return bar0 + 8u * (2 * kNA + s); };
-  auto bempty = [&](int s) { return bar0 + 8u * (2 * kNA + NB + s); };
-  auto tfull = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + s); };
-  auto tempty = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + kNT + s); };
-  auto dfull = [&](int pp, int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + pp * ND + s); };
-  auto dempty = [&](int s) { return bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + NP * ND + s); };
-  const uint32_t mma_done = bar0 + 8u * (2 * kNA + 2 * NB + 2 * kNT + NP * ND + ND);
+  auto aempty = [&](int s) { return bar0 + 8u * (NA + s); };
+  auto bfull = [&](int s) { return bar0 + 8u * (2 * NA + s); };
+  auto bempty = [&](int s) { return bar0 + 8u * (2 * NA + NB + s); };
+  auto tfull = [&](int s) { return bar0 + 8u * (2 * NA + 2 * NB + s); };
+  auto tempty = [&](int s) { return bar0 + 8u * (2 * NA + 2 * NB + NT + s); };
+  auto dfull = [&](int pp, int s) { return bar0 + 8u * (2 * NA + 2 * NB + 2 * NT + pp * ND + s); };
+  auto dempty = [&](int s) { return bar0 + 8u * (2 * NA + 2 * NB + 2 * NT + NP * ND + s); };
+  const uint32_t mma_done = bar0 + 8u * (2 * NA + 2 * NB + 2 * NT + NP * ND + ND);
   // accumulator of pipeline pp for accumulator set d
-  auto dcol = [&](int pp, int d) { return uint32_t(kNT * kAColsPerStage + (d * NP + pp) * BN); };
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + S::kMisc);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + S::kMisc + 4);
+  auto dcol = [&](int pp, int d) { return uint32_t(NT * C::ACOLS + (d * NP + pp) * BN); };
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const Ctl ctl{abort_flag, p.status};
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kNA; ++s) {
+    for (int s = 0; s < NA; ++s) {
       mbar_init(afull(s), 1);
       mbar_init(aempty(s), 4);
     }
@@ -350,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bfull(s), 1);
       mbar_init(bempty(s), 1);
     }
-    for (int s = 0; s < kNT; ++s) {
+    for (int s = 0; s < NT; ++s) {
       mbar_init(tfull(s), 4);
       mbar_init(tempty(s), 1);
     }
@@ -378,24 +383,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ A producer (weights)
     if (lane == 0) {
       uint32_t it = 0;
-      int last[kNA];  // latest iteration that loaded each stage (-1: never)
-      for (int s = 0; s < kNA; ++s) last[s] = -1;
+      int last[NA];  // latest iteration that loaded each stage (-1: never)
+      for (int s = 0; s < NA; ++s) last[s] = -1;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
         const int mt = item % p.n_mtiles;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
-          const int sa = it % kNA;
-          if (!(ok = wait_bar(aempty(sa), ((it / kNA) & 1) ^ 1, ctl, 10))) break;
-          mbar_arrive_expect_tx(afull(sa), kNibBytes + kScaleBytes);
-          tma_load_3d(smem_u32(smem + S::kNib + sa * kNibBytes), &map_a, ks * (kBK / 2), mt * kBM, rb.x, afull(sa));
-          tma_load_3d(smem_u32(smem + S::kScl + sa * kScaleBytes), &map_s, mt * kBM, ks * (kBK / 32), rb.x, afull(sa));
+          const int sa = it % NA;
+          if (!(ok = wait_bar(aempty(sa), ((it / NA) & 1) ^ 1, ctl, 10))) break;
+          mbar_arrive_expect_tx(afull(sa), C::NIB + C::SCL);
+          tma_load_3d(smem_u32(smem + C::OFF_NIB + sa * C::NIB), &map_a, ks * (C::BK / 2), mt * kBM, rb.x, afull(sa));
+          tma_load_3d(smem_u32(smem + C::OFF_SCL + sa * C::SCL), &map_s, mt * kBM, ks * C::GROUPS, rb.x, afull(sa));
           last[sa] = int(it);
         }
       }
       if (!ok)  // aborting: wait (bounded) until no bulk copy still writes shared memory
-        for (int s = 0; s < kNA; ++s)
-          if (last[s] >= 0) drain_wait(afull(s), (uint32_t(last[s]) / kNA) & 1);
+        for (int s = 0; s < NA; ++s)
+          if (last[s] >= 0) drain_wait(afull(s), (uint32_t(last[s]) / NA) & 1);
     }
   } else if (warp == 3) {
     // ------------------------------------------------------------ B producer (token rows)
@@ -410,12 +415,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
           const int sb = it % NB;
           if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
-          mbar_arrive_expect_tx(bfull(sb), uint32_t(npad) * kBK * 2);
+          mbar_arrive_expect_tx(bfull(sb), uint32_t(npad) * C::BK * 2);
 #pragma unroll
-          for (int a = 0; a < kKA; ++a)
+          for (int a = 0; a < KA; ++a)
             for (int j = 0; j < npad; j += 16)
-              tma_load_2d(smem_u32(smem + S::kB + sb * S::kBStage + a * S::kBAtom + j * kAtom * 2), &map_b,
-                          ks * kBK + a * kAtom, rb.y + j, bfull(sb));
+              tma_load_2d(smem_u32(smem + C::OFF_B + sb * C::BSTAGE + a * C::BATOM + j * kAtom * 2), &map_b,
+                          ks * C::BK + a * kAtom, rb.y + j, bfull(sb));
           last[sb] = int(it);
         }
       }
@@ -423,11 +428,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < NB; ++s)
           if (last[s] >= 0) drain_wait(bfull(s), (uint32_t(last[s]) / NB) & 1);
     }
-  } else if (warp == 1 || (DUAL && warp == 2)) {
+  } else if (warp == 1 || (NP > 1 && warp == 2)) {
     // ------------------------------------------------------------ MMA issuers
     const int pp = warp - 1;  // pipeline: K-stages with it % NP == pp
     if (lane == 0) {
-      const bool half_last = ((p.k_in / kAtom) % kKA) != 0;  // last stage holds one valid atom
+      const int atoms_last = (p.k_in / kAtom) - (ks_n - 1) * KA;  // valid atoms in the last stage
       uint32_t it = 0, ic = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
@@ -441,17 +446,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool first = true;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
           if (NP > 1 && int(it % NP) != pp) continue;
-          const int st = it % kNT, sb = it % NB;
-          if (!(ok = wait_bar(tfull(st), (it / kNT) & 1, ctl, 21))) break;
+          const int st = it % NT, sb = it % NB;
+          if (!(ok = wait_bar(tfull(st), (it / NT) & 1, ctl, 21))) break;
           if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
           tc_fence_after();
-          const uint32_t a_tmem = tmem + uint32_t(st * kAColsPerStage);
-          const uint32_t b_base = smem_u32(smem + S::kB + sb * S::kBStage);
-          const int kk_n = (half_last && ks == ks_n - 1) ? kBK / 32 : kBK / 16;
+          const uint32_t a_tmem = tmem + uint32_t(st * C::ACOLS);
+          const uint32_t b_base = smem_u32(smem + C::OFF_B + sb * C::BSTAGE);
+          const int kk_n = 4 * ((ks == ks_n - 1) ? atoms_last : KA);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
+          for (int kk = 0; kk < 4 * KA; ++kk) {
             if (kk < kk_n) {
-              const uint64_t bdesc = sw128_desc(b_base + uint32_t((kk >> 2) * S::kBAtom + (kk & 3) * 32));
+              const uint64_t bdesc = sw128_desc(b_base + uint32_t((kk >> 2) * C::BATOM + (kk & 3) * 32));
               tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
             }
           }
@@ -464,41 +469,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(mma_done);
       drain_wait(mma_done, 0);
     }
-  } else if (warp >= 4 && warp < kEpiWarp0) {
+  } else if (warp >= 4 && warp < 4 + 4 * NT) {
     // ------------------------------------------------------------ dequant
-    const int wg = (warp - 4) >> 2;  // K-stages with it % kDqWGs == wg, TMEM A stage wg
+    const int wg = (warp - 4) >> 2;  // K-stages with it % NT == wg, TMEM A stage wg
     const int q = warp & 3;          // TMEM lane quarter
     const int m = q * 32 + lane;     // weight row within the tile
-    const int sw = (m >> 1) & 3;     // 64-byte swizzle of the nibble tile
-    const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(wg * kAColsPerStage);
+    // nibble tile swizzle: 64-byte rows (KA=2) use the 64B pattern, 128-byte rows (KA=4) the 128B one
+    const int sw = (KA == 2) ? ((m >> 1) & 3) : (m & 7);
+    const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(wg * C::ACOLS);
     uint32_t it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
       for (int ks = 0; ks < ks_n; ++ks, ++it) {
-        if (int(it % kDqWGs) != wg) continue;
-        const int sa = it % kNA;
+        if (int(it % NT) != wg) continue;
+        const int sa = it % NA;
         // every lane waits (acquire), the decision is made warp-uniform so the
         // .sync.aligned tcgen05 instructions below never run divergent
-        ok = wait_bar(afull(sa), (it / kNA) & 1, ctl, 30);
+        ok = wait_bar(afull(sa), (it / NA) & 1, ctl, 30);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
-        const unsigned char* nib = smem + S::kNib + sa * kNibBytes + m * (kBK / 2);
-        const unsigned char* scl = smem + S::kScl + sa * kScaleBytes;
-        uint4 c[4];
-        uint32_t sc[4];
+        const unsigned char* nib = smem + C::OFF_NIB + sa * C::NIB + m * (C::BK / 2);
+        const unsigned char* scl = smem + C::OFF_SCL + sa * C::SCL;
+        uint4 c[C::GROUPS];
+        uint32_t sc[C::GROUPS], smax = 0;
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
+        for (int g = 0; g < C::GROUPS; ++g) {
           c[g] = *reinterpret_cast<const uint4*>(nib + ((g ^ sw) << 4));
           sc[g] = scl[g * kBM + m];
+          smax = smax > sc[g] ? smax : sc[g];
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(aempty(sa));
         // scales above 128 need a second power-of-two factor; decided per warp
-        const bool two = __any_sync(0xffffffffu, (sc[0] | sc[1] | sc[2] | sc[3]) > 128u);
-        ok = wait_bar(tempty(wg), ((it / kNT) & 1) ^ 1, ctl, 31);
+        const bool two = __any_sync(0xffffffffu, smax > 128u);
+        ok = wait_bar(tempty(wg), ((it / NT) & 1) ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         tc_fence_after();
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {  // two halves of 32 columns keep the register footprint small
+        for (int h = 0; h < C::GROUPS / 2; ++h) {  // 32 columns at a time keeps the register footprint small
           uint32_t v[32];
           if (two) {
             dequant_group<true>(c[2 * h], sc[2 * h], v);
@@ -548,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
         }
         if (c0 + 16 >= npad) {
-          // last accumulator columns read: hand the buffer back to the MMA warp early
+          // last accumulator columns read: hand the buffer back to the MMA warps early
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(dempty(d));
@@ -641,25 +648,26 @@ int make_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* b
   return KLC_OK;
 }
 
-template <int PHASE, int BN, int NB, bool DUAL>
+template <int PHASE, class C>
 int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16_t* act, int64_t rows_cap, int experts,
-                    const TcParams& p, int max_rowblocks, cudaStream_t stream) {
-  using S = Smem<PHASE, BN, NB, DUAL>;
+                    TcParams p, int max_rowblocks, cudaStream_t stream) {
   CUtensorMap ma, ms, mb;
   const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out), G = K / 32;
+  p.ksteps = int((K + C::BK - 1) / C::BK);
   {
-    // packed nibbles [E][N][K/2] bytes; box = 128 rows x 64 bytes (128 values), 64-byte swizzle
+    // packed nibbles [E][N][K/2] bytes; box = 128 rows x BK/2 bytes, swizzled like the dequant reads it
     const uint64_t dims[3] = {K / 2, N, uint64_t(experts)};
     const uint64_t strides[2] = {K / 2, N * K / 2};
-    const uint32_t box[3] = {kBK / 2, kBM, 1};
-    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+    const uint32_t box[3] = {uint32_t(C::BK / 2), kBM, 1};
+    const CUtensorMapSwizzle swz = (C::KA == 2) ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, swz);
     if (st != KLC_OK) return st;
   }
   {
-    // scales [E][G][N] bytes; box = 4 groups x 128 rows
+    // scales [E][G][N] bytes; box = BK/32 groups x 128 rows
     const uint64_t dims[3] = {N, G, uint64_t(experts)};
     const uint64_t strides[2] = {N, G * N};
-    const uint32_t box[3] = {kBM, kBK / 32, 1};
+    const uint32_t box[3] = {kBM, uint32_t(C::GROUPS), 1};
     int st = make_map(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, scales_t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != KLC_OK) return st;
   }
@@ -672,32 +680,32 @@ int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16
     if (st != KLC_OK) return st;
   }
   // >= 116 KB of shared memory keeps one CTA (and one 512-column TMEM allocation) per SM
-  const int smem = (S::kBytes + 1024 > 118 * 1024) ? S::kBytes + 1024 : 118 * 1024;
-  KLC_CUDA(cudaFuncSetAttribute(tc_expert_kernel<PHASE, BN, NB, DUAL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int smem = (C::BYTES + 1024 > 118 * 1024) ? C::BYTES + 1024 : 118 * 1024;
+  KLC_CUDA(cudaFuncSetAttribute(tc_expert_kernel<PHASE, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
   const int grid = int(items < sm_count() ? items : sm_count());
   if (grid <= 0) return KLC_OK;
-  tc_expert_kernel<PHASE, BN, NB, DUAL><<<grid, kThreads, smem, stream>>>(ma, ms, mb, p);
+  tc_expert_kernel<PHASE, C><<<grid, kThreads, smem, stream>>>(ma, ms, mb, p);
   KLC_LAUNCH_CHECK("tcgen05 expert launch");
   return KLC_OK;
 }
 
-// DUAL pipelines need at least two K-stages per tile (K > 128)
-template <int PHASE, int BN, int NB>
-int launch_tc_phase_any(const uint8_t* blocks, const uint8_t* scales_t, const uint16_t* act, int64_t rows_cap,
-                        int experts, const TcParams& p, int max_rowblocks, cudaStream_t stream) {
-  if (BN <= 128 && p.ksteps >= 2)
-    return launch_tc_phase<PHASE, BN, NB, (BN <= 128)>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
-  return launch_tc_phase<PHASE, BN, NB, false>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
+// Per-phase choice: two pipelines need at least two K-stages; smaller
+// reductions use a single pipeline.
+template <int PHASE, class CBig, class CSmall>
+int launch_tc_pick(const uint8_t* blocks, const uint8_t* scales_t, const uint16_t* act, int64_t rows_cap, int experts,
+                   const TcParams& p, int max_rowblocks, cudaStream_t stream) {
+  if (p.k_in >= 2 * CBig::BK)
+    return launch_tc_phase<PHASE, CBig>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
+  return launch_tc_phase<PHASE, CSmall>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
 }
 
-template <int BN, int NB>
+template <class CBig, class CSmall>
 int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   const klc_moe_weights& w = *a.wts;
   TcParams p1{};
   p1.n_out = int(2 * a.inter);
   p1.k_in = int(a.hidden);
-  p1.ksteps = int((a.hidden + kBK - 1) / kBK);
   p1.n_mtiles = (p1.n_out + kBM - 1) / kBM;
   p1.rowblocks = a.rowblocks;
   p1.status = a.status_rw;
@@ -709,22 +717,34 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   p1.precision = a.precision;
   p1.limit = w.swiglu_limit;
   p1.alpha = w.alpha;
-  int st = launch_tc_phase_any<1, BN, NB>(w.gu_blocks, w.gu_scales_t, a.xp, a.rows_cap, int(a.experts), p1, a.max_rowblocks, stream);
+  int st = launch_tc_pick<1, CBig, CSmall>(w.gu_blocks, w.gu_scales_t, a.xp, a.rows_cap, int(a.experts), p1,
+                                           a.max_rowblocks, stream);
   if (st != KLC_OK) return st;
   stage_mark(kStageGateUp, stream);
   TcParams p2 = p1;
   p2.n_out = int(a.hidden);
   p2.k_in = int(a.inter);
-  p2.ksteps = int((a.inter + kBK - 1) / kBK);
   p2.n_mtiles = (p2.n_out + kBM - 1) / kBM;
   p2.bias = w.dn_bias;
   p2.out = a.y;
   p2.out_ld = int(a.hidden);
-  st = launch_tc_phase_any<2, BN, NB>(w.dn_blocks, w.dn_scales_t, static_cast<const uint16_t*>(a.gated), a.rows_cap,
-                                  int(a.experts), p2, a.max_rowblocks, stream);
+  st = launch_tc_pick<2, CBig, CSmall>(w.dn_blocks, w.dn_scales_t, static_cast<const uint16_t*>(a.gated), a.rows_cap,
+                                       int(a.experts), p2, a.max_rowblocks, stream);
   stage_mark(kStageDown, stream);
   return st;
 }
+
+// Measured on B200 (decode, T=256): 128-K stages with four dequant
+// warpgroups beat 256-K stages -- the dequant's TMEM writes and the MMA's
+// TMEM reads of the A operand share TMEM bandwidth, so fewer, longer stages
+// do not shorten the MMA chain.
+//                 BN   NB  DUAL   KA NT NA  ND
+using CfgN32  = Cfg<32,  4, true,  2, 4, 8,  2>;
+using CfgN64  = Cfg<64,  4, true,  2, 4, 12, 2>;
+using CfgN128 = Cfg<128, 4, true,  2, 4, 8,  1>;
+using CfgN256 = Cfg<256, 2, false, 2, 4, 8,  1>;
+using CfgSmall32  = Cfg<32,  4, false, 2, 4, 8,  2>;
+using CfgSmall64  = Cfg<64,  4, false, 2, 4, 12, 2>;
 
 }  // namespace
 
@@ -740,12 +760,13 @@ bool tc_path_supported(int64_t hidden, int64_t inter) {
 int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   KLC_CHECK_ARG(a.hidden % kAtom == 0 && a.inter % kAtom == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
   KLC_CHECK_ARG(a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
-  // block_n (the max rows of a row-block) decides the N tile and the B ring depth
+  // block_n (the max rows of a row-block) decides the tile configuration
   switch (a.block_n) {
-    case 64: return launch_tc_both<64, 4>(a, stream);
-    case 128: return launch_tc_both<128, 4>(a, stream);
-    case 256: return launch_tc_both<256, 2>(a, stream);
-    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 64, 128 or 256");
+    case 32: return launch_tc_both<CfgN32, CfgSmall32>(a, stream);
+    case 64: return launch_tc_both<CfgN64, CfgSmall64>(a, stream);
+    case 128: return launch_tc_both<CfgN128, CfgN256>(a, stream);
+    case 256: return launch_tc_both<CfgN256, CfgN256>(a, stream);
+    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 32, 64, 128 or 256");
   }
 }
 
