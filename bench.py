@@ -106,18 +106,27 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def dist_setup(use_gpu: bool = True):
+def dist_setup(use_gpu: bool = True, force_group: bool = False):
     """One process per GPU under torchrun (RANK/LOCAL_RANK/WORLD_SIZE); NCCL for the GPU arm, gloo for the CPU arm."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if use_gpu:
         torch.cuda.set_device(local)
-    if world > 1:
+    if world > 1 or force_group:
         import datetime
 
         import torch.distributed as dist
 
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        if "MASTER_PORT" not in os.environ:
+            import socket
+
+            with socket.socket() as sk:
+                sk.bind(("127.0.0.1", 0))
+                os.environ["MASTER_PORT"] = str(sk.getsockname()[1])
+        os.environ.setdefault("RANK", str(rank))
+        os.environ.setdefault("WORLD_SIZE", str(world))
         if use_gpu:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
         else:
@@ -126,7 +135,9 @@ def dist_setup(use_gpu: bool = True):
 
 
 def barrier(world):
-    if world > 1:
+    import torch.distributed as dist
+
+    if world > 1 or (dist.is_available() and dist.is_initialized()):
         import torch.distributed as dist
 
         dist.barrier()
@@ -348,13 +359,78 @@ def run_ours(args, world, rank, local):
         print(json.dumps(result))
 
 
+def run_ep(args, world, rank, local):
+    """N > 1: experts sharded over the ranks (EP), NCCL all-to-all dispatch and combine."""
+    from kcapw_klcquant_b200 import synthetic as syn
+    from kcapw_klcquant_b200.ep import ExpertParallelMoe
+
+    device = torch.device("cuda", local)
+    strong = args.workload == "ep-prefill"
+    T = (args.tokens // world) if strong else args.tokens
+    zipf = 1.1 if (args.workload == "prefill" or args.zipf) else None
+    layer = syn.make_layer(syn.GPT_OSS_120B, seed=args.seed, zipf=zipf, device=device)  # same seed: same layer on every rank
+    moe = ExpertParallelMoe(0, layer, device, top_k=TOP_K, path=args.path)
+    del layer
+    torch.cuda.empty_cache()
+    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed + rank, device=device)
+    pk = peaks()
+    fwd = lambda: moe.forward(x, precision=args.precision)  # noqa: E731
+    with ClockSampler(local) as clk:
+        times = time_steps(fwd, args.steps, args.warmup, None, world)
+    ms = max_over_ranks(sum(times) / len(times), world)
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e():
+        x_dev.copy_(x_host, non_blocking=True)
+        y, _ = moe.forward(x_dev, precision=args.precision)
+        y_host.copy_(y, non_blocking=True)
+
+    et = time_steps(e2e, args.steps, args.warmup, None, world)
+    e2e_ms = max_over_ranks(sum(et) / len(et), world)
+    epr = GPT_OSS_E // world
+    layer_bytes = epr * BYTES_PER_EXPERT  # per rank: its experts' weights (all are routed to at these sizes)
+    result = {
+        "metric": "moe_layer_tokens_per_s",
+        "value": world * T / (ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong" if strong else "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded GPT-OSS-120B MXFP4 MoE layer, bf16 N(0,1) activations)",
+        "config": {
+            "workload": (f"config 3: expert-parallel MoE layer, {args.tokens} tokens split over {world} ranks" if strong
+                         else f"config 1 layout, expert-parallel decode: T={T} tokens per GPU") + f", E=128 ({epr} per GPU), H=I=2880, top-4"
+                        + (", Zipf(1.1) router bias" if zipf else ", uniform routing"),
+            "precision": args.precision, "expert_path": args.path, "l2": "weights (>=210 MB per GPU) exceed L2",
+            "parallelism": f"ep{world} (NCCL all-to-all dispatch + combine)",
+        },
+        "roofline": {"bound": "hbm" if not strong else "tensor", "kernel": "whole EP layer step (per rank)",
+                     "achieved": layer_bytes / (ms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": layer_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"]},
+        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * GPT_OSS_H * 2,
+                "d2h_bytes_per_step": T * GPT_OSS_H * 2},
+        "gpu_launches": 11 * args.steps,
+        "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(result))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill"], default="decode")
+    ap.add_argument("--workload", choices=["decode", "prefill", "ep-prefill"], default="decode")
+    ap.add_argument("--zipf", action="store_true", help="Zipf(1.1)-skewed router for the EP workloads")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--path", choices=["auto", "simt", "tc"], default="auto")
@@ -366,17 +442,20 @@ def main():
     if args.warmup < 3:
         args.warmup = 3
     if args.tokens is None:
-        args.tokens = 256 if args.workload == "decode" else 4096
-    world, rank, local = dist_setup(use_gpu=args.impl != "reference")
+        args.tokens = {"decode": 256, "prefill": 4096, "ep-prefill": 16384}[args.workload]
+    world, rank, local = dist_setup(use_gpu=args.impl != "reference",
+                                    force_group=(args.impl != "reference" and args.workload == "ep-prefill"))
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif world > 1 or args.workload == "ep-prefill":
+            run_ep(args, world, rank, local)
         else:
             run_ours(args, world, rank, local)
     finally:
-        if world > 1:
-            import torch.distributed as dist
+        import torch.distributed as dist
 
+        if dist.is_available() and dist.is_initialized():
             dist.destroy_process_group()
 
 

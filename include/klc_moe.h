@@ -216,6 +216,20 @@ int klc_stage_times(float* ms, int max_stages, int* n_out);
  * may be NULL.                                                             */
 int klc_workspace_status(const void* workspace, int* code, int* where, int* detail, void* stream);
 
+/* Expert-parallel dispatch packing (no counterpart in the reference, which
+ * runs on one device).  Experts are sharded contiguously: rank r owns
+ * experts [r*experts_per_rank, (r+1)*experts_per_rank).  Groups the (token,
+ * slot) pairs of idx int32 [T,k] by destination rank (stable: token-major,
+ * slot-minor) and writes send_rows bf16 [T*k, H] (x[token] of each pair in
+ * that order), send_expert int32 [T*k] (the pair's expert id local to its
+ * rank), send_counts int32 [nranks] and pair_pos int32 [T*k] (send row of
+ * each pair, the input klc_moe_combine needs once the expert outputs come
+ * back in the same order).  Workspace: klc_moe_workspace_size with dims
+ * {T, 64, 64, max(nranks, k), k, KLC_PATH_SIMT}.                            */
+int klc_ep_pack(const int32_t* idx, int64_t tokens, int k, int64_t experts_per_rank, int nranks, const uint16_t* x,
+                int64_t hidden, uint16_t* send_rows, int32_t* send_expert, int32_t* send_counts, int32_t* pair_pos,
+                void* workspace, size_t workspace_bytes, void* stream);
+
 /* RMSNorm (streamed_attention.py:27-28): y = bf16(bf16(x * bf16(rsqrt(mean(x^2)+eps))) * w). */
 int klc_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int64_t hidden, float eps, uint16_t* y,
                  void* stream);

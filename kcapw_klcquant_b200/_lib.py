@@ -83,6 +83,7 @@ SIGNATURES: dict[str, list] = {
     "klc_moe_combine": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p],
     "klc_moe_bias_only": [c_void_p, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "klc_moe_permute": [c_void_p, c_int64, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_size_t, c_void_p],
+    "klc_ep_pack": [c_void_p, c_int64, c_int, c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "klc_workspace_status": [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int), c_void_p],
     "klc_stage_timing": [c_int],
     "klc_stage_times": [POINTER(c_float), c_int, POINTER(c_int)],

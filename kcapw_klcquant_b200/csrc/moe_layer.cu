@@ -278,3 +278,45 @@ extern "C" int klc_stage_times(float* ms, int max_stages, int* n_out) {
   if (n_out) *n_out = n;
   return KLC_OK;
 }
+
+extern "C" int klc_ep_pack(const int32_t* idx, int64_t tokens, int k, int64_t experts_per_rank, int nranks,
+                           const uint16_t* x, int64_t hidden, uint16_t* send_rows, int32_t* send_expert,
+                           int32_t* send_counts, int32_t* pair_pos, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  KLC_CHECK_ARG(tokens >= 0 && k >= 1 && experts_per_rank >= 1 && nranks >= 1 && nranks <= 1024 && hidden > 0 &&
+                    hidden % 8 == 0,
+                "klc_ep_pack: bad sizes");
+  if (tokens == 0) {
+    if (send_counts) KLC_CUDA(cudaMemsetAsync(send_counts, 0, size_t(nranks) * 4, as_stream(stream)));
+    return KLC_OK;
+  }
+  KLC_CHECK_ARG(idx && x && send_rows && send_expert && send_counts && pair_pos, "klc_ep_pack: null pointer");
+  klc_moe_dims d{tokens, 64, 64, nranks, k, KLC_PATH_SIMT};
+  const WorkspaceLayout L = workspace_layout(d, false);
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(KLC_ERR_WORKSPACE, "klc_ep_pack: workspace too small (need " + std::to_string(L.total) + " bytes)");
+  char* ws = static_cast<char*>(workspace);
+  DeviceStatus* status = reinterpret_cast<DeviceStatus*>(ws + L.status);
+  KLC_CUDA(cudaMemsetAsync(status, 0, sizeof(DeviceStatus), as_stream(stream)));
+  PermuteArgs pa{};
+  pa.idx = idx;
+  pa.tokens = tokens;
+  pa.k = k;
+  pa.experts = nranks;
+  pa.pad = 1;
+  pa.block_n = 1 << 24;
+  pa.counts = send_counts;
+  pa.offsets = reinterpret_cast<int32_t*>(ws + L.offsets);
+  pa.rows = reinterpret_cast<int32_t*>(ws + L.rows);
+  pa.pair_pos = pair_pos;
+  pa.chunk_hist = reinterpret_cast<int32_t*>(ws + L.chunk_hist);
+  pa.rowblocks = reinterpret_cast<int4*>(ws + L.rowblocks);
+  pa.status = status;
+  pa.x = x;
+  pa.hidden = hidden;
+  pa.xp = send_rows;
+  pa.perm_k = 0;
+  pa.div = int(experts_per_rank);
+  pa.aux_out = send_expert;
+  return launch_permute(pa, as_stream(stream));
+}

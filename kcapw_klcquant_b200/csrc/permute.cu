@@ -26,13 +26,14 @@ namespace {
 constexpr int kChunk = 1024;
 
 __global__ void __launch_bounds__(kChunk)
-    hist_kernel(const int32_t* __restrict__ idx, int64_t pairs, int experts, int32_t* __restrict__ chunk_hist) {
+    hist_kernel(const int32_t* __restrict__ idx, int64_t pairs, int experts, int div, int32_t* __restrict__ chunk_hist) {
   extern __shared__ int32_t hist[];
   for (int e = threadIdx.x; e < experts; e += blockDim.x) hist[e] = 0;
   __syncthreads();
   const int64_t p = int64_t(blockIdx.x) * kChunk + threadIdx.x;
   if (p < pairs) {
-    const int e = idx[p];
+    const int v = idx[p];
+    const int e = v >= 0 ? v / div : -1;
     if (e >= 0 && e < experts) atomicAdd(&hist[e], 1);
   }
   __syncthreads();
@@ -106,7 +107,8 @@ __global__ void __launch_bounds__(kChunk)
     scatter_gather_kernel(const int32_t* __restrict__ idx, int64_t pairs, int k, int experts,
                           const int32_t* __restrict__ chunk_base, int32_t* __restrict__ rows,
                           int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x, int64_t hidden,
-                          uint16_t* __restrict__ xp, int perm_k, DeviceStatus* st) {
+                          uint16_t* __restrict__ xp, int perm_k, int div, int32_t* __restrict__ aux_out,
+                          DeviceStatus* st) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                      // [32][experts]
   int32_t* s_pos = sm + 32 * experts;          // [kChunk]
@@ -114,11 +116,12 @@ __global__ void __launch_bounds__(kChunk)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < 32 * experts; i += blockDim.x) warp_cnt[i] = 0;
   const int64_t p = int64_t(blockIdx.x) * kChunk + threadIdx.x;
-  int e = -1;
+  int e = -1, v = -1;
   if (p < pairs) {
-    e = idx[p];
+    v = idx[p];
+    e = v >= 0 ? v / div : -1;
     if (e < 0 || e >= experts) {
-      record_fault(st, KLC_ERR_DEVICE_FAULT, 1, e);
+      record_fault(st, KLC_ERR_DEVICE_FAULT, 1, v);
       e = -1;
     }
   }
@@ -140,6 +143,7 @@ __global__ void __launch_bounds__(kChunk)
   if (e >= 0) {
     pos = chunk_base[int64_t(blockIdx.x) * experts + e] + warp_cnt[warp * experts + e] + rank;
     rows[pos] = int32_t(p);
+    if (aux_out != nullptr) aux_out[pos] = v - e * div;
   }
   if (p < pairs) pair_pos[p] = pos;
   s_pos[threadIdx.x] = pos;
@@ -166,7 +170,8 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
   if (pairs == 0) return KLC_OK;
   const int nchunks = int((pairs + kChunk - 1) / kChunk);
   const int E = int(a.experts);
-  hist_kernel<<<nchunks, kChunk, E * sizeof(int32_t), stream>>>(a.idx, pairs, E, a.chunk_hist);
+  const int div = a.div > 0 ? a.div : 1;
+  hist_kernel<<<nchunks, kChunk, E * sizeof(int32_t), stream>>>(a.idx, pairs, E, div, a.chunk_hist);
   KLC_LAUNCH_CHECK("permute hist launch");
   scan_kernel<<<1, 1024, 0, stream>>>(a.chunk_hist, nchunks, E, a.pad, a.block_n, a.counts, a.offsets, a.rows,
                                       a.rowblocks, a.status);
@@ -174,7 +179,7 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
   const size_t smem = (size_t(32) * E + 2 * kChunk) * sizeof(int32_t);
   KLC_CUDA(cudaFuncSetAttribute(scatter_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   scatter_gather_kernel<<<nchunks, kChunk, smem, stream>>>(a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos,
-                                                          a.x, a.hidden, a.xp, a.perm_k, a.status);
+                                                          a.x, a.hidden, a.xp, a.perm_k, div, a.aux_out, a.status);
   KLC_LAUNCH_CHECK("permute scatter launch");
   return KLC_OK;
 }

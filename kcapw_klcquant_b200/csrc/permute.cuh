@@ -26,6 +26,8 @@ struct PermuteArgs {
   int64_t hidden;
   uint16_t* xp;        // [rows_cap, H] or null
   int perm_k;          // 1: write rows in the tensor-core K order
+  int div;             // group id = idx / div (1: group by expert; experts-per-rank: group by rank)
+  int32_t* aux_out;    // optional [rows_cap]: idx % div of the pair stored at each row
 };
 
 int launch_permute(const PermuteArgs& a, cudaStream_t stream);
