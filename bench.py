@@ -44,6 +44,9 @@ BYTES_PER_EXPERT = (2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H /
 )  # 13,236,480
 GATE_UP_BYTES_PER_EXPERT = 2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H // 32 + 2 * GPT_OSS_I * 2  # 8,824,320
 FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H)  # 199,065,600
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from an ncu capture of
+# this workload at T=256 (ncu --set full, one launch); None where no capture was taken
+PROFILED_GATE_UP_TRAFFIC = {"decode": 1_141_934_000 + 13_405_952}
 
 
 def peaks() -> dict:
@@ -296,7 +299,8 @@ def run_ours(args, world, rank, local):
         bytes_gu = U * GATE_UP_BYTES_PER_EXPERT + T * TOP_K * GPT_OSS_H * 2
         achieved = bytes_gu / (gu_ms / 1e3) / 1e9
         roof = {"bound": "hbm", "kernel": "gate_up GEMM (MXFP4 dequant + SwiGLU epilogue)", "achieved": achieved, "peak": pk["hbm_gbs"],
-                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"],
+                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
+                "traffic": PROFILED_GATE_UP_TRAFFIC.get("decode") if T == 256 else None,
                 "algorithmic_bytes": bytes_gu, "unique_experts": U}
         layer_bytes = U * BYTES_PER_EXPERT + GPT_OSS_E * GPT_OSS_H * 2 + GPT_OSS_E * 2 + T * GPT_OSS_H * 4
         layer_roof = {"bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9, "frac": layer_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"]}
