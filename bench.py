@@ -27,7 +27,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -59,54 +58,67 @@ def peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock and clock-event reasons polled through NVML (read-only queries) every
+    millisecond between start() and stop(), i.e. while the timed steps run on the GPU."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown", "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown", "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
-
-    def __enter__(self):
+    def __init__(self, cuda_index: int):
+        self.samples: list[int] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self.h = None
+        self._stop = threading.Event()
+        self._t = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
-        return self
+            import pynvml as nv
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            nv.nvmlInit()
+            self.nv = nv
+            self.h = self._handle(cuda_index)
+            self.max_mhz = nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM)
+        except Exception:  # no NVML: the line says so through samples == 0
+            self.h = None
 
-    def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+    def _handle(self, i: int):
+        nv = self.nv
+        p = torch.cuda.get_device_properties(i)
+        if all(hasattr(p, a) for a in ("pci_domain_id", "pci_bus_id", "pci_device_id")):
             try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+                return nv.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0")
+            except Exception:
+                pass
+        return nv.nvmlDeviceGetHandleByIndex(i)
+
+    def _poll(self):
+        nv = self.nv
+        bits = {n: getattr(nv, a) for n, a in self.REASONS.items()}
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.reasons.update(n for n, b in bits.items() if r & b)
+            except Exception:
+                return
+            time.sleep(0.001)
+
+    def start(self):
+        if self.h is not None:
+            self._stop.clear()
+            self._t = threading.Thread(target=self._poll, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t is not None:
+            self._stop.set()
+            self._t.join(timeout=5)
+            self._t = None
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        sm = self.samples
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(sm), "source": "nvml" if self.h is not None else "unavailable"}
 
 
 def dist_setup(use_gpu: bool = True, force_group: bool = False):
@@ -165,8 +177,9 @@ def make_layer(workload: str, seed: int, device):
     return MoeLayer.from_tensors(0, layer, device, top_k=TOP_K)
 
 
-def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None, world: int):
-    """Per-step device times (ms) of ``fn`` with CUDA events on the current stream."""
+def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None, world: int, clk: ClockSampler | None = None):
+    """Per-step device times (ms) of ``fn`` with CUDA events on the current stream; ``clk``
+    samples clocks from the first timed launch to the end of the last timed step."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -174,6 +187,8 @@ def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None, world: i
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    if clk is not None:
+        clk.start()
     for i in range(steps):
         if flush is not None:
             flush.add_(1)
@@ -181,6 +196,8 @@ def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None, world: i
         fn()
         ev[i][1].record(stream)
     torch.cuda.synchronize()
+    if clk is not None:
+        clk.stop()
     barrier(world)
     return [a.elapsed_time(b) for a, b in ev]
 
@@ -265,8 +282,8 @@ def run_ours(args, world, rank, local):
     fwd = lambda: ml.forward(x, precision=args.precision, out=out, path=args.path)  # noqa: E731
 
     U = unique_experts(ml, x)
-    with ClockSampler(local) as clk:
-        times = time_steps(fwd, args.steps, args.warmup, flush, world)
+    clk = ClockSampler(local)
+    times = time_steps(fwd, args.steps, args.warmup, flush, world, clk)
     ms = max_over_ranks(sum(times) / len(times), world)
     tokens_per_s = world * T / (ms / 1e3)
 
@@ -379,8 +396,8 @@ def run_ep(args, world, rank, local):
     x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed + rank, device=device)
     pk = peaks()
     fwd = lambda: moe.forward(x, precision=args.precision)  # noqa: E731
-    with ClockSampler(local) as clk:
-        times = time_steps(fwd, args.steps, args.warmup, None, world)
+    clk = ClockSampler(local)
+    times = time_steps(fwd, args.steps, args.warmup, None, world, clk)
     ms = max_over_ranks(sum(times) / len(times), world)
     x_host = x.cpu().pin_memory()
     y_host = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16).pin_memory()
@@ -430,7 +447,7 @@ def run_ep(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["decode", "prefill", "ep-prefill"], default="decode")

@@ -16,6 +16,10 @@
 //   3. per chunk: stable rank of each pair among equal experts (warp
 //      match_any + per-warp counts), scatter of rows/pair_pos, and the copy of
 //      x[token] into its padded row (optionally in the tensor-core K order).
+//      A chunk is split over `split` CTAs: each ranks the whole chunk (a few
+//      microseconds of shared-memory work) and copies 1/split of its rows, so
+//      a decode batch of one or two chunks still spreads its row copies over
+//      the SMs; only the first CTA of a chunk writes the index arrays.
 #include "klc_common.cuh"
 #include "permute.cuh"
 
@@ -108,20 +112,23 @@ __global__ void __launch_bounds__(kChunk)
                           const int32_t* __restrict__ chunk_base, int32_t* __restrict__ rows,
                           int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x, int64_t hidden,
                           uint16_t* __restrict__ xp, int perm_k, int div, int32_t* __restrict__ aux_out,
-                          DeviceStatus* st) {
+                          int split, DeviceStatus* st) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                      // [32][experts]
   int32_t* s_pos = sm + 32 * experts;          // [kChunk]
   int32_t* s_tok = s_pos + kChunk;             // [kChunk]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < 32 * experts; i += blockDim.x) warp_cnt[i] = 0;
-  const int64_t p = int64_t(blockIdx.x) * kChunk + threadIdx.x;
+  const int64_t chunk = blockIdx.x / split;
+  const int sub = int(blockIdx.x % split);
+  const bool writer = sub == 0;
+  const int64_t p = chunk * kChunk + threadIdx.x;
   int e = -1, v = -1;
   if (p < pairs) {
     v = idx[p];
     e = v >= 0 ? v / div : -1;
     if (e < 0 || e >= experts) {
-      record_fault(st, KLC_ERR_DEVICE_FAULT, 1, v);
+      if (writer) record_fault(st, KLC_ERR_DEVICE_FAULT, 1, v);
       e = -1;
     }
   }
@@ -141,17 +148,21 @@ __global__ void __launch_bounds__(kChunk)
   __syncthreads();
   int pos = -1;
   if (e >= 0) {
-    pos = chunk_base[int64_t(blockIdx.x) * experts + e] + warp_cnt[warp * experts + e] + rank;
-    rows[pos] = int32_t(p);
-    if (aux_out != nullptr) aux_out[pos] = v - e * div;
+    pos = chunk_base[chunk * experts + e] + warp_cnt[warp * experts + e] + rank;
+    if (writer) {
+      rows[pos] = int32_t(p);
+      if (aux_out != nullptr) aux_out[pos] = v - e * div;
+    }
   }
-  if (p < pairs) pair_pos[p] = pos;
+  if (writer && p < pairs) pair_pos[p] = pos;
   s_pos[threadIdx.x] = pos;
   s_tok[threadIdx.x] = (p < pairs) ? int32_t(p / k) : -1;
   __syncthreads();
   if (xp == nullptr) return;
   const int chunks = int(hidden / 8);
-  for (int i = warp; i < kChunk; i += 32) {
+  const int per = (kChunk + split - 1) / split;
+  const int i_end = min(kChunk, (sub + 1) * per);
+  for (int i = sub * per + warp; i < i_end; i += 32) {
     const int dst = s_pos[i];
     if (dst < 0) continue;
     const uint4* src = reinterpret_cast<const uint4*>(x + int64_t(s_tok[i]) * hidden);
@@ -178,8 +189,17 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
   KLC_LAUNCH_CHECK("permute scan launch");
   const size_t smem = (size_t(32) * E + 2 * kChunk) * sizeof(int32_t);
   KLC_CUDA(cudaFuncSetAttribute(scatter_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  scatter_gather_kernel<<<nchunks, kChunk, smem, stream>>>(a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos,
-                                                          a.x, a.hidden, a.xp, a.perm_k, div, a.aux_out, a.status);
+  // split each chunk's row copies over enough CTAs to cover the SMs twice (at most 8 rows per CTA)
+  int split = 1;
+  if (a.xp != nullptr) {
+    const int64_t want = (2 * int64_t(sm_count()) + nchunks - 1) / nchunks;
+    split = int(want < kChunk / 8 ? want : kChunk / 8);
+    if (split < 1) split = 1;
+  }
+  KLC_CHECK_ARG(int64_t(nchunks) * split <= 0x7fffffff, "permute: too many pairs");
+  scatter_gather_kernel<<<unsigned(int64_t(nchunks) * split), kChunk, smem, stream>>>(
+      a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos, a.x, a.hidden, a.xp, a.perm_k, div, a.aux_out, split,
+      a.status);
   KLC_LAUNCH_CHECK("permute scatter launch");
   return KLC_OK;
 }

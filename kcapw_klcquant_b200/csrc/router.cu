@@ -3,13 +3,19 @@
 // Replaces streamed_moe_router.py:269-284 (F.linear in bf16, topk of the
 // fp32 logits, softmax of the selected fp32 scores cast to bf16).
 //
-// One CTA handles kTok tokens.  The tokens' activations sit in shared memory
-// (bf16), each warp streams router rows (E x H bf16, L2-resident after the
-// first CTA) with 16-byte loads and accumulates kTok dot products in fp32;
-// a butterfly reduction finishes each dot product, the bias is added in fp32
-// and the logit is rounded once to bf16.  Then one warp per token runs k
-// rounds of a warp-wide arg-max (value descending, lower index on ties) and a
-// k-way softmax.
+// A thread-block cluster of C CTAs handles kTok tokens; CTA r of the cluster
+// computes the logits of experts [r*epc, (r+1)*epc) for those tokens, so a
+// decode batch of a few hundred tokens still spreads over every SM.  Each CTA
+// stages the tokens' activations in shared memory (bf16); each warp streams
+// router rows (E x H bf16, L2-resident after the first CTA) with 16-byte
+// loads, four in flight per lane, and accumulates kTok dot products in fp32.
+// A butterfly reduction finishes each dot product, the bias is added in fp32
+// and the logit is rounded once to bf16.  After a cluster barrier, one warp
+// per token gathers the token's E logits from the cluster's shared memory
+// (distributed shared memory), then runs k rounds of a warp-wide arg-max
+// (value descending, lower index on ties) and a k-way softmax.
+#include <cooperative_groups.h>
+
 #include "klc_common.cuh"
 
 namespace klc {
@@ -19,6 +25,7 @@ namespace {
 constexpr int kTok = 8;       // tokens per CTA
 constexpr int kWarps = 8;     // warps per CTA
 constexpr int kMaxK = 8;
+constexpr int kMaxCluster = 8;  // portable cluster size
 
 // k rounds of a warp-wide arg-max over `row` (value descending, lower index
 // on ties), then softmax over the k selected fp32 scores (max-subtracted,
@@ -86,14 +93,58 @@ __device__ void select_softmax_warp(const float* row, int experts, int k, bool k
   }
 }
 
+// dot products of one router row with the kTok staged tokens; lanes split the
+// 16-byte chunks of the row, four loads in flight per lane
+__device__ __forceinline__ void router_row_dots(const uint16_t* __restrict__ wr, const uint16_t* xs, int64_t hidden,
+                                                int chunks, float (&acc)[kTok]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
+  auto fma_chunk = [&](const uint4 wv, int c) {
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    float wf[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      wf[2 * j] = __uint_as_float(ww[j] << 16);
+      wf[2 * j + 1] = __uint_as_float(ww[j] & 0xffff0000u);
+    }
+#pragma unroll
+    for (int t = 0; t < kTok; ++t) {
+      const uint4 xv = reinterpret_cast<const uint4*>(xs + size_t(t) * hidden)[c];
+      const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[t] = fmaf(wf[2 * j], __uint_as_float(xx[j] << 16), acc[t]);
+        acc[t] = fmaf(wf[2 * j + 1], __uint_as_float(xx[j] & 0xffff0000u), acc[t]);
+      }
+    }
+  };
+  int c = lane;
+  for (; c + 96 < chunks; c += 128) {
+    uint4 wv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) wv[u] = ldg_nc_v4(wr + (c + 32 * u) * 8);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) fma_chunk(wv[u], c + 32 * u);
+  }
+  for (; c < chunks; c += 32) fma_chunk(ldg_nc_v4(wr + c * 8), c);
+#pragma unroll
+  for (int t = 0; t < kTok; ++t) acc[t] = warp_sum(acc[t]);
+}
+
 __global__ void __launch_bounds__(kWarps * 32)
     router_kernel(const uint16_t* __restrict__ x, int64_t tokens, int64_t hidden, const uint16_t* __restrict__ w,
-                  const uint16_t* __restrict__ b, int experts, int k, const float* __restrict__ adjust,
+                  const uint16_t* __restrict__ b, int experts, int k, int epc, const float* __restrict__ adjust,
                   int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = int(cluster.num_blocks());
+  const int crank = int(cluster.block_rank());
   extern __shared__ __align__(16) unsigned char smem[];
-  uint16_t* xs = reinterpret_cast<uint16_t*>(smem);                                      // [kTok][hidden]
-  float* logit_s = reinterpret_cast<float*>(smem + size_t(kTok) * hidden * 2);          // [kTok][experts]
-  const int64_t t0 = int64_t(blockIdx.x) * kTok;
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem);                                   // [kTok][hidden]
+  float* part = reinterpret_cast<float*>(smem + size_t(kTok) * hidden * 2);          // [kTok][epc]
+  float* rows = part + size_t(kTok) * epc;                                           // [ceil(kTok/C)][experts]
+  const int64_t t0 = int64_t(blockIdx.x / C) * kTok;
   const int ntok = int(tokens - t0 < kTok ? tokens - t0 : kTok);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
@@ -107,53 +158,36 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
   __syncthreads();
 
-  for (int e = warp; e < experts; e += kWarps) {
+  const int e_lo = crank * epc;
+  const int e_hi = min(experts, e_lo + epc);
+  for (int e = e_lo + warp; e < e_hi; e += kWarps) {
     float acc[kTok];
-#pragma unroll
-    for (int t = 0; t < kTok; ++t) acc[t] = 0.f;
-    const uint16_t* wr = w + int64_t(e) * hidden;
-    for (int c = lane; c < chunks_per_row; c += 32) {
-      const uint4 wv = ldg_nc_v4(wr + c * 8);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-      float wf[8];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        wf[2 * j] = __uint_as_float(ww[j] << 16);
-        wf[2 * j + 1] = __uint_as_float(ww[j] & 0xffff0000u);
-      }
-#pragma unroll
-      for (int t = 0; t < kTok; ++t) {
-        const uint4 xv = reinterpret_cast<const uint4*>(xs + size_t(t) * hidden)[c];
-        const uint32_t xx[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc[t] = fmaf(wf[2 * j], __uint_as_float(xx[j] << 16), acc[t]);
-          acc[t] = fmaf(wf[2 * j + 1], __uint_as_float(xx[j] & 0xffff0000u), acc[t]);
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < kTok; ++t) acc[t] = warp_sum(acc[t]);
+    router_row_dots(w + int64_t(e) * hidden, xs, hidden, chunks_per_row, acc);
     if (lane == 0) {
       const float bias = bf16_to_f32(b[e]);
       for (int t = 0; t < ntok; ++t) {
         const uint16_t lb = f32_to_bf16(acc[t] + bias);
-        logit_s[t * experts + e] = bf16_to_f32(lb);
+        part[t * epc + (e - e_lo)] = bf16_to_f32(lb);
         if (out_logits) out_logits[(t0 + t) * experts + e] = lb;
       }
     }
   }
-  __syncthreads();
+  cluster.sync();
 
-  // top-k + softmax: one warp per token
-  for (int t = warp; t < ntok; t += kWarps) {
-    float* row = logit_s + t * experts;
-    if (adjust) {
-      for (int e = lane; e < experts; e += 32) row[e] += adjust[e];
+  // top-k + softmax: token crank + C*j goes to warp j of CTA crank
+  const int t = crank + C * warp;
+  if (warp * C < kTok && t < ntok) {
+    float* row = rows + size_t(warp) * experts;
+    for (int e = lane; e < experts; e += 32) {
+      const float* src = cluster.map_shared_rank(part, e / epc);
+      float v = src[t * epc + e % epc];
+      if (adjust) v += adjust[e];
+      row[e] = v;
     }
     __syncwarp();
     select_softmax_warp(row, experts, k, false, out_idx + (t0 + t) * k, out_w + (t0 + t) * k);
   }
+  cluster.sync();  // no CTA leaves while its logits may still be read
 }
 
 __global__ void select_kernel(const float* __restrict__ scores, int64_t tokens, int experts, int k, int keep_order,
@@ -178,13 +212,29 @@ int launch_router(const uint16_t* x, int64_t tokens, int64_t hidden, const uint1
   KLC_CHECK_ARG(x && w && b && out_idx && out_w, "klc_router_topk: null pointer");
   KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
                 "klc_router_topk: x and w must be 16-byte aligned");
-  const size_t smem = size_t(kTok) * hidden * 2 + size_t(kTok) * experts * 4;
+  // cluster size: enough CTAs to cover the SMs twice, at least 8 experts per CTA
+  const int64_t nblocks = (tokens + kTok - 1) / kTok;
+  int C = 1;
+  while (C < kMaxCluster && nblocks * C < 2 * int64_t(sm_count()) && 2 * C * 8 <= experts) C *= 2;
+  const int epc = int((experts + C - 1) / C);
+  const size_t smem = size_t(kTok) * hidden * 2 + size_t(kTok) * epc * 4 + size_t((kTok + C - 1) / C) * experts * 4;
   KLC_CHECK_ARG(smem <= 200 * 1024, "klc_router_topk: hidden size too large for one CTA tile");
   KLC_CUDA(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  const int64_t grid = (tokens + kTok - 1) / kTok;
-  KLC_CHECK_ARG(grid <= 0x7fffffff, "klc_router_topk: too many tokens");
-  router_kernel<<<unsigned(grid), kWarps * 32, smem, stream>>>(x, tokens, hidden, w, b, int(experts), k, adjust,
-                                                               out_idx, out_w, out_logits);
+  KLC_CHECK_ARG(nblocks * C <= 0x7fffffff, "klc_router_topk: too many tokens");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(nblocks * C));
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  KLC_CUDA(cudaLaunchKernelEx(&cfg, router_kernel, x, tokens, hidden, w, b, int(experts), k, epc, adjust, out_idx,
+                              out_w, out_logits));
   KLC_LAUNCH_CHECK("klc_router_topk launch");
   return KLC_OK;
 }
