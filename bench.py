@@ -291,9 +291,10 @@ def run_ours(args, world, rank, local):
     _lib.stage_timing(True)
     stage = {}
     for _ in range(3):
-        if flush is not None:
-            flush.add_(1)
-        fwd()
+        for _ in range(2):  # the first call keeps the GPU busy while the second's launches are issued
+            if flush is not None:
+                flush.add_(1)
+            fwd()
         stage = _lib.stage_times()
     _lib.stage_timing(False)
     # end-to-end through the public API with host buffers

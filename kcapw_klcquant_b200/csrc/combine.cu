@@ -14,6 +14,8 @@ namespace klc {
 
 namespace {
 
+constexpr int kMaxTopK = 8;
+
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ pair_pos,
                                const uint16_t* __restrict__ w, int k, int64_t hidden,
                                const uint16_t* __restrict__ residual, uint16_t* __restrict__ out,
@@ -24,16 +26,27 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
     const int64_t q = t * k * 2 + threadIdx.x;
     norms[q] = sqrtf(normsq[q]);
   }
+  int pos[kMaxTopK];
+  float wsel[kMaxTopK];
+#pragma unroll
+  for (int s = 0; s < kMaxTopK; ++s) {
+    pos[s] = s < k ? pair_pos[t * k + s] : -1;
+    wsel[s] = s < k ? bf16_to_f32(w[t * k + s]) : 0.f;
+  }
   for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    // all k rows in flight before the dependent bf16 chain
+    uint4 v[kMaxTopK];
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s)
+      v[s] = pos[s] >= 0 ? reinterpret_cast<const uint4*>(y + int64_t(pos[s]) * hidden)[c] : make_uint4(0, 0, 0, 0);
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-    for (int s = 0; s < k; ++s) {
-      const int pos = pair_pos[t * k + s];
-      if (pos < 0) continue;  // pair dropped by the permute's index check (recorded in the status word)
-      const float ws = bf16_to_f32(w[t * k + s]);
-      const uint4 v = reinterpret_cast<const uint4*>(y + int64_t(pos) * hidden)[c];
-      const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s) {
+      if (pos[s] < 0) continue;  // past k, or a pair dropped by the permute's index check (recorded in the status word)
+      const float ws = wsel[s];
+      const uint32_t vv[4] = {v[s].x, v[s].y, v[s].z, v[s].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
@@ -113,6 +126,7 @@ int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w
                    cudaStream_t stream) {
   if (tokens == 0) return KLC_OK;
   KLC_CHECK_ARG(tokens <= 0x7fffffff, "combine: too many tokens");
+  KLC_CHECK_ARG(k >= 1 && k <= kMaxTopK, "combine: need 1 <= k <= 8");
   int64_t threads = (hidden / 8 + 31) / 32 * 32;
   threads = threads < 64 ? 64 : (threads > 256 ? 256 : threads);
   combine_kernel<<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq, norms);

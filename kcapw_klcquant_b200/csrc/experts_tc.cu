@@ -9,18 +9,22 @@
 // I for down).  One persistent CTA per SM walks the (row-block, m-tile)
 // work list.
 //
-// Per CTA, warp-specialised:
-//   warp 0      TMA producer: packed E2M1 nibbles (128 rows x 32 B, 32B
-//               swizzle) + E8M0 scales (2 groups x 128 rows) into an A ring,
-//               token rows (n x 64 bf16, 128B swizzle) into a B ring
-//   warp 1      TMEM allocator and MMA issuer (one thread):
-//               tcgen05.mma.cta_group::1.kind::f16, A from TMEM, B from smem
-//   warps 4-11  two dequant warpgroups (alternating K-steps): one thread per
-//               weight row converts 64 E2M1 values x 2^(s-127) to exact bf16
-//               and writes them straight into a TMEM A stage (tcgen05.st) --
-//               the dequantized weights never touch shared memory
-//   warps 12-15 epilogue: tcgen05.ld of the fp32 accumulators, bias,
-//               SwiGLU (gate_up) or bias (down), bf16 stores
+// Per CTA, warp-specialised (832 threads):
+//   warps 0-3   MMA issuers, one thread each (warp 0 also allocates TMEM):
+//               tcgen05.mma.cta_group::1.kind::f16, A from TMEM, B from smem;
+//               K-stage `it` goes to issuer it % NP and its own accumulator
+//   warps 4-19  four dequant warpgroups (K-stage `it` to warpgroup it % 4):
+//               one thread per weight row converts 128 E2M1 values x
+//               2^(s-127) to exact bf16 and writes them straight into the
+//               warpgroup's TMEM A stage (tcgen05.st) -- the dequantized
+//               weights never touch shared memory
+//   warps 20-23 epilogue: tcgen05.ld of the fp32 accumulators (summed over
+//               the pipelines in a fixed order), bias, SwiGLU (gate_up) or
+//               bias (down), bf16 stores
+//   warp 24     TMA producer: packed E2M1 nibbles (128 rows x 64 B, 64B
+//               swizzle) + E8M0 scales (4 groups x 128 rows) into an A ring
+//   warp 25     TMA producer: token rows (16-row boxes of 64 bf16, 128B
+//               swizzle) into a B ring
 // Inside every 8-element K chunk the dequant emits the order
 // {0,4,1,5,2,6,3,7} (cheapest bit extraction); the activation rows are
 // written in the same order by the permute/gather and by the gate_up
@@ -40,9 +44,11 @@ namespace klc {
 
 namespace {
 
-constexpr int kDqWGs = 4;                       // dequant warpgroups (warps 4..19)
-constexpr int kEpiWarp0 = 4 + 4 * kDqWGs;       // first epilogue warp (20)
-constexpr int kThreads = (kEpiWarp0 + 4) * 32;  // 768
+constexpr int kMaxIssuers = 4;                   // MMA issuer warps 0..3 (one per SM sub-partition)
+constexpr int kDqWGs = 4;                        // dequant warpgroups (warps 4..19)
+constexpr int kEpiWarp0 = 4 + 4 * kDqWGs;        // first epilogue warp (20)
+constexpr int kProdWarp0 = kEpiWarp0 + 4;        // TMA producers: A in warp 24, B in warp 25
+constexpr int kThreads = (kProdWarp0 + 2) * 32;  // 832
 constexpr int kBM = 128;                        // weight rows per tile (MMA M)
 constexpr int kAtom = 64;                       // K per 128-byte swizzle atom of bf16
 constexpr uint64_t kWaitNs = 2000000000ull;      // drain bound: 2 s of %globaltimer
@@ -110,36 +116,6 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Ct
   }
 }
 
-__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Spinning variant for the single MMA-issuing thread: non-suspending polls,
-// so it observes a completed phase with the least latency.
-__device__ __forceinline__ bool spin_bar(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
-  if (mbar_test_wait(bar, parity)) return true;
-  const long long t0 = clock64();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test_wait(bar, parity)) return true;
-    if ((i & 255) == 0) {
-      if (*c.abort) return false;
-      if (clock64() - t0 > kWaitCycles) {
-        *c.abort = 1;
-        record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
-        return false;
-      }
-    }
-  }
-}
-
 // Drain-time wait: bounded, ignores the abort flag.
 __device__ __noinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer();
@@ -149,12 +125,17 @@ __device__ __noinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
+// After an abort: wait (bounded) for the latest load issued into each slot of
+// a ring of `n` full-barriers (8 bytes apart) that received `issued` loads in
+// slot order (load i went to slot i % n, completing phase (i / n) & 1).
+__device__ __noinline__ void drain_ring(uint32_t full0, int n, uint32_t issued) {
+  for (int s = 0; s < n; ++s) {
+    if (issued <= uint32_t(s)) break;
+    const uint32_t last = issued - 1 - ((issued - 1 - uint32_t(s)) % uint32_t(n));
+    drain_wait(full0 + 8u * s, (last / uint32_t(n)) & 1);
+  }
 }
+
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
   asm volatile(
@@ -189,21 +170,6 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st64(uint32_t taddr, const uint32_t (&v)[64]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,"
-      "%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,"
-      "%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
-      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
-      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]), "r"(v[32]), "r"(v[33]), "r"(v[34]), "r"(v[35]), "r"(v[36]),
-      "r"(v[37]), "r"(v[38]), "r"(v[39]), "r"(v[40]), "r"(v[41]), "r"(v[42]), "r"(v[43]), "r"(v[44]), "r"(v[45]),
-      "r"(v[46]), "r"(v[47]), "r"(v[48]), "r"(v[49]), "r"(v[50]), "r"(v[51]), "r"(v[52]), "r"(v[53]), "r"(v[54]),
-      "r"(v[55]), "r"(v[56]), "r"(v[57]), "r"(v[58]), "r"(v[59]), "r"(v[60]), "r"(v[61]), "r"(v[62]), "r"(v[63])
-      : "memory");
-}
 
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile(
@@ -288,35 +254,42 @@ struct TcParams {
 // Tile / pipeline configuration.
 //   BN    max token rows of a tile (MMA N <= BN)
 //   NB    token (B) ring depth
-//   DUAL  two MMA pipelines (even / odd K-stages into separate fp32
-//         accumulators summed by the epilogue), so one issuer's commit /
-//         fence / wait overhead overlaps the other's MMAs
-//   KA    64-wide K atoms per stage (16 * KA MMAs per stage)
+//   NP    MMA pipelines: K-stage `it` goes to issuer warp it % NP, which
+//         accumulates into its own fp32 accumulator; the epilogue sums the
+//         NP accumulators in pipeline order (deterministic).  One thread
+//         issuing tcgen05.mma at small N is latency-bound (about 60 cycles
+//         per instruction alone, over 120 next to busy dequant warps), so
+//         several issuers keep the tensor pipe fed
+//   KA    64-wide K atoms per MMA stage (16 * KA MMAs per stage)
 //   NT    TMEM A stages (KA * 32 columns each), one per active dequant warpgroup
-//   NA    weight (A) ring depth
+//   NA    weight (A) ring depth; a weight slot holds SKA = 2 MMA stages (256 K:
+//         128-byte nibble rows, which the copy engine streams from HBM about
+//         twice as fast as 64-byte rows, and half the producer work per stage)
+//   SKB   MMA stages per token (B) slot
 //   ND    accumulator sets in flight (epilogue of one tile overlaps the next)
-template <int BN_, int NB_, bool DUAL_, int KA_, int NT_, int NA_, int ND_>
+template <int BN_, int NB_, int NP_, int KA_, int NT_, int NA_, int ND_, int SKB_>
 struct Cfg {
-  static constexpr int BN = BN_, NB = NB_, KA = KA_, NT = NT_, NA = NA_, ND = ND_;
-  static constexpr bool DUAL = DUAL_;
-  static constexpr int NP = DUAL ? 2 : 1;
-  static constexpr int BK = kAtom * KA;         // K per stage
+  static constexpr int BN = BN_, NB = NB_, NP = NP_, KA = KA_, NT = NT_, NA = NA_, ND = ND_, SKB = SKB_;
+  static constexpr int SKA = 2;
+  static constexpr int BK = kAtom * KA;         // K per MMA stage
   static constexpr int ACOLS = BK / 2;          // TMEM columns per A stage
-  static constexpr int NIB = kBM * BK / 2;      // nibble bytes per stage
-  static constexpr int SCL = kBM * BK / 32;     // scale bytes per stage
-  static constexpr int GROUPS = BK / 32;        // scale groups per stage
+  static constexpr int GROUPS = BK / 32;        // scale groups per MMA stage
+  static constexpr int NIB = kBM * SKA * BK / 2;  // nibble bytes per weight slot (128 rows x 128 B)
+  static constexpr int SCL = kBM * SKA * BK / 32; // scale bytes per weight slot
   static constexpr int BATOM = BN * kAtom * 2;  // bytes of one K atom of BN token rows
-  static constexpr int BSTAGE = KA * BATOM;
+  static constexpr int BSLOT = SKB * KA * BATOM;
   // shared memory layout
   static constexpr int OFF_NIB = 0;
   static constexpr int OFF_SCL = OFF_NIB + NA * NIB;
   static constexpr int OFF_B = (OFF_SCL + NA * SCL + 1023) / 1024 * 1024;
-  static constexpr int OFF_BAR = OFF_B + NB * BSTAGE;
+  static constexpr int OFF_BAR = OFF_B + NB * BSLOT;
   static constexpr int NUM_BARS = 2 * NA + 2 * NB + 2 * NT + NP * ND + ND + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static_assert(NT * ACOLS + ND * NP * BN <= 512, "TMEM budget");
   static_assert(NT <= kDqWGs, "one dequant warpgroup per TMEM A stage");
+  static_assert(NP >= 1 && NP <= kMaxIssuers, "issuer warps");
+  static_assert(KA == 2 && (SKB == 1 || SKB == 2), "slot shapes");
   static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
 };
 
@@ -349,11 +322,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NA; ++s) {
       mbar_init(afull(s), 1);
-      mbar_init(aempty(s), 4);
+      mbar_init(aempty(s), 4 * C::SKA);  // four dequant warps per MMA stage of the slot
     }
     for (int s = 0; s < NB; ++s) {
       mbar_init(bfull(s), 1);
-      mbar_init(bempty(s), 1);
+      mbar_init(bempty(s), C::SKB);  // one MMA commit per MMA stage of the slot
     }
     for (int s = 0; s < NT; ++s) {
       mbar_init(tfull(s), 4);
@@ -367,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
+  if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_holder)));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
@@ -377,60 +350,57 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_holder;
   const int nrb = p.status->rowblocks;
   const int total = nrb * p.n_mtiles;
-  const int ks_n = p.ksteps;
+  const int ks_n = p.ksteps;  // MMA stages per item
+  // Ring slots hold SKA (weights) / SKB (tokens) consecutive MMA stages of one
+  // item; an item with an odd stage count leaves the last weight slot half
+  // used, and the consumers of that stage then arrive for both halves.
+  const int spa = (ks_n + C::SKA - 1) / C::SKA;  // weight slots per item
+  const int spb = (ks_n + C::SKB - 1) / C::SKB;  // token slots per item
 
-  if (warp == 0) {
+  if (warp == kProdWarp0) {
     // ------------------------------------------------------------ A producer (weights)
     if (lane == 0) {
-      uint32_t it = 0;
-      int last[NA];  // latest iteration that loaded each stage (-1: never)
-      for (int s = 0; s < NA; ++s) last[s] = -1;
+      uint32_t it = 0;  // loads issued so far
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
         const int mt = item % p.n_mtiles;
-        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+        for (int j = 0; j < spa && ok; ++j, ++it) {
           const int sa = it % NA;
           if (!(ok = wait_bar(aempty(sa), ((it / NA) & 1) ^ 1, ctl, 10))) break;
           mbar_arrive_expect_tx(afull(sa), C::NIB + C::SCL);
-          tma_load_3d(smem_u32(smem + C::OFF_NIB + sa * C::NIB), &map_a, ks * (C::BK / 2), mt * kBM, rb.x, afull(sa));
-          tma_load_3d(smem_u32(smem + C::OFF_SCL + sa * C::SCL), &map_s, mt * kBM, ks * C::GROUPS, rb.x, afull(sa));
-          last[sa] = int(it);
+          tma_load_3d(smem_u32(smem + C::OFF_NIB + sa * C::NIB), &map_a, j * (C::SKA * C::BK / 2), mt * kBM, rb.x,
+                      afull(sa));
+          tma_load_3d(smem_u32(smem + C::OFF_SCL + sa * C::SCL), &map_s, mt * kBM, j * (C::SKA * C::GROUPS), rb.x,
+                      afull(sa));
         }
       }
-      if (!ok)  // aborting: wait (bounded) until no bulk copy still writes shared memory
-        for (int s = 0; s < NA; ++s)
-          if (last[s] >= 0) drain_wait(afull(s), (uint32_t(last[s]) / NA) & 1);
+      if (!ok) drain_ring(afull(0), NA, it);  // aborting: no bulk copy may still write shared memory
     }
-  } else if (warp == 3) {
+  } else if (warp == kProdWarp0 + 1) {
     // ------------------------------------------------------------ B producer (token rows)
+    // One copy per slot: the map views the rows as [K/64 atoms][rows][64] and
+    // its box is SKB*KA atoms x BN rows, so the slot lands atom-major exactly
+    // as the MMA descriptors address it.  Rows past the row-block (up to BN)
+    // are loaded but not read by the MMA (N = the block's padded row count);
+    // rows and atoms past the buffer are zero-filled.
     if (lane == 0) {
       uint32_t it = 0;
-      int last[NB];
-      for (int s = 0; s < NB; ++s) last[s] = -1;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
-        const int npad = (rb.z + 15) & ~15;
-        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+        for (int j = 0; j < spb && ok; ++j, ++it) {
           const int sb = it % NB;
           if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
-          mbar_arrive_expect_tx(bfull(sb), uint32_t(npad) * C::BK * 2);
-#pragma unroll
-          for (int a = 0; a < KA; ++a)
-            for (int j = 0; j < npad; j += 16)
-              tma_load_2d(smem_u32(smem + C::OFF_B + sb * C::BSTAGE + a * C::BATOM + j * kAtom * 2), &map_b,
-                          ks * C::BK + a * kAtom, rb.y + j, bfull(sb));
-          last[sb] = int(it);
+          mbar_arrive_expect_tx(bfull(sb), C::BSLOT);
+          tma_load_3d(smem_u32(smem + C::OFF_B + sb * C::BSLOT), &map_b, 0, rb.y, j * (C::SKB * KA), bfull(sb));
         }
       }
-      if (!ok)
-        for (int s = 0; s < NB; ++s)
-          if (last[s] >= 0) drain_wait(bfull(s), (uint32_t(last[s]) / NB) & 1);
+      if (!ok) drain_ring(bfull(0), NB, it);
     }
-  } else if (warp == 1 || (NP > 1 && warp == 2)) {
+  } else if (warp < NP) {
     // ------------------------------------------------------------ MMA issuers
-    const int pp = warp - 1;  // pipeline: K-stages with it % NP == pp
+    const int pp = warp;  // pipeline: K-stages with it % NP == pp
     if (lane == 0) {
       const int atoms_last = (p.k_in / kAtom) - (ks_n - 1) * KA;  // valid atoms in the last stage
       uint32_t it = 0, ic = 0;
@@ -446,23 +416,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool first = true;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
           if (NP > 1 && int(it % NP) != pp) continue;
-          const int st = it % NT, sb = it % NB;
+          const int st = it % NT;
+          const uint32_t ib = ic * uint32_t(spb) + uint32_t(ks / C::SKB);  // token slot counter
+          const int sb = ib % NB, hb = ks % C::SKB;
           if (!(ok = wait_bar(tfull(st), (it / NT) & 1, ctl, 21))) break;
-          if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
+          if (!(ok = wait_bar(bfull(sb), (ib / NB) & 1, ctl, 22))) break;
           tc_fence_after();
           const uint32_t a_tmem = tmem + uint32_t(st * C::ACOLS);
-          const uint32_t b_base = smem_u32(smem + C::OFF_B + sb * C::BSTAGE);
+          // descriptors of the stage's K-slices differ only in the start-address field
+          // (address >> 4, no carry out of the field below 256 KB of shared memory)
+          const uint64_t bdesc0 = sw128_desc(smem_u32(smem + C::OFF_B + sb * C::BSLOT + hb * KA * C::BATOM));
           const int kk_n = 4 * ((ks == ks_n - 1) ? atoms_last : KA);
 #pragma unroll
           for (int kk = 0; kk < 4 * KA; ++kk) {
-            if (kk < kk_n) {
-              const uint64_t bdesc = sw128_desc(b_base + uint32_t((kk >> 2) * C::BATOM + (kk & 3) * 32));
-              tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (first && kk == 0) ? 0u : 1u);
-            }
+            if (kk < kk_n)
+              tc_mma_ts(d_tmem, a_tmem + kk * 8, bdesc0 + uint64_t(((kk >> 2) * C::BATOM + (kk & 3) * 32) >> 4), idesc,
+                        (first && kk == 0) ? 0u : 1u);
           }
           first = false;
           tc_commit(tempty(st));
           tc_commit(bempty(sb));
+          if (C::SKB == 2 && ks == ks_n - 1 && hb == 0) tc_commit(bempty(sb));  // no second stage in this slot
         }
         if (ok) tc_commit(dfull(pp, d));
       }
@@ -474,31 +448,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wg = (warp - 4) >> 2;  // K-stages with it % NT == wg, TMEM A stage wg
     const int q = warp & 3;          // TMEM lane quarter
     const int m = q * 32 + lane;     // weight row within the tile
-    // nibble tile swizzle: 64-byte rows (KA=2) use the 64B pattern, 128-byte rows (KA=4) the 128B one
-    const int sw = (KA == 2) ? ((m >> 1) & 3) : (m & 7);
+    // 128-byte nibble rows, 128B swizzle: 16-byte chunk g of row m sits at chunk g ^ (m & 7)
+    const int sw = m & 7;
     const uint32_t tbase = tmem + (uint32_t(q * 32) << 16) + uint32_t(wg * C::ACOLS);
-    uint32_t it = 0;
+    uint32_t it = 0, ic = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
       for (int ks = 0; ks < ks_n; ++ks, ++it) {
         if (int(it % NT) != wg) continue;
-        const int sa = it % NA;
+        const uint32_t ia = ic * uint32_t(spa) + uint32_t(ks / C::SKA);  // weight slot counter
+        const int sa = ia % NA, ha = ks % C::SKA;
         // every lane waits (acquire), the decision is made warp-uniform so the
         // .sync.aligned tcgen05 instructions below never run divergent
-        ok = wait_bar(afull(sa), (it / NA) & 1, ctl, 30);
+        ok = wait_bar(afull(sa), (ia / NA) & 1, ctl, 30);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
-        const unsigned char* nib = smem + C::OFF_NIB + sa * C::NIB + m * (C::BK / 2);
-        const unsigned char* scl = smem + C::OFF_SCL + sa * C::SCL;
+        const unsigned char* nib = smem + C::OFF_NIB + sa * C::NIB + m * (C::SKA * C::BK / 2);
+        const unsigned char* scl = smem + C::OFF_SCL + sa * C::SCL + ha * C::GROUPS * kBM;
         uint4 c[C::GROUPS];
         uint32_t sc[C::GROUPS], smax = 0;
 #pragma unroll
         for (int g = 0; g < C::GROUPS; ++g) {
-          c[g] = *reinterpret_cast<const uint4*>(nib + ((g ^ sw) << 4));
+          c[g] = *reinterpret_cast<const uint4*>(nib + (((ha * C::GROUPS + g) ^ sw) << 4));
           sc[g] = scl[g * kBM + m];
           smax = smax > sc[g] ? smax : sc[g];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(aempty(sa));
+        if (lane == 0) {
+          mbar_arrive(aempty(sa));
+          if (ks == ks_n - 1 && ha == 0) mbar_arrive(aempty(sa));  // the slot's second half is past K
+        }
         // scales above 128 need a second power-of-two factor; decided per warp
         const bool two = __any_sync(0xffffffffu, smax > 128u);
         ok = wait_bar(tempty(wg), ((it / NT) & 1) ^ 1, ctl, 31);
@@ -537,22 +515,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int j = mt * kBM + m;  // output feature
       const bool jok = j < p.n_out;
       const float bias = jok ? bf16_to_f32(p.bias[int64_t(e) * p.n_out + j]) : 0.f;
-      ok = wait_bar(dfull(0, d), (ic / ND) & 1, ctl, 40);
-      if (NP > 1 && ok) ok = wait_bar(dfull(NP - 1, d), (ic / ND) & 1, ctl, 41);
+      for (int pp = 0; pp < NP && ok; ++pp) ok = wait_bar(dfull(pp, d), (ic / ND) & 1, ctl, 40 + pp);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
+      // pipeline pp received a K-stage of this item unless the item has fewer
+      // stages than pipelines (stage `it` of the launch goes to it % NP)
+      const uint32_t first_pp = uint32_t((uint64_t(ic) * uint64_t(ks_n)) % NP);
       const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
       for (int c0 = 0; c0 < npad; c0 += 16) {
         uint32_t raw[16];
-        tmem_ld16(lane_base + dcol(0, d) + uint32_t(c0), raw);
-        if (NP > 1) {
+        tmem_ld16(lane_base + dcol(int(first_pp), d) + uint32_t(c0), raw);
+        tmem_wait_ld();
+        for (int j2 = 1; j2 < NP && j2 < ks_n; ++j2) {
           uint32_t raw2[16];
-          tmem_ld16(lane_base + dcol(NP - 1, d) + uint32_t(c0), raw2);
+          tmem_ld16(lane_base + dcol(int((first_pp + j2) % NP), d) + uint32_t(c0), raw2);
           tmem_wait_ld();
 #pragma unroll
           for (int cc = 0; cc < 16; ++cc) raw[cc] = __float_as_uint(__uint_as_float(raw[cc]) + __uint_as_float(raw2[cc]));
-        } else {
-          tmem_wait_ld();
         }
         if (c0 + 16 >= npad) {
           // last accumulator columns read: hand the buffer back to the MMA warps early
@@ -605,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
 }
 
 // ---------------------------------------------------------------------------
@@ -655,28 +634,28 @@ int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16
   const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out), G = K / 32;
   p.ksteps = int((K + C::BK - 1) / C::BK);
   {
-    // packed nibbles [E][N][K/2] bytes; box = 128 rows x BK/2 bytes, swizzled like the dequant reads it
+    // packed nibbles [E][N][K/2] bytes; box = 128 rows x 128 bytes (one weight slot), 128B swizzle
     const uint64_t dims[3] = {K / 2, N, uint64_t(experts)};
     const uint64_t strides[2] = {K / 2, N * K / 2};
-    const uint32_t box[3] = {uint32_t(C::BK / 2), kBM, 1};
-    const CUtensorMapSwizzle swz = (C::KA == 2) ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
-    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, swz);
+    const uint32_t box[3] = {uint32_t(C::SKA * C::BK / 2), kBM, 1};
+    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != KLC_OK) return st;
   }
   {
-    // scales [E][G][N] bytes; box = BK/32 groups x 128 rows
+    // scales [E][G][N] bytes; box = (one weight slot's) 8 groups x 128 rows
     const uint64_t dims[3] = {N, G, uint64_t(experts)};
     const uint64_t strides[2] = {N, G * N};
-    const uint32_t box[3] = {kBM, uint32_t(C::GROUPS), 1};
+    const uint32_t box[3] = {kBM, uint32_t(C::SKA * C::GROUPS), 1};
     int st = make_map(&ms, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, scales_t, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
     if (st != KLC_OK) return st;
   }
   {
-    // token rows [rows_cap][K] bf16; box = 16 rows x one 64-wide atom, 128-byte swizzle
-    const uint64_t dims[2] = {K, uint64_t(rows_cap)};
-    const uint64_t strides[1] = {K * 2};
-    const uint32_t box[2] = {kAtom, 16};
-    int st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, act, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    // token rows [rows_cap][K] bf16 viewed as [K/64 atoms][rows_cap][64]; box = SKB*KA atoms x BN rows x 64,
+    // 128-byte swizzle (one copy per token slot)
+    const uint64_t dims[3] = {kAtom, uint64_t(rows_cap), K / kAtom};
+    const uint64_t strides[2] = {K * 2, kAtom * 2};
+    const uint32_t box[3] = {kAtom, uint32_t(C::BN), uint32_t(C::SKB * C::KA)};
+    int st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, act, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != KLC_OK) return st;
   }
   // >= 116 KB of shared memory keeps one CTA (and one 512-column TMEM allocation) per SM
@@ -690,17 +669,7 @@ int launch_tc_phase(const uint8_t* blocks, const uint8_t* scales_t, const uint16
   return KLC_OK;
 }
 
-// Per-phase choice: two pipelines need at least two K-stages; smaller
-// reductions use a single pipeline.
-template <int PHASE, class CBig, class CSmall>
-int launch_tc_pick(const uint8_t* blocks, const uint8_t* scales_t, const uint16_t* act, int64_t rows_cap, int experts,
-                   const TcParams& p, int max_rowblocks, cudaStream_t stream) {
-  if (p.k_in >= 2 * CBig::BK)
-    return launch_tc_phase<PHASE, CBig>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
-  return launch_tc_phase<PHASE, CSmall>(blocks, scales_t, act, rows_cap, experts, p, max_rowblocks, stream);
-}
-
-template <class CBig, class CSmall>
+template <class C>
 int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   const klc_moe_weights& w = *a.wts;
   TcParams p1{};
@@ -717,7 +686,7 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   p1.precision = a.precision;
   p1.limit = w.swiglu_limit;
   p1.alpha = w.alpha;
-  int st = launch_tc_pick<1, CBig, CSmall>(w.gu_blocks, w.gu_scales_t, a.xp, a.rows_cap, int(a.experts), p1,
+  int st = launch_tc_phase<1, C>(w.gu_blocks, w.gu_scales_t, a.xp, a.rows_cap, int(a.experts), p1,
                                            a.max_rowblocks, stream);
   if (st != KLC_OK) return st;
   stage_mark(kStageGateUp, stream);
@@ -728,7 +697,7 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
   p2.bias = w.dn_bias;
   p2.out = a.y;
   p2.out_ld = int(a.hidden);
-  st = launch_tc_pick<2, CBig, CSmall>(w.dn_blocks, w.dn_scales_t, static_cast<const uint16_t*>(a.gated), a.rows_cap,
+  st = launch_tc_phase<2, C>(w.dn_blocks, w.dn_scales_t, static_cast<const uint16_t*>(a.gated), a.rows_cap,
                                        int(a.experts), p2, a.max_rowblocks, stream);
   stage_mark(kStageDown, stream);
   return st;
@@ -737,14 +706,16 @@ int launch_tc_both(const ExpertArgs& a, cudaStream_t stream) {
 // Measured on B200 (decode, T=256): 128-K stages with four dequant
 // warpgroups beat 256-K stages -- the dequant's TMEM writes and the MMA's
 // TMEM reads of the A operand share TMEM bandwidth, so fewer, longer stages
-// do not shorten the MMA chain.
-//                 BN   NB  DUAL   KA NT NA  ND
-using CfgN32  = Cfg<32,  4, true,  2, 4, 8,  2>;
-using CfgN64  = Cfg<64,  4, true,  2, 4, 12, 2>;
-using CfgN128 = Cfg<128, 4, true,  2, 4, 8,  1>;
-using CfgN256 = Cfg<256, 2, false, 2, 4, 8,  1>;
-using CfgSmall32  = Cfg<32,  4, false, 2, 4, 8,  2>;
-using CfgSmall64  = Cfg<64,  4, false, 2, 4, 12, 2>;
+// do not shorten the MMA chain.  The token (B) ring runs several stages
+// per pipeline ahead: a slot is refilled only after the MMAs that read it
+// complete, and the refill comes from L2 with a latency of about a
+// microsecond.  TMEM: 4 A stages x 64 columns + ND x NP x BN accumulator
+// columns = 512.
+//                 BN   NB NP KA NT NA ND SKB
+using CfgN32  = Cfg<32,  3, 4, 2, 4, 10, 2, 2>;
+using CfgN64  = Cfg<64,  2, 2, 2, 4, 8,  2, 2>;
+using CfgN128 = Cfg<128, 2, 2, 2, 4, 4,  1, 2>;
+using CfgN256 = Cfg<256, 2, 1, 2, 4, 4,  1, 1>;
 
 }  // namespace
 
@@ -762,10 +733,10 @@ int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   KLC_CHECK_ARG(a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
   // block_n (the max rows of a row-block) decides the tile configuration
   switch (a.block_n) {
-    case 32: return launch_tc_both<CfgN32, CfgSmall32>(a, stream);
-    case 64: return launch_tc_both<CfgN64, CfgSmall64>(a, stream);
-    case 128: return launch_tc_both<CfgN128, CfgN256>(a, stream);
-    case 256: return launch_tc_both<CfgN256, CfgN256>(a, stream);
+    case 32: return launch_tc_both<CfgN32>(a, stream);
+    case 64: return launch_tc_both<CfgN64>(a, stream);
+    case 128: return launch_tc_both<CfgN128>(a, stream);
+    case 256: return launch_tc_both<CfgN256>(a, stream);
     default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 32, 64, 128 or 256");
   }
 }

@@ -34,6 +34,7 @@ int pick_block_n(const klc_moe_dims& d, bool tc) {
   // tokens per expert on average; row-blocks hold up to block_n rows (one
   // weight pass each), the tensor-core N tile is <= 256
   const int64_t per_expert = (d.tokens * d.top_k + d.experts - 1) / std::max<int64_t>(d.experts, 1);
+  if (per_expert <= 12) return 32;
   if (per_expert <= 24) return 64;
   if (per_expert <= 64) return 128;
   return 256;

@@ -148,14 +148,17 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int ntok = int(tokens - t0 < kTok ? tokens - t0 : kTok);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
-  // stage activations (16-byte chunks); rows past the end are zero
+  // stage activations with asynchronous 16-byte copies (all in flight at
+  // once); rows past the end are zero-filled (source size 0)
   const int chunks_per_row = int(hidden / 8);
   for (int i = threadIdx.x; i < kTok * chunks_per_row; i += blockDim.x) {
     const int r = i / chunks_per_row, c = i % chunks_per_row;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < ntok) v = *reinterpret_cast<const uint4*>(x + (t0 + r) * hidden + c * 8);
-    reinterpret_cast<uint4*>(xs + size_t(r) * hidden)[c] = v;
+    const uint16_t* src = x + (t0 + (r < ntok ? r : 0)) * hidden + c * 8;
+    const uint32_t dst = uint32_t(__cvta_generic_to_shared(xs + size_t(r) * hidden + c * 8));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(r < ntok ? 16 : 0)
+                 : "memory");
   }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
   __syncthreads();
 
   const int e_lo = crank * epc;

@@ -140,13 +140,20 @@ def test_select_softmax_keep_order():
 # ---------------------------------------------------------------------------
 
 
-@pytest.mark.parametrize("T,k,E", [(1, 4, 128), (5, 2, 8), (300, 4, 128), (4096, 4, 128), (2000, 3, 37)])
-def test_permute_exact(T, k, E):
+# up to 16384 pairs the permute is one fused launch, above it three launches
+@pytest.mark.parametrize("skew", [False, True])
+@pytest.mark.parametrize("T,k,E", [(1, 4, 128), (5, 2, 8), (300, 4, 128), (4096, 4, 128), (4097, 4, 128), (2000, 3, 37),
+                                   (9000, 2, 1024)])
+def test_permute_exact(T, k, E, skew):
     import ctypes
     from kcapw_klcquant_b200 import _lib
 
     rng = np.random.default_rng(T + E)
-    idx = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+    p = None
+    if skew:  # most pairs on a handful of experts (contended histogram bins)
+        p = 1.0 / np.arange(1, E + 1) ** 2.0
+        p /= p.sum()
+    idx = np.stack([rng.choice(E, k, replace=False, p=p) for _ in range(T)]).astype(np.int32)
     pad = 16
     rows_cap = T * k + E * (pad - 1)
     d_idx = torch.from_numpy(idx).to(DEV)

@@ -49,6 +49,9 @@ def test_host_validation_without_gpu():
     assert st == _lib.KLC_ERR_INVALID
     st, msg = _status_and_msg(L.klc_runtime_dequant(1, None, 0, None, None, 0, 4, 10, ctypes.c_void_p(16), 0, None))
     assert st == _lib.KLC_ERR_INVALID and "scale" in msg
+    fake = ctypes.c_void_p(256)
+    st, msg = _status_and_msg(L.klc_moe_combine(fake, fake, fake, 4, 9, 2880, None, fake, None))
+    assert st == _lib.KLC_ERR_INVALID and "k <= 8" in msg
 
 
 def test_check_maps_invalid_to_value_error():
