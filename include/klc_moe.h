@@ -87,6 +87,18 @@ int klc_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t out_
 int klc_mxfp4_transpose_scales(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups,
                                uint8_t* scales_t, void* stream);
 
+/* Scales for the tensor-core (block-scaled MMA) path, once per layer: the
+ * same scales re-laid as the 512-byte blocks the MMA's scale copies read,
+ * one per (expert, 128-row tile, 128-K stage): byte r0*16 + r1*4 + kb is the
+ * scale of row r0 + 32*r1, 32-K block kb; entries past the matrix are 0.
+ * Output size (klc_mxfp4_scales_mx_bytes) = E * ceil(rows/128) *
+ * ceil(groups/4) * 512 bytes.
+ * No reference counterpart: layout preparation for the B200 kernel, like
+ * the transpose above.                                                     */
+int klc_mxfp4_scales_mx_bytes(int64_t experts, int64_t rows, int64_t groups, size_t* out_bytes);
+int klc_mxfp4_scales_mx(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups, uint8_t* out,
+                        void* stream);
+
 /* ---- router ------------------------------------------------------------ *
  * Replaces the router part of StreamedMoERouter.route
  * (streamed_moe_router.py:269-284): logits = bf16(x @ W^T + b) with fp32
@@ -127,7 +139,9 @@ int klc_moe_workspace_size(const klc_moe_dims* dims, size_t* out_bytes);
  * dn_blocks  uint8 [E, H, I/32, 16]    down_proj_blocks
  * dn_scales_t uint8 [E, I/32, H]
  * dn_bias    bf16 [E, H]
- * router_w   bf16 [E, H], router_b bf16 [E]                               */
+ * router_w   bf16 [E, H], router_b bf16 [E]
+ * gu_scales_mx / dn_scales_mx: the scales re-laid by klc_mxfp4_scales_mx;
+ *            required by the tensor-core path, may be NULL for SIMT       */
 typedef struct klc_moe_weights {
   const uint8_t* gu_blocks;
   const uint8_t* gu_scales_t;
@@ -139,6 +153,8 @@ typedef struct klc_moe_weights {
   const uint16_t* router_b;
   float swiglu_limit; /* 7.0   (streamed_moe_router.py:242) */
   float alpha;        /* 1.702 (streamed_moe_router.py:248) */
+  const uint8_t* gu_scales_mx; /* klc_mxfp4_scales_mx of gate_up_proj_scales (tensor-core path) */
+  const uint8_t* dn_scales_mx; /* klc_mxfp4_scales_mx of down_proj_scales */
 } klc_moe_weights;
 
 /* Expert execution + combine for given routing (idx, weights), the body of

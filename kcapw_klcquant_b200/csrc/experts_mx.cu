@@ -1,0 +1,567 @@
+// Tensor-core grouped expert GEMMs for sm_100a on native MXFP4 weights.
+//
+// Both expert GEMMs of the reference's _execute_mxfp4_experts
+// (streamed_moe_router.py:500-511) for every (expert, row-block) of the
+// permuted tokens, with the bias and the clamped SwiGLU (:524-529) fused into
+// the epilogue, computed by the block-scaled tensor-core MMA
+// (tcgen05.mma.kind::mxf8f6f4.block_scale, M = 128, K = 32 per instruction):
+//
+//   A  the expert's packed E2M1 weights (128 output features of one m-tile),
+//      read from shared memory, with their E8M0 scales (one per 32 K) copied
+//      into TMEM -- the weights are never dequantized by the SM;
+//   B  the row-block's activations, each bf16 row split into two E4M3 rows
+//      (hi = the top 4 significant bits, lo = the next 4) with one E8M0 scale
+//      per 32 K (mx_quant.cu); hi and lo are consecutive rows of B, so one
+//      instruction computes both and the epilogue adds the column pair;
+//   D  fp32 accumulators in TMEM.
+// hi + lo reproduces every bf16 activation within 2^9 of its 32-block maximum
+// exactly (smaller ones to within 2^-17 of that maximum), so each product is
+// the bf16 product the reference forms, accumulated in fp32.
+//
+// The MMA reads E2M1 operands in the 16-byte-group layout (16 values in 8
+// bytes, 8 bytes padding).  The weights stream from HBM packed, as 128-byte
+// rows (256 K) through a TMA ring; repack warps copy each 8-byte group into
+// its padded slot of a small staging ring (no bit manipulation).
+//
+// One persistent CTA per SM walks the (row-block, m-tile) work list;
+// warp-specialised (512 threads):
+//   warp 0      TMA producer: packed weights (128 rows x 128 B, 128B swizzle)
+//               + the two 512-byte scale blocks of the slot (bulk copy)
+//   warp 1      TMA producer: hi/lo activation rows (N2 x 128 B) + their
+//               scale blocks
+//   warps 2-3   MMA issuers (one thread each; stage `it` to issuer it % NP):
+//               shared -> TMEM scale copies, then 4 (or 8) MMAs per stage
+//   warps 4-7   epilogue: TMEM loads, hi + lo, pipelines summed in a fixed
+//               order, bias, SwiGLU (gate_up) or bias (down), bf16 stores
+//   warps 8-15  two repack warpgroups (stage `it` to warpgroup it % 2)
+//
+// Every mbarrier wait is bounded (tc_common.cuh): a timed-out role records
+// KLC_ERR_DEVICE_TIMEOUT, raises the CTA abort flag, and all roles drain
+// before the TMEM is freed and the CTA exits.
+#include <mutex>
+
+#include "permute.cuh"
+#include "tc_common.cuh"
+
+namespace klc {
+
+using namespace tc;
+
+namespace {
+
+constexpr int kBM = 128;        // weight rows per tile (MMA M)
+constexpr int kStageK = 128;    // K per MMA stage: 4 MMAs of K = 32 (4 scale blocks)
+constexpr int kSlotK = 256;     // K per weight slot (128-byte packed rows)
+constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpEpi0 = 4, kWarpRep0 = 8;
+constexpr int kThreads = 16 * 32;
+constexpr int kTmemCols = 512;
+
+// Tile / pipeline configuration.
+//   BN  max token rows of a row-block (B holds N2 = 2*BN hi/lo rows; an MMA
+//       covers at most 128 of them, NCH = ceil(N2 / 128) MMAs per K step)
+//   NA  weight slots (256 K of packed E2M1, 16 KB + 1 KB of scales each)
+//   NS  staging slots (one MMA stage of padded E2M1, 16 KB + 512 B scales)
+//   NB  activation slots (one MMA stage, N2 x 128 B + NCH x 512 B scales)
+//   NP  MMA issuers, each with its own accumulators and scale TMEM
+//   ND  accumulator sets per issuer (the epilogue of one tile overlaps the next)
+template <int BN_, int NA_, int NS_, int NB_, int NP_, int ND_>
+struct MxCfg {
+  static constexpr int BN = BN_, NA = NA_, NS = NS_, NB = NB_, NP = NP_, ND = ND_;
+  static constexpr int N2 = 2 * BN;
+  static constexpr int NCH = (N2 + 127) / 128;
+  static constexpr int ASLOT = kBM * kSlotK / 2;     // 16384 packed bytes
+  static constexpr int SSLOT = kBM * kStageK;        // 16384 padded bytes
+  static constexpr int BSLOT = N2 * kStageK;         // N2 rows x 128 B of E4M3
+  // shared memory (swizzled tiles 1024-byte aligned)
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_S = OFF_A + NA * ASLOT;
+  static constexpr int OFF_B = OFF_S + NS * SSLOT;
+  static constexpr int OFF_ASF = OFF_B + NB * BSLOT;       // NA x 1024
+  static constexpr int OFF_SSF = OFF_ASF + NA * 1024;      // NS x 512
+  static constexpr int OFF_BSF = OFF_SSF + NS * 512;       // NB x NCH x 512
+  static constexpr int OFF_BAR = OFF_BSF + NB * NCH * 512;
+  static constexpr int NUM_BARS = 2 * NA + 2 * NS + 2 * NB + NP * ND + ND + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  // TMEM: accumulators, then per issuer 4 scale columns for A and 4 per B chunk
+  static constexpr int ACC_COLS = ND * NP * N2;
+  static constexpr int SF_COLS = 4 + 4 * NCH;
+  static_assert(ACC_COLS + NP * SF_COLS <= kTmemCols, "TMEM budget");
+  static_assert(NP >= 1 && NP <= 2 && N2 <= 256, "issuers / tile");
+  static_assert(BSLOT % 1024 == 0, "activation slots stay 1024-byte aligned");
+  static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
+};
+
+// kind::mxf8f6f4 instruction descriptor: A E2M1, B E4M3, fp32 accumulate,
+// both K-major, E8M0 scales, M = 128, N = n; scale-factor byte ids a_id/b_id.
+__device__ __forceinline__ uint32_t mx_idesc(int n, uint32_t a_id, uint32_t b_id) {
+  return (b_id << 4) | (5u << 7) | (0u << 10) | (uint32_t(n >> 3) << 17) | (1u << 23) | (uint32_t(kBM >> 4) << 24) |
+         (a_id << 29);
+}
+
+__device__ __forceinline__ void mx_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                       uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb));
+}
+
+// shared -> TMEM copy of one 512-byte scale block (32 lines x 16 B, broadcast
+// to the four lane quarters): lane r0, column r1, byte kb = scale of row
+// r0 + 32 r1, 32-K block kb
+__device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc));
+}
+
+struct MxParams {
+  int n_out;            // weight rows of one expert (2I or H)
+  int k_in;             // reduction length (H or I), a multiple of 64
+  int ksteps;           // ceil(k_in / 128) MMA stages per item
+  int n_mtiles;         // ceil(n_out / 128)
+  const int4* rowblocks;
+  DeviceStatus* status;
+  const int32_t* rows;
+  const uint8_t* sfa;   // [E][n_mtiles][ksteps][512]
+  const uint8_t* sfb;   // [max_rowblocks][ksteps][NCH][512]
+  const uint16_t* bias; // [E, n_out]
+  uint16_t* out;        // phase 1: gated [rows_cap, n_out/2]; phase 2: [rows_cap, n_out]
+  int out_ld;
+  float* normsq;
+  int precision;
+  float limit, alpha;
+};
+
+template <int PHASE, class C>
+__global__ void __launch_bounds__(kThreads, 1)
+    mx_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, MxParams p) {
+  constexpr int NA = C::NA, NS = C::NS, NB = C::NB, NP = C::NP, ND = C::ND, N2 = C::N2, NCH = C::NCH;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
+  auto afull = [&](int s) { return bar0 + 8u * s; };
+  auto aempty = [&](int s) { return bar0 + 8u * (NA + s); };
+  auto sfull = [&](int s) { return bar0 + 8u * (2 * NA + s); };
+  auto sempty = [&](int s) { return bar0 + 8u * (2 * NA + NS + s); };
+  auto bfull = [&](int s) { return bar0 + 8u * (2 * NA + 2 * NS + s); };
+  auto bempty = [&](int s) { return bar0 + 8u * (2 * NA + 2 * NS + NB + s); };
+  auto dfull = [&](int pp, int d) { return bar0 + 8u * (2 * NA + 2 * NS + 2 * NB + pp * ND + d); };
+  auto dempty = [&](int d) { return bar0 + 8u * (2 * NA + 2 * NS + 2 * NB + NP * ND + d); };
+  const uint32_t mma_done = bar0 + 8u * (2 * NA + 2 * NS + 2 * NB + NP * ND + ND);
+  auto dcol = [&](int pp, int d) { return uint32_t((d * NP + pp) * N2); };
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const Ctl ctl{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NA; ++s) {
+      mbar_init(afull(s), 1);
+      mbar_init(aempty(s), 8);  // four repack warps for each of the slot's two stages
+    }
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(sfull(s), 4);
+      mbar_init(sempty(s), 1);
+    }
+    for (int s = 0; s < NB; ++s) {
+      mbar_init(bfull(s), 1);
+      mbar_init(bempty(s), 1);
+    }
+    for (int d = 0; d < ND; ++d) {
+      for (int pp = 0; pp < NP; ++pp) mbar_init(dfull(pp, d), 1);
+      mbar_init(dempty(d), 4);
+    }
+    mbar_init(mma_done, NP);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kWarpMma0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int nrb = p.status->rowblocks;
+  const int total = nrb * p.n_mtiles;
+  const int ks_n = p.ksteps;
+  const int spa = (ks_n + 1) / 2;  // weight slots per item (the last may hold one stage)
+
+  if (warp == kWarpA) {
+    // ------------------------------------------------------------ weights
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int mt = item % p.n_mtiles;
+        const uint8_t* sfa_item = p.sfa + (int64_t(rb.x) * p.n_mtiles + mt) * int64_t(ks_n) * 512;
+        for (int j = 0; j < spa && ok; ++j, ++it) {
+          const int sa = it % NA;
+          if (!(ok = wait_bar(aempty(sa), ((it / NA) & 1) ^ 1, ctl, 10))) break;
+          const int nsf = (2 * j + 1 < ks_n) ? 2 : 1;  // scale blocks of the slot's stages
+          mbar_arrive_expect_tx(afull(sa), uint32_t(C::ASLOT + nsf * 512));
+          tma_load_3d(smem_u32(smem + C::OFF_A + sa * C::ASLOT), &map_a, j * (kSlotK / 2), mt * kBM, rb.x, afull(sa));
+          bulk_load(smem_u32(smem + C::OFF_ASF + sa * 1024), sfa_item + int64_t(2 * j) * 512, uint32_t(nsf * 512),
+                    afull(sa));
+        }
+      }
+      if (!ok) drain_ring(afull(0), NA, it);  // aborting: no bulk copy may still write shared memory
+    }
+  } else if (warp == kWarpB) {
+    // ------------------------------------------------------------ activations
+    // Rows N2 past the row-block are loaded but not read by the MMA (N = 2 x
+    // the block's rows rounded up to 8); rows and K past the buffer are zero-filled.
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int rbi = item / p.n_mtiles;
+        const int4 rb = p.rowblocks[rbi];
+        const uint8_t* sfb_rb = p.sfb + int64_t(rbi) * ks_n * NCH * 512;
+        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+          const int sb = it % NB;
+          if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
+          mbar_arrive_expect_tx(bfull(sb), uint32_t(C::BSLOT + NCH * 512));
+          tma_load_2d(smem_u32(smem + C::OFF_B + sb * C::BSLOT), &map_b, ks * kStageK, 2 * rb.y, bfull(sb));
+          bulk_load(smem_u32(smem + C::OFF_BSF + sb * NCH * 512), sfb_rb + int64_t(ks) * NCH * 512, uint32_t(NCH * 512),
+                    bfull(sb));
+        }
+      }
+      if (!ok) drain_ring(bfull(0), NB, it);
+    }
+  } else if (warp >= kWarpMma0 && warp < kWarpMma0 + NP) {
+    // ------------------------------------------------------------ MMA issuers
+    const int pp = warp - kWarpMma0;
+    if (lane == 0) {
+      const uint32_t sfa_t = tmem + uint32_t(C::ACC_COLS + pp * C::SF_COLS);
+      const uint32_t sfb_t = sfa_t + 4;
+      uint32_t it = 0, ic = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int n2 = 2 * ((rb.z + 7) & ~7);  // hi/lo rows the MMA reads
+        const int d = ic % ND;
+        const uint32_t d_tmem = tmem + dcol(pp, d);
+        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
+        tc_fence_after();
+        bool first = true;
+        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+          if (NP > 1 && int(it % NP) != pp) continue;
+          const int ss = it % NS, sb = it % NB;
+          if (!(ok = wait_bar(sfull(ss), (it / NS) & 1, ctl, 21))) break;
+          if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
+          tc_fence_after();
+          sf_copy(sfa_t, plain_desc(smem_u32(smem + C::OFF_SSF + ss * 512)));
+#pragma unroll
+          for (int ch = 0; ch < NCH; ++ch)
+            sf_copy(sfb_t + 4 * ch, plain_desc(smem_u32(smem + C::OFF_BSF + (sb * NCH + ch) * 512)));
+          const uint64_t adesc0 = sw128_desc(smem_u32(smem + C::OFF_S + ss * C::SSLOT));
+          const uint64_t bdesc0 = sw128_desc(smem_u32(smem + C::OFF_B + sb * C::BSLOT));
+          const int kb_n = min(4, (p.k_in - ks * kStageK) / 32);  // 32-K blocks in this stage
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            if (kk < kb_n) {
+              const uint32_t acc = (first && kk == 0) ? 0u : 1u;
+#pragma unroll
+              for (int ch = 0; ch < NCH; ++ch) {
+                const int nn = min(128, n2 - 128 * ch);
+                if (nn > 0)
+                  // descriptor start addresses advance by 32 B per K block and by 16 KB per 128 B rows
+                  mx_mma(d_tmem + uint32_t(128 * ch), adesc0 + uint64_t(kk * 2),
+                         bdesc0 + uint64_t(kk * 2 + ch * (128 * kStageK >> 4)), mx_idesc(nn, kk, kk),
+                         sfa_t | (uint32_t(kk) << 30), (sfb_t + 4 * ch) | (uint32_t(kk) << 30), acc);
+              }
+            }
+          }
+          first = false;
+          tc_commit(sempty(ss));
+          tc_commit(bempty(sb));
+        }
+        if (ok) tc_commit(dfull(pp, d));
+      }
+      tc_commit(mma_done);
+      drain_wait(mma_done, 0);
+    }
+  } else if (warp >= kWarpRep0) {
+    // ------------------------------------------------------------ repack
+    const int wg = (warp - kWarpRep0) >> 2;  // stages with it % 2 == wg
+    const int m = ((warp - kWarpRep0) & 3) * 32 + lane;
+    const int sw = m & 7;
+    uint32_t it = 0, ic = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+      for (int ks = 0; ks < ks_n; ++ks, ++it) {
+        if (int(it & 1) != wg) continue;
+        const uint32_t ia = ic * uint32_t(spa) + uint32_t(ks >> 1);
+        const int sa = ia % NA, h = ks & 1, ss = it % NS;
+        // every lane waits (acquire); the decision is warp-uniform
+        ok = wait_bar(afull(sa), (ia / NA) & 1, ctl, 30);
+        if (ok) ok = wait_bar(sempty(ss), ((it / NS) & 1) ^ 1, ctl, 31);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        // packed row m, 64-byte half h: chunks 4h..4h+3 of the 128B-swizzled row
+        const unsigned char* src = smem + C::OFF_A + sa * C::ASLOT + m * 128;
+        uint4 c[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) c[i] = *reinterpret_cast<const uint4*>(src + (((4 * h + i) ^ sw) << 4));
+        const uint32_t scl = *reinterpret_cast<const uint32_t*>(smem + C::OFF_ASF + sa * 1024 + h * 512 + m * 4);
+        // padded row m: 8 groups of 16 values, group g in the first 8 bytes of 16-byte chunk g ^ (m & 7)
+        unsigned char* dst = smem + C::OFF_S + ss * C::SSLOT + (m >> 3) * 1024 + (m & 7) * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          *reinterpret_cast<uint4*>(dst + (((2 * i) ^ sw) << 4)) = make_uint4(c[i].x, c[i].y, 0u, 0u);
+          *reinterpret_cast<uint4*>(dst + (((2 * i + 1) ^ sw) << 4)) = make_uint4(c[i].z, c[i].w, 0u, 0u);
+        }
+        *reinterpret_cast<uint32_t*>(smem + C::OFF_SSF + ss * 512 + m * 4) = scl;
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(aempty(sa));
+          if (h == 0 && ks == ks_n - 1) mbar_arrive(aempty(sa));  // the slot has no second stage
+          mbar_arrive(sfull(ss));
+        }
+      }
+    }
+  } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter of this warp
+    const int m = q * 32 + lane;
+    uint32_t ic = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+      const int4 rb = p.rowblocks[item / p.n_mtiles];
+      const int mt = item % p.n_mtiles;
+      const int e = rb.x, r0 = rb.y, nrows = rb.z;
+      const int npad = (nrows + 7) & ~7;
+      const int d = ic % ND;
+      const int j = mt * kBM + m;  // output feature
+      const bool jok = j < p.n_out;
+      const float bias = jok ? bf16_to_f32(p.bias[int64_t(e) * p.n_out + j]) : 0.f;
+      for (int pp = 0; pp < NP && ok; ++pp) ok = wait_bar(dfull(pp, d), (ic / ND) & 1, ctl, 40 + pp);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      // pipeline pp received a K-stage of this item unless the item has fewer
+      // stages than pipelines (stage `it` of the launch goes to it % NP)
+      const uint32_t first_pp = uint32_t((uint64_t(ic) * uint64_t(ks_n)) % NP);
+      const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
+      for (int t0 = 0; t0 < npad; t0 += 8) {
+        uint32_t raw[16];  // columns 2t (hi) and 2t+1 (lo) of tokens t0..t0+7
+        tmem_ld16(lane_base + dcol(int(first_pp), d) + uint32_t(2 * t0), raw);
+        tmem_wait_ld();
+        float v8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v8[i] = __uint_as_float(raw[2 * i]) + __uint_as_float(raw[2 * i + 1]);
+        for (int j2 = 1; j2 < NP && j2 < ks_n; ++j2) {
+          tmem_ld16(lane_base + dcol(int((first_pp + j2) % NP), d) + uint32_t(2 * t0), raw);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v8[i] += __uint_as_float(raw[2 * i]) + __uint_as_float(raw[2 * i + 1]);
+        }
+        if (t0 + 8 >= npad) {
+          // last accumulator columns read: hand the set back to the MMA warps early
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dempty(d));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int n = t0 + i;
+          float v = v8[i];
+          if (p.precision == KLC_PREC_BF16) v = round_bf16(v);
+          v += bias;
+          const bool nok = n < nrows;
+          if (PHASE == 1) {
+            // rows 2i (gate) and 2i+1 (up) of the interleaved gate_up projection
+            const float up_raw = __shfl_xor_sync(0xffffffffu, v, 1);
+            float g2 = 0.f;
+            if ((lane & 1) == 0 && jok && nok) {
+              const float gate = fminf(v, p.limit);
+              const float up = fminf(fmaxf(up_raw, -p.limit), p.limit);
+              const float glu = gate * (1.0f / (1.0f + expf(-(gate * p.alpha))));
+              const float gated = (up + 1.0f) * glu;
+              const uint16_t gb = f32_to_bf16(gated);
+              p.out[int64_t(r0 + n) * p.out_ld + (j >> 1)] = gb;
+              const float gr = bf16_to_f32(gb);
+              g2 = (p.precision == KLC_PREC_BF16) ? gr * gr : gated * gated;
+            }
+            if (p.normsq != nullptr) {
+              g2 = warp_sum(g2);
+              if (lane == 0 && nok) atomicAdd(&p.normsq[int64_t(p.rows[r0 + n]) * 2 + 0], g2);
+            }
+          } else {
+            float o2 = 0.f;
+            if (jok && nok) {
+              p.out[int64_t(r0 + n) * p.out_ld + j] = f32_to_bf16(v);
+              o2 = v * v;
+            }
+            if (p.normsq != nullptr) {
+              o2 = warp_sum(o2);
+              if (lane == 0 && nok) atomicAdd(&p.normsq[int64_t(p.rows[r0 + n]) * 2 + 1], o2);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kWarpMma0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <int PHASE, class C>
+int launch_mx_phase(const uint8_t* blocks, const uint8_t* act_q, int64_t rows_cap, int experts, MxParams p,
+                    int max_rowblocks, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out);
+  p.ksteps = int((K + kStageK - 1) / kStageK);
+  {
+    // packed E2M1 [E][N][K/2] bytes; box = 128 rows x 128 bytes (one 256-K slot), 128B swizzle
+    const uint64_t dims[3] = {K / 2, N, uint64_t(experts)};
+    const uint64_t strides[2] = {K / 2, N * K / 2};
+    const uint32_t box[3] = {kSlotK / 2, kBM, 1};
+    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, blocks, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  {
+    // hi/lo E4M3 rows [2 rows_cap][K] bytes; box = N2 rows x 128 bytes (one stage), 128B swizzle
+    const uint64_t dims[2] = {K, 2 * uint64_t(rows_cap)};
+    const uint64_t strides[1] = {K};
+    const uint32_t box[2] = {kStageK, uint32_t(C::N2)};
+    int st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, act_q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  // >= 116 KB of shared memory keeps one CTA (and one 512-column TMEM allocation) per SM
+  const int smem = (C::BYTES + 1024 > 118 * 1024) ? C::BYTES + 1024 : 118 * 1024;
+  KLC_CUDA(cudaFuncSetAttribute(mx_expert_kernel<PHASE, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
+  const int grid = int(items < sm_count() ? items : sm_count());
+  if (grid <= 0) return KLC_OK;
+  mx_expert_kernel<PHASE, C><<<grid, kThreads, smem, stream>>>(ma, mb, p);
+  KLC_LAUNCH_CHECK("tcgen05 expert launch");
+  return KLC_OK;
+}
+
+template <class C>
+int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
+  const klc_moe_weights& w = *a.wts;
+  KLC_CHECK_ARG(w.gu_scales_mx != nullptr && w.dn_scales_mx != nullptr,
+                "tensor-core path: gu_scales_mx / dn_scales_mx are required (klc_mxfp4_scales_mx)");
+  MxParams p1{};
+  p1.n_out = int(2 * a.inter);
+  p1.k_in = int(a.hidden);
+  p1.n_mtiles = (p1.n_out + kBM - 1) / kBM;
+  p1.rowblocks = a.rowblocks;
+  p1.status = a.status_rw;
+  p1.rows = a.rows;
+  p1.sfa = w.gu_scales_mx;
+  p1.sfb = a.sfb1;
+  p1.bias = w.gu_bias;
+  p1.out = static_cast<uint16_t*>(a.gated);
+  p1.out_ld = int(a.inter);
+  p1.normsq = a.normsq;
+  p1.precision = a.precision;
+  p1.limit = w.swiglu_limit;
+  p1.alpha = w.alpha;
+  int st = launch_quantize_rows(a.x, a.hidden, a.rows, a.k, a.rowblocks, a.status, a.max_rowblocks, C::NCH, a.xq,
+                                a.sfb1, stream);
+  if (st != KLC_OK) return st;
+  st = launch_mx_phase<1, C>(w.gu_blocks, a.xq, a.rows_cap, int(a.experts), p1, a.max_rowblocks, stream);
+  if (st != KLC_OK) return st;
+  stage_mark(kStageGateUp, stream);
+  st = launch_quantize_rows(static_cast<const uint16_t*>(a.gated), a.inter, nullptr, 1, a.rowblocks, a.status,
+                            a.max_rowblocks, C::NCH, a.gq, a.sfb2, stream);
+  if (st != KLC_OK) return st;
+  MxParams p2 = p1;
+  p2.n_out = int(a.hidden);
+  p2.k_in = int(a.inter);
+  p2.n_mtiles = (p2.n_out + kBM - 1) / kBM;
+  p2.sfa = w.dn_scales_mx;
+  p2.sfb = a.sfb2;
+  p2.bias = w.dn_bias;
+  p2.out = a.y;
+  p2.out_ld = int(a.hidden);
+  st = launch_mx_phase<2, C>(w.dn_blocks, a.gq, a.rows_cap, int(a.experts), p2, a.max_rowblocks, stream);
+  stage_mark(kStageDown, stream);
+  return st;
+}
+
+//                BN  NA NS NB NP ND
+using MxN32  = MxCfg<32, 8, 3, 3, 2, 2>;
+using MxN64  = MxCfg<64, 7, 3, 3, 1, 2>;
+using MxN128 = MxCfg<128, 5, 2, 3, 1, 1>;
+
+}  // namespace
+
+namespace tc {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static int encode_fn(EncodeTiledFn* out) {
+  static std::once_flag once;
+  static EncodeTiledFn fn = nullptr;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  if (fn == nullptr) return fail(KLC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  *out = fn;
+  return KLC_OK;
+}
+
+int make_map(CUtensorMap* map, CUtensorMapDataType type, int rank, const void* base, const uint64_t* dims,
+             const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = nullptr;
+  int st = encode_fn(&fn);
+  if (st != KLC_OK) return st;
+  cuuint64_t gd[5], gs[4];
+  cuuint32_t bx[5], es[5] = {1, 1, 1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+  const CUresult r = fn(map, type, cuuint32_t(rank), const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KLC_ERR_CUDA, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(int(r)));
+  return KLC_OK;
+}
+
+}  // namespace tc
+
+bool tc_path_supported(int64_t hidden, int64_t inter) {
+  int dev = 0, major = 0, minor = 0;
+  if (hidden % 64 != 0 || inter % 64 != 0) return false;
+  if (cudaGetDevice(&dev) != cudaSuccess) return true;  // no device: report the build's capability
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return true;
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+int mx_sfb_chunks(int block_n) { return (2 * block_n + 127) / 128; }
+
+int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
+  KLC_CHECK_ARG(a.hidden % 64 == 0 && a.inter % 64 == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
+  KLC_CHECK_ARG(2 * a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
+  switch (a.block_n) {
+    case 32: return launch_mx_both<MxN32>(a, stream);
+    case 64: return launch_mx_both<MxN64>(a, stream);
+    case 128: return launch_mx_both<MxN128>(a, stream);
+    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 32, 64 or 128");
+  }
+}
+
+}  // namespace klc

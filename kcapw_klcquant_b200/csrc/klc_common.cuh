@@ -107,16 +107,4 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// K-order permutation used by the tensor-core path inside every 8-element
-// chunk: position p holds element PERM8[p] = {0,4,1,5,2,6,3,7}.  Applied to a
-// chunk held as four bf16x2 words (w0=(e0,e1) .. w3=(e6,e7)).
-__device__ __forceinline__ uint4 perm8_bf16(uint4 v) {
-  uint4 o;
-  o.x = __byte_perm(v.x, v.z, 0x5410);  // (e0, e4)
-  o.y = __byte_perm(v.x, v.z, 0x7632);  // (e1, e5)
-  o.z = __byte_perm(v.y, v.w, 0x5410);  // (e2, e6)
-  o.w = __byte_perm(v.y, v.w, 0x7632);  // (e3, e7)
-  return o;
-}
-
 }  // namespace klc

@@ -32,12 +32,12 @@ constexpr int kPad = 16;  // rows of each expert group are padded to 16 (MMA N g
 int pick_block_n(const klc_moe_dims& d, bool tc) {
   if (!tc) return 64;
   // tokens per expert on average; row-blocks hold up to block_n rows (one
-  // weight pass each), the tensor-core N tile is <= 256
+  // weight pass each); a tensor-core tile holds at most 128 rows (256 hi/lo
+  // operand rows)
   const int64_t per_expert = (d.tokens * d.top_k + d.experts - 1) / std::max<int64_t>(d.experts, 1);
   if (per_expert <= 12) return 32;
   if (per_expert <= 24) return 64;
-  if (per_expert <= 64) return 128;
-  return 256;
+  return 128;
 }
 
 }  // namespace
@@ -71,9 +71,15 @@ WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffer
   L.pair_pos = take(size_t(L.pairs) * 4);
   L.rowblocks = take(size_t(L.max_rowblocks) * sizeof(int4));
   L.normsq = take(size_t(L.pairs) * 2 * 4);
-  L.xp = take(size_t(L.rows_cap) * d.hidden * 2);
+  L.xp = take(size_t(L.rows_cap) * d.hidden * 2);  // SIMT: bf16 rows; TC: hi/lo E4M3 rows (same size)
   L.gated = take(size_t(L.rows_cap) * d.intermediate * (tc ? 2 : 4));
   L.y = take(size_t(L.rows_cap) * d.hidden * 2);
+  if (tc) {
+    const size_t nch = size_t(mx_sfb_chunks(L.block_n));
+    L.gq = take(size_t(L.rows_cap) * 2 * d.intermediate);
+    L.sfb1 = take(size_t(L.max_rowblocks) * size_t((d.hidden + 127) / 128) * nch * 512);
+    L.sfb2 = take(size_t(L.max_rowblocks) * size_t((d.intermediate + 127) / 128) * nch * 512);
+  }
   if (need_routing_buffers) {
     L.idx = take(size_t(L.pairs) * 4);
     L.w = take(size_t(L.pairs) * 2);
@@ -130,8 +136,8 @@ int run_experts(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_
   pa.status = status;
   pa.x = x;
   pa.hidden = d.hidden;
-  pa.xp = reinterpret_cast<uint16_t*>(ws + L.xp);
-  pa.perm_k = tc ? 1 : 0;
+  // SIMT gathers bf16 rows here; the tensor-core path quantizes straight from x per row-block
+  pa.xp = tc ? nullptr : reinterpret_cast<uint16_t*>(ws + L.xp);
   stage_mark(kStageRouted, stream);
   int st = launch_permute(pa, stream);
   if (st != KLC_OK) return st;
@@ -150,6 +156,13 @@ int run_experts(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_
   ea.status = status;
   ea.status_rw = status;
   ea.xp = pa.xp;
+  ea.x = x;
+  if (tc) {
+    ea.xq = reinterpret_cast<uint8_t*>(ws + L.xp);
+    ea.gq = reinterpret_cast<uint8_t*>(ws + L.gq);
+    ea.sfb1 = reinterpret_cast<uint8_t*>(ws + L.sfb1);
+    ea.sfb2 = reinterpret_cast<uint8_t*>(ws + L.sfb2);
+  }
   ea.gated = ws + L.gated;
   ea.y = reinterpret_cast<uint16_t*>(ws + L.y);
   ea.normsq = normsq;
@@ -316,7 +329,6 @@ extern "C" int klc_ep_pack(const int32_t* idx, int64_t tokens, int k, int64_t ex
   pa.x = x;
   pa.hidden = hidden;
   pa.xp = send_rows;
-  pa.perm_k = 0;
   pa.div = int(experts_per_rank);
   pa.aux_out = send_expert;
   return launch_permute(pa, as_stream(stream));

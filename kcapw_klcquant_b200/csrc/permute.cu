@@ -15,7 +15,7 @@
 //      list of row-blocks (<= block_n rows of one expert) the GEMMs iterate
 //   3. per chunk: stable rank of each pair among equal experts (warp
 //      match_any + per-warp counts), scatter of rows/pair_pos, and the copy of
-//      x[token] into its padded row (optionally in the tensor-core K order).
+//      x[token] into its padded row.
 //      A chunk is split over `split` CTAs: each ranks the whole chunk (a few
 //      microseconds of shared-memory work) and copies 1/split of its rows, so
 //      a decode batch of one or two chunks still spreads its row copies over
@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(kChunk)
     scatter_gather_kernel(const int32_t* __restrict__ idx, int64_t pairs, int k, int experts,
                           const int32_t* __restrict__ chunk_base, int32_t* __restrict__ rows,
                           int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x, int64_t hidden,
-                          uint16_t* __restrict__ xp, int perm_k, int div, int32_t* __restrict__ aux_out,
+                          uint16_t* __restrict__ xp, int div, int32_t* __restrict__ aux_out,
                           int split, DeviceStatus* st) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                      // [32][experts]
@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kChunk)
     uint4* out = reinterpret_cast<uint4*>(xp + int64_t(dst) * hidden);
     for (int c = lane; c < chunks; c += 32) {
       uint4 v = src[c];
-      out[c] = perm_k ? perm8_bf16(v) : v;
+      out[c] = v;
     }
   }
 }
@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kChunk)
     fused_permute_kernel(const int32_t* __restrict__ idx, int64_t pairs, int k, int experts, int pad, int block_n,
                          int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
                          int4* __restrict__ rowblocks, int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x,
-                         int64_t hidden, uint16_t* __restrict__ xp, int perm_k, int div, int32_t* __restrict__ aux_out,
+                         int64_t hidden, uint16_t* __restrict__ xp, int div, int32_t* __restrict__ aux_out,
                          int split, DeviceStatus* st) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                    // [32][experts]
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kChunk)
     uint4* out = reinterpret_cast<uint4*>(xp + int64_t(dst) * hidden);
     for (int c = lane; c < chunks; c += 32) {
       uint4 vv = src[c];
-      out[c] = perm_k ? perm8_bf16(vv) : vv;
+      out[c] = vv;
     }
   }
 }
@@ -323,7 +323,7 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
     KLC_CUDA(cudaFuncSetAttribute(fused_permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     fused_permute_kernel<<<unsigned(int64_t(nchunks) * split), kChunk, smem, stream>>>(
         a.idx, pairs, a.k, E, a.pad, a.block_n, a.counts, a.offsets, a.rows, a.rowblocks, a.pair_pos, a.x, a.hidden,
-        a.xp, a.perm_k, div, a.aux_out, split, a.status);
+        a.xp, div, a.aux_out, split, a.status);
     KLC_LAUNCH_CHECK("permute (fused) launch");
     return KLC_OK;
   }
@@ -335,7 +335,7 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
   const size_t smem = (size_t(32) * E + 2 * kChunk) * sizeof(int32_t);
   KLC_CUDA(cudaFuncSetAttribute(scatter_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   scatter_gather_kernel<<<unsigned(int64_t(nchunks) * split), kChunk, smem, stream>>>(
-      a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos, a.x, a.hidden, a.xp, a.perm_k, div, a.aux_out, split,
+      a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos, a.x, a.hidden, a.xp, div, a.aux_out, split,
       a.status);
   KLC_LAUNCH_CHECK("permute scatter launch");
   return KLC_OK;

@@ -25,7 +25,6 @@ struct PermuteArgs {
   const uint16_t* x;   // [T, H] or null (no gather)
   int64_t hidden;
   uint16_t* xp;        // [rows_cap, H] or null
-  int perm_k;          // 1: write rows in the tensor-core K order
   int div;             // group id = idx / div (1: group by expert; experts-per-rank: group by rank)
   int32_t* aux_out;    // optional [rows_cap]: idx % div of the pair stored at each row
 };
@@ -42,7 +41,9 @@ int launch_router(const uint16_t* x, int64_t tokens, int64_t hidden, const uint1
 struct WorkspaceLayout {
   int64_t pairs, rows_cap, max_rowblocks, nchunks;
   int pad, block_n;
-  size_t status, counts, offsets, chunk_hist, rows, pair_pos, rowblocks, normsq, xp, gated, y, idx, w, total;
+  size_t status, counts, offsets, chunk_hist, rows, pair_pos, rowblocks, normsq, xp, gated, y, idx, w;
+  size_t gq, sfb1, sfb2;  // tensor-core path: hi/lo E4M3 down-pass rows and activation scale blocks
+  size_t total;
 };
 
 WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffers);
@@ -60,7 +61,12 @@ struct ExpertArgs {
   const int32_t* rows;
   const DeviceStatus* status;  // rowblocks count lives here
   DeviceStatus* status_rw;
-  const uint16_t* xp;          // [rows_cap, H]
+  const uint16_t* xp;          // [rows_cap, H] (SIMT)
+  const uint16_t* x;           // [T, H] layer input (TC: quantized per row-block through `rows`)
+  uint8_t* xq;                 // [rows_cap, 2, H] hi/lo E4M3 gate_up operand (TC)
+  uint8_t* gq;                 // [rows_cap, 2, I] hi/lo E4M3 down operand (TC)
+  uint8_t* sfb1;               // [max_rowblocks, H/128, nch, 512] activation scales (TC)
+  uint8_t* sfb2;               // [max_rowblocks, I/128, nch, 512]
   void* gated;                 // [rows_cap, I] fp32 (SIMT) or bf16 (TC)
   uint16_t* y;                 // [rows_cap, H]
   float* normsq;               // [pairs, 2] or null
@@ -71,6 +77,13 @@ struct ExpertArgs {
 int launch_experts_simt(const ExpertArgs& a, cudaStream_t stream);
 int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream);
 bool tc_path_supported(int64_t hidden, int64_t inter);
+// 512-byte activation-scale blocks per (row-block, 128-K stage) of the tensor-core path
+int mx_sfb_chunks(int block_n);
+// bf16 rows -> hi/lo E4M3 rows + scale blocks for every row-block (mx_quant.cu);
+// rows_map != null: source row = rows_map[row] / k (the permuted pair's token)
+int launch_quantize_rows(const uint16_t* src, int64_t K, const int32_t* rows_map, int k, const int4* rowblocks,
+                         const DeviceStatus* status, int max_rowblocks, int nch, uint8_t* q, uint8_t* sfb,
+                         cudaStream_t stream);
 
 // ---------------------------------------------------------------------------
 // optional per-stage CUDA-event timing (klc_stage_timing / klc_stage_times)

@@ -81,6 +81,7 @@ class MoeLayer:
             packed.gu_blocks.data_ptr(), packed.gu_scales_t.data_ptr(), self.gate_up_bias.data_ptr(),
             packed.dn_blocks.data_ptr(), packed.dn_scales_t.data_ptr(), self.down_bias.data_ptr(),
             self.router_weight.data_ptr(), self.router_bias.data_ptr(), float(swiglu_limit), float(alpha),
+            _lib.ptr(packed.gu_scales_mx), _lib.ptr(packed.dn_scales_mx),
         )
 
     @classmethod

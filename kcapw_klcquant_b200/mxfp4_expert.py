@@ -20,6 +20,7 @@ reference's field names.
 """
 from __future__ import annotations
 
+import ctypes
 import json
 import threading
 import time
@@ -73,6 +74,21 @@ def transpose_scales(scales: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def scales_mx(scales: torch.Tensor) -> torch.Tensor:
+    """E8M0 scales [E, rows, groups] -> the tensor-core path's 512-byte scale blocks
+    [E, ceil(rows/128), ceil(groups/4), 512] (klc_mxfp4_scales_mx)."""
+    scales = scales.to(torch.uint8).contiguous()
+    _lib.require_cuda(scales)
+    E, rows, groups = scales.shape
+    n = ctypes.c_size_t(0)
+    _lib.check(_lib.lib().klc_mxfp4_scales_mx_bytes(E, rows, groups, ctypes.byref(n)))
+    out = torch.empty((E, (rows + 127) // 128, (groups + 3) // 4, 512), dtype=torch.uint8, device=scales.device)
+    assert out.numel() == n.value
+    with torch.cuda.device(scales.device):
+        _lib.check(_lib.lib().klc_mxfp4_scales_mx(scales.data_ptr(), E, rows, groups, out.data_ptr(), _lib.stream_ptr()))
+    return out
+
+
 @dataclass
 class PackedLayer:
     """One layer's expert weights resident on the device (packed MXFP4)."""
@@ -83,6 +99,8 @@ class PackedLayer:
     dn_scales_t: torch.Tensor  # uint8 [E, I/32, H]
     gu_scales: torch.Tensor | None = None  # original [E, 2I, H/32] (kept for load_expert_matrix)
     dn_scales: torch.Tensor | None = None
+    gu_scales_mx: torch.Tensor | None = None  # tensor-core scale blocks (scales_mx)
+    dn_scales_mx: torch.Tensor | None = None
 
     @property
     def experts(self) -> int:
@@ -98,7 +116,8 @@ class PackedLayer:
 
     @property
     def nbytes(self) -> int:
-        return sum(t.numel() for t in (self.gu_blocks, self.gu_scales_t, self.dn_blocks, self.dn_scales_t))
+        ts = (self.gu_blocks, self.gu_scales_t, self.dn_blocks, self.dn_scales_t, self.gu_scales_mx, self.dn_scales_mx)
+        return sum(t.numel() for t in ts if t is not None)
 
     @classmethod
     def from_checkpoint_tensors(
@@ -113,7 +132,7 @@ class PackedLayer:
             raise ValueError(f"inconsistent MXFP4 layer shapes {gb.shape} {gs.shape} {db.shape} {ds.shape}")
         if db.shape[1] != g_h * 32 or db.shape[2] * 64 != two_i:
             raise ValueError("down_proj must be [E, H, I/32, 16] with gate_up [E, 2I, H/32, 16]")
-        return cls(gb, transpose_scales(gs), db, transpose_scales(ds), gs, ds)
+        return cls(gb, transpose_scales(gs), db, transpose_scales(ds), gs, ds, scales_mx(gs), scales_mx(ds))
 
 
 @dataclass
