@@ -24,13 +24,16 @@
 // its padded slot of a small staging ring (no bit manipulation).
 //
 // One persistent CTA per SM walks the (row-block, m-tile) work list;
-// warp-specialised (512 threads):
+// warp-specialised (608 threads):
 //   warp 0      TMA producer: packed weights (128 rows x 128 B, 128B swizzle)
 //               + the two 512-byte scale blocks of the slot (bulk copy)
-//   warp 1      TMA producer: hi/lo activation rows (N2 x 128 B) + their
-//               scale blocks
-//   warps 2-3   MMA issuers (one thread each; stage `it` to issuer it % NP):
-//               shared -> TMEM scale copies, then 4 (or 8) MMAs per stage
+//   warps 1,18  TMA producers: hi/lo activation rows (N2 x 128 B) + their
+//               scale blocks, even / odd stages
+//   warps 2-3,  MMA issuers (one thread each; stage `it` to issuer it % NP):
+//   16-17       shared -> TMEM scale copies, then 4 (or 8) MMAs per stage.
+//               A single thread issuing tcgen05 operations next to busy
+//               warps waits a few hundred cycles per stage, so several
+//               issuers with their own accumulators keep the tensor pipe fed
 //   warps 4-7   epilogue: TMEM loads, hi + lo, pipelines summed in a fixed
 //               order, bias, SwiGLU (gate_up) or bias (down), bf16 stores
 //   warps 8-15  two repack warpgroups (stage `it` to warpgroup it % 2)
@@ -52,8 +55,12 @@ namespace {
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kStageK = 128;    // K per MMA stage: 4 MMAs of K = 32 (4 scale blocks)
 constexpr int kSlotK = 256;     // K per weight slot (128-byte packed rows)
-constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpEpi0 = 4, kWarpRep0 = 8;
-constexpr int kThreads = 16 * 32;
+constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpMma2 = 16, kWarpB2 = 18;
+constexpr int kThreads = 19 * 32;
+__device__ __forceinline__ int issuer_of_warp(int warp) {  // MMA pipeline of a warp, or -1
+  return (warp == kWarpMma0 || warp == kWarpMma0 + 1) ? warp - kWarpMma0
+       : (warp == kWarpMma2 || warp == kWarpMma2 + 1) ? 2 + warp - kWarpMma2 : -1;
+}
 constexpr int kTmemCols = 512;
 
 // Tile / pipeline configuration.
@@ -63,6 +70,10 @@ constexpr int kTmemCols = 512;
 //   NS  staging slots (one MMA stage of padded E2M1, 16 KB + 512 B scales)
 //   NB  activation slots (one MMA stage, N2 x 128 B + NCH x 512 B scales)
 //   NP  MMA issuers, each with its own accumulators and scale TMEM
+// Every staging and activation slot serves a single issuer (NS and NB are
+// multiples of NP) and a single repack warpgroup, so no waiter can run two
+// phases ahead of a slot's mbarrier -- a parity wait would then pass on the
+// stale phase.
 //   ND  accumulator sets per issuer (the epilogue of one tile overlaps the next)
 template <int BN_, int NA_, int NS_, int NB_, int NP_, int ND_>
 struct MxCfg {
@@ -87,10 +98,23 @@ struct MxCfg {
   static constexpr int ACC_COLS = ND * NP * N2;
   static constexpr int SF_COLS = 4 + 4 * NCH;
   static_assert(ACC_COLS + NP * SF_COLS <= kTmemCols, "TMEM budget");
-  static_assert(NP >= 1 && NP <= 2 && N2 <= 256, "issuers / tile");
+  static_assert((NP == 1 || NP == 2 || NP == 4) && N2 <= 256, "issuers / tile");
+  static_assert(NS % NP == 0 && NB % NP == 0 && NB % 2 == 0 && (NS / NP) % (NP == 1 ? 2 : 1) == 0, "slot ownership");
+  static constexpr int NSP = NS / NP;  // staging slots per issuer
   static_assert(BSLOT % 1024 == 0, "activation slots stay 1024-byte aligned");
   static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
 };
+
+// Staging slot of MMA stage s (issuer s % NP, its (s / NP)-th stage) and the
+// mbarrier phase parity of that use.  The repack warpgroup of stage s is s & 1
+// (NP is 1, 2 or 4), so each slot is filled by one warpgroup and drained by
+// one issuer, both in stage order.
+template <class C>
+__device__ __forceinline__ void staging_slot(uint32_t s, int& slot, uint32_t& parity) {
+  const uint32_t pp = s % C::NP, li = s / C::NP;
+  slot = int(pp * C::NSP + li % C::NSP);
+  parity = (li / C::NSP) & 1;
+}
 
 // kind::mxf8f6f4 instruction descriptor: A E2M1, B E4M3, fp32 accumulate,
 // both K-major, E8M0 scales, M = 128, N = n; scale-factor byte ids a_id/b_id.
@@ -211,32 +235,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) drain_ring(afull(0), NA, it);  // aborting: no bulk copy may still write shared memory
     }
-  } else if (warp == kWarpB) {
+  } else if (warp == kWarpB || warp == kWarpB2) {
     // ------------------------------------------------------------ activations
-    // Rows N2 past the row-block are loaded but not read by the MMA (N = 2 x
-    // the block's rows rounded up to 8); rows and K past the buffer are zero-filled.
+    // Two producers (stage parity q), one copy each per stage, so the per-stage
+    // issue latency of a single thread does not bound the stage rate; with NB
+    // even, each slot is filled by one producer.  Rows N2 past the row-block
+    // are loaded but not read by the MMA (N = 2 x the block's rows rounded up
+    // to 8); rows and K past the buffer are zero-filled.
+    const uint32_t q = warp == kWarpB ? 0u : 1u;
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t it = 0, mine = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
         const int rbi = item / p.n_mtiles;
         const int4 rb = p.rowblocks[rbi];
         const uint8_t* sfb_rb = p.sfb + int64_t(rbi) * ks_n * NCH * 512;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
+          if ((it & 1u) != q) continue;
           const int sb = it % NB;
           if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
           mbar_arrive_expect_tx(bfull(sb), uint32_t(C::BSLOT + NCH * 512));
           tma_load_2d(smem_u32(smem + C::OFF_B + sb * C::BSLOT), &map_b, ks * kStageK, 2 * rb.y, bfull(sb));
           bulk_load(smem_u32(smem + C::OFF_BSF + sb * NCH * 512), sfb_rb + int64_t(ks) * NCH * 512, uint32_t(NCH * 512),
                     bfull(sb));
+          ++mine;
         }
       }
-      if (!ok) drain_ring(bfull(0), NB, it);
+      if (!ok) {
+        // the latest load of each of this producer's slots: stages q + 2i, i < mine
+        const uint32_t first = mine > uint32_t(NB / 2) ? mine - uint32_t(NB / 2) : 0u;
+        for (uint32_t i = first; i < mine; ++i) {
+          const uint32_t st = q + 2 * i;
+          drain_wait(bfull(int(st % NB)), (st / NB) & 1);
+        }
+      }
     }
-  } else if (warp >= kWarpMma0 && warp < kWarpMma0 + NP) {
+  } else if (issuer_of_warp(warp) >= 0) {
     // ------------------------------------------------------------ MMA issuers
-    const int pp = warp - kWarpMma0;
-    if (lane == 0) {
+    const int pp = issuer_of_warp(warp);
+    if (lane == 0 && pp < NP) {
       const uint32_t sfa_t = tmem + uint32_t(C::ACC_COLS + pp * C::SF_COLS);
       const uint32_t sfb_t = sfa_t + 4;
       uint32_t it = 0, ic = 0;
@@ -251,8 +288,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool first = true;
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
           if (NP > 1 && int(it % NP) != pp) continue;
-          const int ss = it % NS, sb = it % NB;
-          if (!(ok = wait_bar(sfull(ss), (it / NS) & 1, ctl, 21))) break;
+          int ss;
+          uint32_t sph;
+          staging_slot<C>(it, ss, sph);
+          const int sb = it % NB;
+          if (!(ok = wait_bar(sfull(ss), sph, ctl, 21))) break;
           if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
           tc_fence_after();
           sf_copy(sfa_t, plain_desc(smem_u32(smem + C::OFF_SSF + ss * 512)));
@@ -286,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(mma_done);
       drain_wait(mma_done, 0);
     }
-  } else if (warp >= kWarpRep0) {
+  } else if (warp >= kWarpRep0 && warp < kWarpRep0 + 8) {
     // ------------------------------------------------------------ repack
     const int wg = (warp - kWarpRep0) >> 2;  // stages with it % 2 == wg
     const int m = ((warp - kWarpRep0) & 3) * 32 + lane;
@@ -297,10 +337,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int ks = 0; ks < ks_n; ++ks, ++it) {
         if (int(it & 1) != wg) continue;
         const uint32_t ia = ic * uint32_t(spa) + uint32_t(ks >> 1);
-        const int sa = ia % NA, h = ks & 1, ss = it % NS;
+        const int sa = ia % NA, h = ks & 1;
+        int ss;
+        uint32_t sph;
+        staging_slot<C>(it, ss, sph);
         // every lane waits (acquire); the decision is warp-uniform
         ok = wait_bar(afull(sa), (ia / NA) & 1, ctl, 30);
-        if (ok) ok = wait_bar(sempty(ss), ((it / NS) & 1) ^ 1, ctl, 31);
+        if (ok) ok = wait_bar(sempty(ss), sph ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         // packed row m, 64-byte half h: chunks 4h..4h+3 of the 128B-swizzled row
         const unsigned char* src = smem + C::OFF_A + sa * C::ASLOT + m * 128;
@@ -495,9 +538,9 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 }
 
 //                BN  NA NS NB NP ND
-using MxN32  = MxCfg<32, 8, 3, 3, 2, 2>;
-using MxN64  = MxCfg<64, 7, 3, 3, 1, 2>;
-using MxN128 = MxCfg<128, 5, 2, 3, 1, 1>;
+using MxN32  = MxCfg<32, 7, 4, 4, 4, 1>;
+using MxN64  = MxCfg<64, 7, 2, 4, 2, 1>;
+using MxN128 = MxCfg<128, 5, 2, 2, 1, 1>;
 
 }  // namespace
 
