@@ -99,6 +99,16 @@ int klc_mxfp4_scales_mx_bytes(int64_t experts, int64_t rows, int64_t groups, siz
 int klc_mxfp4_scales_mx(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups, uint8_t* out,
                         void* stream);
 
+/* Activation operand of the tensor-core path: each bf16 row [K] split into
+ * two E4M3 rows hi, lo with one E8M0 scale per 32 values (S = floor(log2
+ * block max) - 7; hi = x with its low four mantissa bits cleared, lo = x -
+ * hi, both / 2^S), so hi + lo == x exactly for |x| within 2^9 of the block
+ * maximum.  x bf16 [rows, K]; q u8 [rows, 2, K] (hi row, lo row); scales u8
+ * [rows, K/32].  The expert kernels run the same split on the permuted
+ * rows; this entry exposes it for callers and tests.  No reference
+ * counterpart (the reference multiplies bf16 activations directly).       */
+int klc_mx_quantize_rows(const uint16_t* x, int64_t rows, int64_t K, uint8_t* q, uint8_t* scales, void* stream);
+
 /* ---- router ------------------------------------------------------------ *
  * Replaces the router part of StreamedMoERouter.route
  * (streamed_moe_router.py:269-284): logits = bf16(x @ W^T + b) with fp32

@@ -75,9 +75,10 @@ constexpr int kTmemCols = 512;
 // phases ahead of a slot's mbarrier -- a parity wait would then pass on the
 // stale phase.
 //   ND  accumulator sets per issuer (the epilogue of one tile overlaps the next)
-template <int BN_, int NA_, int NS_, int NB_, int NP_, int ND_>
+//   PF  weight slots prefetched into L2 beyond the shared-memory ring
+template <int BN_, int NA_, int NS_, int NB_, int NP_, int ND_, int PF_>
 struct MxCfg {
-  static constexpr int BN = BN_, NA = NA_, NS = NS_, NB = NB_, NP = NP_, ND = ND_;
+  static constexpr int BN = BN_, NA = NA_, NS = NS_, NB = NB_, NP = NP_, ND = ND_, PF = PF_;
   static constexpr int N2 = 2 * BN;
   static constexpr int NCH = (N2 + 127) / 128;
   static constexpr int ASLOT = kBM * kSlotK / 2;     // 16384 packed bytes
@@ -216,14 +217,35 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpA) {
     // ------------------------------------------------------------ weights
+    // The shared-memory ring holds NA slots; an L2 prefetch cursor runs PF
+    // slots further ahead (the same boxes, no shared memory), so about
+    // (NA + PF) x 16 KB per SM are in flight to HBM.
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
+      int pf_item = blockIdx.x, pf_j = 0;
+      uint32_t pf_n = 0;
+      int4 pf_rb = pf_item < total ? p.rowblocks[pf_item / p.n_mtiles] : make_int4(0, 0, 0, 0);
+      auto prefetch_ahead = [&](uint32_t upto) {
+        while (pf_n < upto && pf_item < total) {
+          const int pmt = pf_item % p.n_mtiles;
+          tma_prefetch_3d(&map_a, pf_j * (kSlotK / 2), pmt * kBM, pf_rb.x);
+          const int pnsf = (2 * pf_j + 1 < ks_n) ? 2 : 1;
+          bulk_prefetch_l2(p.sfa + ((int64_t(pf_rb.x) * p.n_mtiles + pmt) * ks_n + 2 * pf_j) * 512, uint32_t(pnsf * 512));
+          ++pf_n;
+          if (++pf_j == spa) {
+            pf_j = 0;
+            pf_item += gridDim.x;
+            if (pf_item < total) pf_rb = p.rowblocks[pf_item / p.n_mtiles];
+          }
+        }
+      };
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
         const int mt = item % p.n_mtiles;
         const uint8_t* sfa_item = p.sfa + (int64_t(rb.x) * p.n_mtiles + mt) * int64_t(ks_n) * 512;
         for (int j = 0; j < spa && ok; ++j, ++it) {
+          prefetch_ahead(it + NA + C::PF);
           const int sa = it % NA;
           if (!(ok = wait_bar(aempty(sa), ((it / NA) & 1) ^ 1, ctl, 10))) break;
           const int nsf = (2 * j + 1 < ks_n) ? 2 : 1;  // scale blocks of the slot's stages
@@ -537,10 +559,10 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
   return st;
 }
 
-//                BN  NA NS NB NP ND
-using MxN32  = MxCfg<32, 7, 4, 4, 4, 1>;
-using MxN64  = MxCfg<64, 7, 2, 4, 2, 1>;
-using MxN128 = MxCfg<128, 5, 2, 2, 1, 1>;
+//                BN  NA NS NB NP ND PF
+using MxN32  = MxCfg<32, 7, 4, 4, 4, 1, 8>;
+using MxN64  = MxCfg<64, 7, 2, 4, 2, 1, 8>;
+using MxN128 = MxCfg<128, 5, 2, 2, 1, 1, 4>;
 
 }  // namespace
 

@@ -46,6 +46,56 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo_elem, float hi_elem) {
   return r;
 }
 
+// One 32-value block: 32 bf16 at src -> 32 E4M3 hi at hi, 32 E4M3 lo at lo;
+// returns the E8M0 scale byte S + 127.
+__device__ __forceinline__ uint8_t quantize_block(const uint4* __restrict__ src, uint8_t* __restrict__ hi,
+                                                  uint8_t* __restrict__ lo) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 v = src[i];
+    w[4 * i] = v.x;
+    w[4 * i + 1] = v.y;
+    w[4 * i + 2] = v.z;
+    w[4 * i + 3] = v.w;
+  }
+  // block maximum exponent from the bf16 bit patterns (sign dropped)
+  uint32_t emax = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t a = (w[i] >> 7) & 0xFFu, b = (w[i] >> 23) & 0xFFu;
+    emax = max(emax, max(a, b));
+  }
+  // S = (emax - 127) - 7, kept where 2^S and 2^-S are normal fp32 (the E8M0
+  // byte S + 127 is then in [1, 253]); all-zero blocks get S = 0
+  int S = emax == 0 ? 0 : int(emax) - 134;
+  S = S < -126 ? -126 : (S > 126 ? 126 : S);
+  const float inv = __uint_as_float(uint32_t(127 - S) << 23);  // 2^-S
+  uint32_t hi_w[8], lo_w[8];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint32_t b0 = w[i] & 0xFFFFu, b1 = w[i] >> 16;
+    const float x0 = __uint_as_float(b0 << 16), x1 = __uint_as_float(b1 << 16);
+    const float h0 = __uint_as_float((b0 & 0xFFF0u) << 16), h1 = __uint_as_float((b1 & 0xFFF0u) << 16);
+    const uint32_t hp = e4m3x2(h0 * inv, h1 * inv);  // bytes (elem 2i, elem 2i+1)
+    const uint32_t lp = e4m3x2((x0 - h0) * inv, (x1 - h1) * inv);
+    if (i & 1) {
+      hi_w[i >> 1] |= hp << 16;
+      lo_w[i >> 1] |= lp << 16;
+    } else {
+      hi_w[i >> 1] = hp;
+      lo_w[i >> 1] = lp;
+    }
+  }
+  uint4* dh = reinterpret_cast<uint4*>(hi);
+  uint4* dl = reinterpret_cast<uint4*>(lo);
+  dh[0] = make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
+  dh[1] = make_uint4(hi_w[4], hi_w[5], hi_w[6], hi_w[7]);
+  dl[0] = make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
+  dl[1] = make_uint4(lo_w[4], lo_w[5], lo_w[6], lo_w[7]);
+  return uint8_t(S + 127);
+}
+
 // One warp per row; lane l handles 32-K blocks l, l+32, ...
 __global__ void __launch_bounds__(256)
     quantize_rows_kernel(const uint16_t* __restrict__ src, int64_t K, const int32_t* __restrict__ rows_map, int k,
@@ -63,50 +113,7 @@ __global__ void __launch_bounds__(256)
     const uint4* s4 = reinterpret_cast<const uint4*>(src + srow * K);
     uint8_t* qh = q + row * 2 * K;
     for (int kb = lane; kb < G; kb += 32) {
-      uint32_t w[16];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = s4[kb * 4 + i];
-        w[4 * i] = v.x;
-        w[4 * i + 1] = v.y;
-        w[4 * i + 2] = v.z;
-        w[4 * i + 3] = v.w;
-      }
-      // block maximum exponent from the bf16 bit patterns (sign dropped)
-      uint32_t emax = 0;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t a = (w[i] >> 7) & 0xFFu, b = (w[i] >> 23) & 0xFFu;
-        emax = max(emax, max(a, b));
-      }
-      // S = (emax - 127) - 7, kept where 2^S and 2^-S are normal fp32 (the
-      // E8M0 byte S + 127 is then in [1, 253]); all-zero blocks get S = 0
-      int S = emax == 0 ? 0 : int(emax) - 134;
-      S = S < -126 ? -126 : (S > 126 ? 126 : S);
-      const float inv = __uint_as_float(uint32_t(127 - S) << 23);  // 2^-S
-      uint32_t hi_w[8], lo_w[8];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t b0 = w[i] & 0xFFFFu, b1 = w[i] >> 16;
-        const float x0 = __uint_as_float(b0 << 16), x1 = __uint_as_float(b1 << 16);
-        const float h0 = __uint_as_float((b0 & 0xFFF0u) << 16), h1 = __uint_as_float((b1 & 0xFFF0u) << 16);
-        const uint32_t hp = e4m3x2(h0 * inv, h1 * inv);          // bytes (elem 2i, elem 2i+1)
-        const uint32_t lp = e4m3x2((x0 - h0) * inv, (x1 - h1) * inv);
-        if (i & 1) {
-          hi_w[i >> 1] |= hp << 16;
-          lo_w[i >> 1] |= lp << 16;
-        } else {
-          hi_w[i >> 1] = hp;
-          lo_w[i >> 1] = lp;
-        }
-      }
-      uint4* dh = reinterpret_cast<uint4*>(qh + int64_t(kb) * 32);
-      uint4* dl = reinterpret_cast<uint4*>(qh + K + int64_t(kb) * 32);
-      dh[0] = make_uint4(hi_w[0], hi_w[1], hi_w[2], hi_w[3]);
-      dh[1] = make_uint4(hi_w[4], hi_w[5], hi_w[6], hi_w[7]);
-      dl[0] = make_uint4(lo_w[0], lo_w[1], lo_w[2], lo_w[3]);
-      dl[1] = make_uint4(lo_w[4], lo_w[5], lo_w[6], lo_w[7]);
-      const uint8_t sb = uint8_t(S + 127);
+      const uint8_t sb = quantize_block(s4 + kb * 4, qh + int64_t(kb) * 32, qh + K + int64_t(kb) * 32);
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int n2 = 2 * n + h;
@@ -115,6 +122,18 @@ __global__ void __launch_bounds__(256)
       }
     }
   }
+}
+
+// Plain layout for callers: rows [R, K] -> q [R, 2, K] (hi, lo), scales [R, K/32]
+__global__ void __launch_bounds__(256)
+    quantize_plain_kernel(const uint16_t* __restrict__ src, int64_t rows, int64_t K, uint8_t* __restrict__ q,
+                          uint8_t* __restrict__ scales) {
+  const int64_t G = K / 32;
+  const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // one 32-value block per thread
+  if (b >= rows * G) return;
+  const int64_t r = b / G, kb = b % G;
+  uint8_t* qr = q + r * 2 * K;
+  scales[b] = quantize_block(reinterpret_cast<const uint4*>(src + r * K) + kb * 4, qr + kb * 32, qr + K + kb * 32);
 }
 
 }  // namespace
@@ -130,6 +149,21 @@ int launch_quantize_rows(const uint16_t* src, int64_t K, const int32_t* rows_map
 }
 
 }  // namespace klc
+
+extern "C" int klc_mx_quantize_rows(const uint16_t* x, int64_t rows, int64_t K, uint8_t* q, uint8_t* scales,
+                                    void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(rows >= 0 && K > 0 && K % 32 == 0, "klc_mx_quantize_rows: K must be a positive multiple of 32");
+  if (rows == 0) return KLC_OK;
+  KLC_CHECK_ARG(x && q && scales, "klc_mx_quantize_rows: null pointer");
+  KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0,
+                "klc_mx_quantize_rows: x and q must be 16-byte aligned");
+  const int64_t blocks = (rows * (K / 32) + 255) / 256;
+  KLC_CHECK_ARG(blocks <= 0x7fffffff, "klc_mx_quantize_rows: too many rows");
+  quantize_plain_kernel<<<unsigned(blocks), 256, 0, as_stream(stream)>>>(x, rows, K, q, scales);
+  KLC_LAUNCH_CHECK("klc_mx_quantize_rows launch");
+  return KLC_OK;
+}
 
 extern "C" int klc_mxfp4_scales_mx_bytes(int64_t experts, int64_t rows, int64_t groups, size_t* out_bytes) {
   using namespace klc;
