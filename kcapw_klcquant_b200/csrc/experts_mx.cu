@@ -560,6 +560,7 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 }
 
 //                BN  NA NS NB NP ND PF
+using MxN16  = MxCfg<16, 7, 4, 4, 4, 2, 8>;
 using MxN32  = MxCfg<32, 7, 4, 4, 4, 1, 8>;
 using MxN64  = MxCfg<64, 7, 2, 4, 2, 1, 8>;
 using MxN128 = MxCfg<128, 5, 2, 2, 1, 1, 4>;
@@ -622,10 +623,11 @@ int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   KLC_CHECK_ARG(a.hidden % 64 == 0 && a.inter % 64 == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
   KLC_CHECK_ARG(2 * a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
   switch (a.block_n) {
+    case 16: return launch_mx_both<MxN16>(a, stream);
     case 32: return launch_mx_both<MxN32>(a, stream);
     case 64: return launch_mx_both<MxN64>(a, stream);
     case 128: return launch_mx_both<MxN128>(a, stream);
-    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 32, 64 or 128");
+    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 16, 32, 64 or 128");
   }
 }
 

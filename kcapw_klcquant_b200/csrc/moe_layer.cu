@@ -35,6 +35,7 @@ int pick_block_n(const klc_moe_dims& d, bool tc) {
   // weight pass each); a tensor-core tile holds at most 128 rows (256 hi/lo
   // operand rows)
   const int64_t per_expert = (d.tokens * d.top_k + d.experts - 1) / std::max<int64_t>(d.experts, 1);
+  if (per_expert <= 8) return 16;
   if (per_expert <= 12) return 32;
   if (per_expert <= 24) return 64;
   return 128;
