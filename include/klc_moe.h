@@ -121,6 +121,11 @@ int klc_router_topk(const uint16_t* x, int64_t tokens, int64_t hidden, const uin
                     int64_t experts, int k, const float* adjust, int32_t* out_idx, uint16_t* out_w,
                     uint16_t* out_logits, void* stream);
 
+/* Device faults of the router (a bounded wait of the tensor-core form that
+ * timed out): synchronises `stream`, returns KLC_OK or the recorded status
+ * (and its site) and clears it.  No reference counterpart.                */
+int klc_router_status(int* code, int* where, void* stream);
+
 /* Selection + softmax on given fp32 scores [T, E] (the locality path: the
  * host applies the reference's bias / guard policy, streamed_moe_router.py:
  * 331-394, to logits read back from klc_router_topk).  keep_order != 0:

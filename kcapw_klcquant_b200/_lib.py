@@ -78,6 +78,7 @@ SIGNATURES: dict[str, list] = {
     "klc_mxfp4_scales_mx_bytes": [c_int64, c_int64, c_int64, POINTER(c_size_t)],
     "klc_mxfp4_scales_mx": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "klc_mx_quantize_rows": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
+    "klc_router_status": [POINTER(c_int), POINTER(c_int), c_void_p],
     "klc_router_topk": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "klc_select_softmax": [c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
     "klc_moe_workspace_size": [POINTER(KlcDims), POINTER(c_size_t)],

@@ -14,9 +14,20 @@
 // per token gathers the token's E logits from the cluster's shared memory
 // (distributed shared memory), then runs k rounds of a warp-wide arg-max
 // (value descending, lower index on ties) and a k-way softmax.
+//
+// Tensor-core form (E <= 128, H a multiple of 64, H <= 3072): a cluster of C
+// = ceil(H / 384) CTAs splits the reduction for a tile of NT tokens; CTA r
+// multiplies the router rows [128 experts x 384 K] (rows past E zero) by the
+// tokens' [NT x 384 K] slice with tcgen05.mma (bf16, fp32 accumulate in
+// TMEM), leaves its partial logits in shared memory, and after a cluster
+// barrier each token's logits are the partials summed in rank order (fixed,
+// deterministic), the bias added in fp32 and rounded once to bf16.  The
+// CUDA-core form above covers the other shapes.
 #include <cooperative_groups.h>
 
 #include "klc_common.cuh"
+#include "permute.cuh"
+#include "tc_common.cuh"
 
 namespace klc {
 
@@ -193,6 +204,159 @@ __global__ void __launch_bounds__(kWarps * 32)
   cluster.sync();  // no CTA leaves while its logits may still be read
 }
 
+// ---------------------------------------------------------------------------
+// tensor-core router
+// ---------------------------------------------------------------------------
+constexpr int kRtK = 384;  // reduction slice per cluster rank (6 swizzle atoms of 64 bf16)
+
+__device__ DeviceStatus g_router_status;  // bounded-wait timeouts of the tensor-core router
+
+template <int NT>
+__global__ void __launch_bounds__(128, 1)
+    router_tc_kernel(const uint16_t* __restrict__ x, int64_t tokens, int64_t hidden, const uint16_t* __restrict__ w,
+                     const uint16_t* __restrict__ b, int experts, int k, const float* __restrict__ adjust,
+                     int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  namespace cg = cooperative_groups;
+  using namespace tc;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = int(cluster.num_blocks());
+  const int crank = int(cluster.block_rank());
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* ws = smem;                      // router rows: 6 atoms x 128 rows x 128 B (later: partials)
+  unsigned char* xs = smem + 6 * 16384;          // tokens: 6 atoms x NT rows x 128 B (later: per-warp rows)
+  __shared__ __align__(8) uint64_t mma_bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ int failed;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t0 = int64_t(blockIdx.x / C) * NT;
+  const int ntok = int(tokens - t0 < NT ? tokens - t0 : NT);
+  const int k0 = crank * kRtK;
+  const int kc = int(hidden - k0 < kRtK ? hidden - k0 : kRtK);  // a multiple of 64
+  const int na = kc / 64;
+
+  // stage both operands in the 128B-swizzled K-major layout (16-byte async
+  // copies; rows past E / past the tokens are zero-filled)
+  for (int i = threadIdx.x; i < na * 128 * 8; i += blockDim.x) {
+    const int a = i / 1024, r = (i >> 3) & 127, c = i & 7;
+    const uint16_t* src = w + int64_t(r < experts ? r : 0) * hidden + k0 + a * 64 + c * 8;
+    const uint32_t dst = smem_u32(ws + a * 16384 + (r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(r < experts ? 16 : 0)
+                 : "memory");
+  }
+  for (int i = threadIdx.x; i < na * NT * 8; i += blockDim.x) {
+    const int a = i / (NT * 8), t = (i >> 3) % NT, c = i & 7;
+    const uint16_t* src = x + (t0 + (t < ntok ? t : 0)) * hidden + k0 + a * 64 + c * 8;
+    const uint32_t dst = smem_u32(xs + a * (NT * 128) + (t >> 3) * 1024 + (t & 7) * 128 + ((c ^ (t & 7)) << 4));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(t < ntok ? 16 : 0)
+                 : "memory");
+  }
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&mma_bar), 1);
+    failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_holder)),
+                 "r"(NT < 32 ? 32 : NT));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+  if (threadIdx.x == 0) {
+    // kind::f16: bf16 A and B, fp32 accumulate, both K-major, M = 128, N = NT
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(NT >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+    const uint64_t ad = sw128_desc(smem_u32(ws)), bd = sw128_desc(smem_u32(xs));
+    for (int a = 0; a < na; ++a)
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t acc = (a | kk) ? 1u : 0u;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+            "l"(ad + uint64_t((a * 16384 + kk * 32) >> 4)), "l"(bd + uint64_t((a * NT * 128 + kk * 32) >> 4)),
+            "r"(idesc), "r"(acc));
+      }
+    tc_commit(smem_u32(&mma_bar));
+  }
+  // every thread waits for the accumulators (bounded)
+  {
+    bool ok = mbar_try_wait(smem_u32(&mma_bar), 0);
+    const long long ts = clock64();
+    while (!ok) {
+      ok = mbar_try_wait(smem_u32(&mma_bar), 0);
+      if (!ok && clock64() - ts > kWaitCycles) {
+        failed = 1;
+        record_fault(&g_router_status, KLC_ERR_DEVICE_TIMEOUT, 50, 0);
+        break;
+      }
+    }
+  }
+  tc_fence_after();
+  // partial logits [128 experts][NT tokens] fp32 into shared memory (the operand space is free now)
+  float* part = reinterpret_cast<float*>(ws);
+#pragma unroll
+  for (int c0 = 0; c0 < NT; c0 += 16) {
+    uint32_t v[16];
+    tmem_ld16(tmem + (uint32_t(warp * 32) << 16) + uint32_t(c0), v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) part[(warp * 32 + lane) * NT + c0 + j] = __uint_as_float(v[j]);
+  }
+  tc_fence_before();
+  cluster.sync();
+
+  // tokens t = crank + C*j of the tile: sum the C partials in rank order, bias, one bf16 rounding,
+  // then top-k + softmax (one warp per token)
+  float* rows = reinterpret_cast<float*>(xs);  // [4 warps][experts]
+  for (int t = crank + C * warp; t < ntok; t += C * 4) {
+    float* row = rows + warp * experts;
+    for (int e = lane; e < experts; e += 32) {
+      float acc = 0.f;
+      for (int r = 0; r < C; ++r) acc += cluster.map_shared_rank(part, r)[e * NT + t];
+      const uint16_t lb = f32_to_bf16(acc + bf16_to_f32(b[e]));
+      if (out_logits) out_logits[(t0 + t) * experts + e] = lb;
+      row[e] = bf16_to_f32(lb) + (adjust ? adjust[e] : 0.f);
+    }
+    __syncwarp();
+    if (!failed) select_softmax_warp(row, experts, k, false, out_idx + (t0 + t) * k, out_w + (t0 + t) * k);
+    __syncwarp();
+  }
+  cluster.sync();  // no CTA leaves while its partials may still be read
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT < 32 ? 32 : NT));
+}
+
+template <int NT>
+int launch_router_tc(const uint16_t* x, int64_t tokens, int64_t hidden, const uint16_t* w, const uint16_t* b,
+                     int experts, int k, const float* adjust, int32_t* out_idx, uint16_t* out_w, uint16_t* out_logits,
+                     cudaStream_t stream) {
+  const int C = int((hidden + kRtK - 1) / kRtK);
+  const int64_t tiles = (tokens + NT - 1) / NT;
+  KLC_CHECK_ARG(tiles * C <= 0x7fffffff, "klc_router_topk: too many tokens");
+  const size_t smem = 6 * 16384 + 6 * NT * 128 + 1024;
+  KLC_CUDA(cudaFuncSetAttribute(router_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(tiles * C));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  KLC_CUDA(cudaLaunchKernelEx(&cfg, router_tc_kernel<NT>, x, tokens, hidden, w, b, experts, k, adjust, out_idx, out_w,
+                              out_logits));
+  KLC_LAUNCH_CHECK("klc_router_topk launch");
+  return KLC_OK;
+}
+
 __global__ void select_kernel(const float* __restrict__ scores, int64_t tokens, int experts, int k, int keep_order,
                               int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w) {
   const int lane = threadIdx.x & 31;
@@ -215,6 +379,16 @@ int launch_router(const uint16_t* x, int64_t tokens, int64_t hidden, const uint1
   KLC_CHECK_ARG(x && w && b && out_idx && out_w, "klc_router_topk: null pointer");
   KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
                 "klc_router_topk: x and w must be 16-byte aligned");
+  if (experts <= 128 && hidden % 64 == 0 && hidden <= 8 * kRtK && tc_path_supported(hidden, 64)) {
+    // token tile: as few router-weight passes as keep every SM busy
+    const int C = int((hidden + kRtK - 1) / kRtK);
+    const int64_t want = 2 * int64_t(sm_count());
+    if ((tokens + 15) / 16 * C <= want)
+      return launch_router_tc<16>(x, tokens, hidden, w, b, int(experts), k, adjust, out_idx, out_w, out_logits, stream);
+    if ((tokens + 31) / 32 * C <= want)
+      return launch_router_tc<32>(x, tokens, hidden, w, b, int(experts), k, adjust, out_idx, out_w, out_logits, stream);
+    return launch_router_tc<64>(x, tokens, hidden, w, b, int(experts), k, adjust, out_idx, out_w, out_logits, stream);
+  }
   // cluster size: enough CTAs to cover the SMs twice, at least 8 experts per CTA
   const int64_t nblocks = (tokens + kTok - 1) / kTok;
   int C = 1;
@@ -256,6 +430,20 @@ extern "C" int klc_select_softmax(const float* scores, int64_t tokens, int64_t e
   select_kernel<<<unsigned(blocks), 256, 0, as_stream(stream)>>>(scores, tokens, int(experts), k, keep_order, out_idx, out_w);
   KLC_LAUNCH_CHECK("klc_select_softmax launch");
   return KLC_OK;
+}
+
+extern "C" int klc_router_status(int* code, int* where, void* stream) {
+  using namespace klc;
+  KLC_CUDA(cudaStreamSynchronize(as_stream(stream)));
+  DeviceStatus st{};
+  KLC_CUDA(cudaMemcpyFromSymbol(&st, g_router_status, sizeof(st)));
+  if (code) *code = st.code;
+  if (where) *where = st.where;
+  if (st.code != 0) {
+    const DeviceStatus zero{};
+    KLC_CUDA(cudaMemcpyToSymbol(g_router_status, &zero, sizeof(zero)));
+  }
+  return st.code == 0 ? KLC_OK : st.code;
 }
 
 extern "C" int klc_router_topk(const uint16_t* x, int64_t tokens, int64_t hidden, const uint16_t* w,

@@ -77,7 +77,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Ct
 }
 
 // Drain-time wait: bounded, ignores the abort flag.
-__device__ __noinline__ void drain_wait(uint32_t bar, uint32_t parity) {
+static __device__ __noinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
     if (globaltimer() - t0 > kWaitNs) return;
@@ -88,7 +88,7 @@ __device__ __noinline__ void drain_wait(uint32_t bar, uint32_t parity) {
 // After an abort: wait (bounded) for the latest load issued into each slot of
 // a ring of `n` full-barriers (8 bytes apart) that received `issued` loads in
 // slot order (load i went to slot i % n, completing phase (i / n) & 1).
-__device__ __noinline__ void drain_ring(uint32_t full0, int n, uint32_t issued) {
+static __device__ __noinline__ void drain_ring(uint32_t full0, int n, uint32_t issued) {
   for (int s = 0; s < n; ++s) {
     if (issued <= uint32_t(s)) break;
     const uint32_t last = issued - 1 - ((issued - 1 - uint32_t(s)) % uint32_t(n));

@@ -135,6 +135,44 @@ def test_select_softmax_keep_order():
     np.testing.assert_array_equal(bits_of(w)[0], orc.softmax_weights_bits(s.cpu().numpy())[0])
 
 
+# Both router forms against the oracle's logits (fp32 accumulation, one bf16
+# rounding): E <= 128 with H a multiple of 64 runs the tensor-core split-K
+# router, the other shapes the CUDA-core router; token counts cross the
+# 16 / 32 / 64-token tile choices.
+@pytest.mark.parametrize("T,E,H,k", [(1, 128, 2880, 4), (37, 32, 2880, 4), (300, 128, 2880, 4), (5000, 128, 2880, 4),
+                                     (20, 8, 64, 2), (33, 128, 3072, 4), (40, 192, 256, 4), (24, 64, 200, 3)])
+def test_router_shapes_vs_oracle(T, E, H, k):
+    from kcapw_klcquant_b200 import _lib
+
+    rng = np.random.default_rng(T * 7 + E)
+    x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(torch.bfloat16)
+    wr = torch.from_numpy((rng.standard_normal((E, H)) * 0.05).astype(np.float32)).to(torch.bfloat16)
+    br = torch.from_numpy((rng.standard_normal(E) * 0.1).astype(np.float32)).to(torch.bfloat16)
+    xd, wd, bd = x.to(DEV), wr.to(DEV), br.to(DEV)
+    idx = torch.empty((T, k), dtype=torch.int32, device=DEV)
+    w = torch.empty((T, k), dtype=torch.bfloat16, device=DEV)
+    lg = torch.empty((T, E), dtype=torch.bfloat16, device=DEV)
+    _lib.check(_lib.lib().klc_router_topk(xd.data_ptr(), T, H, wd.data_ptr(), bd.data_ptr(), E, k, None, idx.data_ptr(),
+                                          w.data_ptr(), lg.data_ptr(), _lib.stream_ptr()))
+    assert _lib.lib().klc_router_status(None, None, _lib.stream_ptr()) == _lib.KLC_OK
+    ref = orc.router_logits_bits(bits_of(x), bits_of(wr), bits_of(br))
+    got = bits_of(lg)
+    d = parity.ulp_distance_bf16(got, ref)
+    assert np.mean(d > 0) <= 0.01
+    # one bf16 ulp, or (near-cancelling sums) an fp32 accumulation error of at most
+    # 2^-18 of the sum of |products|: fp32 sums in another order than the oracle's
+    xf, wf = x.float().numpy(), wr.float().numpy()
+    mag = np.abs(xf) @ np.abs(wf).T + np.abs(br.float().numpy())
+    err = np.abs(orc.bf16_bits_to_f32(got).astype(np.float64) - orc.bf16_bits_to_f32(ref))
+    ok = (d <= 1) | (err <= mag * 2.0**-18)
+    assert ok.all(), (d.max(), float((err / mag).max()))
+    got_idx = idx.cpu().numpy()
+    parity.check_selection(got, got_idx, k)
+    scores = np.take_along_axis(orc.bf16_bits_to_f32(got), got_idx.astype(np.int64), axis=1)
+    wdist = parity.ulp_distance_bf16(bits_of(w), orc.softmax_weights_bits(scores))
+    assert wdist.max() <= 1 and np.mean(wdist > 0) <= 0.02
+
+
 # ---------------------------------------------------------------------------
 # permutation (bit-exact vs the stable-sort oracle)
 # ---------------------------------------------------------------------------
