@@ -24,7 +24,7 @@
 // its padded slot of a small staging ring (no bit manipulation).
 //
 // One persistent CTA per SM walks the (row-block, m-tile) work list;
-// warp-specialised (608 threads):
+// warp-specialised (864 threads):
 //   warp 0      TMA producer: packed weights (128 rows x 128 B, 128B swizzle)
 //               + the two 512-byte scale blocks of the slot (bulk copy)
 //   warps 1,18  TMA producers: hi/lo activation rows (N2 x 128 B) + their
@@ -36,7 +36,8 @@
 //               issuers with their own accumulators keep the tensor pipe fed
 //   warps 4-7   epilogue: TMEM loads, hi + lo, pipelines summed in a fixed
 //               order, bias, SwiGLU (gate_up) or bias (down), bf16 stores
-//   warps 8-15  two repack warpgroups (stage `it` to warpgroup it % 2)
+//   warps 8-15, four repack warpgroups (stage `it` to warpgroup it % 4)
+//   19-26
 //
 // Every mbarrier wait is bounded (tc_common.cuh): a timed-out role records
 // KLC_ERR_DEVICE_TIMEOUT, raises the CTA abort flag, and all roles drain
@@ -55,8 +56,14 @@ namespace {
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kStageK = 128;    // K per MMA stage: 4 MMAs of K = 32 (4 scale blocks)
 constexpr int kSlotK = 256;     // K per weight slot (128-byte packed rows)
-constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpMma2 = 16, kWarpB2 = 18;
-constexpr int kThreads = 19 * 32;
+constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpMma2 = 16, kWarpB2 = 18,
+              kWarpRep2 = 19;
+constexpr int kRepWGs = 4;  // repack warpgroups: warps 8-15 and 19-26, stage s to warpgroup s % 4
+constexpr int kThreads = 27 * 32;
+__device__ __forceinline__ int repack_wg_of_warp(int warp) {  // repack warpgroup of a warp, or -1
+  return (warp >= kWarpRep0 && warp < kWarpRep0 + 8) ? (warp - kWarpRep0) >> 2
+       : (warp >= kWarpRep2 && warp < kWarpRep2 + 8) ? 2 + ((warp - kWarpRep2) >> 2) : -1;
+}
 __device__ __forceinline__ int issuer_of_warp(int warp) {  // MMA pipeline of a warp, or -1
   return (warp == kWarpMma0 || warp == kWarpMma0 + 1) ? warp - kWarpMma0
        : (warp == kWarpMma2 || warp == kWarpMma2 + 1) ? 2 + warp - kWarpMma2 : -1;
@@ -100,16 +107,16 @@ struct MxCfg {
   static constexpr int SF_COLS = 4 + 4 * NCH;
   static_assert(ACC_COLS + NP * SF_COLS <= kTmemCols, "TMEM budget");
   static_assert((NP == 1 || NP == 2 || NP == 4) && N2 <= 256, "issuers / tile");
-  static_assert(NS % NP == 0 && NB % NP == 0 && NB % 2 == 0 && (NS / NP) % (NP == 1 ? 2 : 1) == 0, "slot ownership");
+  static_assert(NS == kRepWGs && NB % NP == 0 && NB % 2 == 0, "slot ownership");
   static constexpr int NSP = NS / NP;  // staging slots per issuer
   static_assert(BSLOT % 1024 == 0, "activation slots stay 1024-byte aligned");
   static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
 };
 
 // Staging slot of MMA stage s (issuer s % NP, its (s / NP)-th stage) and the
-// mbarrier phase parity of that use.  The repack warpgroup of stage s is s & 1
-// (NP is 1, 2 or 4), so each slot is filled by one warpgroup and drained by
-// one issuer, both in stage order.
+// mbarrier phase parity of that use.  With NS = 4 the slot is s % 4 for NP of
+// 1, 2 or 4, the repack warpgroup of stage s is s % 4 too, so each slot is
+// filled by one warpgroup and drained by one issuer, both in stage order.
 template <class C>
 __device__ __forceinline__ void staging_slot(uint32_t s, int& slot, uint32_t& parity) {
   const uint32_t pp = s % C::NP, li = s / C::NP;
@@ -348,16 +355,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(mma_done);
       drain_wait(mma_done, 0);
     }
-  } else if (warp >= kWarpRep0 && warp < kWarpRep0 + 8) {
+  } else if (repack_wg_of_warp(warp) >= 0) {
     // ------------------------------------------------------------ repack
-    const int wg = (warp - kWarpRep0) >> 2;  // stages with it % 2 == wg
-    const int m = ((warp - kWarpRep0) & 3) * 32 + lane;
+    const int wg = repack_wg_of_warp(warp);  // stages with it % 4 == wg
+    const int m = (warp & 3) * 32 + lane;
     const int sw = m & 7;
     uint32_t it = 0, ic = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
       for (int ks = 0; ks < ks_n; ++ks, ++it) {
-        if (int(it & 1) != wg) continue;
+        if (int(it % kRepWGs) != wg) continue;
         const uint32_t ia = ic * uint32_t(spa) + uint32_t(ks >> 1);
         const int sa = ia % NA, h = ks & 1;
         int ss;
@@ -562,8 +569,8 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 //                BN  NA NS NB NP ND PF
 using MxN16  = MxCfg<16, 7, 4, 4, 4, 2, 8>;
 using MxN32  = MxCfg<32, 7, 4, 4, 4, 1, 8>;
-using MxN64  = MxCfg<64, 7, 2, 4, 2, 1, 8>;
-using MxN128 = MxCfg<128, 5, 2, 2, 1, 1, 4>;
+using MxN64  = MxCfg<64, 6, 4, 2, 2, 1, 8>;
+using MxN128 = MxCfg<128, 5, 4, 2, 1, 1, 4>;
 
 }  // namespace
 
