@@ -24,9 +24,10 @@
 // its padded slot of a small staging ring (no bit manipulation).
 //
 // One persistent CTA per SM walks the (row-block, m-tile) work list;
-// warp-specialised (864 threads):
-//   warp 0      TMA producer: packed weights (128 rows x 128 B, 128B swizzle)
-//               + the two 512-byte scale blocks of the slot (bulk copy)
+// warp-specialised (896 threads):
+//   warps 0,27  TMA producers: packed weights (128 rows x 128 B, 128B
+//               swizzle) + the two 512-byte scale blocks of the slot (bulk
+//               copy), even / odd slots
 //   warps 1,18  TMA producers: hi/lo activation rows (N2 x 128 B) + their
 //               scale blocks, even / odd stages
 //   warps 2-3,  MMA issuers (one thread each; stage `it` to issuer it % NP):
@@ -57,9 +58,9 @@ constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kStageK = 128;    // K per MMA stage: 4 MMAs of K = 32 (4 scale blocks)
 constexpr int kSlotK = 256;     // K per weight slot (128-byte packed rows)
 constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpMma2 = 16, kWarpB2 = 18,
-              kWarpRep2 = 19;
+              kWarpRep2 = 19, kWarpA2 = 27;
 constexpr int kRepWGs = 4;  // repack warpgroups: warps 8-15 and 19-26, stage s to warpgroup s % 4
-constexpr int kThreads = 27 * 32;
+constexpr int kThreads = 28 * 32;
 __device__ __forceinline__ int repack_wg_of_warp(int warp) {  // repack warpgroup of a warp, or -1
   return (warp >= kWarpRep0 && warp < kWarpRep0 + 8) ? (warp - kWarpRep0) >> 2
        : (warp >= kWarpRep2 && warp < kWarpRep2 + 8) ? 2 + ((warp - kWarpRep2) >> 2) : -1;
@@ -107,7 +108,7 @@ struct MxCfg {
   static constexpr int SF_COLS = 4 + 4 * NCH;
   static_assert(ACC_COLS + NP * SF_COLS <= kTmemCols, "TMEM budget");
   static_assert((NP == 1 || NP == 2 || NP == 4) && N2 <= 256, "issuers / tile");
-  static_assert(NS == kRepWGs && NB % NP == 0 && NB % 2 == 0, "slot ownership");
+  static_assert(NS == kRepWGs && NB % NP == 0 && NB % 2 == 0 && NA % 2 == 0, "slot ownership");
   static constexpr int NSP = NS / NP;  // staging slots per issuer
   static_assert(BSLOT % 1024 == 0, "activation slots stay 1024-byte aligned");
   static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
@@ -222,23 +223,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int ks_n = p.ksteps;
   const int spa = (ks_n + 1) / 2;  // weight slots per item (the last may hold one stage)
 
-  if (warp == kWarpA) {
+  if (warp == kWarpA || warp == kWarpA2) {
     // ------------------------------------------------------------ weights
-    // The shared-memory ring holds NA slots; an L2 prefetch cursor runs PF
-    // slots further ahead (the same boxes, no shared memory), so about
-    // (NA + PF) x 16 KB per SM are in flight to HBM.
+    // Two producers (slot parity q; NA even, so each slot has one producer):
+    // one thread's per-slot issue latency next to busy warps would otherwise
+    // bound the stage rate.  The shared-memory ring holds NA slots; an L2
+    // prefetch cursor runs PF slots further ahead (the same boxes, no shared
+    // memory), so about (NA + PF) x 16 KB per SM are in flight to HBM.
+    const uint32_t q = warp == kWarpA ? 0u : 1u;
     if (lane == 0) {
-      uint32_t it = 0;
+      uint32_t it = 0, mine = 0;
       bool ok = true;
       int pf_item = blockIdx.x, pf_j = 0;
       uint32_t pf_n = 0;
       int4 pf_rb = pf_item < total ? p.rowblocks[pf_item / p.n_mtiles] : make_int4(0, 0, 0, 0);
       auto prefetch_ahead = [&](uint32_t upto) {
         while (pf_n < upto && pf_item < total) {
-          const int pmt = pf_item % p.n_mtiles;
-          tma_prefetch_3d(&map_a, pf_j * (kSlotK / 2), pmt * kBM, pf_rb.x);
-          const int pnsf = (2 * pf_j + 1 < ks_n) ? 2 : 1;
-          bulk_prefetch_l2(p.sfa + ((int64_t(pf_rb.x) * p.n_mtiles + pmt) * ks_n + 2 * pf_j) * 512, uint32_t(pnsf * 512));
+          if ((pf_n & 1u) == q) {
+            const int pmt = pf_item % p.n_mtiles;
+            tma_prefetch_3d(&map_a, pf_j * (kSlotK / 2), pmt * kBM, pf_rb.x);
+            const int pnsf = (2 * pf_j + 1 < ks_n) ? 2 : 1;
+            bulk_prefetch_l2(p.sfa + ((int64_t(pf_rb.x) * p.n_mtiles + pmt) * ks_n + 2 * pf_j) * 512,
+                             uint32_t(pnsf * 512));
+          }
           ++pf_n;
           if (++pf_j == spa) {
             pf_j = 0;
@@ -252,6 +259,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int mt = item % p.n_mtiles;
         const uint8_t* sfa_item = p.sfa + (int64_t(rb.x) * p.n_mtiles + mt) * int64_t(ks_n) * 512;
         for (int j = 0; j < spa && ok; ++j, ++it) {
+          if ((it & 1u) != q) continue;
           prefetch_ahead(it + NA + C::PF);
           const int sa = it % NA;
           if (!(ok = wait_bar(aempty(sa), ((it / NA) & 1) ^ 1, ctl, 10))) break;
@@ -260,9 +268,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(smem_u32(smem + C::OFF_A + sa * C::ASLOT), &map_a, j * (kSlotK / 2), mt * kBM, rb.x, afull(sa));
           bulk_load(smem_u32(smem + C::OFF_ASF + sa * 1024), sfa_item + int64_t(2 * j) * 512, uint32_t(nsf * 512),
                     afull(sa));
+          ++mine;
         }
       }
-      if (!ok) drain_ring(afull(0), NA, it);  // aborting: no bulk copy may still write shared memory
+      if (!ok) {
+        // aborting: no bulk copy may still write shared memory -- the latest load of each of
+        // this producer's slots (slot counters q + 2i, i < mine)
+        const uint32_t first = mine > uint32_t(NA / 2) ? mine - uint32_t(NA / 2) : 0u;
+        for (uint32_t i = first; i < mine; ++i) {
+          const uint32_t sl = q + 2 * i;
+          drain_wait(afull(int(sl % NA)), (sl / NA) & 1);
+        }
+      }
     }
   } else if (warp == kWarpB || warp == kWarpB2) {
     // ------------------------------------------------------------ activations
@@ -567,10 +584,10 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 }
 
 //                BN  NA NS NB NP ND PF
-using MxN16  = MxCfg<16, 7, 4, 4, 4, 2, 8>;
-using MxN32  = MxCfg<32, 7, 4, 4, 4, 1, 8>;
+using MxN16  = MxCfg<16, 6, 4, 8, 4, 2, 8>;
+using MxN32  = MxCfg<32, 6, 4, 4, 4, 1, 8>;
 using MxN64  = MxCfg<64, 6, 4, 2, 2, 1, 8>;
-using MxN128 = MxCfg<128, 5, 4, 2, 1, 1, 4>;
+using MxN128 = MxCfg<128, 4, 4, 2, 1, 1, 4>;
 
 }  // namespace
 
