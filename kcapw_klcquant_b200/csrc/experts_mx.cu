@@ -108,16 +108,17 @@ struct MxCfg {
   static constexpr int SF_COLS = 4 + 4 * NCH;
   static_assert(ACC_COLS + NP * SF_COLS <= kTmemCols, "TMEM budget");
   static_assert((NP == 1 || NP == 2 || NP == 4) && N2 <= 256, "issuers / tile");
-  static_assert(NS == kRepWGs && NB % NP == 0 && NB % 2 == 0 && NA % 2 == 0, "slot ownership");
+  static_assert(NS % kRepWGs == 0 && NS % NP == 0 && NB % NP == 0 && NB % 2 == 0 && NA % 2 == 0, "slot ownership");
   static constexpr int NSP = NS / NP;  // staging slots per issuer
   static_assert(BSLOT % 1024 == 0, "activation slots stay 1024-byte aligned");
   static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
 };
 
 // Staging slot of MMA stage s (issuer s % NP, its (s / NP)-th stage) and the
-// mbarrier phase parity of that use.  With NS = 4 the slot is s % 4 for NP of
-// 1, 2 or 4, the repack warpgroup of stage s is s % 4 too, so each slot is
-// filled by one warpgroup and drained by one issuer, both in stage order.
+// mbarrier phase parity of that use.  Stages sharing a slot are congruent
+// modulo NS (a multiple of 4) for NP of 1, 2 or 4, and the repack warpgroup of
+// stage s is s % 4, so each slot is filled by one warpgroup and drained by one
+// issuer, both in stage order; with NS = 8 every issuer double-buffers.
 template <class C>
 __device__ __forceinline__ void staging_slot(uint32_t s, int& slot, uint32_t& parity) {
   const uint32_t pp = s % C::NP, li = s / C::NP;
@@ -387,9 +388,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         int ss;
         uint32_t sph;
         staging_slot<C>(it, ss, sph);
-        // every lane waits (acquire); the decision is warp-uniform
+        // every lane waits (acquire); the decision is warp-uniform.  The packed
+        // half and its scales are read before waiting for the staging slot, so
+        // only the stores follow the MMA that frees it.
         ok = wait_bar(afull(sa), (ia / NA) & 1, ctl, 30);
-        if (ok) ok = wait_bar(sempty(ss), sph ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         // packed row m, 64-byte half h: chunks 4h..4h+3 of the 128B-swizzled row
         const unsigned char* src = smem + C::OFF_A + sa * C::ASLOT + m * 128;
@@ -397,6 +399,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) c[i] = *reinterpret_cast<const uint4*>(src + (((4 * h + i) ^ sw) << 4));
         const uint32_t scl = *reinterpret_cast<const uint32_t*>(smem + C::OFF_ASF + sa * 1024 + h * 512 + m * 4);
+        __syncwarp();  // every lane's reads of the weight slot precede the release
+        if (lane == 0) {
+          mbar_arrive(aempty(sa));
+          if (h == 0 && ks == ks_n - 1) mbar_arrive(aempty(sa));  // the slot has no second stage
+        }
+        ok = wait_bar(sempty(ss), sph ^ 1, ctl, 31);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
         // padded row m: 8 groups of 16 values, group g in the first 8 bytes of 16-byte chunk g ^ (m & 7)
         unsigned char* dst = smem + C::OFF_S + ss * C::SSLOT + (m >> 3) * 1024 + (m & 7) * 128;
 #pragma unroll
@@ -407,11 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<uint32_t*>(smem + C::OFF_SSF + ss * 512 + m * 4) = scl;
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(aempty(sa));
-          if (h == 0 && ks == ks_n - 1) mbar_arrive(aempty(sa));  // the slot has no second stage
-          mbar_arrive(sfull(ss));
-        }
+        if (lane == 0) mbar_arrive(sfull(ss));
       }
     }
   } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
