@@ -309,6 +309,7 @@ def run_ours(args, world, rank, local):
 
     et = time_steps(e2e, args.steps, args.warmup, flush, world)
     e2e_ms = max_over_ranks(sum(et) / len(et), world)
+    ml.check_device_status()  # a kernel that gave up on a bounded wait would make every number above invalid
 
     # roofline of the dominant kernel (gate_up GEMM for decode)
     decode = args.workload == "decode"
@@ -411,6 +412,7 @@ def run_ep(args, world, rank, local):
 
     et = time_steps(e2e, args.steps, args.warmup, None, world)
     e2e_ms = max_over_ranks(sum(et) / len(et), world)
+    moe.check_device_status()
     epr = GPT_OSS_E // world
     layer_bytes = epr * BYTES_PER_EXPERT  # per rank: its experts' weights (all are routed to at these sizes)
     result = {

@@ -103,10 +103,15 @@ struct MxCfg {
   static constexpr int NUM_BARS = 2 * NA + 2 * NS + 2 * NB + NP * ND + ND + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int BYTES = OFF_MISC + 16;
-  // TMEM: accumulators, then per issuer 4 scale columns for A and 4 per B chunk
+  // TMEM: accumulators, then per staging slot 4 scale columns for A and 4
+  // per B chunk.  An MMA followed by a tcgen05.cp from the same thread is not
+  // ordered, so the scales of a stage must not overwrite columns an earlier
+  // MMA may still read: keyed by staging slot, a scale set is rewritten only
+  // for the slot's next use, which the repack fills after the MMAs of the
+  // previous use completed (the issuer waits for that fill).
   static constexpr int ACC_COLS = ND * NP * N2;
   static constexpr int SF_COLS = 4 + 4 * NCH;
-  static_assert(ACC_COLS + NP * SF_COLS <= kTmemCols, "TMEM budget");
+  static_assert(ACC_COLS + NS * SF_COLS <= kTmemCols, "TMEM budget");
   static_assert((NP == 1 || NP == 2 || NP == 4) && N2 <= 256, "issuers / tile");
   static_assert(NS % kRepWGs == 0 && NS % NP == 0 && NB % NP == 0 && NB % 2 == 0 && NA % 2 == 0, "slot ownership");
   static constexpr int NSP = NS / NP;  // staging slots per issuer
@@ -321,8 +326,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuers
     const int pp = issuer_of_warp(warp);
     if (lane == 0 && pp < NP) {
-      const uint32_t sfa_t = tmem + uint32_t(C::ACC_COLS + pp * C::SF_COLS);
-      const uint32_t sfb_t = sfa_t + 4;
       uint32_t it = 0, ic = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
@@ -342,6 +345,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!(ok = wait_bar(sfull(ss), sph, ctl, 21))) break;
           if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
           tc_fence_after();
+          const uint32_t sfa_t = tmem + uint32_t(C::ACC_COLS + ss * C::SF_COLS);  // the staging slot's scale set
+          const uint32_t sfb_t = sfa_t + 4;
           sf_copy(sfa_t, plain_desc(smem_u32(smem + C::OFF_SSF + ss * 512)));
 #pragma unroll
           for (int ch = 0; ch < NCH; ++ch)

@@ -130,6 +130,12 @@ class ExpertParallelMoe:
         dist.all_to_all_single(out, send, output_split_sizes=recv_counts, input_split_sizes=send_counts, group=self.group)
         return out
 
+    def check_device_status(self) -> None:
+        """Raise if a kernel of the last local expert call recorded a device-side fault (synchronises)."""
+        local = getattr(self.backend, "local", None)  # host backends have no device status
+        if local is not None:
+            local.check_device_status()
+
     def forward(self, x: torch.Tensor, precision: str = "bf16", residual: torch.Tensor | None = None) -> tuple[torch.Tensor, RouteBatch]:
         be = self.backend
         idx, w = be.router(x)

@@ -47,6 +47,7 @@ def test_ep_single_rank_matches_layer():
         ep = ExpertParallelMoe(0, layer, dev, top_k=4)
         y, rb = ep.forward(x, precision="bf16")
         torch.cuda.synchronize()
+        ep.check_device_status()
         assert torch.equal(rb.indices, rb_ref.indices)
         m = parity.assert_output_close(_bits(y), _bits(ref), "ep1 vs layer")
         assert m["bit_equal_frac"] >= 0.99, m
@@ -70,6 +71,7 @@ def _worker(rank, world, port, q):
         ep = ExpertParallelMoe(0, layer, dev, top_k=4)
         for _ in range(2):  # repeated steps reuse the exchange buffers
             y, rb = ep.forward(x, precision="bf16")
+            ep.check_device_status()
         torch.cuda.synchronize()
         q.put((rank, bool(torch.equal(rb.indices, rb_ref.indices)), _bits(y), _bits(ref)))
     finally:
