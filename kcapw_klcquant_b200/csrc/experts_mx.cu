@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuers
     const int pp = issuer_of_warp(warp);
     if (lane == 0 && pp < NP) {
-      uint32_t it = 0, ic = 0;
+      uint32_t it = uint32_t(pp), ic = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
@@ -336,8 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
         tc_fence_after();
         bool first = true;
-        for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
-          if (NP > 1 && int(it % NP) != pp) continue;
+        const uint32_t it0 = ic * uint32_t(ks_n), it_end = it0 + uint32_t(ks_n);
+        for (; it < it_end && ok; it += NP) {
+          const int ks = int(it - it0);
           int ss;
           uint32_t sph;
           staging_slot<C>(it, ss, sph);
@@ -593,11 +594,19 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
   return st;
 }
 
+// Two tile shapes.  Measured on B200 (gate_up + down, GPT-OSS-120B layer):
+// 16-row tiles are best up to 16 rows per expert; above that 64-row tiles
+// with a 4-deep activation ring win (T = 1024: 0.96 ms vs 1.06-1.59 ms for
+// 32/128-row tiles; T = 4096: 2.95 ms vs 3.42-3.85 ms).  A 2-deep activation
+// ring exposes a copy latency per slot reuse, which made wider tiles slower.
+// One MMA issuer: with several threads issuing tcgen05 operations at the
+// same time, B200 produced occasional wrong tiles (nondeterministic, about
+// one 128 x 16 tile in 10^4 at T = 4096; never with a single issuer or with
+// the issuers forced into one global order), so every tcgen05 MMA, scale copy
+// and commit of a CTA comes from one thread.
 //                BN  NA NS NB NP ND PF
-using MxN16  = MxCfg<16, 6, 4, 8, 4, 2, 8>;
-using MxN32  = MxCfg<32, 6, 4, 4, 4, 1, 8>;
-using MxN64  = MxCfg<64, 6, 4, 2, 2, 1, 8>;
-using MxN128 = MxCfg<128, 4, 4, 2, 1, 1, 4>;
+using MxN16  = MxCfg<16, 6, 4, 8, 1, 2, 8>;
+using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0>;
 
 }  // namespace
 
@@ -658,10 +667,8 @@ int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   KLC_CHECK_ARG(2 * a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
   switch (a.block_n) {
     case 16: return launch_mx_both<MxN16>(a, stream);
-    case 32: return launch_mx_both<MxN32>(a, stream);
     case 64: return launch_mx_both<MxN64>(a, stream);
-    case 128: return launch_mx_both<MxN128>(a, stream);
-    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 16, 32, 64 or 128");
+    default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 16 or 64");
   }
 }
 

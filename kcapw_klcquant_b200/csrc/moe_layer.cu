@@ -32,13 +32,10 @@ constexpr int kPad = 16;  // rows of each expert group are padded to 16 (MMA N g
 int pick_block_n(const klc_moe_dims& d, bool tc) {
   if (!tc) return 64;
   // tokens per expert on average; row-blocks hold up to block_n rows (one
-  // weight pass each); a tensor-core tile holds at most 128 rows (256 hi/lo
-  // operand rows)
+  // weight pass each).  The tensor-core kernels have 16- and 64-row tiles;
+  // 16-row tiles win up to 16 rows per expert (experts_mx.cu has the timings)
   const int64_t per_expert = (d.tokens * d.top_k + d.experts - 1) / std::max<int64_t>(d.experts, 1);
-  if (per_expert <= 8) return 16;
-  if (per_expert <= 12) return 32;
-  if (per_expert <= 24) return 64;
-  return 128;
+  return per_expert <= 16 ? 16 : 64;
 }
 
 }  // namespace
