@@ -75,7 +75,7 @@ constexpr int kTmemCols = 512;
 //   BN  max token rows of a row-block (B holds N2 = 2*BN hi/lo rows; an MMA
 //       covers at most 128 of them, NCH = ceil(N2 / 128) MMAs per K step)
 //   NA  weight slots (256 K of packed E2M1, 16 KB + 1 KB of scales each)
-//   NS  staging slots (one MMA stage of padded E2M1, 16 KB + 512 B scales)
+//   NS  staging slots (one MMA stage of padded E2M1, 16 KB, + its TMEM scale set)
 //   NB  activation slots (one MMA stage, N2 x 128 B + NCH x 512 B scales)
 //   NP  MMA issuers, each with its own accumulators and scale TMEM
 // Every staging and activation slot serves a single issuer (NS and NB are
@@ -97,18 +97,16 @@ struct MxCfg {
   static constexpr int OFF_S = OFF_A + NA * ASLOT;
   static constexpr int OFF_B = OFF_S + NS * SSLOT;
   static constexpr int OFF_ASF = OFF_B + NB * BSLOT;       // NA x 1024
-  static constexpr int OFF_SSF = OFF_ASF + NA * 1024;      // NS x 512
-  static constexpr int OFF_BSF = OFF_SSF + NS * 512;       // NB x NCH x 512
+  static constexpr int OFF_BSF = OFF_ASF + NA * 1024;      // NB x NCH x 512
   static constexpr int OFF_BAR = OFF_BSF + NB * NCH * 512;
   static constexpr int NUM_BARS = 2 * NA + 2 * NS + 2 * NB + NP * ND + ND + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int BYTES = OFF_MISC + 16;
-  // TMEM: accumulators, then per staging slot 4 scale columns for A and 4
-  // per B chunk.  An MMA followed by a tcgen05.cp from the same thread is not
-  // ordered, so the scales of a stage must not overwrite columns an earlier
-  // MMA may still read: keyed by staging slot, a scale set is rewritten only
-  // for the slot's next use, which the repack fills after the MMAs of the
-  // previous use completed (the issuer waits for that fill).
+  // TMEM: accumulators, then per staging slot a scale set: 4 columns for A
+  // and 4 per B chunk, lane r0 column r1 byte kb = scale of row r0 + 32 r1,
+  // 32-K block kb, replicated in the four lane quarters.  The repack warps
+  // write a stage's scales (tcgen05.st) together with its staging slot, so a
+  // set is rewritten only after the MMAs of the slot's previous use completed.
   static constexpr int ACC_COLS = ND * NP * N2;
   static constexpr int SF_COLS = 4 + 4 * NCH;
   static_assert(ACC_COLS + NS * SF_COLS <= kTmemCols, "TMEM budget");
@@ -144,13 +142,6 @@ __device__ __forceinline__ void mx_mma(uint32_t d, uint64_t a, uint64_t b, uint3
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb));
-}
-
-// shared -> TMEM copy of one 512-byte scale block (32 lines x 16 B, broadcast
-// to the four lane quarters): lane r0, column r1, byte kb = scale of row
-// r0 + 32 r1, 32-K block kb
-__device__ __forceinline__ void sf_copy(uint32_t taddr, uint64_t sdesc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc));
 }
 
 struct MxParams {
@@ -343,15 +334,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t sph;
           staging_slot<C>(it, ss, sph);
           const int sb = it % NB;
+          // the repack warps signal a stage once its staging slot, its TMEM
+          // scales and (waited for by them) its activation slot are ready
           if (!(ok = wait_bar(sfull(ss), sph, ctl, 21))) break;
-          if (!(ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 22))) break;
           tc_fence_after();
           const uint32_t sfa_t = tmem + uint32_t(C::ACC_COLS + ss * C::SF_COLS);  // the staging slot's scale set
           const uint32_t sfb_t = sfa_t + 4;
-          sf_copy(sfa_t, plain_desc(smem_u32(smem + C::OFF_SSF + ss * 512)));
-#pragma unroll
-          for (int ch = 0; ch < NCH; ++ch)
-            sf_copy(sfb_t + 4 * ch, plain_desc(smem_u32(smem + C::OFF_BSF + (sb * NCH + ch) * 512)));
           const uint64_t adesc0 = sw128_desc(smem_u32(smem + C::OFF_S + ss * C::SSLOT));
           const uint64_t bdesc0 = sw128_desc(smem_u32(smem + C::OFF_B + sb * C::BSLOT));
           const int kb_n = min(4, (p.k_in - ks * kStageK) / 32);  // 32-K blocks in this stage
@@ -404,7 +392,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint4 c[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) c[i] = *reinterpret_cast<const uint4*>(src + (((4 * h + i) ^ sw) << 4));
-        const uint32_t scl = *reinterpret_cast<const uint32_t*>(smem + C::OFF_ASF + sa * 1024 + h * 512 + m * 4);
+        // scale-set line `lane` of the stage's weight scales (16 bytes; every warp reads the block)
+        const uint4 sfa4 = *reinterpret_cast<const uint4*>(smem + C::OFF_ASF + sa * 1024 + h * 512 + lane * 16);
         __syncwarp();  // every lane's reads of the weight slot precede the release
         if (lane == 0) {
           mbar_arrive(aempty(sa));
@@ -419,8 +408,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint4*>(dst + (((2 * i) ^ sw) << 4)) = make_uint4(c[i].x, c[i].y, 0u, 0u);
           *reinterpret_cast<uint4*>(dst + (((2 * i + 1) ^ sw) << 4)) = make_uint4(c[i].z, c[i].w, 0u, 0u);
         }
-        *reinterpret_cast<uint32_t*>(smem + C::OFF_SSF + ss * 512 + m * 4) = scl;
+        // the activation slot of this stage, then both scale sets into TMEM
+        // (this warp's lane quarter)
+        const int sb = it % NB;
+        ok = wait_bar(bfull(sb), (it / NB) & 1, ctl, 32);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        const uint32_t sf_t = tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(C::ACC_COLS + ss * C::SF_COLS);
+        tmem_st4(sf_t, sfa4);
+#pragma unroll
+        for (int ch = 0; ch < NCH; ++ch)
+          tmem_st4(sf_t + 4 + 4 * ch,
+                   *reinterpret_cast<const uint4*>(smem + C::OFF_BSF + (sb * NCH + ch) * 512 + lane * 16));
+        tmem_wait_st();
         fence_proxy_async();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sfull(ss));
       }

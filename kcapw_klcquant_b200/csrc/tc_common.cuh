@@ -150,6 +150,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 4 columns of 32 bits from registers into TMEM (lanes of the
+// calling warp's quarter: taddr carries lane 32 * (warp % 4))
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, uint4 v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row groups
 // 1024 bytes apart (SBO), leading offset unused (1), descriptor version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
