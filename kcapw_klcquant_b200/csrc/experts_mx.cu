@@ -113,6 +113,13 @@ struct MxCfg {
   static_assert((NP == 1 || NP == 2 || NP == 4) && N2 <= 256, "issuers / tile");
   static_assert(NS % kRepWGs == 0 && NS % NP == 0 && NB % NP == 0 && NB % 2 == 0 && NA % 2 == 0, "slot ownership");
   static constexpr int NSP = NS / NP;  // staging slots per issuer
+  // concurrent tcgen05 issue from several threads gave occasional wrong tiles
+  static_assert(NP == 1, "one MMA issuer");
+  // with at least twice as many activation slots as staging slots, the repack
+  // warps release an activation slot (when they reacquire the staging slot of
+  // its stage, the stage's MMAs are complete) and the issuer commits once per
+  // stage; otherwise the issuer's second commit releases it
+  static constexpr bool kRepackReleasesB = NB >= 2 * NS;
   static_assert(BSLOT % 1024 == 0, "activation slots stay 1024-byte aligned");
   static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
 };
@@ -196,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int s = 0; s < NB; ++s) {
       mbar_init(bfull(s), 1);
-      mbar_init(bempty(s), 1);
+      mbar_init(bempty(s), C::kRepackReleasesB ? 4 : 1);
     }
     for (int d = 0; d < ND; ++d) {
       for (int pp = 0; pp < NP; ++pp) mbar_init(dfull(pp, d), 1);
@@ -317,7 +324,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuers
     const int pp = issuer_of_warp(warp);
     if (lane == 0 && pp < NP) {
-      uint32_t it = uint32_t(pp), ic = 0;
+      uint32_t it = 0, ic = 0;
+      int ss = 0, sb = 0;     // staging / activation slot of stage `it`
+      uint32_t sph = 0;       // phase parity of the staging slot's use
       bool ok = true;
       for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
@@ -327,13 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 20))) break;
         tc_fence_after();
         bool first = true;
-        const uint32_t it0 = ic * uint32_t(ks_n), it_end = it0 + uint32_t(ks_n);
-        for (; it < it_end && ok; it += NP) {
-          const int ks = int(it - it0);
-          int ss;
-          uint32_t sph;
-          staging_slot<C>(it, ss, sph);
-          const int sb = it % NB;
+        for (int ks = 0; ks < ks_n && ok; ++ks) {
           // the repack warps signal a stage once its staging slot, its TMEM
           // scales and (waited for by them) its activation slot are ready
           if (!(ok = wait_bar(sfull(ss), sph, ctl, 21))) break;
@@ -360,7 +363,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           first = false;
           tc_commit(sempty(ss));
-          tc_commit(bempty(sb));
+          if (!C::kRepackReleasesB) tc_commit(bempty(sb));
+          ++it;
+          if (++ss == NS) {
+            ss = 0;
+            sph ^= 1u;
+          }
+          if (++sb == NB) sb = 0;
         }
         if (ok) tc_commit(dfull(pp, d));
       }
@@ -401,6 +410,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ok = wait_bar(sempty(ss), sph ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        // the MMAs of stage it - NS (this slot's previous use) are complete:
+        // its activation slot is free
+        if (C::kRepackReleasesB && lane == 0 && it >= uint32_t(NS)) mbar_arrive(bempty(int((it - NS) % NB)));
         // padded row m: 8 groups of 16 values, group g in the first 8 bytes of 16-byte chunk g ^ (m & 7)
         unsigned char* dst = smem + C::OFF_S + ss * C::SSLOT + (m >> 3) * 1024 + (m & 7) * 128;
 #pragma unroll
