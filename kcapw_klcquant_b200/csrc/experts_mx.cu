@@ -24,21 +24,21 @@
 // its padded slot of a small staging ring (no bit manipulation).
 //
 // One persistent CTA per SM walks the (row-block, m-tile) work list;
-// warp-specialised (896 threads):
-//   warps 0,27  TMA producers: packed weights (128 rows x 128 B, 128B
+// warp-specialised (544 threads):
+//   warps 0,3   TMA producers: packed weights (128 rows x 128 B, 128B
 //               swizzle) + the two 512-byte scale blocks of the slot (bulk
 //               copy), even / odd slots
-//   warps 1,18  TMA producers: hi/lo activation rows (N2 x 128 B) + their
+//   warps 1,16  TMA producers: hi/lo activation rows (N2 x 128 B) + their
 //               scale blocks, even / odd stages
-//   warps 2-3,  MMA issuers (one thread each; stage `it` to issuer it % NP):
-//   16-17       shared -> TMEM scale copies, then 4 (or 8) MMAs per stage.
-//               A single thread issuing tcgen05 operations next to busy
-//               warps waits a few hundred cycles per stage, so several
-//               issuers with their own accumulators keep the tensor pipe fed
-//   warps 4-7   epilogue: TMEM loads, hi + lo, pipelines summed in a fixed
-//               order, bias, SwiGLU (gate_up) or bias (down), bf16 stores
-//   warps 8-15, four repack warpgroups (stage `it` to warpgroup it % 4)
-//   19-26
+//   warp 2      the MMA issuer (one thread): 4 (or 8) MMAs and the commits
+//               of each stage.  Every tcgen05 MMA and commit of the CTA comes
+//               from this thread: with several threads issuing them at the
+//               same time, B200 produced occasional wrong tiles.
+//   warps 4-7   epilogue: TMEM loads, hi + lo, bias, SwiGLU (gate_up) or
+//               bias (down), bf16 stores
+//   warps 8-15  two repack warpgroups (stage `it` to warpgroup it % 2): the
+//               padded E2M1 staging tile and, with tcgen05.st (each warp its
+//               TMEM lane quarter), the stage's weight and activation scales
 //
 // Every mbarrier wait is bounded (tc_common.cuh): a timed-out role records
 // KLC_ERR_DEVICE_TIMEOUT, raises the CTA abort flag, and all roles drain
@@ -57,17 +57,14 @@ namespace {
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kStageK = 128;    // K per MMA stage: 4 MMAs of K = 32 (4 scale blocks)
 constexpr int kSlotK = 256;     // K per weight slot (128-byte packed rows)
-constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpMma2 = 16, kWarpB2 = 18,
-              kWarpRep2 = 19, kWarpA2 = 27;
-constexpr int kRepWGs = 4;  // repack warpgroups: warps 8-15 and 19-26, stage s to warpgroup s % 4
-constexpr int kThreads = 28 * 32;
+constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpA2 = 3, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpB2 = 16;
+constexpr int kRepWGs = 2;  // repack warpgroups: warps 8-11 and 12-15, stage s to warpgroup s % 2
+constexpr int kThreads = 17 * 32;
 __device__ __forceinline__ int repack_wg_of_warp(int warp) {  // repack warpgroup of a warp, or -1
-  return (warp >= kWarpRep0 && warp < kWarpRep0 + 8) ? (warp - kWarpRep0) >> 2
-       : (warp >= kWarpRep2 && warp < kWarpRep2 + 8) ? 2 + ((warp - kWarpRep2) >> 2) : -1;
+  return (warp >= kWarpRep0 && warp < kWarpRep0 + 4 * kRepWGs) ? (warp - kWarpRep0) >> 2 : -1;
 }
 __device__ __forceinline__ int issuer_of_warp(int warp) {  // MMA pipeline of a warp, or -1
-  return (warp == kWarpMma0 || warp == kWarpMma0 + 1) ? warp - kWarpMma0
-       : (warp == kWarpMma2 || warp == kWarpMma2 + 1) ? 2 + warp - kWarpMma2 : -1;
+  return warp == kWarpMma0 ? 0 : -1;
 }
 constexpr int kTmemCols = 512;
 
@@ -78,10 +75,12 @@ constexpr int kTmemCols = 512;
 //   NS  staging slots (one MMA stage of padded E2M1, 16 KB, + its TMEM scale set)
 //   NB  activation slots (one MMA stage, N2 x 128 B + NCH x 512 B scales)
 //   NP  MMA issuers, each with its own accumulators and scale TMEM
-// Every staging and activation slot serves a single issuer (NS and NB are
-// multiples of NP) and a single repack warpgroup, so no waiter can run two
-// phases ahead of a slot's mbarrier -- a parity wait would then pass on the
-// stale phase.
+// A parity wait is only sound while the waiter is within one phase of the
+// barrier (two ahead it passes on a stale phase; two behind it waits for a
+// phase that needs the waiter itself).  So every waiter of a slot waits for
+// every use of it in order, and every use needs every waiter: each staging
+// and activation slot serves a single issuer (NS and NB are multiples of NP)
+// and a single repack warpgroup.
 //   ND  accumulator sets per issuer (the epilogue of one tile overlaps the next)
 //   PF  weight slots prefetched into L2 beyond the shared-memory ring
 template <int BN_, int NA_, int NS_, int NB_, int NP_, int ND_, int PF_>
@@ -126,9 +125,9 @@ struct MxCfg {
 
 // Staging slot of MMA stage s (issuer s % NP, its (s / NP)-th stage) and the
 // mbarrier phase parity of that use.  Stages sharing a slot are congruent
-// modulo NS (a multiple of 4) for NP of 1, 2 or 4, and the repack warpgroup of
-// stage s is s % 4, so each slot is filled by one warpgroup and drained by one
-// issuer, both in stage order; with NS = 8 every issuer double-buffers.
+// modulo NS (a multiple of kRepWGs and of NP), and the repack warpgroup of
+// stage s is s % kRepWGs, so each slot is filled by one warpgroup and drained
+// by one issuer, both in stage order.
 template <class C>
 __device__ __forceinline__ void staging_slot(uint32_t s, int& slot, uint32_t& parity) {
   const uint32_t pp = s % C::NP, li = s / C::NP;
@@ -195,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NA; ++s) {
       mbar_init(afull(s), 1);
-      mbar_init(aempty(s), 8);  // four repack warps for each of the slot's two stages
+      mbar_init(aempty(s), 8);  // a repack warpgroup (four warps) for each of the slot's two stages
     }
     for (int s = 0; s < NS; ++s) {
       mbar_init(sfull(s), 4);
@@ -378,7 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (repack_wg_of_warp(warp) >= 0) {
     // ------------------------------------------------------------ repack
-    const int wg = repack_wg_of_warp(warp);  // stages with it % 4 == wg
+    const int wg = repack_wg_of_warp(warp);  // stages with it % kRepWGs == wg
     const int m = (warp & 3) * 32 + lane;
     const int sw = m & 7;
     uint32_t it = 0, ic = 0;
