@@ -380,11 +380,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int wg = repack_wg_of_warp(warp);  // stages with it % kRepWGs == wg
     const int m = (warp & 3) * 32 + lane;
     const int sw = m & 7;
-    uint32_t it = 0, ic = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
-      for (int ks = 0; ks < ks_n; ++ks, ++it) {
-        if (int(it % kRepWGs) != wg) continue;
+    // own stages it = wg, wg + kRepWGs, ... over the CTA's items; the item
+    // counter ic and the stage ks inside the item follow incrementally
+    uint32_t it = uint32_t(wg), ic = 0;
+    int ks = wg, item = blockIdx.x;
+    while (ks >= ks_n) {
+      ks -= ks_n;
+      ++ic;
+      item += gridDim.x;
+    }
+    for (; item < total; it += kRepWGs) {
+      {
         const uint32_t ia = ic * uint32_t(spa) + uint32_t(ks >> 1);
         const int sa = ia % NA, h = ks & 1;
         int ss;
@@ -435,6 +442,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(sfull(ss));
+      }
+      ks += kRepWGs;
+      while (ks >= ks_n) {
+        ks -= ks_n;
+        ++ic;
+        item += gridDim.x;
       }
     }
   } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
