@@ -416,6 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ok = wait_bar(sempty(ss), sph ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        tc_fence_after();  // the slot's TMEM scale set is rewritten after the MMAs that read it
         // the MMAs of stage it - NS (this slot's previous use) are complete:
         // its activation slot is free
         if (C::kRepackReleasesB && lane == 0 && it >= uint32_t(NS)) mbar_arrive(bempty(int((it - NS) % NB)));
