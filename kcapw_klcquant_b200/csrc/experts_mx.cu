@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int j = mt * kBM + m;  // output feature
       const bool jok = j < p.n_out;
       const float bias = jok ? bf16_to_f32(p.bias[int64_t(e) * p.n_out + j]) : 0.f;
-      for (int pp = 0; pp < NP && ok; ++pp) ok = wait_bar(dfull(pp, d), (ic / ND) & 1, ctl, 40 + pp);
+      for (int pp = 0; pp < NP && ok; ++pp) ok = wait_bar_backoff(dfull(pp, d), (ic / ND) & 1, ctl, 40 + pp);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
       // pipeline pp received a K-stage of this item unless the item has fewer

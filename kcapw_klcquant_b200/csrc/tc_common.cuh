@@ -76,6 +76,23 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Ct
   }
 }
 
+// Bounded wait for roles that wait long and are not on the critical path:
+// sleeping between polls leaves issue slots to the warps that share the
+// scheduler (the MMA issuer above all).
+__device__ __forceinline__ bool wait_bar_backoff(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*c.abort) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *c.abort = 1;
+      record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
+      return false;
+    }
+    __nanosleep(256);
+  }
+  return true;
+}
+
 // Drain-time wait: bounded, ignores the abort flag.
 static __device__ __noinline__ void drain_wait(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer();
