@@ -620,11 +620,13 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
   return st;
 }
 
-// Two tile shapes.  Measured on B200 (gate_up + down, GPT-OSS-120B layer):
-// 16-row tiles are best up to 16 rows per expert; above that 64-row tiles
-// with a 4-deep activation ring win (T = 1024: 0.96 ms vs 1.06-1.59 ms for
-// 32/128-row tiles; T = 4096: 2.95 ms vs 3.42-3.85 ms).  A 2-deep activation
-// ring exposes a copy latency per slot reuse, which made wider tiles slower.
+// Two tile shapes.  Measured on B200 with one MMA issuer (gate_up + down,
+// GPT-OSS-120B layer, rows per expert on average): 4 rows 0.53 ms (16-row
+// tiles) vs 0.57 (64-row), 8 rows 0.54 vs 0.58, 16 rows 0.78 vs 0.60, 24 rows
+// 1.04 vs 0.63, so 16-row tiles up to about 12 rows per expert and 64-row tiles
+// with a 4-deep activation ring above (32- and 128-row tiles were slower in an
+// earlier generation: T = 4096 3.42 / 3.59 ms vs 2.95 for 64 rows).  A 2-deep
+// activation ring exposes a copy latency per slot reuse.
 // One MMA issuer: with several threads issuing tcgen05 operations at the
 // same time, B200 produced occasional wrong tiles (nondeterministic, about
 // one 128 x 16 tile in 10^4 at T = 4096; never with a single issuer or with

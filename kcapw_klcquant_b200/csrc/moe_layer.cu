@@ -33,9 +33,10 @@ int pick_block_n(const klc_moe_dims& d, bool tc) {
   if (!tc) return 64;
   // tokens per expert on average; row-blocks hold up to block_n rows (one
   // weight pass each).  The tensor-core kernels have 16- and 64-row tiles;
-  // 16-row tiles win up to 16 rows per expert (experts_mx.cu has the timings)
+  // 16-row tiles win up to about 12 rows per expert (experts_mx.cu has the
+  // timings)
   const int64_t per_expert = (d.tokens * d.top_k + d.experts - 1) / std::max<int64_t>(d.experts, 1);
-  return per_expert <= 16 ? 16 : 64;
+  return per_expert <= 12 ? 16 : 64;
 }
 
 }  // namespace
