@@ -24,7 +24,7 @@
 // its padded slot of a small staging ring (no bit manipulation).
 //
 // One persistent CTA per SM walks the (row-block, m-tile) work list;
-// warp-specialised (544 threads):
+// warp-specialised (544 threads; 672 with a second epilogue warpgroup):
 //   warps 0,3   TMA producers: packed weights (128 rows x 128 B, 128B
 //               swizzle) + the two 512-byte scale blocks of the slot (bulk
 //               copy), even / odd slots
@@ -35,7 +35,8 @@
 //               from this thread: with several threads issuing them at the
 //               same time, B200 produced occasional wrong tiles.
 //   warps 4-7   epilogue: TMEM loads, hi + lo, bias, SwiGLU (gate_up) or
-//               bias (down), bf16 stores
+//   (17-20)     bias (down), bf16 stores; 64-row tiles split each item's
+//               8-token blocks between two epilogue warpgroups
 //   warps 8-15  two repack warpgroups (stage `it` to warpgroup it % 2): the
 //               padded E2M1 staging tile and, with tcgen05.st (each warp its
 //               TMEM lane quarter), the stage's weight and activation scales
@@ -57,9 +58,9 @@ namespace {
 constexpr int kBM = 128;        // weight rows per tile (MMA M)
 constexpr int kStageK = 128;    // K per MMA stage: 4 MMAs of K = 32 (4 scale blocks)
 constexpr int kSlotK = 256;     // K per weight slot (128-byte packed rows)
-constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpA2 = 3, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpB2 = 16;
+constexpr int kWarpA = 0, kWarpB = 1, kWarpMma0 = 2, kWarpA2 = 3, kWarpEpi0 = 4, kWarpRep0 = 8, kWarpB2 = 16,
+              kWarpEpi2 = 17;
 constexpr int kRepWGs = 2;  // repack warpgroups: warps 8-11 and 12-15, stage s to warpgroup s % 2
-constexpr int kThreads = 17 * 32;
 __device__ __forceinline__ int repack_wg_of_warp(int warp) {  // repack warpgroup of a warp, or -1
   return (warp >= kWarpRep0 && warp < kWarpRep0 + 4 * kRepWGs) ? (warp - kWarpRep0) >> 2 : -1;
 }
@@ -83,9 +84,13 @@ constexpr int kTmemCols = 512;
 // and a single repack warpgroup.
 //   ND  accumulator sets per issuer (the epilogue of one tile overlaps the next)
 //   PF  weight slots prefetched into L2 beyond the shared-memory ring
-template <int BN_, int NA_, int NS_, int NB_, int NP_, int ND_, int PF_>
+//   EPI epilogue warpgroups (warps 4-7, and 17-20 for a second one), splitting
+//       each item's 8-token blocks
+template <int BN_, int NA_, int NS_, int NB_, int NP_, int ND_, int PF_, int EPI_>
 struct MxCfg {
-  static constexpr int BN = BN_, NA = NA_, NS = NS_, NB = NB_, NP = NP_, ND = ND_, PF = PF_;
+  static constexpr int BN = BN_, NA = NA_, NS = NS_, NB = NB_, NP = NP_, ND = ND_, PF = PF_, EPI = EPI_;
+  static constexpr int THREADS = (EPI == 2 ? 21 : 17) * 32;
+  static_assert(EPI == 1 || EPI == 2, "epilogue warpgroups");
   static constexpr int N2 = 2 * BN;
   static constexpr int NCH = (N2 + 127) / 128;
   static constexpr int ASLOT = kBM * kSlotK / 2;     // 16384 packed bytes
@@ -169,7 +174,7 @@ struct MxParams {
 };
 
 template <int PHASE, class C>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(C::THREADS, 1)
     mx_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, MxParams p) {
   constexpr int NA = C::NA, NS = C::NS, NB = C::NB, NP = C::NP, ND = C::ND, N2 = C::N2, NCH = C::NCH;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -206,7 +211,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int d = 0; d < ND; ++d) {
       for (int pp = 0; pp < NP; ++pp) mbar_init(dfull(pp, d), 1);
-      mbar_init(dempty(d), 4);
+      mbar_init(dempty(d), 4 * C::EPI);  // every epilogue warp
     }
     mbar_init(mma_done, NP);
     *abort_flag = 0;
@@ -451,10 +456,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         item += gridDim.x;
       }
     }
-  } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
+  } else if ((warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) || (C::EPI == 2 && warp >= kWarpEpi2 && warp < kWarpEpi2 + 4)) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter of this warp
     const int m = q * 32 + lane;
+    const int eg = warp >= kWarpEpi2 ? 1 : 0;  // epilogue warpgroup: 8-token blocks eg, eg + EPI, ...
     uint32_t ic = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
@@ -473,7 +479,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // stages than pipelines (stage `it` of the launch goes to it % NP)
       const uint32_t first_pp = uint32_t((uint64_t(ic) * uint64_t(ks_n)) % NP);
       const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16);
-      for (int t0 = 0; t0 < npad; t0 += 8) {
+      if (8 * eg >= npad) {
+        // no block of this item for this warpgroup: release the set at once
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dempty(d));
+      }
+      for (int t0 = 8 * eg; t0 < npad; t0 += 8 * C::EPI) {
         uint32_t raw[16];  // columns 2t (hi) and 2t+1 (lo) of tokens t0..t0+7
         tmem_ld16(lane_base + dcol(int(first_pp), d) + uint32_t(2 * t0), raw);
         tmem_wait_ld();
@@ -486,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 8; ++i) v8[i] += __uint_as_float(raw[2 * i]) + __uint_as_float(raw[2 * i + 1]);
         }
-        if (t0 + 8 >= npad) {
+        if (t0 + 8 * C::EPI >= npad) {
           // last accumulator columns read: hand the set back to the MMA warps early
           tc_fence_before();
           __syncwarp();
@@ -571,7 +583,7 @@ int launch_mx_phase(const uint8_t* blocks, const uint8_t* act_q, int64_t rows_ca
   const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
   const int grid = int(items < sm_count() ? items : sm_count());
   if (grid <= 0) return KLC_OK;
-  mx_expert_kernel<PHASE, C><<<grid, kThreads, smem, stream>>>(ma, mb, p);
+  mx_expert_kernel<PHASE, C><<<grid, C::THREADS, smem, stream>>>(ma, mb, p);
   KLC_LAUNCH_CHECK("tcgen05 expert launch");
   return KLC_OK;
 }
@@ -632,9 +644,11 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 // one 128 x 16 tile in 10^4 at T = 4096; never with a single issuer or with
 // the issuers forced into one global order), so every tcgen05 MMA, scale copy
 // and commit of a CTA comes from one thread.
-//                BN  NA NS NB NP ND PF
-using MxN16  = MxCfg<16, 6, 4, 8, 1, 2, 8>;
-using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0>;
+// 64-row tiles get a second epilogue warpgroup: with one, the epilogue of an
+// item (64 tokens x 128 features) took longer than the item's MMAs.
+//                BN  NA NS NB NP ND PF EPI
+using MxN16  = MxCfg<16, 6, 4, 8, 1, 2, 8, 1>;
+using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0, 2>;
 
 }  // namespace
 
