@@ -74,7 +74,8 @@ constexpr int kTmemCols = 512;
 //       covers at most 128 of them, NCH = ceil(N2 / 128) MMAs per K step)
 //   NA  weight slots (256 K of packed E2M1, 16 KB + 1 KB of scales each)
 //   NS  staging slots (one MMA stage of padded E2M1, 16 KB, + its TMEM scale set)
-//   NB  activation slots (one MMA stage, N2 x 128 B + NCH x 512 B scales)
+//   NB  activation slots (one MMA stage, N2 x 128 B + NCH x 512 B scales);
+//       NB == NS, so one commit frees a stage's staging and activation slot
 //   NP  MMA issuers, each with its own accumulators and scale TMEM
 // A parity wait is only sound while the waiter is within one phase of the
 // barrier (two ahead it passes on a stale phase; two behind it waits for a
@@ -103,7 +104,7 @@ struct MxCfg {
   static constexpr int OFF_ASF = OFF_B + NB * BSLOT;       // NA x 1024
   static constexpr int OFF_BSF = OFF_ASF + NA * 1024;      // NB x NCH x 512
   static constexpr int OFF_BAR = OFF_BSF + NB * NCH * 512;
-  static constexpr int NUM_BARS = 2 * NA + 2 * NS + 2 * NB + NP * ND + ND + 1;
+  static constexpr int NUM_BARS = 2 * NA + 2 * NS + NB + NP * ND + ND + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   // TMEM: accumulators, then per staging slot a scale set: 4 columns for A
@@ -119,11 +120,12 @@ struct MxCfg {
   static constexpr int NSP = NS / NP;  // staging slots per issuer
   // concurrent tcgen05 issue from several threads gave occasional wrong tiles
   static_assert(NP == 1, "one MMA issuer");
-  // with at least twice as many activation slots as staging slots, the repack
-  // warps release an activation slot (when they reacquire the staging slot of
-  // its stage, the stage's MMAs are complete) and the issuer commits once per
-  // stage; otherwise the issuer's second commit releases it
-  static constexpr bool kRepackReleasesB = NB >= 2 * NS;
+  // Stage s uses staging slot and activation slot s % NS: the issuer's one
+  // commit per stage (sempty) frees both, and the activation producers wait on
+  // it.  (Releasing activation slots from the repack warps instead, with
+  // NB >= 2 NS, gave nondeterministic wrong tiles on B200 in a 2-staging /
+  // 6-activation layout; a second issuer commit per stage cost 12% at decode.)
+  static_assert(NB == NS, "activation slots follow the staging slots");
   static_assert(BSLOT % 1024 == 0, "activation slots stay 1024-byte aligned");
   static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
 };
@@ -187,10 +189,9 @@ __global__ void __launch_bounds__(C::THREADS, 1)
   auto sfull = [&](int s) { return bar0 + 8u * (2 * NA + s); };
   auto sempty = [&](int s) { return bar0 + 8u * (2 * NA + NS + s); };
   auto bfull = [&](int s) { return bar0 + 8u * (2 * NA + 2 * NS + s); };
-  auto bempty = [&](int s) { return bar0 + 8u * (2 * NA + 2 * NS + NB + s); };
-  auto dfull = [&](int pp, int d) { return bar0 + 8u * (2 * NA + 2 * NS + 2 * NB + pp * ND + d); };
-  auto dempty = [&](int d) { return bar0 + 8u * (2 * NA + 2 * NS + 2 * NB + NP * ND + d); };
-  const uint32_t mma_done = bar0 + 8u * (2 * NA + 2 * NS + 2 * NB + NP * ND + ND);
+  auto dfull = [&](int pp, int d) { return bar0 + 8u * (2 * NA + 2 * NS + NB + pp * ND + d); };
+  auto dempty = [&](int d) { return bar0 + 8u * (2 * NA + 2 * NS + NB + NP * ND + d); };
+  const uint32_t mma_done = bar0 + 8u * (2 * NA + 2 * NS + NB + NP * ND + ND);
   auto dcol = [&](int pp, int d) { return uint32_t((d * NP + pp) * N2); };
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
@@ -205,10 +206,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       mbar_init(sfull(s), 4);
       mbar_init(sempty(s), 1);
     }
-    for (int s = 0; s < NB; ++s) {
-      mbar_init(bfull(s), 1);
-      mbar_init(bempty(s), C::kRepackReleasesB ? 4 : 1);
-    }
+    for (int s = 0; s < NB; ++s) mbar_init(bfull(s), 1);
     for (int d = 0; d < ND; ++d) {
       for (int pp = 0; pp < NP; ++pp) mbar_init(dfull(pp, d), 1);
       mbar_init(dempty(d), 4 * C::EPI);  // every epilogue warp
@@ -293,7 +291,9 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     // ------------------------------------------------------------ activations
     // Two producers (stage parity q), one copy each per stage, so the per-stage
     // issue latency of a single thread does not bound the stage rate; with NB
-    // even, each slot is filled by one producer.  Rows N2 past the row-block
+    // even, each slot is filled by one producer.  A slot is free again once the
+    // MMAs of its previous stage completed (the staging slot's commit, sempty:
+    // the two rings have the same depth).  Rows N2 past the row-block
     // are loaded but not read by the MMA (N = 2 x the block's rows rounded up
     // to 8); rows and K past the buffer are zero-filled.
     const uint32_t q = warp == kWarpB ? 0u : 1u;
@@ -307,7 +307,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         for (int ks = 0; ks < ks_n && ok; ++ks, ++it) {
           if ((it & 1u) != q) continue;
           const int sb = it % NB;
-          if (!(ok = wait_bar(bempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
+          if (!(ok = wait_bar(sempty(sb), ((it / NB) & 1) ^ 1, ctl, 11))) break;
           mbar_arrive_expect_tx(bfull(sb), uint32_t(C::BSLOT + NCH * 512));
           tma_load_2d(smem_u32(smem + C::OFF_B + sb * C::BSLOT), &map_b, ks * kStageK, 2 * rb.y, bfull(sb));
           bulk_load(smem_u32(smem + C::OFF_BSF + sb * NCH * 512), sfb_rb + int64_t(ks) * NCH * 512, uint32_t(NCH * 512),
@@ -366,8 +366,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             }
           }
           first = false;
-          tc_commit(sempty(ss));
-          if (!C::kRepackReleasesB) tc_commit(bempty(sb));
+          tc_commit(sempty(ss));  // frees the staging slot and the activation slot
           ++it;
           if (++ss == NS) {
             ss = 0;
@@ -422,9 +421,6 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         ok = wait_bar(sempty(ss), sph ^ 1, ctl, 31);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         tc_fence_after();  // the slot's TMEM scale set is rewritten after the MMAs that read it
-        // the MMAs of stage it - NS (this slot's previous use) are complete:
-        // its activation slot is free
-        if (C::kRepackReleasesB && lane == 0 && it >= uint32_t(NS)) mbar_arrive(bempty(int((it - NS) % NB)));
         // padded row m: 8 groups of 16 values, group g in the first 8 bytes of 16-byte chunk g ^ (m & 7)
         unsigned char* dst = smem + C::OFF_S + ss * C::SSLOT + (m >> 3) * 1024 + (m & 7) * 128;
 #pragma unroll
@@ -647,7 +643,7 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 // 64-row tiles get a second epilogue warpgroup: with one, the epilogue of an
 // item (64 tokens x 128 features) took longer than the item's MMAs.
 //                BN  NA NS NB NP ND PF EPI
-using MxN16  = MxCfg<16, 6, 4, 8, 1, 2, 8, 1>;
+using MxN16  = MxCfg<16, 4, 6, 6, 1, 2, 8, 1>;
 using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0, 2>;
 
 }  // namespace
