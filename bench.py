@@ -45,7 +45,7 @@ GATE_UP_BYTES_PER_EXPERT = 2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_
 FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H)  # 199,065,600
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from an ncu capture of
 # this workload at T=256 (ncu --set full, one launch); None where no capture was taken
-PROFILED_GATE_UP_TRAFFIC = {"decode": 1_146_406_000 + 10_152_192}
+PROFILED_GATE_UP_TRAFFIC = {"decode": 1_145_114_000 + 8_942_592}
 
 
 def peaks() -> dict:
