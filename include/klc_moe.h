@@ -21,6 +21,8 @@
  *   klc_moe_bias_only        <- execute_experts=False path      streamed_moe_router.py:317-329
  *   klc_moe_forward          <- StreamedMoERouter.route as a whole, batched over tokens
  *   klc_rms_norm             <- rms_norm                        streamed_attention.py:27-28
+ *   klc_moe_combine_rmsnorm  <- combine, `hidden += moe_out` and the next layer's
+ *   klc_moe_forward_rmsnorm     input rms_norm in one kernel    streamed_transformer_executor.py:235,260
  *   klc_runtime_dequant      <- RuntimeDequantizer.dequantize   runtime_dequantizer.py:30-52
  *                               (unpack_lowbit adaptive_quantizer.py:183-213,
  *                                reconstruct_pruned tensor_pruner.py:62-69)
@@ -215,6 +217,26 @@ int klc_moe_forward(const klc_moe_dims* dims, const klc_moe_weights* wts, const 
  * y_rows bf16 [*, H]; pair_pos int32 [T*k]; w bf16 [T,k]; out bf16 [T,H]. */
 int klc_moe_combine(const uint16_t* y_rows, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,
                     int64_t hidden, const uint16_t* residual, uint16_t* out, void* stream);
+
+/* klc_moe_combine with residual, fused with the next layer's input RMSNorm:
+ * out = residual + combine (bf16, as klc_moe_combine; residual may be NULL)
+ * and normed = bf16(bf16(out * bf16(rsqrt(mean(out^2) + eps))) * norm_w), the
+ * executor's `hidden += moe_out` (streamed_transformer_executor.py:260)
+ * followed by the next layer's rms_norm(hidden, input_layernorm.weight)
+ * (:235, streamed_attention.py:27-28).  norm_w bf16 [H]; normed bf16 [T,H];
+ * norm_w and normed 16-byte aligned.                                       */
+int klc_moe_combine_rmsnorm(const uint16_t* y_rows, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,
+                            int64_t hidden, const uint16_t* residual, const uint16_t* norm_w, float eps, uint16_t* out,
+                            uint16_t* normed, void* stream);
+
+/* klc_moe_forward whose combine also writes the next layer's RMSNorm input
+ * (normed, as klc_moe_combine_rmsnorm): one decode layer's MoE half plus
+ * the residual add and the following norm, without a separate norm launch
+ * or a re-read of y.                                                       */
+int klc_moe_forward_rmsnorm(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
+                            const float* adjust, int precision, uint16_t* y, int32_t* out_idx, uint16_t* out_w,
+                            uint16_t* out_logits, float* norms, const uint16_t* residual, const uint16_t* norm_w,
+                            float eps, uint16_t* normed, void* workspace, size_t workspace_bytes, void* stream);
 
 /* execute_experts=False path (streamed_moe_router.py:317-329):
  * y[t] = sum_s bf16(bias[idx[t,s]] * w[t,s]) accumulated in fp32, rounded once. */

@@ -8,6 +8,13 @@
 // outputs.  One CTA per token; each thread owns 8 hidden elements and
 // gathers them (16-byte loads) from the k permuted rows of the token.
 // Memory-bound: k*H*2 bytes read + H*2 written per token.
+//
+// The fused form (kNorm) also applies the next layer's input RMSNorm to the
+// residual sum, the executor's `hidden += moe_out` (streamed_transformer_
+// executor.py:260) followed by `rms_norm(hidden, input_layernorm.weight)`
+// (:235, streamed_attention.py:27-28): the token's sum of squares is taken
+// from the bf16 values as they are stored, and each thread re-reads only the
+// chunks it stored itself, so no second kernel re-reads the hidden state.
 #include "permute.cuh"
 
 namespace klc {
@@ -16,11 +23,28 @@ namespace {
 
 constexpr int kMaxTopK = 8;
 
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float u = (lane < int(blockDim.x >> 5)) ? red[lane] : 0.f;
+    u = warp_sum(u);
+    if (lane == 0) red[0] = u;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+template <bool kNorm>
 __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ pair_pos,
                                const uint16_t* __restrict__ w, int k, int64_t hidden,
                                const uint16_t* __restrict__ residual, uint16_t* __restrict__ out,
-                               const float* __restrict__ normsq, float* __restrict__ norms) {
+                               const float* __restrict__ normsq, float* __restrict__ norms,
+                               const uint16_t* __restrict__ norm_w, float eps, uint16_t* __restrict__ normed) {
   const int64_t t = blockIdx.x;
+  float ss = 0.f;  // sum of squares of the stored row (kNorm)
   const int chunks = int(hidden / 8);
   if (norms != nullptr && threadIdx.x < 2 * k) {
     const int64_t q = t * k * 2 + threadIdx.x;
@@ -69,6 +93,28 @@ __global__ void combine_kernel(const uint16_t* __restrict__ y, const int32_t* __
     o.z = uint32_t(f32_to_bf16(acc[4])) | (uint32_t(f32_to_bf16(acc[5])) << 16);
     o.w = uint32_t(f32_to_bf16(acc[6])) | (uint32_t(f32_to_bf16(acc[7])) << 16);
     reinterpret_cast<uint4*>(out + t * hidden)[c] = o;
+    if (kNorm) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(acc[j], acc[j], ss);  // acc holds the stored bf16 values
+    }
+  }
+  if (kNorm) {
+    __shared__ float red[32];
+    const float total = block_sum(ss, red);
+    const float inv = round_bf16(1.0f / sqrtf(total / float(hidden) + eps));
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+      const uint4 o = reinterpret_cast<const uint4*>(out + t * hidden)[c];  // this thread's own store
+      const uint4 g = reinterpret_cast<const uint4*>(norm_w)[c];
+      const uint32_t oo[4] = {o.x, o.y, o.z, o.w}, gg[4] = {g.x, g.y, g.z, g.w};
+      uint32_t r[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = round_bf16(__uint_as_float(oo[j] << 16) * inv) * __uint_as_float(gg[j] << 16);
+        const float hi = round_bf16(__uint_as_float(oo[j] & 0xffff0000u) * inv) * __uint_as_float(gg[j] & 0xffff0000u);
+        r[j] = uint32_t(f32_to_bf16(lo)) | (uint32_t(f32_to_bf16(hi)) << 16);
+      }
+      reinterpret_cast<uint4*>(normed + t * hidden)[c] = make_uint4(r[0], r[1], r[2], r[3]);
+    }
   }
 }
 
@@ -101,17 +147,7 @@ __global__ void rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* 
     const float v = bf16_to_f32(xr[h]);
     ss = fmaf(v, v, ss);
   }
-  ss = warp_sum(ss);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (lane == 0) red[warp] = ss;
-  __syncthreads();
-  if (warp == 0) {
-    float v = (lane < int(blockDim.x >> 5)) ? red[lane] : 0.f;
-    v = warp_sum(v);
-    if (lane == 0) red[0] = v;
-  }
-  __syncthreads();
-  const float mean = red[0] / float(hidden);
+  const float mean = block_sum(ss, red) / float(hidden);
   const float inv = round_bf16(1.0f / sqrtf(mean + eps));
   for (int64_t h = threadIdx.x; h < hidden; h += blockDim.x) {
     const float v = round_bf16(bf16_to_f32(xr[h]) * inv);
@@ -123,13 +159,22 @@ __global__ void rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* 
 
 int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,
                    int64_t hidden, const uint16_t* residual, uint16_t* out, const float* normsq, float* norms,
-                   cudaStream_t stream) {
+                   const PostNorm* post, cudaStream_t stream) {
   if (tokens == 0) return KLC_OK;
   KLC_CHECK_ARG(tokens <= 0x7fffffff, "combine: too many tokens");
   KLC_CHECK_ARG(k >= 1 && k <= kMaxTopK, "combine: need 1 <= k <= 8");
   int64_t threads = (hidden / 8 + 31) / 32 * 32;
   threads = threads < 64 ? 64 : (threads > 256 ? 256 : threads);
-  combine_kernel<<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq, norms);
+  if (post != nullptr) {
+    KLC_CHECK_ARG(post->weight && post->normed, "combine: null RMSNorm weight or output");
+    KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(post->weight) & 15) == 0 && (reinterpret_cast<uintptr_t>(post->normed) & 15) == 0,
+                  "combine: RMSNorm weight and output must be 16-byte aligned");
+    combine_kernel<true><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
+                                                                    norms, post->weight, post->eps, post->normed);
+  } else {
+    combine_kernel<false><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
+                                                                     norms, nullptr, 0.f, nullptr);
+  }
   KLC_LAUNCH_CHECK("combine launch");
   return KLC_OK;
 }
@@ -166,5 +211,19 @@ extern "C" int klc_moe_combine(const uint16_t* y_rows, const int32_t* pair_pos, 
   KLC_CHECK_ARG(tokens >= 0 && k >= 1 && hidden > 0 && hidden % 8 == 0, "klc_moe_combine: bad sizes");
   if (tokens == 0) return KLC_OK;
   KLC_CHECK_ARG(y_rows && pair_pos && w && out, "klc_moe_combine: null pointer");
-  return launch_combine(y_rows, pair_pos, w, tokens, k, hidden, residual, out, nullptr, nullptr, as_stream(stream));
+  return launch_combine(y_rows, pair_pos, w, tokens, k, hidden, residual, out, nullptr, nullptr, nullptr,
+                        as_stream(stream));
+}
+
+extern "C" int klc_moe_combine_rmsnorm(const uint16_t* y_rows, const int32_t* pair_pos, const uint16_t* w,
+                                       int64_t tokens, int k, int64_t hidden, const uint16_t* residual,
+                                       const uint16_t* norm_w, float eps, uint16_t* out, uint16_t* normed,
+                                       void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(tokens >= 0 && k >= 1 && hidden > 0 && hidden % 8 == 0, "klc_moe_combine_rmsnorm: bad sizes");
+  if (tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(y_rows && pair_pos && w && out && norm_w && normed, "klc_moe_combine_rmsnorm: null pointer");
+  const PostNorm post{norm_w, eps, normed};
+  return launch_combine(y_rows, pair_pos, w, tokens, k, hidden, residual, out, nullptr, nullptr, &post,
+                        as_stream(stream));
 }

@@ -108,9 +108,11 @@ static int validate_weights(const klc_moe_weights* w) {
   return KLC_OK;
 }
 
-int run_experts(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx,
-                const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual, char* ws,
-                const WorkspaceLayout& L, cudaStream_t stream) {
+// Permute, expert GEMMs and combine for given routing; `post` (or null) fuses
+// the next layer's input RMSNorm into the combine.
+static int run_experts_post(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx,
+                            const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
+                            const PostNorm* post, char* ws, const WorkspaceLayout& L, cudaStream_t stream) {
   const bool tc = use_tc_path(d);
   DeviceStatus* status = reinterpret_cast<DeviceStatus*>(ws + L.status);
   KLC_CUDA(cudaMemsetAsync(status, 0, sizeof(DeviceStatus), stream));
@@ -169,9 +171,54 @@ int run_experts(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_
   ea.block_n = L.block_n;
   st = tc ? launch_experts_tc(ea, stream) : launch_experts_simt(ea, stream);
   if (st != KLC_OK) return st;
-  st = launch_combine(ea.y, pa.pair_pos, w, d.tokens, d.top_k, d.hidden, residual, y, normsq, norms, stream);
+  st = launch_combine(ea.y, pa.pair_pos, w, d.tokens, d.top_k, d.hidden, residual, y, normsq, norms, post, stream);
   stage_mark(kStageCombined, stream);
   return st;
+}
+
+int run_experts(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx,
+                const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual, char* ws,
+                const WorkspaceLayout& L, cudaStream_t stream) {
+  return run_experts_post(d, wts, x, idx, w, precision, y, norms, residual, nullptr, ws, L, stream);
+}
+
+// klc_moe_experts, with the optional fused RMSNorm of klc_moe_forward_rmsnorm.
+static int experts_entry(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x, const int32_t* idx,
+                         const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
+                         const PostNorm* post, void* workspace, size_t workspace_bytes, void* stream) {
+  int st = validate_dims(dims);
+  if (st != KLC_OK) return st;
+  st = validate_weights(wts);
+  if (st != KLC_OK) return st;
+  KLC_CHECK_ARG(precision == KLC_PREC_FP32 || precision == KLC_PREC_BF16, "precision must be KLC_PREC_FP32 or KLC_PREC_BF16");
+  if (dims->tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(x && idx && w && y, "klc_moe_experts: null pointer");
+  const WorkspaceLayout L = workspace_layout(*dims, false);
+  if (workspace == nullptr || workspace_bytes < L.total)
+    return fail(KLC_ERR_WORKSPACE, "klc_moe_experts: workspace too small (need " + std::to_string(L.total) + " bytes)");
+  KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
+  return run_experts_post(*dims, *wts, x, idx, w, precision, y, norms, residual, post, static_cast<char*>(workspace), L,
+                          as_stream(stream));
+}
+
+// klc_moe_forward: router, then experts_entry on its routing.
+static int forward_entry(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x, const float* adjust,
+                         int precision, uint16_t* y, int32_t* out_idx, uint16_t* out_w, uint16_t* out_logits,
+                         float* norms, const uint16_t* residual, const PostNorm* post, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  int st = validate_dims(dims);
+  if (st != KLC_OK) return st;
+  st = validate_weights(wts);
+  if (st != KLC_OK) return st;
+  KLC_CHECK_ARG(wts->router_w && wts->router_b, "klc_moe_forward: null router weights");
+  KLC_CHECK_ARG(out_idx && out_w, "klc_moe_forward: null routing outputs");
+  if (dims->tokens == 0) return KLC_OK;
+  stage_mark(kStageStart, as_stream(stream));
+  st = launch_router(x, dims->tokens, dims->hidden, wts->router_w, wts->router_b, dims->experts, dims->top_k, adjust,
+                     out_idx, out_w, out_logits, as_stream(stream));
+  if (st != KLC_OK) return st;
+  return experts_entry(dims, wts, x, out_idx, out_w, precision, y, norms, residual, post, workspace, workspace_bytes,
+                       stream);
 }
 
 }  // namespace klc
@@ -189,38 +236,26 @@ extern "C" int klc_moe_workspace_size(const klc_moe_dims* dims, size_t* out_byte
 extern "C" int klc_moe_experts(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
                                const int32_t* idx, const uint16_t* w, int precision, uint16_t* y, float* norms,
                                const uint16_t* residual, void* workspace, size_t workspace_bytes, void* stream) {
-  int st = validate_dims(dims);
-  if (st != KLC_OK) return st;
-  st = validate_weights(wts);
-  if (st != KLC_OK) return st;
-  KLC_CHECK_ARG(precision == KLC_PREC_FP32 || precision == KLC_PREC_BF16, "precision must be KLC_PREC_FP32 or KLC_PREC_BF16");
-  if (dims->tokens == 0) return KLC_OK;
-  KLC_CHECK_ARG(x && idx && w && y, "klc_moe_experts: null pointer");
-  const WorkspaceLayout L = workspace_layout(*dims, false);
-  if (workspace == nullptr || workspace_bytes < L.total)
-    return fail(KLC_ERR_WORKSPACE, "klc_moe_experts: workspace too small (need " + std::to_string(L.total) + " bytes)");
-  KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "workspace must be 256-byte aligned");
-  return run_experts(*dims, *wts, x, idx, w, precision, y, norms, residual, static_cast<char*>(workspace), L,
-                     as_stream(stream));
+  return experts_entry(dims, wts, x, idx, w, precision, y, norms, residual, nullptr, workspace, workspace_bytes, stream);
 }
 
 extern "C" int klc_moe_forward(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
                                const float* adjust, int precision, uint16_t* y, int32_t* out_idx, uint16_t* out_w,
                                uint16_t* out_logits, float* norms, const uint16_t* residual, void* workspace,
                                size_t workspace_bytes, void* stream) {
-  int st = validate_dims(dims);
-  if (st != KLC_OK) return st;
-  st = validate_weights(wts);
-  if (st != KLC_OK) return st;
-  KLC_CHECK_ARG(wts->router_w && wts->router_b, "klc_moe_forward: null router weights");
-  KLC_CHECK_ARG(out_idx && out_w, "klc_moe_forward: null routing outputs");
-  if (dims->tokens == 0) return KLC_OK;
-  stage_mark(kStageStart, as_stream(stream));
-  st = launch_router(x, dims->tokens, dims->hidden, wts->router_w, wts->router_b, dims->experts, dims->top_k, adjust,
-                     out_idx, out_w, out_logits, as_stream(stream));
-  if (st != KLC_OK) return st;
-  return klc_moe_experts(dims, wts, x, out_idx, out_w, precision, y, norms, residual, workspace, workspace_bytes,
-                         stream);
+  return forward_entry(dims, wts, x, adjust, precision, y, out_idx, out_w, out_logits, norms, residual, nullptr,
+                       workspace, workspace_bytes, stream);
+}
+
+extern "C" int klc_moe_forward_rmsnorm(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
+                                       const float* adjust, int precision, uint16_t* y, int32_t* out_idx,
+                                       uint16_t* out_w, uint16_t* out_logits, float* norms, const uint16_t* residual,
+                                       const uint16_t* norm_w, float eps, uint16_t* normed, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  KLC_CHECK_ARG(norm_w && normed, "klc_moe_forward_rmsnorm: null RMSNorm weight or output");
+  const PostNorm post{norm_w, eps, normed};
+  return forward_entry(dims, wts, x, adjust, precision, y, out_idx, out_w, out_logits, norms, residual, &post,
+                       workspace, workspace_bytes, stream);
 }
 
 extern "C" int klc_moe_permute(const int32_t* idx, int64_t tokens, int k, int64_t experts, int pad, int32_t* pair_pos,

@@ -91,8 +91,15 @@ int launch_quantize_rows(const uint16_t* src, int64_t K, const int32_t* rows_map
 enum Stage { kStageStart = 0, kStageRouted = 1, kStagePermuted = 2, kStageGateUp = 3, kStageDown = 4, kStageCombined = 5, kStageCount = 6 };
 void stage_mark(int stage, cudaStream_t stream);
 
+// The next layer's input RMSNorm fused into the combine (weight bf16 [H], output bf16 [T,H]).
+struct PostNorm {
+  const uint16_t* weight;
+  float eps;
+  uint16_t* normed;
+};
+
 int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,
                    int64_t hidden, const uint16_t* residual, uint16_t* out, const float* normsq, float* norms,
-                   cudaStream_t stream);
+                   const PostNorm* post, cudaStream_t stream);
 
 }  // namespace klc

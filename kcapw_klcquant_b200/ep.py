@@ -79,14 +79,23 @@ class CudaBackend:
         y, _ = self.local.experts_forward(rows, local_ids.reshape(R, 1), ones, precision=precision)
         return y
 
-    def combine(self, y_rows: torch.Tensor, pair_pos: torch.Tensor, w: torch.Tensor, residual=None) -> torch.Tensor:
+    def combine(self, y_rows: torch.Tensor, pair_pos: torch.Tensor, w: torch.Tensor, residual=None,
+                next_norm=None) -> torch.Tensor | tuple[torch.Tensor, torch.Tensor]:
+        """Weighted combine of the returned rows; with ``next_norm=(weight, eps)`` also the RMSNorm of the result."""
         T, k = w.shape
         H = int(y_rows.shape[1])
         out = torch.empty((T, H), dtype=torch.bfloat16, device=self.device)
         with torch.cuda.device(self.device):
-            _lib.check(_lib.lib().klc_moe_combine(y_rows.data_ptr(), pair_pos.data_ptr(), w.data_ptr(), T, k, H,
-                                                  _lib.ptr(residual), out.data_ptr(), _lib.stream_ptr()))
-        return out
+            if next_norm is None:
+                _lib.check(_lib.lib().klc_moe_combine(y_rows.data_ptr(), pair_pos.data_ptr(), w.data_ptr(), T, k, H,
+                                                      _lib.ptr(residual), out.data_ptr(), _lib.stream_ptr()))
+                return out
+            norm_w = next_norm[0].to(device=self.device, dtype=torch.bfloat16).contiguous()
+            normed = torch.empty_like(out)
+            _lib.check(_lib.lib().klc_moe_combine_rmsnorm(y_rows.data_ptr(), pair_pos.data_ptr(), w.data_ptr(), T, k, H,
+                                                          _lib.ptr(residual), norm_w.data_ptr(), float(next_norm[1]),
+                                                          out.data_ptr(), normed.data_ptr(), _lib.stream_ptr()))
+        return out, normed
 
 
 def _rows_as_bytes(t: torch.Tensor) -> torch.Tensor:

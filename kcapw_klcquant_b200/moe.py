@@ -42,6 +42,7 @@ class RouteBatch:
     weights: torch.Tensor
     logits: torch.Tensor | None = None
     norms: torch.Tensor | None = None  # fp32 [T,k,2]: (||gated||, ||out||) per selected expert
+    normed: torch.Tensor | None = None  # bf16 [T,H]: the next layer's input RMSNorm of the output (next_norm)
 
 
 class MoeLayer:
@@ -126,8 +127,16 @@ class MoeLayer:
         residual: torch.Tensor | None = None,
         out: torch.Tensor | None = None,
         path: str | None = None,
+        next_norm: tuple[torch.Tensor, float] | None = None,
     ) -> tuple[torch.Tensor, RouteBatch]:
-        """Router + experts + combine for ``x`` bf16 [T, H] -> (y bf16 [T, H], routing)."""
+        """Router + experts + combine for ``x`` bf16 [T, H] -> (y bf16 [T, H], routing).
+
+        ``next_norm=(weight, eps)`` also returns ``routing.normed`` =
+        ``rms_norm(y, weight, eps)`` -- the executor's ``hidden += moe_out``
+        followed by the next layer's input norm
+        (streamed_transformer_executor.py:235,260) -- computed by the combine
+        kernel itself.
+        """
         T = int(x.shape[0])
         x = as_bf16(x, self.device)
         dims = self.dims(T, path)
@@ -143,15 +152,30 @@ class MoeLayer:
             adjust = adjust.to(device=self.device, dtype=torch.float32).contiguous()
         nbytes = self.workspace_bytes(T, path)
         ws = workspace(self.device, nbytes)
+        normed = None
         with torch.cuda.device(self.device):
-            _lib.check(
-                _lib.lib().klc_moe_forward(
-                    ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
-                    _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
-                    _lib.ptr(norms), _lib.ptr(residual), ws.data_ptr(), ws.numel(), _lib.stream_ptr(),
+            if next_norm is None:
+                _lib.check(
+                    _lib.lib().klc_moe_forward(
+                        ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
+                        _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
+                        _lib.ptr(norms), _lib.ptr(residual), ws.data_ptr(), ws.numel(), _lib.stream_ptr(),
+                    )
                 )
-            )
-        return y, RouteBatch(idx, w, logits, norms)
+            else:
+                norm_w = as_bf16(next_norm[0], self.device)
+                if norm_w.numel() != self.hidden:
+                    raise ValueError(f"next_norm weight must have {self.hidden} elements")
+                normed = torch.empty_like(y)
+                _lib.check(
+                    _lib.lib().klc_moe_forward_rmsnorm(
+                        ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
+                        _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
+                        _lib.ptr(norms), _lib.ptr(residual), norm_w.data_ptr(), float(next_norm[1]), normed.data_ptr(),
+                        ws.data_ptr(), ws.numel(), _lib.stream_ptr(),
+                    )
+                )
+        return y, RouteBatch(idx, w, logits, norms, normed)
 
     def experts_forward(
         self,

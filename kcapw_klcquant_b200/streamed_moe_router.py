@@ -334,13 +334,16 @@ class StreamedMoERouter:
     # ------------------------------------------------------------------
     def route_batch(self, layer_idx: int, hidden: torch.Tensor, tensors: dict[str, torch.Tensor], expert_store: Mxfp4ExpertStore,
                     *, return_logits: bool = False, return_norms: bool = False, residual: torch.Tensor | None = None,
-                    record_stats: bool = False, position: int = 0) -> tuple[torch.Tensor, RouteBatch]:
+                    record_stats: bool = False, position: int = 0,
+                    next_norm: tuple[torch.Tensor, float] | None = None) -> tuple[torch.Tensor, RouteBatch]:
         """Route and execute T tokens at once: hidden bf16 [T, H] -> (output [T, H], RouteBatch).
 
         Equivalent to calling ``route()`` per token with locality disabled
         (the batched path does not apply the per-token sticky policy).  With
         ``record_stats`` the routing is copied to the host and recorded as
-        positions ``position .. position+T-1``.
+        positions ``position .. position+T-1``.  ``next_norm=(weight, eps)``
+        fuses the next layer's input RMSNorm of the output into the combine
+        (``RouteBatch.normed``).
         """
         if self.locality_config.enabled:
             raise ValueError("route_batch() routes without the per-token locality policy; use route() when locality is enabled")
@@ -348,7 +351,8 @@ class StreamedMoERouter:
         E = int(tensors[f"{p}.router.weight"].shape[0])
         k = self._effective_expert_count(layer_idx, E)
         layer = self._moe_layer(layer_idx, tensors, expert_store, k)
-        y, rb = layer.forward(hidden, precision=self.matmul_precision, return_logits=return_logits, return_norms=return_norms, residual=residual)
+        y, rb = layer.forward(hidden, precision=self.matmul_precision, return_logits=return_logits, return_norms=return_norms,
+                              residual=residual, next_norm=next_norm)
         if record_stats:
             ids, ws = rb.indices.tolist(), rb.weights.float().tolist()
             for t, (e, w) in enumerate(zip(ids, ws)):

@@ -1,0 +1,114 @@
+"""The combine fused with the residual add and the next layer's input RMSNorm
+(klc_moe_combine_rmsnorm, klc_moe_forward_rmsnorm) against the oracle.
+
+The executor adds the MoE output to the residual stream
+(streamed_transformer_executor.py:260) and the next layer starts with
+rms_norm(hidden, input_layernorm.weight) (:235, streamed_attention.py:27-28).
+The residual sum is bit-exact (bf16 arithmetic in a fixed order); the norm
+sums squares in a different order than torch, so it is held to the
+standalone RMSNorm's tolerance: at most 1 bf16 ulp, on under 1 % of values.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as orc
+from tests import parity
+from tests.test_gpu_parity import DEV, PATHS, bits_of, case_cache, load  # noqa: F401  (fixture re-export)
+
+pytestmark = pytest.mark.gpu
+
+EPS = 1e-5
+
+
+def _bf16_bits(a: np.ndarray) -> np.ndarray:
+    return orc.f32_to_bf16_bits(np.asarray(a, dtype=np.float32))
+
+
+def _dev(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16).to(DEV)
+
+
+def _residual_add_bits(acc_bits: np.ndarray, res_bits: np.ndarray) -> np.ndarray:
+    return orc.f32_to_bf16_bits(orc.round_bf16(orc.bf16_bits_to_f32(res_bits) + orc.bf16_bits_to_f32(acc_bits)))
+
+
+def _check_norm(got_bits: np.ndarray, want_bits: np.ndarray) -> None:
+    d = parity.ulp_distance_bf16(got_bits, want_bits)
+    assert d.max() <= 1 and np.mean(d > 0) < 0.01, (int(d.max()), float(np.mean(d > 0)))
+
+
+@pytest.mark.parametrize("with_residual", [False, True])
+@pytest.mark.parametrize("T,k,H", [(1, 4, 2880), (37, 4, 2880), (16, 1, 128), (9, 8, 64), (300, 4, 2880)])
+def test_combine_rmsnorm_vs_oracle(T, k, H, with_residual):
+    from kcapw_klcquant_b200 import _lib, rms_norm
+
+    rng = np.random.default_rng(T * 131 + k * 7 + H + with_residual)
+    R = T * k + 5  # a few rows that no pair reads
+    y_bits = _bf16_bits(rng.standard_normal((R, H)) * 2.0)
+    pair_pos = rng.permutation(R)[: T * k].astype(np.int32)
+    w_bits = _bf16_bits(rng.random((T, k)) / k)
+    res_bits = _bf16_bits(rng.standard_normal((T, H)) * 4.0) if with_residual else None
+    g_bits = _bf16_bits(1.0 + 0.1 * rng.standard_normal(H))
+
+    y, pp, w, g = _dev(y_bits), torch.from_numpy(pair_pos).to(DEV), _dev(w_bits), _dev(g_bits)
+    res = _dev(res_bits) if with_residual else None
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=DEV)
+    normed = torch.empty_like(out)
+    out_plain = torch.empty_like(out)
+    L = _lib.lib()
+    with torch.cuda.device(DEV):
+        _lib.check(L.klc_moe_combine_rmsnorm(y.data_ptr(), pp.data_ptr(), w.data_ptr(), T, k, H, _lib.ptr(res),
+                                             g.data_ptr(), EPS, out.data_ptr(), normed.data_ptr(), _lib.stream_ptr()))
+        _lib.check(L.klc_moe_combine(y.data_ptr(), pp.data_ptr(), w.data_ptr(), T, k, H, _lib.ptr(res),
+                                     out_plain.data_ptr(), _lib.stream_ptr()))
+    torch.cuda.synchronize()
+
+    rows = orc.bf16_bits_to_f32(y_bits)[pair_pos].reshape(T, k, H)
+    want_out = orc.combine_bits(rows, w_bits)
+    if with_residual:
+        want_out = _residual_add_bits(want_out, res_bits)
+    got_out = bits_of(out)
+    assert np.array_equal(got_out, want_out)
+    assert np.array_equal(got_out, bits_of(out_plain))  # the fused form stores the same residual sum
+    _check_norm(bits_of(normed), orc.rms_norm_bits(want_out, g_bits, EPS))
+    _check_norm(bits_of(normed), bits_of(rms_norm(out, g, EPS)))
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_forward_next_norm(case_cache, path):  # noqa: F811
+    fx, dims, layer, x, ml = load(case_cache, "mini_e16_h256_t32")
+    rng = np.random.default_rng(5)
+    H = ml.hidden
+    res = _dev(_bf16_bits(rng.standard_normal((x.shape[0], H))))
+    g = _dev(_bf16_bits(1.0 + 0.1 * rng.standard_normal(H)))
+    y0, rb0 = ml.forward(x.to(DEV), precision="bf16", residual=res, path=path)
+    y1, rb1 = ml.forward(x.to(DEV), precision="bf16", residual=res, path=path, next_norm=(g, EPS))
+    ml.check_device_status()
+    assert rb0.normed is None and rb1.normed is not None
+    assert torch.equal(rb0.indices, rb1.indices)
+    assert np.array_equal(bits_of(y0), bits_of(y1))
+    _check_norm(bits_of(rb1.normed), orc.rms_norm_bits(bits_of(y1), bits_of(g), EPS))
+
+
+def test_ep_combine_next_norm():
+    """The expert-parallel backend's combine with the fused norm (returned rows already local)."""
+    from kcapw_klcquant_b200.ep import CudaBackend
+
+    rng = np.random.default_rng(11)
+    T, k, H = 8, 4, 256
+    y_bits = _bf16_bits(rng.standard_normal((T * k, H)))
+    pair_pos = rng.permutation(T * k).astype(np.int32)
+    w_bits = _bf16_bits(rng.random((T, k)) / k)
+    res_bits = _bf16_bits(rng.standard_normal((T, H)))
+    g_bits = _bf16_bits(1.0 + 0.1 * rng.standard_normal(H))
+    backend = CudaBackend.__new__(CudaBackend)  # combine needs only the device
+    backend.device = DEV
+    y, pp, w, g, res = _dev(y_bits), torch.from_numpy(pair_pos).to(DEV), _dev(w_bits), _dev(g_bits), _dev(res_bits)
+    out, normed = backend.combine(y, pp, w, residual=res, next_norm=(g, EPS))
+    plain = backend.combine(y, pp, w, residual=res)
+    want = _residual_add_bits(orc.combine_bits(orc.bf16_bits_to_f32(y_bits)[pair_pos].reshape(T, k, H), w_bits), res_bits)
+    assert np.array_equal(bits_of(out), want) and np.array_equal(bits_of(plain), want)
+    _check_norm(bits_of(normed), orc.rms_norm_bits(want, g_bits, EPS))

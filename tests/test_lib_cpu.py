@@ -52,6 +52,19 @@ def test_host_validation_without_gpu():
     fake = ctypes.c_void_p(256)
     st, msg = _status_and_msg(L.klc_moe_combine(fake, fake, fake, 4, 9, 2880, None, fake, None))
     assert st == _lib.KLC_ERR_INVALID and "k <= 8" in msg
+    st, msg = _status_and_msg(L.klc_moe_combine_rmsnorm(fake, fake, fake, 4, 2, 2880, None, None, 1e-5, fake, fake, None))
+    assert st == _lib.KLC_ERR_INVALID and "null" in msg
+    st, msg = _status_and_msg(L.klc_moe_combine_rmsnorm(fake, fake, fake, 4, 2, 2884, None, fake, 1e-5, fake, fake, None))
+    assert st == _lib.KLC_ERR_INVALID and "sizes" in msg
+    st, msg = _status_and_msg(L.klc_moe_combine_rmsnorm(fake, fake, fake, 4, 2, 2880, None, fake, 1e-5, fake,
+                                                        ctypes.c_void_p(264), None))
+    assert st == _lib.KLC_ERR_INVALID and "aligned" in msg
+    st, msg = _status_and_msg(L.klc_moe_combine_rmsnorm(None, None, None, 0, 2, 2880, None, None, 1e-5, None, None, None))
+    assert st == _lib.KLC_OK  # no tokens: nothing to do
+    d = _lib.KlcDims(4, 2880, 2880, 128, 4, _lib.PATH_CODE["auto"])
+    st, msg = _status_and_msg(L.klc_moe_forward_rmsnorm(ctypes.byref(d), None, fake, None, 0, fake, fake, fake, None, None,
+                                                        None, None, 1e-5, fake, fake, 0, None))
+    assert st == _lib.KLC_ERR_INVALID and "RMSNorm" in msg
 
 
 def test_check_maps_invalid_to_value_error():
