@@ -44,8 +44,9 @@ BYTES_PER_EXPERT = (2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H /
 GATE_UP_BYTES_PER_EXPERT = 2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H // 32 + 2 * GPT_OSS_I * 2  # 8,824,320
 FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H)  # 199,065,600
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from an ncu capture of
-# this workload at T=256 (ncu --set full, one launch); None where no capture was taken
-PROFILED_GATE_UP_TRAFFIC = {"decode": 1_145_114_000 + 8_942_592}
+# this workload at T=256 (decode) and T=4096 (prefill) (ncu --set full, one launch); None where
+# no capture was taken
+PROFILED_GATE_UP_TRAFFIC = {"decode": 1_145_114_000 + 8_942_592, "prefill": 1_024_244_000 + 95_751_424}
 
 
 def peaks() -> dict:
@@ -377,7 +378,8 @@ def run_ours(args, world, rank, local):
         flops_gu = 2 * T * TOP_K * GPT_OSS_H * 2 * GPT_OSS_I
         achieved = flops_gu / (gu_ms / 1e3) / 1e12
         roof = {"bound": "tensor", "kernel": "gate_up GEMM", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / pk["bf16_tflops"], "traffic": None, "peak_source": pk["source"], "algorithmic_flops": flops_gu}
+                "frac": achieved / pk["bf16_tflops"], "peak_source": pk["source"], "algorithmic_flops": flops_gu,
+                "traffic": PROFILED_GATE_UP_TRAFFIC.get("prefill") if args.workload == "prefill" and T == 4096 else None}
         layer_roof = {"flops": T * FLOPS_PER_TOKEN, "achieved_tflops": T * FLOPS_PER_TOKEN / (ms / 1e3) / 1e12}
 
     result = {
