@@ -16,6 +16,9 @@ from . import _lib
 from .mxfp4_expert import PackedLayer
 
 _WORKSPACES: dict[int, torch.Tensor] = {}
+# workspaces replaced by larger ones stay allocated: a CUDA graph captured
+# while one was current still writes to it on replay
+_RETIRED_WORKSPACES: list[torch.Tensor] = []
 
 
 def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
@@ -23,6 +26,8 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     idx = device.index if device.index is not None else torch.cuda.current_device()
     ws = _WORKSPACES.get(idx)
     if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _RETIRED_WORKSPACES.append(ws)
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
         _WORKSPACES[idx] = ws
     return ws
