@@ -106,3 +106,24 @@ def test_experts_reject_small_workspace():
     w = _lib.KlcWeights(16, 16, 16, 16, 16, 16, 16, 16, 7.0, 1.702)
     st = L.klc_moe_experts(ctypes.byref(d), ctypes.byref(w), 16, 16, 16, 0, 16, None, None, 256, 64, None)
     assert st == _lib.KLC_ERR_WORKSPACE
+
+
+def test_workspace_growth_keeps_replaced_buffers(monkeypatch):
+    """A larger call replaces the per-device workspace but keeps the old one
+    allocated (a CUDA graph captured with it still writes there on replay)."""
+    import torch
+
+    from kcapw_klcquant_b200 import moe
+
+    real_empty = torch.empty
+    monkeypatch.setattr(moe.torch, "empty", lambda n, dtype=None, device=None: real_empty(n, dtype=dtype))
+    monkeypatch.setattr(moe, "_WORKSPACES", {})
+    monkeypatch.setattr(moe, "_RETIRED_WORKSPACES", [])
+    dev = torch.device("cuda", 0)
+    a = moe.workspace(dev, 1000)
+    assert a.numel() >= 1 << 20  # at least 1 MiB
+    assert moe.workspace(dev, 5000) is a  # reused while large enough
+    b = moe.workspace(dev, (1 << 20) + 1)
+    assert b is not a and b.numel() >= (1 << 20) + 1
+    assert moe._RETIRED_WORKSPACES == [a]
+    assert moe.workspace(dev, 10) is b
