@@ -63,7 +63,7 @@ enum klc_precision { KLC_PREC_FP32 = 0, KLC_PREC_BF16 = 1 };
 enum klc_expert_path {
   KLC_PATH_AUTO = 0, /* tcgen05 grouped GEMM when available, else SIMT       */
   KLC_PATH_SIMT = 1, /* CUDA-core dequant + FMA kernels                      */
-  KLC_PATH_TC = 2    /* tcgen05/TMEM grouped GEMM, dequant into TMEM         */
+  KLC_PATH_TC = 2    /* tcgen05 block-scaled MMA on the packed E2M1 weights  */
 };
 
 int klc_version(void);
@@ -189,19 +189,25 @@ int klc_moe_experts(const klc_moe_dims* dims, const klc_moe_weights* wts, const 
  * reference).  For callers that cannot allocate device memory themselves --
  * e.g. a host runtime reaching this library through an FFI without a CUDA
  * allocator, or an application whose device memory belongs to another pool.
- * Same arguments as klc_moe_experts minus the workspace; the scratch is a
- * static 16 MiB device array inside the library (held by every GPU that
- * loads it until the process exits; klc_moe_noalloc_scratch_bytes reports
- * the size).  Always runs the CUDA-core expert kernels.  A batch whose
- * scratch would exceed the array is rejected with KLC_ERR_INVALID.  The first
- * call on a device looks up the array's address (cudaGetSymbolAddress): make
- * it before any stream capture on that device.  All calls on a device share
- * the array, so calls that overlap on the GPU race: serialise them.  Calls no
- * cudaMalloc/cudaFree or allocating library routine.                       */
+ * Same arguments and argument checks as klc_moe_experts minus the workspace;
+ * the scratch is a static 16 MiB device array inside the library (held by
+ * every GPU that loads it until the process exits;
+ * klc_moe_noalloc_scratch_bytes reports the size).  Always runs the
+ * CUDA-core expert kernels.  A batch whose scratch would exceed the array is
+ * rejected with KLC_ERR_INVALID.  The first call on a device looks up the
+ * array's address (cudaGetSymbolAddress): make it before any stream capture
+ * on that device; the address is cached for the process, so do not call the
+ * library again after cudaDeviceReset.  All calls on a device share the
+ * array, so calls that overlap on the GPU race: serialise them.  Calls no
+ * cudaMalloc/cudaFree or allocating library routine.
+ * klc_moe_noalloc_status reads the device status word of the last call on
+ * the current device (as klc_workspace_status does for a workspace): an
+ * expert id outside [0, E) is reported as KLC_ERR_DEVICE_FAULT.            */
 int klc_moe_experts_noalloc(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x, const int32_t* idx,
                             const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
                             void* stream);
 int klc_moe_noalloc_scratch_bytes(size_t* out_bytes);
+int klc_moe_noalloc_status(int* code, int* where, int* detail, void* stream);
 
 /* Router + experts + combine in one call (StreamedMoERouter.route batched).
  * out_idx/out_w receive the routing (int32 [T,k], bf16 [T,k]); out_logits

@@ -85,6 +85,7 @@ SIGNATURES: dict[str, list] = {
     "klc_moe_experts": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "klc_moe_experts_noalloc": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "klc_moe_noalloc_scratch_bytes": [POINTER(c_size_t)],
+    "klc_moe_noalloc_status": [POINTER(c_int), POINTER(c_int), POINTER(c_int), c_void_p],
     "klc_moe_forward": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "klc_moe_combine": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p],
     "klc_moe_combine_rmsnorm": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p],

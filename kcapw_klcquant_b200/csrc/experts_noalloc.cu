@@ -12,7 +12,12 @@
 // Contract:
 //  * The first call on a device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it; make that
-//    first call before any stream capture on that device.
+//    first call before any stream capture on that device.  The cached address
+//    belongs to the device's primary context: after cudaDeviceReset (or any
+//    teardown of that context) this library must not be called again in the
+//    process.
+//  * Device-side checks (an expert id outside [0, E)) record their status at
+//    the start of the array; klc_moe_noalloc_status reads it back.
 //  * The scratch is shared by every call on a device and keeps the previous
 //    call's contents; the kernels clear what must start at zero.  Calls that
 //    overlap on the GPU (different streams, or threads without ordering) race
@@ -97,29 +102,36 @@ extern "C" int klc_moe_experts_noalloc(const klc_moe_dims* dims, const klc_moe_w
                                        const int32_t* idx, const uint16_t* w, int precision, uint16_t* y, float* norms,
                                        const uint16_t* residual, void* stream) {
   using namespace klc;
-  KLC_CHECK_ARG(dims != nullptr && wts != nullptr, "klc_moe_experts_noalloc: null dims or weights");
-  KLC_CHECK_ARG(dims->tokens >= 0, "klc_moe_experts_noalloc: tokens must be >= 0");
-  KLC_CHECK_ARG(dims->hidden > 0 && dims->hidden % 64 == 0 && dims->intermediate > 0 && dims->intermediate % 64 == 0,
-                "klc_moe_experts_noalloc: hidden and intermediate must be positive multiples of 64");
-  KLC_CHECK_ARG(dims->experts > 0 && dims->experts <= 1024, "klc_moe_experts_noalloc: experts must be in [1, 1024]");
-  KLC_CHECK_ARG(dims->top_k >= 1 && dims->top_k <= 8 && dims->top_k <= dims->experts,
-                "klc_moe_experts_noalloc: top_k must be in [1, min(8, experts)]");
-  KLC_CHECK_ARG(precision == KLC_PREC_FP32 || precision == KLC_PREC_BF16, "klc_moe_experts_noalloc: bad precision");
-  KLC_CHECK_ARG(wts->gu_blocks && wts->gu_scales_t && wts->gu_bias && wts->dn_blocks && wts->dn_scales_t && wts->dn_bias,
-                "klc_moe_experts_noalloc: null expert weight pointer");
-  if (dims->tokens == 0) return KLC_OK;
-  KLC_CHECK_ARG(x && idx && w && y, "klc_moe_experts_noalloc: null pointer");
+  KLC_CHECK_ARG(dims != nullptr, "klc_moe_experts_noalloc: null dims");
   klc_moe_dims d = *dims;
   d.path = KLC_PATH_SIMT;
+  // the same checks as klc_moe_experts (sizes, token bound, weight pointers
+  // and their 16-byte alignment), before any size arithmetic or launch
+  int st = validate_dims(&d);
+  if (st != KLC_OK) return st;
+  st = validate_weights(wts);
+  if (st != KLC_OK) return st;
+  KLC_CHECK_ARG(precision == KLC_PREC_FP32 || precision == KLC_PREC_BF16, "klc_moe_experts_noalloc: bad precision");
+  if (d.tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(x && idx && w && y, "klc_moe_experts_noalloc: null pointer");
   const WorkspaceLayout L = noalloc_layout(d);
   if (L.total > kNoAllocScratchBytes)
     return fail(KLC_ERR_INVALID, "klc_moe_experts_noalloc: this batch needs " + std::to_string(L.total) +
                                      " bytes of scratch, more than the " + std::to_string(kNoAllocScratchBytes) +
                                      "-byte static buffer; use klc_moe_experts with a caller workspace");
   char* scratch = nullptr;
-  const int st = scratch_address(&scratch);
+  st = scratch_address(&scratch);
   if (st != KLC_OK) return st;
   return run_experts(d, *wts, x, idx, w, precision, y, norms, residual, scratch, L, as_stream(stream));
+}
+
+extern "C" int klc_moe_noalloc_status(int* code, int* where, int* detail, void* stream) {
+  using namespace klc;
+  char* scratch = nullptr;
+  int st = scratch_address(&scratch);
+  if (st != KLC_OK) return st;
+  // the status word sits at offset 0 of the array (noalloc_layout)
+  return klc_workspace_status(scratch, code, where, detail, stream);
 }
 
 extern "C" int klc_moe_noalloc_scratch_bytes(size_t* out_bytes) {

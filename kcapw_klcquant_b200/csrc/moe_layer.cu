@@ -87,11 +87,12 @@ WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffer
   return L;
 }
 
-static int validate_dims(const klc_moe_dims* d) {
+int validate_dims(const klc_moe_dims* d) {
   KLC_CHECK_ARG(d != nullptr, "null dims");
   KLC_CHECK_ARG(d->tokens >= 0, "tokens must be >= 0");
-  KLC_CHECK_ARG(d->hidden > 0 && d->hidden % 64 == 0, "hidden must be a positive multiple of 64");
-  KLC_CHECK_ARG(d->intermediate > 0 && d->intermediate % 64 == 0, "intermediate must be a positive multiple of 64");
+  KLC_CHECK_ARG(d->hidden > 0 && d->hidden % 64 == 0 && d->hidden <= 65536, "hidden must be a positive multiple of 64, at most 65536");
+  KLC_CHECK_ARG(d->intermediate > 0 && d->intermediate % 64 == 0 && d->intermediate <= 65536,
+                "intermediate must be a positive multiple of 64, at most 65536");
   KLC_CHECK_ARG(d->experts > 0 && d->experts <= 1024, "experts must be in [1, 1024]");
   KLC_CHECK_ARG(d->top_k >= 1 && d->top_k <= 8 && d->top_k <= d->experts, "top_k must be in [1, min(8, experts)]");
   KLC_CHECK_ARG(d->path >= KLC_PATH_AUTO && d->path <= KLC_PATH_TC, "unknown expert path");
@@ -99,7 +100,7 @@ static int validate_dims(const klc_moe_dims* d) {
   return KLC_OK;
 }
 
-static int validate_weights(const klc_moe_weights* w) {
+int validate_weights(const klc_moe_weights* w) {
   KLC_CHECK_ARG(w != nullptr, "null weights");
   KLC_CHECK_ARG(w->gu_blocks && w->gu_scales_t && w->gu_bias && w->dn_blocks && w->dn_scales_t && w->dn_bias,
                 "null expert weight pointer");

@@ -48,6 +48,12 @@ struct WorkspaceLayout {
 
 WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffers);
 
+// Argument checks shared by every layer entry point (KLC_ERR_INVALID and a
+// message on failure): sizes, the expert path, and the expert weight pointers
+// (non-null, blocks 16-byte aligned for the 128-bit weight loads).
+int validate_dims(const klc_moe_dims* d);
+int validate_weights(const klc_moe_weights* w);
+
 // ---------------------------------------------------------------------------
 // expert kernels
 // ---------------------------------------------------------------------------

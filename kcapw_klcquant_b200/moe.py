@@ -8,6 +8,7 @@ stream.  All math runs in the CUDA kernels of libklcmoe.so.
 from __future__ import annotations
 
 import ctypes
+import threading
 from dataclasses import dataclass
 
 import torch
@@ -15,21 +16,31 @@ import torch
 from . import _lib
 from .mxfp4_expert import PackedLayer
 
-_WORKSPACES: dict[int, torch.Tensor] = {}
+# One workspace per (device, stream): calls on different streams (or from
+# different host threads on their own streams) never share scratch, while calls
+# on one stream reuse it in stream order.
+_WORKSPACES: dict[tuple[int, int], torch.Tensor] = {}
 # workspaces replaced by larger ones stay allocated: a CUDA graph captured
 # while one was current still writes to it on replay
 _RETIRED_WORKSPACES: list[torch.Tensor] = []
+_WS_LOCK = threading.Lock()
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A device byte buffer of at least ``nbytes`` (256-byte aligned), reused across calls."""
+def workspace(device: torch.device, nbytes: int, stream: int | None = None) -> torch.Tensor:
+    """A device byte buffer of at least ``nbytes`` (256-byte aligned) for calls on
+    ``stream`` (a raw ``cudaStream_t``; default: the device's current stream),
+    reused by later calls on the same stream."""
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _WORKSPACES.get(idx)
-    if ws is None or ws.numel() < nbytes:
-        if ws is not None:
-            _RETIRED_WORKSPACES.append(ws)
-        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
-        _WORKSPACES[idx] = ws
+    if stream is None:
+        stream = torch.cuda.current_stream(idx).cuda_stream
+    key = (idx, int(stream))
+    with _WS_LOCK:
+        ws = _WORKSPACES.get(key)
+        if ws is None or ws.numel() < nbytes:
+            if ws is not None:
+                _RETIRED_WORKSPACES.append(ws)
+            ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+            _WORKSPACES[key] = ws
     return ws
 
 
@@ -78,6 +89,7 @@ class MoeLayer:
         self.down_bias = as_bf16(down_bias, dev)
         self.top_k = int(top_k)
         self.path = path
+        self._last = threading.local()  # workspace + stream of this thread's last call
         E, H, I = packed.experts, packed.hidden, packed.intermediate
         if self.router_weight.shape != (E, H) or self.router_bias.shape != (E,):
             raise ValueError(f"router weight/bias must be [{E},{H}] / [{E}]")
@@ -156,7 +168,9 @@ class MoeLayer:
         if adjust is not None:
             adjust = adjust.to(device=self.device, dtype=torch.float32).contiguous()
         nbytes = self.workspace_bytes(T, path)
-        ws = workspace(self.device, nbytes)
+        stream = _lib.stream_ptr(self.device)
+        ws = workspace(self.device, nbytes, stream)
+        self._last.ws, self._last.stream = ws, stream
         normed = None
         with torch.cuda.device(self.device):
             if next_norm is None:
@@ -164,7 +178,7 @@ class MoeLayer:
                     _lib.lib().klc_moe_forward(
                         ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
                         _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
-                        _lib.ptr(norms), _lib.ptr(residual), ws.data_ptr(), ws.numel(), _lib.stream_ptr(),
+                        _lib.ptr(norms), _lib.ptr(residual), ws.data_ptr(), ws.numel(), stream,
                     )
                 )
             else:
@@ -177,7 +191,7 @@ class MoeLayer:
                         ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
                         _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
                         _lib.ptr(norms), _lib.ptr(residual), norm_w.data_ptr(), float(next_norm[1]), normed.data_ptr(),
-                        ws.data_ptr(), ws.numel(), _lib.stream_ptr(),
+                        ws.data_ptr(), ws.numel(), stream,
                     )
                 )
         return y, RouteBatch(idx, w, logits, norms, normed)
@@ -205,24 +219,29 @@ class MoeLayer:
         if residual is not None:
             residual = as_bf16(residual, self.device)
         nbytes = self.workspace_bytes(T, path)
-        ws = workspace(self.device, nbytes)
+        stream = _lib.stream_ptr(self.device)
+        ws = workspace(self.device, nbytes, stream)
+        self._last.ws, self._last.stream = ws, stream
         with torch.cuda.device(self.device):
             _lib.check(
                 _lib.lib().klc_moe_experts(
                     ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), idx.data_ptr(), w.data_ptr(),
                     _lib.PRECISION_CODE[precision], y.data_ptr(), _lib.ptr(norms), _lib.ptr(residual),
-                    ws.data_ptr(), ws.numel(), _lib.stream_ptr(),
+                    ws.data_ptr(), ws.numel(), stream,
                 )
             )
         return y, norms
 
     def check_device_status(self) -> None:
-        """Raise if a kernel of the last call recorded a device-side fault (synchronises)."""
-        ws = _WORKSPACES.get(self.device.index if self.device.index is not None else torch.cuda.current_device())
+        """Raise if a kernel of this thread's last call recorded a device-side fault.
+
+        Reads the status word of the workspace that call used, on the stream it
+        ran on (synchronises that stream)."""
+        ws = getattr(self._last, "ws", None)
         if ws is None:
             return
         with torch.cuda.device(self.device):
-            _lib.check(_lib.lib().klc_workspace_status(ws.data_ptr(), None, None, None, _lib.stream_ptr()))
+            _lib.check(_lib.lib().klc_workspace_status(ws.data_ptr(), None, None, None, self._last.stream))
 
 
 def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:

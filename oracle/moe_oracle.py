@@ -271,13 +271,18 @@ def combine_bits(outs: np.ndarray, weight_bits: np.ndarray) -> np.ndarray:
 class DenseExperts:
     """Lazily dequantized dense expert matrices (float32, bf16-exact values)."""
 
-    def __init__(self, gu_blocks, gu_scales, d_blocks, d_scales):
+    def __init__(self, gu_blocks, gu_scales, d_blocks, d_scales, max_cached: int | None = None):
         self.gu_blocks, self.gu_scales = np.asarray(gu_blocks), np.asarray(gu_scales)
         self.d_blocks, self.d_scales = np.asarray(d_blocks), np.asarray(d_scales)
         self.cache: dict[int, tuple[np.ndarray, np.ndarray]] = {}
+        # at the 120B layout one dense expert is ~100 MB of float32: a bound keeps
+        # host memory flat when a check walks many experts once each
+        self.max_cached = max_cached
 
     def get(self, e: int) -> tuple[np.ndarray, np.ndarray]:
         if e not in self.cache:
+            if self.max_cached is not None and len(self.cache) >= self.max_cached:
+                self.cache.pop(next(iter(self.cache)))
             # E2M1 x E8M0 values are exact in bf16 (same exponent range as fp32,
             # two significant bits), so the float32 values equal the bf16 matrix
             # the reference caches.  Stored as [in, out] views of [out, in] arrays.

@@ -109,8 +109,9 @@ def test_experts_reject_small_workspace():
 
 
 def test_workspace_growth_keeps_replaced_buffers(monkeypatch):
-    """A larger call replaces the per-device workspace but keeps the old one
-    allocated (a CUDA graph captured with it still writes there on replay)."""
+    """A larger call replaces the workspace of its (device, stream) but keeps the
+    old one allocated (a CUDA graph captured with it still writes there on
+    replay); another stream gets a workspace of its own."""
     import torch
 
     from kcapw_klcquant_b200 import moe
@@ -120,10 +121,36 @@ def test_workspace_growth_keeps_replaced_buffers(monkeypatch):
     monkeypatch.setattr(moe, "_WORKSPACES", {})
     monkeypatch.setattr(moe, "_RETIRED_WORKSPACES", [])
     dev = torch.device("cuda", 0)
-    a = moe.workspace(dev, 1000)
+    a = moe.workspace(dev, 1000, stream=0)
     assert a.numel() >= 1 << 20  # at least 1 MiB
-    assert moe.workspace(dev, 5000) is a  # reused while large enough
-    b = moe.workspace(dev, (1 << 20) + 1)
+    assert moe.workspace(dev, 5000, stream=0) is a  # reused while large enough
+    other = moe.workspace(dev, 1000, stream=0x1234)
+    assert other is not a  # a second stream never shares scratch with the first
+    b = moe.workspace(dev, (1 << 20) + 1, stream=0)
     assert b is not a and b.numel() >= (1 << 20) + 1
     assert moe._RETIRED_WORKSPACES == [a]
-    assert moe.workspace(dev, 10) is b
+    assert moe.workspace(dev, 10, stream=0) is b
+    assert moe.workspace(dev, 10, stream=0x1234) is other
+
+
+def test_noalloc_validates_like_the_workspace_entry_point():
+    """klc_moe_experts_noalloc runs the same host checks as klc_moe_experts before
+    any size arithmetic or launch: misaligned expert blocks, an unbounded token
+    count and bad shapes come back as KLC_ERR_INVALID (no GPU is touched)."""
+    L = _lib.lib()
+    d = _lib.KlcDims(8, 2880, 2880, 32, 4, _lib.KLC_PATH_SIMT)
+    good = _lib.KlcWeights(256, 256, 256, 256, 256, 256, 256, 256, 7.0, 1.702)
+    for field in ("gu_blocks", "dn_blocks"):
+        w = _lib.KlcWeights(256, 256, 256, 256, 256, 256, 256, 256, 7.0, 1.702)
+        setattr(w, field, 256 + 8)  # 8-byte aligned only: the 128-bit weight loads would fault
+        st, msg = _status_and_msg(L.klc_moe_experts_noalloc(ctypes.byref(d), ctypes.byref(w), 256, 256, 256,
+                                                            _lib.KLC_PREC_BF16, 256, None, None, None))
+        assert st == _lib.KLC_ERR_INVALID and "aligned" in msg, (field, msg)
+    huge = _lib.KlcDims(1 << 40, 2880, 2880, 32, 4, _lib.KLC_PATH_SIMT)
+    st, msg = _status_and_msg(L.klc_moe_experts_noalloc(ctypes.byref(huge), ctypes.byref(good), 256, 256, 256,
+                                                        _lib.KLC_PREC_BF16, 256, None, None, None))
+    assert st == _lib.KLC_ERR_INVALID and "tokens" in msg
+    bad = _lib.KlcDims(8, 2881, 2880, 32, 4, _lib.KLC_PATH_SIMT)
+    st, _ = _status_and_msg(L.klc_moe_experts_noalloc(ctypes.byref(bad), ctypes.byref(good), 256, 256, 256,
+                                                      _lib.KLC_PREC_BF16, 256, None, None, None))
+    assert st == _lib.KLC_ERR_INVALID
