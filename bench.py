@@ -1,25 +1,39 @@
 """Benchmark of the B200 MoE block (BASELINE.json metric: MoE-layer tokens/s
-and HBM GB/s or tensor-pipe % of peak).
+and HBM GB/s or tensor-pipe % of peak at 1/2/4/8 B200).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload decode|prefill] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ep|decode|prefill|stack]
+                    [--impl ours|reference] [--zipf]
 
 Workloads (synthetic, seeded, GPT-OSS-120B MoE layout: E=128, H=I=2880, top-4):
-  decode   config 1: T=256 tokens per GPU (headline), plus a sweep over T=1,8,64,256
+  ep       (default) config 3: one MoE layer over 16 384 tokens shared evenly by
+           the N ranks (strong scaling).  N=1 runs the whole layer on one GPU;
+           N>1 shards the experts (rank r holds experts [r*E/N, (r+1)*E/N)) and
+           exchanges token rows and expert outputs between the ranks.  Routing
+           uniform (headline) and Zipf(1.1)-skewed (the ``zipf`` key).
+  decode   config 1: T=256 decode tokens per GPU, plus a sweep over T=1,8,64,256
   prefill  config 2: T=4096 tokens, router biased to a Zipf(1.1) expert popularity
+  stack    config 4: a 36-layer MoE-only stack (RMSNorm + residual between the
+           blocks), 32 sequences x 128 decode steps, experts sharded over the ranks
 
 A step is one MoE-layer forward (router -> dispatch -> MXFP4 SwiGLU experts ->
-combine) over the step's tokens with the weights resident in HBM.  With N>1
-(one process per GPU under torchrun) every rank runs the same per-GPU
-workload on its own layer replica (weak scaling; the layer needs no
-collective when tokens are split by rank).  Timing: W untimed warm-up steps,
-then K steps bracketed by a barrier and cuda synchronize, CUDA events on the
-launching stream, max over ranks.  The weights (1.7 GB per layer) exceed the
-126 MB L2, so each step streams them from HBM; for T <= 8 (52-380 MB of
-weights touched) a 256 MB buffer is written between timed steps to flush L2.
+combine) over the step's tokens with the weights resident in HBM.  Timing: W
+untimed warm-up steps, then K steps inside one pair of CUDA events on the
+launching stream, bracketed by a barrier and a device synchronize on both
+sides; the value is the maximum over ranks.  The layer's weights (1.7 GB, or
+1.7/N GB per rank) exceed the 126 MB L2; where the touched weights would fit
+(decode T <= 8), a 256 MB buffer is written between timed steps to flush L2.
 
-``--impl reference`` times the reference algorithm on the host CPU (the numpy
-restatement in oracle/, used only here and in tests) on the same layer,
-rank 0 only.
+On N=1 the line also carries the config-1 decode figures with the HBM
+roofline of the gate_up kernel (``decode``), the config-2 prefill figures with
+its tensor-pipe fraction (``prefill_c2``), the oracle parity of a token
+subsample (``parity``) and the CPU baseline (``cpu_baseline``).  On N>1 every
+rank compares its expert-parallel output with the single-GPU layer on the same
+tokens (``parity``).
+
+``--impl reference`` times the reference algorithm on the host cores (the
+numpy restatement in oracle/, used only here and in tests) on the same
+workload's layer, one token per call as the reference's route() runs, with
+every host thread; rank 0 only.
 """
 from __future__ import annotations
 
@@ -38,14 +52,13 @@ sys.path.insert(0, str(REPO))
 import torch  # noqa: E402
 
 GPT_OSS_E, GPT_OSS_H, GPT_OSS_I, TOP_K = 128, 2880, 2880, 4
-BYTES_PER_EXPERT = (2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H // 32 + 2 * GPT_OSS_I * 2) + (
-    GPT_OSS_H * GPT_OSS_I // 2 + GPT_OSS_H * GPT_OSS_I // 32 + GPT_OSS_H * 2
-)  # 13,236,480
 GATE_UP_BYTES_PER_EXPERT = 2 * GPT_OSS_I * GPT_OSS_H // 2 + 2 * GPT_OSS_I * GPT_OSS_H // 32 + 2 * GPT_OSS_I * 2  # 8,824,320
+DOWN_BYTES_PER_EXPERT = GPT_OSS_H * GPT_OSS_I // 2 + GPT_OSS_H * GPT_OSS_I // 32 + GPT_OSS_H * 2  # 4,412,160
+BYTES_PER_EXPERT = GATE_UP_BYTES_PER_EXPERT + DOWN_BYTES_PER_EXPERT  # 13,236,480
 FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H)  # 199,065,600
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from an ncu capture of
-# this workload at T=256 (decode) and T=4096 (prefill) (ncu --set full, one launch); None where
-# no capture was taken
+GATE_UP_FLOPS_PER_PAIR = 2 * GPT_OSS_H * 2 * GPT_OSS_I  # 33,177,600
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from ncu captures
+# (profiles/): decode T=256, prefill T=4096 Zipf.  None where no capture was taken.
 PROFILED_GATE_UP_TRAFFIC = {"decode": 1_145_114_000 + 8_942_592, "prefill": 1_024_244_000 + 95_751_424}
 
 
@@ -122,27 +135,24 @@ class ClockSampler:
                 "samples": len(sm), "source": "nvml" if self.h is not None else "unavailable"}
 
 
-def dist_setup(use_gpu: bool = True, force_group: bool = False):
+# ---------------------------------------------------------------------------
+# process group and timing helpers
+# ---------------------------------------------------------------------------
+
+
+def dist_setup(use_gpu: bool = True):
     """One process per GPU under torchrun (RANK/LOCAL_RANK/WORLD_SIZE); NCCL for the GPU arm, gloo for the CPU arm."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if use_gpu:
         torch.cuda.set_device(local)
-    if world > 1 or force_group:
+    if world > 1:
         import datetime
 
         import torch.distributed as dist
 
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        if "MASTER_PORT" not in os.environ:
-            import socket
-
-            with socket.socket() as sk:
-                sk.bind(("127.0.0.1", 0))
-                os.environ["MASTER_PORT"] = str(sk.getsockname()[1])
-        os.environ.setdefault("RANK", str(rank))
-        os.environ.setdefault("WORLD_SIZE", str(world))
         if use_gpu:
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
         else:
@@ -151,45 +161,62 @@ def dist_setup(use_gpu: bool = True, force_group: bool = False):
 
 
 def barrier(world):
-    import torch.distributed as dist
-
-    if world > 1 or (dist.is_available() and dist.is_initialized()):
+    if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
 
 
-def max_over_ranks(v: float, world: int) -> float:
+def reduce_over_ranks(v: float, world: int, op: str = "max") -> float:
     if world == 1:
         return v
     import torch.distributed as dist
 
     t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op={"max": dist.ReduceOp.MAX, "min": dist.ReduceOp.MIN, "sum": dist.ReduceOp.SUM}[op])
     return float(t.item())
 
 
-def make_layer(workload: str, seed: int, device):
-    from kcapw_klcquant_b200 import MoeLayer
-    from kcapw_klcquant_b200 import synthetic as syn
+def launch_count() -> int:
+    from kcapw_klcquant_b200 import _lib
 
-    zipf = 1.1 if workload == "prefill" else None
-    layer = syn.make_layer(syn.GPT_OSS_120B, seed=seed, zipf=zipf, device=device)
-    return MoeLayer.from_tensors(0, layer, device, top_k=TOP_K)
+    return _lib.launch_count()
 
 
-def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None, world: int, clk: ClockSampler | None = None):
-    """Per-step device times (ms) of ``fn`` with CUDA events on the current stream; ``clk``
-    samples clocks from the first timed launch to the end of the last timed step."""
+def time_window(fn, steps: int, warmup: int, world: int, clk: ClockSampler | None = None) -> tuple[float, float]:
+    """(ms per step, library kernel launches per step) of ``fn``: W warm-up calls, then K
+    calls inside one pair of CUDA events on the current stream, with a barrier and a
+    device synchronize on both sides.  ``clk`` samples clocks over the timed calls."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if clk is not None:
         clk.start()
+    n0 = launch_count()
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    n1 = launch_count()
+    torch.cuda.synchronize()
+    if clk is not None:
+        clk.stop()
+    barrier(world)
+    return a.elapsed_time(b) / steps, (n1 - n0) / steps
+
+
+def time_steps_flushed(fn, steps: int, warmup: int, flush: torch.Tensor | None) -> float:
+    """Mean ms of ``fn`` over K calls, each timed alone with CUDA events; when ``flush``
+    is given, a buffer larger than L2 is written before every call (outside the events)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     for i in range(steps):
         if flush is not None:
             flush.add_(1)
@@ -197,10 +224,7 @@ def time_steps(fn, steps: int, warmup: int, flush: torch.Tensor | None, world: i
         fn()
         ev[i][1].record(stream)
     torch.cuda.synchronize()
-    if clk is not None:
-        clk.stop()
-    barrier(world)
-    return [a.elapsed_time(b) for a, b in ev]
+    return sum(x.elapsed_time(y) for x, y in ev) / steps
 
 
 def time_e2e(forward, x_host: torch.Tensor, steps: int, warmup: int, world: int) -> float:
@@ -260,19 +284,140 @@ def time_e2e(forward, x_host: torch.Tensor, steps: int, warmup: int, world: int)
     return t0.elapsed_time(t1) / steps
 
 
-def unique_experts(ml, x) -> int:
-    _, rb = ml.forward(x, precision="bf16")
-    return int(torch.unique(rb.indices).numel())
+def stage_pass(fn, reps: int = 3, flush: torch.Tensor | None = None) -> dict[str, float]:
+    """Per-stage milliseconds of ``fn`` (klc_stage_timing), last of ``reps`` passes."""
+    from kcapw_klcquant_b200 import _lib
+
+    _lib.stage_timing(True)
+    stage = {}
+    try:
+        for _ in range(reps):
+            for _ in range(2):  # the first call keeps the GPU busy while the second's launches are issued
+                if flush is not None:
+                    flush.add_(1)
+                fn()
+            stage = _lib.stage_times()
+    finally:
+        _lib.stage_timing(False)
+    return stage
 
 
-def cpu_baseline_sample(layer: dict[str, torch.Tensor], x_host: torch.Tensor, n_tokens: int) -> dict:
-    """Time the CPU restatement of the reference (oracle/) on the first tokens, dense experts cached.
+# ---------------------------------------------------------------------------
+# layers and parity
+# ---------------------------------------------------------------------------
 
-    ``layer`` holds the checkpoint-named tensors on the CPU.  Mirrors the
-    reference's warm decode path: one route() per token (bf16 logits, top-k,
-    softmax, per-expert GEMVs with the dequantized experts already cached,
-    bf16 combine).
-    """
+
+def make_tensors(seed: int, device, zipf: float | None = None) -> dict[str, torch.Tensor]:
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    return syn.make_layer(syn.GPT_OSS_120B, seed=seed, zipf=zipf, device=device)
+
+
+def with_router_bias(tensors: dict[str, torch.Tensor], zipf: float, seed: int) -> dict[str, torch.Tensor]:
+    """The same layer with the Zipf(s) router bias (configs 2 and 3-skewed): only the bias differs."""
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    t = dict(tensors)
+    key = "model.layers.0.mlp.router.bias"
+    t[key] = syn.zipf_router_bias(GPT_OSS_E, seed, s=zipf).to(tensors[key].device)
+    return t
+
+
+def layer_from(tensors, device, packed=None):
+    """A single-GPU MoeLayer over checkpoint-named tensors (``packed``: reuse resident expert weights)."""
+    from kcapw_klcquant_b200 import MoeLayer
+    from kcapw_klcquant_b200.mxfp4_expert import PackedLayer
+
+    p = "model.layers.0.mlp"
+    if packed is None:
+        packed = PackedLayer.from_checkpoint_tensors(tensors[f"{p}.experts.gate_up_proj_blocks"], tensors[f"{p}.experts.gate_up_proj_scales"],
+                                                     tensors[f"{p}.experts.down_proj_blocks"], tensors[f"{p}.experts.down_proj_scales"], device)
+    return MoeLayer(packed, tensors[f"{p}.router.weight"], tensors[f"{p}.router.bias"], tensors[f"{p}.experts.gate_up_proj_bias"],
+                    tensors[f"{p}.experts.down_proj_bias"], top_k=TOP_K)
+
+
+def compare(y: torch.Tensor, ref: torch.Tensor) -> dict:
+    """cosine, max-abs / max|ref| and the fraction of bit-identical bf16 outputs."""
+    a, b = y.float().flatten(), ref.float().flatten()
+    cos = float((a @ b) / (a.norm() * b.norm()).clamp_min(1e-30))
+    nmax = float((a - b).abs().max() / b.abs().max().clamp_min(1e-30))
+    beq = float((y.view(torch.int16) == ref.view(torch.int16)).float().mean())
+    return {"cosine": cos, "norm_max_abs": nmax, "bit_equal_frac": beq}
+
+
+def oracle_parity(tensors: dict[str, torch.Tensor], x: torch.Tensor, y: torch.Tensor, idx: torch.Tensor, w: torch.Tensor,
+                  n_tokens: int) -> dict:
+    """The first ``n_tokens`` outputs against the CPU oracle (the reference's bf16 expert
+    path restated) on the device's own routing, one dense expert in host memory at a time."""
+    import numpy as np
+
+    from oracle import moe_oracle as orc
+
+    p = "model.layers.0.mlp"
+
+    def bits(t):
+        return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    sel = idx[:n_tokens].cpu().numpy()
+    used = np.unique(sel)
+    # only the experts the sample routes to cross to the host
+    blocks = {n: tensors[f"{p}.experts.{n}"] for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "down_proj_blocks", "down_proj_scales")}
+    sub = {n: t[torch.from_numpy(used).to(t.device).long()].cpu().numpy() for n, t in blocks.items()}
+    remap = {int(e): i for i, e in enumerate(used)}
+    ex = orc.DenseExperts(sub["gate_up_proj_blocks"], sub["gate_up_proj_scales"], sub["down_proj_blocks"], sub["down_proj_scales"], max_cached=1)
+    local_idx = np.vectorize(remap.get)(sel)
+    gub = bits(tensors[f"{p}.experts.gate_up_proj_bias"])[used]
+    dnb = bits(tensors[f"{p}.experts.down_proj_bias"])[used]
+    want = orc.moe_layer(bits(x[:n_tokens]), local_idx, bits(w[:n_tokens]), ex, gub, dnb, "bf16")
+    got = bits(y[:n_tokens])
+    a = orc.bf16_bits_to_f32(got).astype(np.float64).ravel()
+    b = orc.bf16_bits_to_f32(want).astype(np.float64).ravel()
+    return {"tokens": n_tokens, "experts": int(used.size), "cosine": float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b))),
+            "norm_max_abs": float(np.abs(a - b).max() / np.abs(b).max()), "bit_equal_frac": float(np.mean(got == want))}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (the reference algorithm on the host cores)
+# ---------------------------------------------------------------------------
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def use_all_host_threads() -> int:
+    """Every host thread for torch and numpy's BLAS (torchrun sets OMP_NUM_THREADS=1)."""
+    n = host_threads()
+    torch.set_num_threads(n)
+    try:
+        import threadpoolctl
+
+        threadpoolctl.threadpool_limits(n)
+    except Exception:
+        pass
+    return n
+
+
+def cpu_reference_sample(tensors_cpu: dict[str, torch.Tensor], x_host: torch.Tensor, n_tokens: int, precision: str = "bf16",
+                         cold: bool = False) -> float:
+    """Tokens/s of the CPU restatement of the reference's route() on the first tokens,
+    one token per call (router logits, top-k, softmax, one expert at a time, bf16
+    combine).  Warm: the dense experts those tokens use are dequantized before the
+    clock starts (the reference's warm cache); cold: the dequantization of each
+    expert on first use is timed too (the reference's cache misses)."""
     import numpy as np
 
     from oracle import moe_oracle as orc
@@ -280,245 +425,314 @@ def cpu_baseline_sample(layer: dict[str, torch.Tensor], x_host: torch.Tensor, n_
     p = "model.layers.0.mlp"
     bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
     xs = bits(x_host[:n_tokens])
-    rw, rbias = bits(layer[f"{p}.router.weight"]), bits(layer[f"{p}.router.bias"])
-    lg = orc.router_logits_bits(xs, rw, rbias)
-    idx, _ = orc.select_topk(orc.bf16_bits_to_f32(lg), TOP_K)
-    ex = orc.DenseExperts(*(layer[f"{p}.experts.{n}"].cpu().numpy() for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "down_proj_blocks", "down_proj_scales")))
-    for e in np.unique(idx):  # warm the dequantized-expert cache (the reference's warm path)
-        ex.get(int(e))
-    gub, dnb = bits(layer[f"{p}.experts.gate_up_proj_bias"]), bits(layer[f"{p}.experts.down_proj_bias"])
+    rw, rbias = bits(tensors_cpu[f"{p}.router.weight"]), bits(tensors_cpu[f"{p}.router.bias"])
+    ex = orc.DenseExperts(*(tensors_cpu[f"{p}.experts.{n}"].numpy() for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "down_proj_blocks", "down_proj_scales")))
+    if not cold:
+        lg = orc.router_logits_bits(xs, rw, rbias)
+        idx, _ = orc.select_topk(orc.bf16_bits_to_f32(lg), TOP_K)
+        for e in np.unique(idx):
+            ex.get(int(e))
+    gub, dnb = bits(tensors_cpu[f"{p}.experts.gate_up_proj_bias"]), bits(tensors_cpu[f"{p}.experts.down_proj_bias"])
     t0 = time.perf_counter()
     for t in range(n_tokens):  # one token at a time, as route() does
         lgt = orc.router_logits_bits(xs[t : t + 1], rw, rbias)
         it, st = orc.select_topk(orc.bf16_bits_to_f32(lgt), TOP_K)
-        orc.moe_layer(xs[t : t + 1], it, orc.softmax_weights_bits(st), ex, gub, dnb, "bf16")
-    dt = time.perf_counter() - t0
-    return {"value": n_tokens / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{n_tokens} tokens of the same layer, one token per route() call, experts pre-dequantized (warm cache), numpy with all host threads"}
+        orc.moe_layer(xs[t : t + 1], it, orc.softmax_weights_bits(st), ex, gub, dnb, precision)
+    return n_tokens / (time.perf_counter() - t0)
+
+
+def cpu_baseline(tensors_cpu: dict[str, torch.Tensor], x_host: torch.Tensor) -> dict:
+    """The reported CPU baseline: warm bf16 (value), warm fp32 and cold bf16, all host threads."""
+    n = use_all_host_threads()
+    warm_bf16 = cpu_reference_sample(tensors_cpu, x_host, 16, "bf16")
+    warm_fp32 = cpu_reference_sample(tensors_cpu, x_host, 8, "fp32")
+    cold_bf16 = cpu_reference_sample(tensors_cpu, x_host[16:], 2, "bf16", cold=True)
+    return {"value": warm_bf16, "unit": "tokens/s", "cores": n, "cpu_model": cpu_model(), "kind": "port",
+            "sample": "route() restated in numpy (oracle/), one token per call on the same layer: 16 tokens warm "
+                      "(their experts dequantized beforehand), matmul_precision bf16; value = that rate",
+            "warm_fp32_tokens_per_s": warm_fp32, "cold_bf16_tokens_per_s": cold_bf16,
+            "cold_sample": "2 tokens with every expert dequantized on first use inside the timed region"}
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+
+def base_line(args, world: int, value: float, ms: float, launches: float, workload: str, scaling: str, parallelism: str,
+              extra_config: dict | None = None) -> dict:
+    cfg = {"workload": workload, "precision": args.precision, "expert_path": args.path, "parallelism": parallelism}
+    cfg.update(extra_config or {})
+    return {"metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic (seeded GPT-OSS-120B MXFP4 MoE layer, bf16 N(0,1) activations)",
+            "config": cfg, "gpu_launches": launches * args.steps, "gpu_launches_per_step": launches}
+
+
+def decode_extras(args, ml, device, pk) -> dict:
+    """Config 1 on the same layer: T=256 with the gate_up HBM roofline, plus the T sweep."""
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    out = {"workload": "config 1: decode MoE layer, E=128, H=I=2880, top-4, uniform routing"}
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device)
+    sweep = {}
+    for t in (1, 8, 64, 256):
+        xs = syn.make_hidden(t, GPT_OSS_H, seed=args.seed + t, device=device)
+        ob = torch.empty((t, GPT_OSS_H), dtype=torch.bfloat16, device=device)
+        _, rb = ml.forward(xs, precision=args.precision)
+        u = int(torch.unique(rb.indices).numel())
+        fl = flush if t <= 8 else None
+        fn = lambda: ml.forward(xs, precision=args.precision, out=ob, path=args.path)  # noqa: E731
+        m = time_steps_flushed(fn, max(args.steps, 10), args.warmup, fl)
+        b = u * BYTES_PER_EXPERT + GPT_OSS_E * GPT_OSS_H * 2 + GPT_OSS_E * 2 + t * GPT_OSS_H * 4
+        sweep[str(t)] = {"tokens_per_s": t / (m / 1e3), "ms": m, "unique_experts": u, "layer_bytes": b,
+                         "layer_gbs": b / (m / 1e3) / 1e9, "layer_frac_hbm": b / (m / 1e3) / 1e9 / pk["hbm_gbs"],
+                         "l2": "flushed between steps" if fl is not None else "weights exceed L2"}
+        if t == 256:
+            stage = stage_pass(fn)
+            gu_ms = stage.get("gate_up", float("nan"))
+            bytes_gu = u * GATE_UP_BYTES_PER_EXPERT + t * TOP_K * GPT_OSS_H * 2
+            ach = bytes_gu / (gu_ms / 1e3) / 1e9
+            out.update({"tokens": t, "tokens_per_s": t / (m / 1e3), "ms_per_step": m, "stages_ms": stage,
+                        "roofline": {"bound": "hbm", "kernel": "gate_up (block-scaled tcgen05 MMA on packed E2M1, SwiGLU epilogue)",
+                                     "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": ach / pk["hbm_gbs"],
+                                     "peak_source": pk["source"], "algorithmic_bytes": bytes_gu, "unique_experts": u,
+                                     "traffic": PROFILED_GATE_UP_TRAFFIC.get("decode")},
+                        "layer_roofline": {"bytes": b, "achieved_gbs": b / (m / 1e3) / 1e9, "frac": b / (m / 1e3) / 1e9 / pk["hbm_gbs"]}})
+    out["sweep"] = sweep
+    return out
+
+
+def prefill_extras(args, ml_zipf, device, pk) -> dict:
+    """Config 2: T=4096 with the Zipf router bias, gate_up tensor-pipe fraction."""
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    T = 4096
+    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed + 2, device=device)
+    ob = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16, device=device)
+    fn = lambda: ml_zipf.forward(x, precision=args.precision, out=ob, path=args.path)  # noqa: E731
+    ms, launches = time_window(fn, args.steps, args.warmup, 1)
+    stage = stage_pass(fn)
+    _, rb = ml_zipf.forward(x, precision=args.precision)
+    counts = torch.bincount(rb.indices.flatten().long(), minlength=GPT_OSS_E)
+    gu_ms = stage.get("gate_up", float("nan"))
+    flops_gu = T * TOP_K * GATE_UP_FLOPS_PER_PAIR
+    ach = flops_gu / (gu_ms / 1e3) / 1e12
+    return {"workload": "config 2: prefill MoE layer, T=4096, E=128, H=I=2880, top-4, Zipf(1.1) router bias",
+            "tokens_per_s": T / (ms / 1e3), "ms_per_step": ms, "gpu_launches_per_step": launches, "stages_ms": stage,
+            "expert_rows": {"max": int(counts.max()), "min": int(counts.min()), "mean": float(counts.float().mean())},
+            "roofline": {"bound": "tensor", "kernel": "gate_up", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": ach / pk["bf16_tflops"], "frac_of_sustained": ach / pk["bf16_tflops_sustained"],
+                         "peak_source": pk["source"], "algorithmic_flops": flops_gu, "traffic": PROFILED_GATE_UP_TRAFFIC.get("prefill")},
+            "layer_tflops": T * FLOPS_PER_TOKEN / (ms / 1e3) / 1e12,
+            "layer_frac": T * FLOPS_PER_TOKEN / (ms / 1e3) / 1e12 / pk["bf16_tflops"]}
+
+
+def run_ep(args, world, rank, local):
+    """Config 3: 16 384 tokens shared evenly by the ranks (strong scaling); N=1 is the
+    whole layer on one GPU, N>1 shards the experts (expert parallelism)."""
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    device = torch.device("cuda", local)
+    pk = peaks()
+    T_total = args.tokens
+    if T_total % world:
+        raise SystemExit(f"--tokens {T_total} is not divisible by {world} ranks")
+    T = T_total // world
+    tensors = make_tensors(args.seed, device)  # same seed and generator: the same layer on every rank
+    x_all = syn.make_hidden(T_total, GPT_OSS_H, seed=args.seed, device=device)
+    x = x_all[rank * T : (rank + 1) * T].contiguous()
+    del x_all
+    zipf_tensors = with_router_bias(tensors, 1.1, args.seed)
+
+    if world == 1:
+        ml = layer_from(tensors, device)
+        ml_zipf = layer_from(zipf_tensors, device, packed=ml.packed)
+        out = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16, device=device)
+        fwd = lambda: ml.forward(x, precision=args.precision, out=out, path=args.path)  # noqa: E731
+        fwd_zipf = lambda: ml_zipf.forward(x, precision=args.precision, out=out, path=args.path)  # noqa: E731
+        e2e_fwd = lambda xd, yd: ml.forward(xd, precision=args.precision, out=yd, path=args.path)[0]  # noqa: E731
+        parallelism = "1 GPU"
+    else:
+        from kcapw_klcquant_b200.ep import ExpertParallelMoe
+
+        moe = ExpertParallelMoe(0, tensors, device, top_k=TOP_K, path=args.path)
+        moe_zipf = ExpertParallelMoe(0, zipf_tensors, device, top_k=TOP_K, path=args.path, share_local=moe)
+        fwd = lambda: moe.forward(x, precision=args.precision)  # noqa: E731
+        fwd_zipf = lambda: moe_zipf.forward(x, precision=args.precision)  # noqa: E731
+        e2e_fwd = lambda xd, yd: moe.forward(xd, precision=args.precision)[0]  # noqa: E731
+        parallelism = f"ep{world}: experts sharded {GPT_OSS_E // world} per GPU, {moe.exchange_name}"
+
+    clk = ClockSampler(local)
+    ms_local, launches = time_window(fwd, args.steps, args.warmup, world, clk)
+    ms = reduce_over_ranks(ms_local, world, "max")
+    ms_zipf = reduce_over_ranks(time_window(fwd_zipf, args.steps, args.warmup, world)[0], world, "max")
+    e2e_ms = reduce_over_ranks(time_e2e(e2e_fwd, x.cpu().pin_memory(), args.steps, args.warmup, world), world, "max")
+
+    # roofline of the dominant kernel: the gate_up grouped GEMM (tensor-bound at these sizes)
+    stage = stage_pass(fwd)
+    if world == 1:
+        pairs = T * TOP_K
+        ml.check_device_status()
+    else:
+        pairs = moe.last_received_rows()
+        moe.check_device_status()
+    gu_ms = stage.get("gate_up", float("nan"))
+    flops_gu = pairs * GATE_UP_FLOPS_PER_PAIR
+    ach = flops_gu / (gu_ms / 1e3) / 1e12
+    roof = {"bound": "tensor", "kernel": "gate_up grouped GEMM (block-scaled tcgen05 MMA, SwiGLU epilogue)" + (" of rank 0" if world > 1 else ""),
+            "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
+            "frac_of_sustained": ach / pk["bf16_tflops_sustained"], "peak_source": pk["source"], "algorithmic_flops": flops_gu,
+            "rows": pairs, "traffic": None}
+
+    # parity: N=1 against the CPU oracle on a token subsample; N>1 every rank's EP
+    # output against the single-GPU layer on the same tokens
+    if world == 1:
+        y, rb = ml.forward(x, precision=args.precision, path=args.path)
+        ys, _ = ml.forward(x, precision=args.precision, path="simt")
+        parity = {"vs_oracle": oracle_parity(tensors, x, y, rb.indices, rb.weights, 6) if not args.no_oracle else None,
+                  "vs_cuda_core_path": compare(y, ys)}
+    else:
+        y, _ = moe.forward(x, precision=args.precision)
+        full = layer_from(tensors, device)
+        yref, _ = full.forward(x, precision=args.precision, path=args.path)
+        m = compare(y, yref)
+        parity = {"vs_single_gpu_layer": {"cosine_min": reduce_over_ranks(m["cosine"], world, "min"),
+                                          "norm_max_abs_max": reduce_over_ranks(m["norm_max_abs"], world, "max"),
+                                          "bit_equal_frac_min": reduce_over_ranks(m["bit_equal_frac"], world, "min")}}
+        del full
+
+    line = base_line(args, world, T_total / (ms / 1e3), ms, launches,
+                     f"config 3: MoE layer over {T_total} tokens shared by {world} rank(s) ({T} each), E=128, H=I=2880, top-4, uniform routing",
+                     "strong", parallelism, {"l2": "layer weights (1.7 GB, 1.7/N GB per rank) exceed L2", "tokens_total": T_total})
+    line.update({
+        "roofline": roof,
+        "stages_ms": stage,
+        "layer_tflops": T_total * FLOPS_PER_TOKEN / (ms / 1e3) / 1e12,
+        "zipf": {"routing": "Zipf(1.1) router bias", "value": T_total / (ms_zipf / 1e3), "ms_per_step": ms_zipf},
+        "e2e": {"value": T_total / (e2e_ms / 1e3), "unit": "tokens/s",
+                "mode": "serving loop: per-step upload and read-back on copy streams, double-buffered",
+                "h2d_bytes_per_step": T_total * GPT_OSS_H * 2, "d2h_bytes_per_step": T_total * GPT_OSS_H * 2},
+        "parity": parity,
+        "clocks": clk.summary(),
+    })
+    if world == 1 and not args.no_extras:
+        line["decode"] = decode_extras(args, ml, device, pk)
+        line["prefill_c2"] = prefill_extras(args, ml_zipf, device, pk)
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = {k: v.cpu() for k, v in tensors.items()}
+        line["cpu_baseline"] = cpu_baseline(cpu, x.cpu())
+    if rank == 0:
+        print(json.dumps(line))
+
+
+def run_layer(args, world, rank, local):
+    """Configs 1 and 2 as single-GPU workloads (N>1: one independent replica per GPU)."""
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    device = torch.device("cuda", local)
+    pk = peaks()
+    decode = args.workload == "decode"
+    T = args.tokens
+    tensors = make_tensors(args.seed, device, zipf=None if decode else 1.1)
+    ml = layer_from(tensors, device)
+    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed + rank, device=device)
+    out = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16, device=device)
+    fwd = lambda: ml.forward(x, precision=args.precision, out=out, path=args.path)  # noqa: E731
+    clk = ClockSampler(local)
+    ms_local, launches = time_window(fwd, args.steps, args.warmup, world, clk)
+    ms = reduce_over_ranks(ms_local, world, "max")
+    e2e_ms = reduce_over_ranks(time_e2e(lambda xd, yd: ml.forward(xd, precision=args.precision, out=yd, path=args.path)[0],
+                                        x.cpu().pin_memory(), args.steps, args.warmup, world), world, "max")
+    stage = stage_pass(fwd)
+    ml.check_device_status()
+    wl = (f"config 1: decode MoE layer, T={T} tokens per GPU" if decode else f"config 2: prefill MoE layer, T={T}, Zipf(1.1) router bias") + ", E=128, H=I=2880, top-4"
+    line = base_line(args, world, world * T / (ms / 1e3), ms, launches, wl, "weak", f"replicas x{world}" if world > 1 else "1 GPU",
+                     {"l2": "weights (>=1.4 GB) exceed L2"})
+    gu_ms = stage.get("gate_up", float("nan"))
+    if decode:
+        _, rb = ml.forward(x, precision=args.precision)
+        u = int(torch.unique(rb.indices).numel())
+        b = u * GATE_UP_BYTES_PER_EXPERT + T * TOP_K * GPT_OSS_H * 2
+        ach = b / (gu_ms / 1e3) / 1e9
+        line["roofline"] = {"bound": "hbm", "kernel": "gate_up", "achieved": ach, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                            "frac": ach / pk["hbm_gbs"], "peak_source": pk["source"], "algorithmic_bytes": b, "unique_experts": u,
+                            "traffic": PROFILED_GATE_UP_TRAFFIC.get("decode") if T == 256 else None}
+    else:
+        f = T * TOP_K * GATE_UP_FLOPS_PER_PAIR
+        ach = f / (gu_ms / 1e3) / 1e12
+        line["roofline"] = {"bound": "tensor", "kernel": "gate_up", "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                            "frac": ach / pk["bf16_tflops"], "peak_source": pk["source"], "algorithmic_flops": f,
+                            "traffic": PROFILED_GATE_UP_TRAFFIC.get("prefill") if T == 4096 else None}
+    line.update({"stages_ms": stage, "clocks": clk.summary(),
+                 "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "mode": "serving loop, double-buffered copies",
+                         "h2d_bytes_per_step": T * GPT_OSS_H * 2, "d2h_bytes_per_step": T * GPT_OSS_H * 2}})
+    if rank == 0:
+        print(json.dumps(line))
 
 
 def run_reference(args, world, rank):
-    """Reference arm: the reference algorithm (CPU restatement) on the host cores, rank 0 only."""
+    """Reference arm: the reference algorithm (CPU restatement) on the host cores, rank 0
+    only, on the same workload's layer; each step a bounded sample of tokens."""
     if rank != 0:
         return
     from kcapw_klcquant_b200 import synthetic as syn
 
-    T = args.tokens
+    n_threads = use_all_host_threads()
     zipf = 1.1 if args.workload == "prefill" else None
-    layer = syn.make_layer(syn.GPT_OSS_120B, seed=args.seed, zipf=zipf, device="cpu")
-    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed, device="cpu")
+    tensors = make_tensors(args.seed, "cpu", zipf=zipf)
+    x = syn.make_hidden(64, GPT_OSS_H, seed=args.seed, device="cpu")
     n = 4
-    vals, r = [], {}
+    vals = []
     for i in range(args.warmup + args.steps):
-        r = cpu_baseline_sample(layer, x, n)
+        v = cpu_reference_sample(tensors, x[(i % 8) * n :], n, args.precision)
         if i >= args.warmup:
-            vals.append(r["value"])
+            vals.append(v)
     v = statistics.median(vals)
+    wl = {"ep": f"config 3: MoE layer over {args.tokens} tokens, E=128, H=I=2880, top-4, uniform routing",
+          "decode": f"config 1: decode MoE layer, T={args.tokens}, E=128, H=I=2880, top-4",
+          "prefill": f"config 2: prefill MoE layer, T={args.tokens}, Zipf(1.1), E=128, H=I=2880, top-4",
+          "stack": "config 4: 36-layer MoE stack, 32 sequences x 128 steps"}[args.workload]
     out = {
         "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": n / v * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"config {'1' if args.workload == 'decode' else '2'}: {args.workload} MoE layer, T={T}, E=128, H=I=2880, top-4",
-                   "cpu_sample_tokens": n},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port", "sample": r["sample"]},
+        "warmup": args.warmup, "ms_per_step": n / v * 1e3, "higher_is_better": True, "scaling": "strong" if args.workload == "ep" else "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": wl, "precision": args.precision, "cpu_sample_tokens_per_step": n},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": n_threads, "cpu_model": cpu_model(), "kind": "port",
+                         "sample": f"{n} tokens per step, one route() call per token restated in numpy (oracle/), experts dequantized beforehand (warm), "
+                                   f"matmul_precision {args.precision}, {n_threads} host threads"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out))
 
 
-def run_ours(args, world, rank, local):
-    from kcapw_klcquant_b200 import _lib
-    from kcapw_klcquant_b200 import synthetic as syn
-
-    device = torch.device("cuda", local)
-    T = args.tokens
-    ml = make_layer(args.workload, args.seed, device)
-    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed + rank, device=device)
-    pk = peaks()
-    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=device) if T <= 8 else None
-    out = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16, device=device)
-    fwd = lambda: ml.forward(x, precision=args.precision, out=out, path=args.path)  # noqa: E731
-
-    U = unique_experts(ml, x)
-    clk = ClockSampler(local)
-    times = time_steps(fwd, args.steps, args.warmup, flush, world, clk)
-    ms = max_over_ranks(sum(times) / len(times), world)
-    tokens_per_s = world * T / (ms / 1e3)
-
-    # stage breakdown (same workload, separate pass)
-    _lib.stage_timing(True)
-    stage = {}
-    for _ in range(3):
-        for _ in range(2):  # the first call keeps the GPU busy while the second's launches are issued
-            if flush is not None:
-                flush.add_(1)
-            fwd()
-        stage = _lib.stage_times()
-    _lib.stage_timing(False)
-    # end-to-end through the public API with host buffers
-    x_host = x.cpu().pin_memory()
-    e2e_ms = max_over_ranks(time_e2e(lambda xd, yd: ml.forward(xd, precision=args.precision, out=yd, path=args.path)[0],
-                                     x_host, args.steps, args.warmup, world), world)
-    ml.check_device_status()  # a kernel that gave up on a bounded wait would make every number above invalid
-
-    # roofline of the dominant kernel (gate_up GEMM for decode)
-    decode = args.workload == "decode"
-    if decode:
-        gu_ms = stage.get("gate_up", float("nan"))
-        bytes_gu = U * GATE_UP_BYTES_PER_EXPERT + T * TOP_K * GPT_OSS_H * 2
-        achieved = bytes_gu / (gu_ms / 1e3) / 1e9
-        roof = {"bound": "hbm", "kernel": "gate_up GEMM (MXFP4 dequant + SwiGLU epilogue)", "achieved": achieved, "peak": pk["hbm_gbs"],
-                "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "peak_source": pk["source"],
-                "traffic": PROFILED_GATE_UP_TRAFFIC.get("decode") if T == 256 else None,
-                "algorithmic_bytes": bytes_gu, "unique_experts": U}
-        layer_bytes = U * BYTES_PER_EXPERT + GPT_OSS_E * GPT_OSS_H * 2 + GPT_OSS_E * 2 + T * GPT_OSS_H * 4
-        layer_roof = {"bytes": layer_bytes, "achieved_gbs": layer_bytes / (ms / 1e3) / 1e9, "frac": layer_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"]}
-    else:
-        gu_ms = stage.get("gate_up", float("nan"))
-        flops_gu = 2 * T * TOP_K * GPT_OSS_H * 2 * GPT_OSS_I
-        achieved = flops_gu / (gu_ms / 1e3) / 1e12
-        roof = {"bound": "tensor", "kernel": "gate_up GEMM", "achieved": achieved, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": achieved / pk["bf16_tflops"], "peak_source": pk["source"], "algorithmic_flops": flops_gu,
-                "traffic": PROFILED_GATE_UP_TRAFFIC.get("prefill") if args.workload == "prefill" and T == 4096 else None}
-        layer_roof = {"flops": T * FLOPS_PER_TOKEN, "achieved_tflops": T * FLOPS_PER_TOKEN / (ms / 1e3) / 1e12}
-
-    result = {
-        "metric": "moe_layer_tokens_per_s",
-        "value": tokens_per_s,
-        "unit": "tokens/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded GPT-OSS-120B MXFP4 MoE layer, bf16 N(0,1) activations)",
-        "config": {
-            "workload": f"config {'1' if decode else '2'}: {args.workload} MoE layer, T={T} tokens per GPU, E=128, H=I=2880, top-4"
-                        + (", Zipf(1.1) router bias" if not decode else ""),
-            "precision": args.precision, "expert_path": args.path, "l2": "L2 flushed between steps" if flush is not None else "weights (>=1.4 GB) exceed L2",
-            "parallelism": f"replicas x{world}" if world > 1 else "1 GPU",
-        },
-        "roofline": roof,
-        "layer_roofline": layer_roof,
-        "stages_ms": stage,
-        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "mode": "serving loop: per-step upload and read-back on copy streams, double-buffered", "h2d_bytes_per_step": T * GPT_OSS_H * 2, "d2h_bytes_per_step": T * GPT_OSS_H * 2},
-        "gpu_launches": 7 * args.steps,
-        "clocks": clk.summary(),
-    }
-    if decode and args.sweep and world == 1:
-        sweep = {}
-        for t in (1, 8, 64, 256):
-            xs = syn.make_hidden(t, GPT_OSS_H, seed=args.seed + t, device=device)
-            ob = torch.empty((t, GPT_OSS_H), dtype=torch.bfloat16, device=device)
-            u = unique_experts(ml, xs)
-            tt = time_steps(lambda: ml.forward(xs, precision=args.precision, out=ob, path=args.path), max(args.steps, 5), args.warmup, flush if t <= 8 else None, 1)
-            m = sum(tt) / len(tt)
-            b = u * BYTES_PER_EXPERT + GPT_OSS_E * GPT_OSS_H * 2 + GPT_OSS_E * 2 + t * GPT_OSS_H * 4
-            sweep[str(t)] = {"tokens_per_s": t / (m / 1e3), "ms": m, "unique_experts": u, "layer_gbs": b / (m / 1e3) / 1e9,
-                             "layer_frac_hbm": b / (m / 1e3) / 1e9 / pk["hbm_gbs"]}
-        result["decode_sweep"] = sweep
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        p = ml.packed
-        layer_cpu = {
-            "model.layers.0.mlp.router.weight": ml.router_weight.cpu(), "model.layers.0.mlp.router.bias": ml.router_bias.cpu(),
-            "model.layers.0.mlp.experts.gate_up_proj_bias": ml.gate_up_bias.cpu(), "model.layers.0.mlp.experts.down_proj_bias": ml.down_bias.cpu(),
-            "model.layers.0.mlp.experts.gate_up_proj_blocks": p.gu_blocks.cpu(), "model.layers.0.mlp.experts.gate_up_proj_scales": p.gu_scales.cpu(),
-            "model.layers.0.mlp.experts.down_proj_blocks": p.dn_blocks.cpu(), "model.layers.0.mlp.experts.down_proj_scales": p.dn_scales.cpu(),
-        }
-        result["cpu_baseline"] = cpu_baseline_sample(layer_cpu, x.cpu(), 4)
-    if rank == 0:
-        print(json.dumps(result))
-
-
-def run_ep(args, world, rank, local):
-    """N > 1: experts sharded over the ranks (EP), NCCL all-to-all dispatch and combine."""
-    from kcapw_klcquant_b200 import synthetic as syn
-    from kcapw_klcquant_b200.ep import ExpertParallelMoe
-
-    device = torch.device("cuda", local)
-    strong = args.workload == "ep-prefill"
-    T = (args.tokens // world) if strong else args.tokens
-    zipf = 1.1 if (args.workload == "prefill" or args.zipf) else None
-    layer = syn.make_layer(syn.GPT_OSS_120B, seed=args.seed, zipf=zipf, device=device)  # same seed: same layer on every rank
-    moe = ExpertParallelMoe(0, layer, device, top_k=TOP_K, path=args.path)
-    del layer
-    torch.cuda.empty_cache()
-    x = syn.make_hidden(T, GPT_OSS_H, seed=args.seed + rank, device=device)
-    pk = peaks()
-    fwd = lambda: moe.forward(x, precision=args.precision)  # noqa: E731
-    clk = ClockSampler(local)
-    times = time_steps(fwd, args.steps, args.warmup, None, world, clk)
-    ms = max_over_ranks(sum(times) / len(times), world)
-    x_host = x.cpu().pin_memory()
-    e2e_ms = max_over_ranks(time_e2e(lambda xd, yd: moe.forward(xd, precision=args.precision)[0], x_host, args.steps,
-                                     args.warmup, world), world)
-    moe.check_device_status()
-    epr = GPT_OSS_E // world
-    layer_bytes = epr * BYTES_PER_EXPERT  # per rank: its experts' weights (all are routed to at these sizes)
-    result = {
-        "metric": "moe_layer_tokens_per_s",
-        "value": world * T / (ms / 1e3),
-        "unit": "tokens/s",
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms,
-        "higher_is_better": True,
-        "scaling": "strong" if strong else "weak",
-        "vs_baseline": None,
-        "dtype": "bf16",
-        "data": "synthetic (seeded GPT-OSS-120B MXFP4 MoE layer, bf16 N(0,1) activations)",
-        "config": {
-            "workload": (f"config 3: expert-parallel MoE layer, {args.tokens} tokens split over {world} ranks" if strong
-                         else f"config 1 layout, expert-parallel decode: T={T} tokens per GPU") + f", E=128 ({epr} per GPU), H=I=2880, top-4"
-                        + (", Zipf(1.1) router bias" if zipf else ", uniform routing"),
-            "precision": args.precision, "expert_path": args.path, "l2": "weights (>=210 MB per GPU) exceed L2",
-            "parallelism": f"ep{world} (NCCL all-to-all dispatch + combine)",
-        },
-        "roofline": {"bound": "hbm" if not strong else "tensor", "kernel": "whole EP layer step (per rank)",
-                     "achieved": layer_bytes / (ms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": layer_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"]},
-        "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s", "mode": "serving loop: per-step upload and read-back on copy streams, double-buffered", "h2d_bytes_per_step": T * GPT_OSS_H * 2,
-                "d2h_bytes_per_step": T * GPT_OSS_H * 2},
-        "gpu_launches": 11 * args.steps,
-        "clocks": clk.summary(),
-    }
-    if rank == 0:
-        print(json.dumps(result))
-
-
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["decode", "prefill", "ep-prefill"], default="decode")
-    ap.add_argument("--zipf", action="store_true", help="Zipf(1.1)-skewed router for the EP workloads")
+    ap.add_argument("--workload", choices=["ep", "decode", "prefill"], default="ep")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--path", choices=["auto", "simt", "tc"], default="auto")
     ap.add_argument("--seed", type=int, default=1)
-    ap.add_argument("--sweep", action="store_true", default=True)
-    ap.add_argument("--no-sweep", dest="sweep", action="store_false")
+    ap.add_argument("--no-extras", action="store_true", help="N=1: skip the decode and config-2 figures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-oracle", action="store_true", help="skip the CPU oracle parity subsample")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.tokens is None:
-        args.tokens = {"decode": 256, "prefill": 4096, "ep-prefill": 16384}[args.workload]
-    world, rank, local = dist_setup(use_gpu=args.impl != "reference",
-                                    force_group=(args.impl != "reference" and args.workload == "ep-prefill"))
+        args.tokens = {"decode": 256, "prefill": 4096, "ep": 16384, "stack": 32}[args.workload]
+    world, rank, local = dist_setup(use_gpu=args.impl != "reference")
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
-        elif world > 1 or args.workload == "ep-prefill":
+        elif args.workload == "ep":
             run_ep(args, world, rank, local)
         else:
-            run_ours(args, world, rank, local)
+            run_layer(args, world, rank, local)
     finally:
         import torch.distributed as dist
 

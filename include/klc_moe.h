@@ -73,6 +73,10 @@ const char* klc_last_error(void);
 int klc_capabilities(int* flags);
 /* Number of SMs of the current device (for host-side planning). */
 int klc_device_sm_count(int* out_sms);
+/* Kernels this library has launched in the process so far (all threads and
+ * devices; a launch that failed is counted too).  No reference counterpart:
+ * measurement support, e.g. launches per step.                            */
+int klc_launch_count(uint64_t* out);
 
 /* ---- MXFP4 dequant ---------------------------------------------------- *
  * Replaces dequantize_mxfp4_matrix(blocks, scales, dtype)

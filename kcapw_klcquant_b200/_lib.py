@@ -72,6 +72,7 @@ class KlcWeights(ctypes.Structure):
 SIGNATURES: dict[str, list] = {
     "klc_version": [],
     "klc_device_sm_count": [POINTER(c_int)],
+    "klc_launch_count": [POINTER(ctypes.c_uint64)],
     "klc_capabilities": [POINTER(c_int)],
     "klc_mxfp4_dequant": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p],
     "klc_mxfp4_transpose_scales": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
@@ -156,6 +157,13 @@ def require_cuda(*tensors: torch.Tensor | None) -> None:
             raise ValueError("kcapw_klcquant_b200 runs on CUDA devices only (no CPU fallback); got a CPU tensor")
         if t is not None and not t.is_contiguous():
             raise ValueError("kcapw_klcquant_b200 expects contiguous tensors")
+
+
+def launch_count() -> int:
+    """Kernels libklcmoe.so has launched in this process so far."""
+    n = ctypes.c_uint64(0)
+    check(lib().klc_launch_count(ctypes.byref(n)))
+    return int(n.value)
 
 
 STAGES = ("router", "permute", "gate_up", "down", "combine")

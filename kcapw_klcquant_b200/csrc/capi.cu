@@ -1,4 +1,5 @@
 // Status / error plumbing of the C ABI.
+#include <atomic>
 #include <cstdio>
 #include <string>
 
@@ -7,6 +8,9 @@
 namespace klc {
 
 static thread_local std::string g_last_error;
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
@@ -49,5 +53,11 @@ extern "C" int klc_device_sm_count(int* out_sms) {
   int dev = 0;
   KLC_CUDA(cudaGetDevice(&dev));
   KLC_CUDA(cudaDeviceGetAttribute(out_sms, cudaDevAttrMultiProcessorCount, dev));
+  return KLC_OK;
+}
+
+extern "C" int klc_launch_count(uint64_t* out) {
+  if (out == nullptr) return klc::fail(KLC_ERR_INVALID, "klc_launch_count: null output");
+  *out = klc::g_launches.load(std::memory_order_relaxed);
   return KLC_OK;
 }

@@ -19,6 +19,7 @@ namespace klc {
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
 int cuda_check(cudaError_t e, const char* what);
+void note_launch();
 
 #define KLC_CHECK_ARG(cond, msg)                               \
   do {                                                         \
@@ -31,8 +32,11 @@ int cuda_check(cudaError_t e, const char* what);
     if (_st != KLC_OK) return _st;                                  \
   } while (0)
 
+// Every kernel launch of the library is followed by this check, which also
+// counts the launch (klc_launch_count).
 #define KLC_LAUNCH_CHECK(what)                                      \
   do {                                                              \
+    ::klc::note_launch();                                           \
     int _st = ::klc::cuda_check(cudaGetLastError(), what);          \
     if (_st != KLC_OK) return _st;                                  \
   } while (0)

@@ -106,8 +106,12 @@ def _rows_as_bytes(t: torch.Tensor) -> torch.Tensor:
 class ExpertParallelMoe:
     """One MoE layer sharded over the ranks of ``group`` (E divisible by the world size)."""
 
+    exchange_name = "NCCL all_to_all_single dispatch and combine (split sizes synchronised through the host)"
+
     def __init__(self, layer_idx: int, tensors: dict[str, torch.Tensor], device, group=None, top_k: int = 4,
-                 path: str = "auto", backend=None):
+                 path: str = "auto", backend=None, share_local: "ExpertParallelMoe | None" = None):
+        """``share_local``: reuse another instance's resident local experts (same expert
+        weights, e.g. the same layer with another router bias)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -121,10 +125,15 @@ class ExpertParallelMoe:
         self.epr = E // self.world
         lo, hi = self.rank * self.epr, (self.rank + 1) * self.epr
         self.local_range = (lo, hi)
+        self._received = 0
         if backend is not None:
             self.backend = backend
             return
         dev = torch.device(device)
+        if share_local is not None:
+            self.backend = CudaBackend(share_local.backend.local, as_bf16(router_w, dev), as_bf16(tensors[f"{p}.router.bias"], dev),
+                                       self.top_k)
+            return
         e = f"{p}.experts"
         packed = PackedLayer.from_checkpoint_tensors(
             tensors[f"{e}.gate_up_proj_blocks"][lo:hi], tensors[f"{e}.gate_up_proj_scales"][lo:hi],
@@ -138,6 +147,10 @@ class ExpertParallelMoe:
         out = torch.empty((sum(recv_counts),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
         dist.all_to_all_single(out, send, output_split_sizes=recv_counts, input_split_sizes=send_counts, group=self.group)
         return out
+
+    def last_received_rows(self) -> int:
+        """(token, expert) pairs this rank's experts processed in the last forward."""
+        return int(self._received)
 
     def check_device_status(self) -> None:
         """Raise if a kernel of the last local expert call recorded a device-side fault (synchronises)."""
@@ -153,6 +166,7 @@ class ExpertParallelMoe:
         dist.all_to_all_single(recv_counts_t, send_counts, group=self.group)
         counts = torch.stack([send_counts, recv_counts_t]).cpu()  # one host sync for both split lists
         sc, rc = counts[0].tolist(), counts[1].tolist()
+        self._received = sum(rc)
         recv_rows = self._exchange(_rows_as_bytes(send_rows), sc, rc).view(send_rows.dtype).reshape(-1, send_rows.shape[1])
         recv_expert = self._exchange(send_expert, sc, rc)
         y_local = be.experts(recv_rows, recv_expert, precision)

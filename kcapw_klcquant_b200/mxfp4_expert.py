@@ -177,7 +177,10 @@ class DenseMatrixCache:
 
     def __init__(self, max_bytes: int) -> None:
         self.max_bytes = int(max_bytes)
-        self.items: OrderedDict[tuple[int, int, str], torch.Tensor] = OrderedDict()
+        # values: a dense matrix from load_expert_matrix, or None for a size-only
+        # entry recorded by touch()
+        self.items: OrderedDict[tuple[int, int, str], torch.Tensor | None] = OrderedDict()
+        self.sizes: dict[tuple[int, int, str], int] = {}
         self.pinned: set[tuple[int, int, str]] = set()
         self.current_bytes = 0
         self.stats = ExpertCacheStats()
@@ -187,7 +190,7 @@ class DenseMatrixCache:
         with self.lock:
             self.stats.lifetime_accesses += 1
             v = self.items.get(key)
-            if v is None:
+            if v is None:  # absent, or only a size-only entry: the caller materialises it
                 self.stats.misses += 1
                 return None
             self.items.move_to_end(key)
@@ -203,23 +206,52 @@ class DenseMatrixCache:
         if self.max_bytes <= 0:
             return
         with self.lock:
-            old = self.items.pop(key, None)
-            if old is not None:
-                self.current_bytes -= old.numel() * old.element_size()
+            if key in self.items:
+                self.items.pop(key)
+                self.current_bytes -= self.sizes.pop(key)
             self.items[key] = value
+            self.sizes[key] = nbytes
             self.current_bytes += nbytes
-            for victim in list(self.items):
-                if self.current_bytes <= self.max_bytes:
-                    break
-                if victim in self.pinned or victim == key:
-                    continue
-                t = self.items.pop(victim)
-                self.current_bytes -= t.numel() * t.element_size()
-                self.stats.evictions += 1
+            self._evict(key)
 
     def contains(self, key) -> bool:
         with self.lock:
             return key in self.items
+
+    def touch(self, key, nbytes: int) -> bool:
+        """Account one use of a dense matrix the fused kernels never materialise.
+
+        Counts a hit when ``key`` is resident (a real entry or an earlier
+        touch), else a miss that makes it resident as a size-only entry, with
+        least-recently-used eviction against the byte budget: the statistics a
+        dense cache of ``max_bytes`` would record for the same access sequence.
+        """
+        with self.lock:
+            self.stats.lifetime_accesses += 1
+            if key in self.items:
+                self.items.move_to_end(key)
+                self.stats.hits += 1
+                self.stats.hit_bytes += int(nbytes)
+                if key in self.pinned:
+                    self.stats.pinned_hits += 1
+                return True
+            self.stats.misses += 1
+            if self.max_bytes > 0:
+                self.items[key] = None
+                self.sizes[key] = int(nbytes)
+                self.current_bytes += int(nbytes)
+                self._evict(key)
+            return False
+
+    def _evict(self, keep) -> None:
+        for victim in list(self.items):
+            if self.current_bytes <= self.max_bytes:
+                break
+            if victim in self.pinned or victim == keep:
+                continue
+            self.items.pop(victim)
+            self.current_bytes -= self.sizes.pop(victim)
+            self.stats.evictions += 1
 
     def to_json(self) -> dict:
         s = self.stats
@@ -243,6 +275,18 @@ class DenseMatrixCache:
             "transfer_time_s": round(s.transfer_time_s, 6),
             "dequant_time_s": round(s.dequant_time_s, 6),
         }
+
+
+def account_expert_use(cache: DenseMatrixCache, layer_idx: int, expert_ids: list[int], hidden: int, intermediate: int,
+                       dtype: torch.dtype) -> None:
+    """One gate_up and one down lookup per expert, in selection order, as the
+    reference's _execute_mxfp4_experts makes them (streamed_moe_router.py:499-501),
+    sized as the dense [in, out] matrices of ``dtype`` it would cache."""
+    esize = torch.empty((), dtype=dtype).element_size()
+    dense = {"gate_up_proj": hidden * 2 * intermediate * esize, "down_proj": intermediate * hidden * esize}
+    for e in expert_ids:
+        for proj in ("gate_up_proj", "down_proj"):
+            cache.touch((int(layer_idx), int(e), proj), dense[proj])
 
 
 def _read_weight_map(support_dir: Path) -> dict[str, str]:
@@ -364,6 +408,21 @@ class Mxfp4ExpertStore:
         self.cache.stats.materializations += 1
         self.cache.put(key, matrix)
         return matrix
+
+    def note_expert_use(self, layer_idx: int, expert_ids: list[int]) -> None:
+        """Record that the fused kernels used these experts' gate_up and down matrices.
+
+        The reference's route() fetches both dense matrices of every selected
+        expert through load_expert_matrix (streamed_moe_router.py:499-501), and
+        its dynamic active-expert cap reads the cache statistics that produces
+        (:478-481).  Here the kernels read packed weights that are always
+        resident, so the same lookups are accounted without materialising
+        anything (DenseMatrixCache.touch): with a budget that holds the used
+        matrices the statistics equal the reference's; a smaller budget evicts
+        in least-recently-used order, where the reference scores its victims.
+        """
+        packed = self.layer(layer_idx)
+        account_expert_use(self.cache, layer_idx, expert_ids, packed.hidden, packed.intermediate, self.dtype)
 
     def protect_experts(self, layer_idx: int, expert_ids: list[int], protect_window: int | None = None) -> None:
         with self._lock:

@@ -263,10 +263,7 @@ class StreamedMoERouter:
         raw_experts = [int(v) for v in idx[0].tolist()]
         blocked = False
         if cfg.enabled:
-            lg = logits[0].float().cpu()
-            adjusted = self._apply_locality_bias(layer_idx, lg, resident_experts or set())
-            adj_top = self._topk_ids(adjusted, k)
-            experts, scores, blocked = self._guarded_expert_selection(lg, adjusted, raw_experts, adj_top, k)
+            raw_experts, experts, scores, blocked = self._locality_select(layer_idx, logits[0].float().cpu(), k, resident_experts or set())
             sc = torch.tensor(scores, dtype=torch.float32, device=dev).reshape(1, k)
             idx = torch.tensor([experts], dtype=torch.int32, device=dev)
             with torch.cuda.device(dev):
@@ -274,14 +271,8 @@ class StreamedMoERouter:
         else:
             experts = raw_experts
         weights_list = [float(v) for v in wts[0].float().tolist()]
-        adjusted_flag = experts != raw_experts
-        predicted = predicted_experts if predicted_experts is not None else self.predict_experts(layer_idx, k)
-        resident = sorted(int(v) for v in (resident_experts or set()))
-        self.stats.record_route(layer_idx, position, experts, weights_list, raw_experts, adjusted_flag,
-                                predicted_experts=[int(v) for v in predicted], resident_experts=resident, active_cap=k,
-                                blocked_adjustment=blocked)
-        self._update_sticky_scores(layer_idx, experts, weights_list)
-        self._update_workload_scores(layer_idx, experts, weights_list)
+        predicted, resident, adjusted_flag = self._record_route(layer_idx, position, experts, weights_list, raw_experts, blocked,
+                                                                predicted_experts, resident_experts, k)
 
         if execute_experts and expert_store is not None:
             before = self._cache_snapshot(expert_store)
@@ -291,6 +282,7 @@ class StreamedMoERouter:
             if gu_b is None or dn_b is None:
                 output, route = torch.zeros_like(hidden), {"experts": experts, "weights": weights_list, "mode": "mxfp4_missing_bias"}
             else:
+                expert_store.note_expert_use(layer_idx, experts)  # the reference's two load_expert_matrix calls per expert
                 layer = self._moe_layer(layer_idx, tensors, expert_store, k)
                 y, norms = layer.experts_forward(x, idx, wts, precision=self.matmul_precision, return_norms=True)
                 output = y.reshape(hidden.shape).to(hidden.dtype)
@@ -304,9 +296,7 @@ class StreamedMoERouter:
                         for i, e in enumerate(experts)
                     ],
                 }
-            after = self._cache_snapshot(expert_store)
-            self.stats.record_cache_delta(layer_idx, position, experts, before, after)
-            self._adapt_active_cap(layer_idx, position, before, after)
+            self._after_execution(layer_idx, position, experts, before, self._cache_snapshot(expert_store))
             route["raw_experts"] = raw_experts
             route["predicted_experts"] = [int(v) for v in predicted]
             route["resident_experts"] = resident
@@ -360,24 +350,55 @@ class StreamedMoERouter:
         return y, rb
 
     # ------------------------------------------------------------------
+    # host-side steps of route(), in the reference's order (:270-315)
+    # ------------------------------------------------------------------
+    def _locality_select(self, layer_idx: int, logits: torch.Tensor, k: int,
+                         resident_experts: set[int]) -> tuple[list[int], list[int], list[float], bool]:
+        """Raw top-k, locality bias, adjusted top-k and the semantic guard on one
+        token's fp32 logits [E] (a host tensor): (raw experts, experts, scores for
+        the softmax, blocked).  The top-k selections use torch.topk on the host
+        tensor, as the reference does (:271-273), so exact ties resolve as there."""
+        raw_experts = [int(e) for e in torch.topk(logits, k=k).indices.tolist()]
+        adjusted = self._apply_locality_bias(layer_idx, logits, resident_experts)
+        adj_top = [int(e) for e in torch.topk(adjusted, k=k).indices.tolist()]
+        experts, scores, blocked = self._guarded_expert_selection(logits, adjusted, raw_experts, adj_top, k)
+        return raw_experts, experts, scores, blocked
+
+    def _record_route(self, layer_idx: int, position: int, experts: list[int], weights: list[float], raw_experts: list[int],
+                      blocked: bool, predicted_experts: list[int] | None, resident_experts: set[int] | None, k: int):
+        """Statistics and sticky / workload state after a selection (:285-302):
+        returns (predicted experts, sorted resident experts, sticky_adjusted)."""
+        adjusted_flag = experts != raw_experts
+        predicted = predicted_experts if predicted_experts is not None else self.predict_experts(layer_idx, k)
+        resident = sorted(int(v) for v in (resident_experts or set()))
+        self.stats.record_route(layer_idx, position, experts, weights, raw_experts, adjusted_flag,
+                                predicted_experts=[int(v) for v in predicted], resident_experts=resident, active_cap=k,
+                                blocked_adjustment=blocked)
+        self._update_sticky_scores(layer_idx, experts, weights)
+        self._update_workload_scores(layer_idx, experts, weights)
+        return predicted, resident, adjusted_flag
+
+    def _after_execution(self, layer_idx: int, position: int, experts: list[int], before: dict, after: dict) -> None:
+        """Cache-delta statistics and the dynamic active-expert cap (:307-309)."""
+        self.stats.record_cache_delta(layer_idx, position, experts, before, after)
+        self._adapt_active_cap(layer_idx, position, before, after)
+
+    # ------------------------------------------------------------------
     # locality policy (host side, reference semantics :331-476)
     # ------------------------------------------------------------------
-    @staticmethod
-    def _topk_ids(values: torch.Tensor, k: int) -> list[int]:
-        order = sorted(range(values.numel()), key=lambda e: (-float(values[e]), e))
-        return order[:k]
-
     def _apply_locality_bias(self, layer_idx: int, logits: torch.Tensor, resident_experts: set[int]) -> torch.Tensor:
+        """Sticky bonus, hot-expert mask and cache-aware bonus (:331-363), with the
+        reference's fp32 tensor arithmetic for the thresholds and bonuses."""
         cfg = self.locality_config
         if not cfg.enabled:
             return logits
         adjusted = logits.clone()
-        k = min(self.experts_per_token, logits.numel())
-        top_ids = self._topk_ids(logits, k)
-        floor = float(logits[top_ids[-1]]) - abs(float(cfg.sticky_candidate_margin))
+        raw_k = min(self.experts_per_token, logits.numel())
+        raw_top = torch.topk(logits, k=raw_k)
+        floor = raw_top.values[-1] - abs(float(cfg.sticky_candidate_margin))  # fp32, as the reference
         scores = self.sticky_scores.get(layer_idx, {})
         if scores and cfg.sticky_strength > 0:
-            eligible = [int(e) for e in scores if float(logits[int(e)]) >= floor]
+            eligible = [int(e) for e in scores if logits[int(e)] >= floor]
             if eligible:
                 ids = torch.tensor(eligible, dtype=torch.long)
                 bonus = torch.tensor([scores[e] for e in eligible], dtype=logits.dtype) * float(cfg.sticky_strength)
@@ -385,14 +406,15 @@ class StreamedMoERouter:
                     bonus = torch.clamp(bonus, max=float(cfg.max_sticky_bonus))
                 adjusted[ids] += bonus
         if cfg.max_hot_experts_per_layer > 0 and len(scores) >= cfg.max_hot_experts_per_layer:
-            hot = set(sorted(scores, key=scores.get, reverse=True)[: cfg.max_hot_experts_per_layer])
-            allowed = hot | set(top_ids[: max(1, self.experts_per_token // 2)])
+            hot = set(int(e) for e in sorted(scores, key=scores.get, reverse=True)[: cfg.max_hot_experts_per_layer])
+            top_ids = raw_top.indices.tolist()
+            allowed = hot | {int(e) for e in top_ids[: max(1, self.experts_per_token // 2)]}
             mask = torch.ones_like(adjusted, dtype=torch.bool)
-            mask[sorted(allowed)] = False
+            mask[list(allowed)] = False
             adjusted[mask] -= abs(float(cfg.exploration_margin))
         if resident_experts and cfg.cache_aware_strength > 0:
             ids = torch.tensor(sorted(resident_experts), dtype=torch.long)
-            threshold = float(torch.max(logits)) - abs(float(cfg.exploration_margin))
+            threshold = torch.max(logits) - abs(float(cfg.exploration_margin))
             eligible = ids[logits[ids] >= threshold]
             if eligible.numel() > 0:
                 adjusted[eligible] += float(cfg.cache_aware_strength)

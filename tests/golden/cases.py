@@ -19,7 +19,40 @@ ROUTE_CASES = {
     "mini_e8_h64_t5_k2": (8, 64, 64, 2, 5, 13, None, 0, True),
     "mini_e8_h128_i192_t6": (8, 128, 192, 4, 6, 14, None, 0, True),
     "tie_e16_h64_t24": (16, 64, 64, 4, 24, 15, None, 4, False),
+    # full layout with more than 12 rows per expert: the tensor-core path's 64-row tiles
+    "mid_e8_h2880_t48": (8, 2880, 2880, 4, 48, 16, None, 0, False),
+    "mid_zipf_e16_h2880_t64": (16, 2880, 2880, 4, 64, 17, 1.1, 0, False),
 }
+
+# Locality-policy cases (the reference's route() with RoutingLocalityConfig on):
+# name -> (E, H, I, k, T, seed, execute_experts, config kwargs or None for the default config)
+LOCALITY_CASES = {
+    "loc_full_e16_h256_t32": (16, 256, 256, 4, 32, 51, True,
+                              dict(enabled=True, sticky_strength=2.0, semantic_guard=True, min_raw_overlap=2, max_sticky_bonus=0.25,
+                                   max_hot_experts_per_layer=6, exploration_margin=0.25, cache_aware_strength=0.3,
+                                   predictive_prefetch=True, dynamic_active_expert_cap=True, active_experts_per_token_cap=3,
+                                   min_active_experts_per_token=2, max_active_experts_per_token=4)),
+    "loc_noguard_e16_h256_t32": (16, 256, 256, 4, 32, 52, False,
+                                 dict(enabled=True, sticky_strength=1.0, semantic_guard=False, max_hot_experts_per_layer=4,
+                                      exploration_margin=0.5, predictive_prefetch=True)),
+    "loc_default_e16_h256_t12": (16, 256, 256, 4, 12, 53, True, None),
+}
+
+
+def correlated_hidden(T: int, H: int, seed: int) -> torch.Tensor:
+    """bf16 [T, H] token sequence whose neighbours are correlated (x_t = 0.8 x_{t-1} + 0.6 noise),
+    so sticky experts carry over between positions."""
+    g = torch.Generator().manual_seed(seed + 31337)
+    x = torch.randn((T, H), generator=g, dtype=torch.float32)
+    for t in range(1, T):
+        x[t] = 0.8 * x[t - 1] + 0.6 * x[t]
+    return x.to(torch.bfloat16)
+
+
+def resident_set(t: int, previous_experts: list[int]) -> set[int]:
+    """Experts a cache-aware caller reports resident at position t: the previous
+    token's experts plus experts 0 and 1."""
+    return set(int(e) for e in previous_experts) | {0, 1}
 
 
 def tie_layer(layer: dict[str, torch.Tensor], tie_rows: int, seed: int) -> None:

@@ -13,6 +13,9 @@ functions return:
 * ``dequantize_mxfp4_matrix``        (klcquant mxfp4_expert.py:357-379)
 * ``StreamedMoERouter.route``        (klcquant streamed_moe_router.py:257-329), per token, both
   ``matmul_precision`` values, through ``Mxfp4ExpertStore`` (mxfp4_expert.py:382-525)
+* ``StreamedMoERouter.route`` with ``RoutingLocalityConfig`` enabled (streamed_moe_router.py:12-35,
+  331-476) on correlated token sequences: per-token routing dicts and the final
+  ``RouterStats.to_json()`` (:38-235)
 * ``rms_norm``                       (klcquant streamed_attention.py:27-28)
 * ``RuntimeDequantizer.dequantize``  (klcquant runtime_dequantizer.py:30-52) on artefacts made by
   ``quantize_for_storage`` / ``prune_for_storage`` (adaptive_quantizer.py:123-143, tensor_pruner.py:46-59)
@@ -37,7 +40,7 @@ REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
 
 from kcapw_klcquant_b200 import synthetic as syn  # noqa: E402
-from tests.golden.cases import ROUTE_CASES, tie_layer  # noqa: E402
+from tests.golden.cases import LOCALITY_CASES, ROUTE_CASES, correlated_hidden, resident_set, tie_layer  # noqa: E402
 
 def bf16_bits(t: torch.Tensor) -> np.ndarray:
     return t.detach().to(torch.bfloat16).contiguous().view(torch.int16).numpy().view(np.uint16).copy()
@@ -144,6 +147,37 @@ def run_route_case(mx, rt, name: str, spec) -> None:
     np.savez_compressed(HERE / f"route_{name}.npz", **out)
 
 
+def run_locality_case(mx, rt, name: str, spec) -> None:
+    E, H, I, k, T, seed, execute, cfg_kw = spec
+    dims = syn.LayerDims(E, H, I, k)
+    layer = syn.make_layer(dims, seed)
+    x = correlated_hidden(T, H, seed)
+    tensors = syn.dense_tensors(layer)
+    cfg = rt.RoutingLocalityConfig(**cfg_kw) if cfg_kw is not None else None
+    out: dict[str, np.ndarray] = {"meta": np.array([E, H, I, k, T, seed, int(execute)], dtype=np.int64)}
+    logits = torch.nn.functional.linear(x, tensors["model.layers.0.mlp.router.weight"], tensors["model.layers.0.mlp.router.bias"])
+    out["logits"] = bf16_bits(logits)
+    with tempfile.TemporaryDirectory() as d:
+        root = Path(d)
+        write_checkpoint(layer, root)
+        store = mx.Mxfp4ExpertStore(root, root, torch.device("cpu"), dtype=torch.bfloat16, cache_bytes=1 << 40) if execute else None
+        router = rt.StreamedMoERouter(experts_per_token=k, swiglu_limit=7.0, locality_config=cfg, matmul_precision="bf16")
+        routes, ys = [], []
+        prev: list[int] = []
+        for t in range(T):
+            resident = resident_set(t, prev) if cfg is not None else None
+            y, route = router.route(0, x[t], tensors, store, execute, t, resident_experts=resident)
+            prev = [int(e) for e in route["experts"]]
+            ys.append(y)
+            routes.append({key: route.get(key) for key in ("experts", "raw_experts", "weights", "sticky_adjusted", "predicted_experts",
+                                                          "resident_experts", "active_expert_cap", "mode")})
+        out["out"] = bf16_bits(torch.stack(ys))
+        out["routes_json"] = np.array(json.dumps(routes))
+        out["stats_json"] = np.array(json.dumps(router.stats.to_json()))
+        out["dynamic_caps_json"] = np.array(json.dumps({str(a): b for a, b in router.dynamic_caps.items()}))
+    np.savez_compressed(HERE / f"locality_{name}.npz", **out)
+
+
 def make_rmsnorm_fixture(at) -> None:
     out = {}
     for H, T, seed in ((2880, 4, 21), (128, 7, 22)):
@@ -202,6 +236,10 @@ def main() -> None:
     for name, spec in ROUTE_CASES.items():
         if only is None or name in only:
             run_route_case(mx, rt, name, spec)
+            print("wrote", name, flush=True)
+    for name, spec in LOCALITY_CASES.items():
+        if only is None or name in only:
+            run_locality_case(mx, rt, name, spec)
             print("wrote", name, flush=True)
 
 

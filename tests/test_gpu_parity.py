@@ -324,21 +324,54 @@ def test_store_load_expert_matrix_matches_dequant(case_cache):
     assert store.resident_experts(0) == set(range(dims.experts))
 
 
-def test_locality_route_guard(case_cache):
-    """Locality policy on: host policy over device logits, experts still on device."""
+@pytest.mark.parametrize("name", list(cases.LOCALITY_CASES))
+def test_locality_route_vs_reference(golden_dir, name):
+    """route() with the locality policy on the device path against the reference's
+    route() on the same token sequence: routing dicts, outputs and to_json()."""
+    import json
+
     from kcapw_klcquant_b200 import Mxfp4ExpertStore, RoutingLocalityConfig, StreamedMoERouter
     from kcapw_klcquant_b200 import synthetic as syn
 
-    fx, dims, layer, x, ml = load(case_cache, "mini_e16_h256_t32")
-    store = Mxfp4ExpertStore.from_layers({0: layer}, DEV)
-    cfg = RoutingLocalityConfig(enabled=True, sticky_strength=2.0, semantic_guard=True, min_raw_overlap=3, predictive_prefetch=True)
-    router = StreamedMoERouter(dims.top_k, 7.0, cfg, matmul_precision="bf16")
-    tensors = {k: v.to(DEV) for k, v in syn.dense_tensors(layer).items()}
-    for t in range(8):
-        y, route = router.route(0, x[t].to(DEV), tensors, store, True, t)
-        assert len(set(route["experts"]) & set(route["raw_experts"])) >= 3
-        assert torch.isfinite(y.float()).all()
-    assert router.stats.to_json()["locality"]["prediction_accuracy"]["sample_count"] > 0
+    E, H, I, k, T, seed, execute, cfg_kw = cases.LOCALITY_CASES[name]
+    fx = np.load(golden_dir / f"locality_{name}.npz")
+    ref_routes = json.loads(str(fx["routes_json"]))
+    layer = syn.make_layer(syn.LayerDims(E, H, I, k), seed)
+    x = cases.correlated_hidden(T, H, seed).to(DEV)
+    store = Mxfp4ExpertStore.from_layers({0: layer}, DEV, cache_bytes=1 << 40) if execute else None
+    cfg = RoutingLocalityConfig(**cfg_kw) if cfg_kw is not None else None
+    router = StreamedMoERouter(k, 7.0, cfg, matmul_precision="bf16")
+    tensors = {kk: v.to(DEV) for kk, v in syn.dense_tensors(layer).items()}
+    w_r, b_r = tensors["model.layers.0.mlp.router.weight"], tensors["model.layers.0.mlp.router.bias"]
+    from kcapw_klcquant_b200 import _lib
+
+    prev: list[int] = []
+    for t in range(T):
+        # the device logits of this token; the comparison holds while they equal the reference's
+        lg = torch.empty((1, E), dtype=torch.bfloat16, device=DEV)
+        idx = torch.empty((1, k), dtype=torch.int32, device=DEV)
+        w = torch.empty((1, k), dtype=torch.bfloat16, device=DEV)
+        _lib.check(_lib.lib().klc_router_topk(x[t : t + 1].contiguous().data_ptr(), 1, H, w_r.data_ptr(), b_r.data_ptr(), E, k, None,
+                                              idx.data_ptr(), w.data_ptr(), lg.data_ptr(), _lib.stream_ptr()))
+        if not np.array_equal(bits_of(lg)[0], fx["logits"][t]):
+            assert parity.ulp_distance_bf16(bits_of(lg)[0], fx["logits"][t]).max() <= 1
+            assert t >= T // 2, f"device logits left the reference's at token {t}"
+            return
+        resident = cases.resident_set(t, prev) if cfg is not None else None
+        y, route = router.route(0, x[t], tensors, store, execute, t, resident_experts=resident)
+        ref = ref_routes[t]
+        for key in ("experts", "raw_experts", "weights", "sticky_adjusted", "mode"):
+            assert route.get(key) == ref[key], (t, key, route.get(key), ref[key])
+        if execute:
+            assert route["predicted_experts"] == ref["predicted_experts"] and route["active_expert_cap"] == ref["active_expert_cap"]
+        parity.assert_output_close(bits_of(y.reshape(1, -1)), fx["out"][t : t + 1], f"{name} t={t}")
+        prev = [int(e) for e in route["experts"]]
+    ref_stats = json.loads(str(fx["stats_json"]))
+    got = json.loads(json.dumps(router.stats.to_json()))
+    assert got["routed_tokens"] == ref_stats["routed_tokens"]
+    assert got["locality"]["dynamic_cap_events"] == ref_stats["locality"]["dynamic_cap_events"]
+    assert got["route_events"] == ref_stats["route_events"]
+    assert got["cache_delta_events"] == ref_stats["cache_delta_events"]
 
 
 # ---------------------------------------------------------------------------
