@@ -478,3 +478,43 @@ def test_full_size_determinism_and_paths(big_layer, T):
         big_layer.check_device_status()
         assert torch.equal(rb3.indices, rb1.indices)
         parity.assert_output_close(bits_of(y3), bits_of(y1), f"tc vs simt T={T}")
+
+
+# ---------------------------------------------------------------------------
+# the benchmark configurations themselves against the oracle (token subsample)
+# ---------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("T,zipf,seed", [(256, None, 1), (4096, 1.1, 2)])
+def test_bench_configs_subsample_vs_oracle(T, zipf, seed, path):
+    """Config 1 (decode T=256, uniform) and config 2 (prefill T=4096, Zipf(1.1)
+    router) on the full 120B layout: every 4th / 64th token of the batch against
+    the oracle on the device's own routing.  At these sizes the tensor-core path
+    runs its 16-row (T=256) and 64-row (T=4096, skewed groups) tiles."""
+    from kcapw_klcquant_b200 import MoeLayer
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    layer = syn.make_layer(syn.GPT_OSS_120B, seed=seed, zipf=zipf, device=DEV)
+    ml = MoeLayer.from_tensors(0, layer, DEV, top_k=4)
+    x = syn.make_hidden(T, 2880, seed=seed, device=DEV)
+    y, rb = ml.forward(x, precision="bf16", path=path)
+    ml.check_device_status()
+    counts = torch.bincount(rb.indices.flatten().long(), minlength=128)
+    if zipf is not None:
+        assert int(counts.max()) > 3 * float(counts.float().mean())  # skewed, load-imbalanced groups
+    sample = torch.arange(0, T, T // 64, device=DEV)
+    sel = rb.indices[sample].cpu().numpy()
+    used = np.unique(sel)
+    p = "model.layers.0.mlp.experts"
+    host = {n: layer[f"{p}.{n}"][torch.from_numpy(used).to(DEV).long()].cpu().numpy()
+            for n in ("gate_up_proj_blocks", "gate_up_proj_scales", "down_proj_blocks", "down_proj_scales")}
+    ex = orc.DenseExperts(host["gate_up_proj_blocks"], host["gate_up_proj_scales"], host["down_proj_blocks"], host["down_proj_scales"],
+                          max_cached=1)
+    remap = np.zeros(128, np.int64)
+    remap[used] = np.arange(used.size)
+    want = orc.moe_layer(bits_of(x[sample]), remap[sel], bits_of(rb.weights[sample]), ex,
+                         bits_of(layer[f"{p}.gate_up_proj_bias"])[used], bits_of(layer[f"{p}.down_proj_bias"])[used], "bf16")
+    m = parity.assert_output_close(bits_of(y[sample]), want, f"T={T} zipf={zipf} {path}")
+    if path == "simt":
+        assert m["bit_equal_frac"] >= 0.99, m
