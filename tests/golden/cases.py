@@ -24,6 +24,11 @@ ROUTE_CASES = {
     "mid_zipf_e16_h2880_t64": (16, 2880, 2880, 4, 64, 17, 1.1, 0, False),
 }
 
+# Cases at the full GPT-OSS layout (H = I = 2880): routing and outputs checked on
+# a token subsample by the CPU oracle tests (each token touches ~25 M weights).
+FULL_LAYOUT_CASES = [n for n, spec in ROUTE_CASES.items() if spec[1] >= 2880]
+SMALL_LAYOUT_CASES = [n for n in ROUTE_CASES if n not in FULL_LAYOUT_CASES]
+
 # Locality-policy cases (the reference's route() with RoutingLocalityConfig on):
 # name -> (E, H, I, k, T, seed, execute_experts, config kwargs or None for the default config)
 LOCALITY_CASES = {

@@ -19,7 +19,7 @@ from tests.golden import cases
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda", 0)
-SMALL_CASES = [n for n in cases.ROUTE_CASES if not n.startswith("c")]
+SMALL_CASES = cases.SMALL_LAYOUT_CASES
 ALL_CASES = list(cases.ROUTE_CASES)
 
 

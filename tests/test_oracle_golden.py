@@ -13,8 +13,8 @@ from oracle import moe_oracle as orc
 from tests import parity
 from tests.golden import cases
 
-SMALL_CASES = [n for n in cases.ROUTE_CASES if not n.startswith("c")]
-BIG_CASES = [n for n in cases.ROUTE_CASES if n.startswith("c")]
+SMALL_CASES = cases.SMALL_LAYOUT_CASES
+BIG_CASES = cases.FULL_LAYOUT_CASES
 
 
 def _fixture_exists(name):
@@ -134,7 +134,7 @@ def test_bias_only_path(name):
 @pytest.mark.slow
 @pytest.mark.parametrize("name", BIG_CASES)
 def test_full_size_layer(name):
-    """Config-0/1 layouts (H = I = 2880): routing exact, outputs within tolerance."""
+    """Full layouts (H = I = 2880): routing exact modulo ties, outputs within tolerance."""
     fx, dims, layer, x = _route_case(name)
     lg = orc.bf16_bits_to_f32(fx["logits"])
     idx, _ = orc.select_topk(lg, dims.top_k)
