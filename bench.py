@@ -556,8 +556,9 @@ def run_ep(args, world, rank, local):
     else:
         from kcapw_klcquant_b200.ep import ExpertParallelMoe
 
-        moe = ExpertParallelMoe(0, tensors, device, top_k=TOP_K, path=args.path)
-        moe_zipf = ExpertParallelMoe(0, zipf_tensors, device, top_k=TOP_K, path=args.path, share_local=moe)
+        moe = ExpertParallelMoe(0, tensors, device, top_k=TOP_K, path=args.path, exchange=args.exchange, max_tokens=T)
+        moe_zipf = ExpertParallelMoe(0, zipf_tensors, device, top_k=TOP_K, path=args.path, share_local=moe, exchange=args.exchange,
+                                     max_tokens=T)
         fwd = lambda: moe.forward(x, precision=args.precision)  # noqa: E731
         fwd_zipf = lambda: moe_zipf.forward(x, precision=args.precision)  # noqa: E731
         e2e_fwd = lambda xd, yd: moe.forward(xd, precision=args.precision)[0]  # noqa: E731
@@ -601,6 +602,8 @@ def run_ep(args, world, rank, local):
                                           "norm_max_abs_max": reduce_over_ranks(m["norm_max_abs"], world, "max"),
                                           "bit_equal_frac_min": reduce_over_ranks(m["bit_equal_frac"], world, "min")}}
         del full
+        moe_zipf.close()
+        moe.close()
 
     line = base_line(args, world, T_total / (ms / 1e3), ms, launches,
                      f"config 3: MoE layer over {T_total} tokens shared by {world} rank(s) ({T} each), E=128, H=I=2880, top-4, uniform routing",
@@ -720,6 +723,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true", help="N=1: skip the decode and config-2 figures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-oracle", action="store_true", help="skip the CPU oracle parity subsample")
+    ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p", help="N>1: the expert-parallel exchange")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -293,6 +293,62 @@ int klc_ep_pack(const int32_t* idx, int64_t tokens, int k, int64_t experts_per_r
                 int64_t hidden, uint16_t* send_rows, int32_t* send_expert, int32_t* send_counts, int32_t* pair_pos,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- expert parallelism over NVLink peer memory ------------------------
+ * No counterpart in the reference (one process, one device): the node-level
+ * sharding of the MoE block, rank r owning experts [r*epr, (r+1)*epr).  One
+ * handle per rank (one process per GPU).  Each handle owns an exchange arena
+ * in its device's memory (cudaMalloc'd by klc_ep_create, freed by
+ * klc_ep_destroy; klc_ep_arena_bytes reports the size: two row buffers of
+ * world * max_tokens * top_k * hidden bf16 plus small tables) that the other
+ * ranks map through CUDA IPC.  Setup: klc_ep_create on every rank ->
+ * klc_ep_ipc_handle (64 bytes) -> exchange the handles between the ranks by
+ * any host transport -> klc_ep_connect with all handles in rank order.
+ * Per forward, on every rank, in the same order: klc_ep_dispatch ->
+ * klc_ep_experts -> klc_ep_combine (or klc_ep_forward for all of it, router
+ * included).  Stream-ordered; no host synchronisation; kernels of different
+ * ranks signal each other through flags in the arenas with bounded waits
+ * (klc_ep_set_wait_limit_ns, default 10 s; an expired wait is reported by
+ * klc_ep_status as KLC_ERR_DEVICE_TIMEOUT).  A handle serves one stream of
+ * one host thread at a time.  Before klc_ep_destroy every rank must have
+ * finished its last forward (a host barrier): peers write into the arena.
+ *
+ * klc_ep_dispatch: idx int32 [T,k] (global expert ids), x bf16 [T,H]; sends
+ *   every (token, slot) pair's row to its owner and writes pair_slot int32
+ *   [T*k] (where its expert output will come back; input of klc_ep_combine).
+ * klc_ep_experts: the local experts (klc_moe_weights of this rank's experts,
+ *   dims {_, H, I, epr, _, path}) on every row received, outputs sent back.
+ * klc_ep_combine: waits for the returned rows, then the weighted bf16 combine
+ *   in top-k order (klc_moe_combine), optional residual, optional fused
+ *   next-layer RMSNorm (norm_w/normed as klc_moe_combine_rmsnorm).
+ * Workspace (caller-owned, shared by the three calls): klc_ep_workspace_size. */
+typedef struct klc_ep klc_ep;
+int klc_ep_create(int rank, int world, int64_t max_tokens, int top_k, int64_t hidden, int64_t experts_per_rank,
+                  klc_ep** out);
+int klc_ep_arena_bytes(const klc_ep* h, size_t* out_bytes);
+int klc_ep_ipc_handle(const klc_ep* h, void* out_64_bytes);
+int klc_ep_connect(klc_ep* h, const void* handles_world_x_64_bytes);
+int klc_ep_set_wait_limit_ns(klc_ep* h, uint64_t ns);
+int klc_ep_workspace_size(const klc_ep* h, const klc_moe_dims* local_dims, size_t* out_bytes);
+int klc_ep_dispatch(klc_ep* h, const int32_t* idx, int64_t tokens, const uint16_t* x, int32_t* pair_slot, void* workspace,
+                    size_t workspace_bytes, void* stream);
+int klc_ep_experts(klc_ep* h, const klc_moe_dims* local_dims, const klc_moe_weights* local_wts, int precision,
+                   void* workspace, size_t workspace_bytes, void* stream);
+int klc_ep_combine(klc_ep* h, const int32_t* pair_slot, const uint16_t* w, int64_t tokens, const uint16_t* residual,
+                   const uint16_t* norm_w, float eps, uint16_t* out, uint16_t* normed, void* stream);
+/* Router (klc_router_topk over all epr*world experts) + dispatch + experts +
+ * combine: one expert-parallel MoE layer forward on this rank's tokens.     */
+int klc_ep_forward(klc_ep* h, const klc_moe_dims* local_dims, const klc_moe_weights* local_wts, const uint16_t* router_w,
+                   const uint16_t* router_b, const uint16_t* x, int64_t tokens, int precision, const uint16_t* residual,
+                   const uint16_t* norm_w, float eps, uint16_t* out, uint16_t* normed, int32_t* out_idx, uint16_t* out_w,
+                   int32_t* pair_slot, void* workspace, size_t workspace_bytes, void* stream);
+/* Device status of the exchange (bounded waits, counts) and of the last
+ * dispatch / local-expert index checks in `workspace` (may be NULL);
+ * synchronises `stream` and clears the arena's word.                       */
+int klc_ep_status(klc_ep* h, const void* workspace, int* code, int* where, void* stream);
+/* Rows this rank received in its last dispatch (sum over sources; synchronises). */
+int klc_ep_received_rows(klc_ep* h, int64_t* out, void* stream);
+int klc_ep_destroy(klc_ep* h);
+
 /* RMSNorm (streamed_attention.py:27-28): y = bf16(bf16(x * bf16(rsqrt(mean(x^2)+eps))) * w). */
 int klc_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, int64_t hidden, float eps, uint16_t* y,
                  void* stream);

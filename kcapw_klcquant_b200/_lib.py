@@ -97,6 +97,20 @@ SIGNATURES: dict[str, list] = {
     "klc_workspace_status": [c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int), c_void_p],
     "klc_stage_timing": [c_int],
     "klc_stage_times": [POINTER(c_float), c_int, POINTER(c_int)],
+    "klc_ep_create": [c_int, c_int, c_int64, c_int, c_int64, c_int64, POINTER(c_void_p)],
+    "klc_ep_arena_bytes": [c_void_p, POINTER(c_size_t)],
+    "klc_ep_ipc_handle": [c_void_p, c_void_p],
+    "klc_ep_connect": [c_void_p, c_void_p],
+    "klc_ep_set_wait_limit_ns": [c_void_p, ctypes.c_uint64],
+    "klc_ep_workspace_size": [c_void_p, POINTER(KlcDims), POINTER(c_size_t)],
+    "klc_ep_dispatch": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
+    "klc_ep_experts": [c_void_p, POINTER(KlcDims), POINTER(KlcWeights), c_int, c_void_p, c_size_t, c_void_p],
+    "klc_ep_combine": [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p],
+    "klc_ep_forward": [c_void_p, POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
+                       c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
+    "klc_ep_status": [c_void_p, c_void_p, POINTER(c_int), POINTER(c_int), c_void_p],
+    "klc_ep_received_rows": [c_void_p, POINTER(c_int64), c_void_p],
+    "klc_ep_destroy": [c_void_p],
     "klc_rms_norm": [c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p, c_void_p],
     "klc_runtime_dequant": [c_int, c_void_p, c_int, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_int, c_void_p],
 }

@@ -109,19 +109,11 @@ int validate_weights(const klc_moe_weights* w) {
   return KLC_OK;
 }
 
-// Permute, expert GEMMs and combine for given routing; `post` (or null) fuses
-// the next layer's input RMSNorm into the combine.
-static int run_experts_post(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx,
-                            const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
-                            const PostNorm* post, char* ws, const WorkspaceLayout& L, cudaStream_t stream) {
+int run_expert_stage(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx, int precision,
+                     float* normsq, bool empty_ok, char* ws, const WorkspaceLayout& L, cudaStream_t stream) {
   const bool tc = use_tc_path(d);
   DeviceStatus* status = reinterpret_cast<DeviceStatus*>(ws + L.status);
   KLC_CUDA(cudaMemsetAsync(status, 0, sizeof(DeviceStatus), stream));
-  float* normsq = nullptr;
-  if (norms != nullptr) {
-    normsq = reinterpret_cast<float*>(ws + L.normsq);
-    KLC_CUDA(cudaMemsetAsync(normsq, 0, size_t(L.pairs) * 2 * 4, stream));
-  }
   PermuteArgs pa{};
   pa.idx = idx;
   pa.tokens = d.tokens;
@@ -138,6 +130,7 @@ static int run_experts_post(const klc_moe_dims& d, const klc_moe_weights& wts, c
   pa.status = status;
   pa.x = x;
   pa.hidden = d.hidden;
+  pa.empty_ok = empty_ok;
   // SIMT gathers bf16 rows here; the tensor-core path quantizes straight from x per row-block
   pa.xp = tc ? nullptr : reinterpret_cast<uint16_t*>(ws + L.xp);
   stage_mark(kStageRouted, stream);
@@ -170,9 +163,23 @@ static int run_experts_post(const klc_moe_dims& d, const klc_moe_weights& wts, c
   ea.normsq = normsq;
   ea.rows_cap = L.rows_cap;
   ea.block_n = L.block_n;
-  st = tc ? launch_experts_tc(ea, stream) : launch_experts_simt(ea, stream);
+  return tc ? launch_experts_tc(ea, stream) : launch_experts_simt(ea, stream);
+}
+
+// Permute, expert GEMMs and combine for given routing; `post` (or null) fuses
+// the next layer's input RMSNorm into the combine.
+static int run_experts_post(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx,
+                            const uint16_t* w, int precision, uint16_t* y, float* norms, const uint16_t* residual,
+                            const PostNorm* post, char* ws, const WorkspaceLayout& L, cudaStream_t stream) {
+  float* normsq = nullptr;
+  if (norms != nullptr) {
+    normsq = reinterpret_cast<float*>(ws + L.normsq);
+    KLC_CUDA(cudaMemsetAsync(normsq, 0, size_t(L.pairs) * 2 * 4, stream));
+  }
+  int st = run_expert_stage(d, wts, x, idx, precision, normsq, false, ws, L, stream);
   if (st != KLC_OK) return st;
-  st = launch_combine(ea.y, pa.pair_pos, w, d.tokens, d.top_k, d.hidden, residual, y, normsq, norms, post, stream);
+  st = launch_combine(reinterpret_cast<const uint16_t*>(ws + L.y), reinterpret_cast<const int32_t*>(ws + L.pair_pos), w,
+                      d.tokens, d.top_k, d.hidden, residual, y, normsq, norms, post, stream);
   stage_mark(kStageCombined, stream);
   return st;
 }

@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kChunk)
                           const int32_t* __restrict__ chunk_base, int32_t* __restrict__ rows,
                           int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x, int64_t hidden,
                           uint16_t* __restrict__ xp, int div, int32_t* __restrict__ aux_out,
-                          int split, DeviceStatus* st) {
+                          int split, int empty_ok, DeviceStatus* st) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                      // [32][experts]
   int32_t* s_pos = sm + 32 * experts;          // [kChunk]
@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kChunk)
   if (p < pairs) {
     v = idx[p];
     e = v >= 0 ? v / div : -1;
-    if (e < 0 || e >= experts) {
+    if (e >= experts || (e < 0 && !empty_ok)) {
       if (writer) record_fault(st, KLC_ERR_DEVICE_FAULT, 1, v);
       e = -1;
     }
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kChunk)
                          int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
                          int4* __restrict__ rowblocks, int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x,
                          int64_t hidden, uint16_t* __restrict__ xp, int div, int32_t* __restrict__ aux_out,
-                         int split, DeviceStatus* st) {
+                         int split, int empty_ok, DeviceStatus* st) {
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                    // [32][experts]
   int32_t* total = warp_cnt + 32 * experts;  // [experts]
@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(kChunk)
   if (p < pairs) {
     v = idx[p];
     e = v >= 0 ? v / div : -1;
-    if (e < 0 || e >= experts) {
+    if (e >= experts || (e < 0 && !empty_ok)) {
       if (writer) record_fault(st, KLC_ERR_DEVICE_FAULT, 1, v);
       e = -1;
     }
@@ -323,7 +323,7 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
     KLC_CUDA(cudaFuncSetAttribute(fused_permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     fused_permute_kernel<<<unsigned(int64_t(nchunks) * split), kChunk, smem, stream>>>(
         a.idx, pairs, a.k, E, a.pad, a.block_n, a.counts, a.offsets, a.rows, a.rowblocks, a.pair_pos, a.x, a.hidden,
-        a.xp, div, a.aux_out, split, a.status);
+        a.xp, div, a.aux_out, split, a.empty_ok ? 1 : 0, a.status);
     KLC_LAUNCH_CHECK("permute (fused) launch");
     return KLC_OK;
   }
@@ -336,7 +336,7 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
   KLC_CUDA(cudaFuncSetAttribute(scatter_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   scatter_gather_kernel<<<unsigned(int64_t(nchunks) * split), kChunk, smem, stream>>>(
       a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos, a.x, a.hidden, a.xp, div, a.aux_out, split,
-      a.status);
+      a.empty_ok ? 1 : 0, a.status);
   KLC_LAUNCH_CHECK("permute scatter launch");
   return KLC_OK;
 }

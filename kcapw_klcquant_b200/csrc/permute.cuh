@@ -27,6 +27,7 @@ struct PermuteArgs {
   uint16_t* xp;        // [rows_cap, H] or null
   int div;             // group id = idx / div (1: group by expert; experts-per-rank: group by rank)
   int32_t* aux_out;    // optional [rows_cap]: idx % div of the pair stored at each row
+  bool empty_ok;       // a negative idx marks an empty slot (skipped, pair_pos -1) instead of a fault
 };
 
 int launch_permute(const PermuteArgs& a, cudaStream_t stream);
@@ -47,6 +48,13 @@ struct WorkspaceLayout {
 };
 
 WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffers);
+
+// Permute + both expert GEMMs for given routing, without the combine: the
+// expert output of pair p is row pair_pos[p] of y (ws + L.pair_pos, ws + L.y;
+// -1 for an empty slot when empty_ok).  `normsq` (or null) accumulates the
+// per-pair squared norms.
+int run_expert_stage(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx, int precision,
+                     float* normsq, bool empty_ok, char* ws, const WorkspaceLayout& L, cudaStream_t stream);
 
 // Argument checks shared by every layer entry point (KLC_ERR_INVALID and a
 // message on failure): sizes, the expert path, and the expert weight pointers

@@ -1,26 +1,31 @@
-"""Expert-parallel MoE layer over torch.distributed (NCCL on GPUs).
+"""Expert-parallel MoE layer: experts sharded over the GPUs of one node.
 
 Experts are sharded contiguously: with N ranks and E experts, rank r holds
 the packed MXFP4 weights of experts [r*E/N, (r+1)*E/N) and the replicated
 router.  One forward on the rank's own tokens:
 
-1. router (all E experts)                      klc_router_topk
-2. pack (token, slot) pairs by owning rank      klc_ep_pack (stable counting sort + row gather)
-3. exchange pair counts, then token rows and    all_to_all_single (NCCL)
-   local expert ids
-4. run the received rows through the local      klc_moe_experts with k = 1, weight 1.0
-   experts (y = out.to(bf16) of each pair)
-5. send the expert outputs back                 all_to_all_single (reverse splits)
-6. weighted bf16 combine in top-k order         klc_moe_combine
+1. router (all E experts)                              klc_router_topk
+2. dispatch every (token, slot) pair's row to the rank that owns its expert
+3. the local experts on the received rows (k = 1)
+4. the expert outputs back to the ranks the tokens came from
+5. weighted bf16 combine in top-k order                klc_moe_combine
+
+Two exchanges implement steps 2 and 4:
+
+* ``exchange="p2p"`` (default on GPUs): the libklcmoe ``klc_ep_*`` kernels
+  store the rows straight into the peers' exchange arenas over NVLink (CUDA
+  IPC mappings) and signal each other through flags with bounded waits; the
+  whole forward is stream-ordered with no host synchronisation
+  (csrc/ep.cu).  The arenas are set up once per layer object by exchanging
+  64-byte IPC handles through ``torch.distributed``.
+* ``exchange="nccl"``: ``klc_ep_pack`` and ``torch.distributed.all_to_all_single``
+  (split sizes read back to the host once per forward).  Any process group
+  backend works, so the tests run it on gloo CPU ranks with a CPU backend.
 
 Because every pair's expert output is computed by the same kernels from the
-same row and weights, and step 6 is the reference's combine order, the
-result matches the single-GPU layer.  The reference has no multi-device
-path (it runs one process on one device); this module is new.
-
-The per-rank compute steps are methods of a backend object, so the
-exchange logic can be exercised with CPU ranks (gloo) and a CPU backend in
-the tests; the product uses :class:`CudaBackend` (libklcmoe.so kernels).
+same row, and step 5 is the reference's combine order, the result matches the
+single-GPU layer.  The reference has no multi-device path (one process, one
+device); this module is new.
 """
 from __future__ import annotations
 
@@ -106,12 +111,13 @@ def _rows_as_bytes(t: torch.Tensor) -> torch.Tensor:
 class ExpertParallelMoe:
     """One MoE layer sharded over the ranks of ``group`` (E divisible by the world size)."""
 
-    exchange_name = "NCCL all_to_all_single dispatch and combine (split sizes synchronised through the host)"
-
     def __init__(self, layer_idx: int, tensors: dict[str, torch.Tensor], device, group=None, top_k: int = 4,
-                 path: str = "auto", backend=None, share_local: "ExpertParallelMoe | None" = None):
+                 path: str = "auto", backend=None, share_local: "ExpertParallelMoe | None" = None,
+                 exchange: str = "auto", max_tokens: int = 4096):
         """``share_local``: reuse another instance's resident local experts (same expert
-        weights, e.g. the same layer with another router bias)."""
+        weights, e.g. the same layer with another router bias).  ``exchange``: "p2p",
+        "nccl" or "auto" (p2p for the CUDA backend); ``max_tokens``: the most tokens a
+        rank passes to one forward (sizes the p2p exchange arenas)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -126,6 +132,12 @@ class ExpertParallelMoe:
         lo, hi = self.rank * self.epr, (self.rank + 1) * self.epr
         self.local_range = (lo, hi)
         self._received = 0
+        self._ep = None
+        self.exchange = "nccl" if backend is not None else ("p2p" if exchange == "auto" else exchange)
+        if self.exchange not in ("p2p", "nccl"):
+            raise ValueError(f"unknown exchange {exchange!r}")
+        self.exchange_name = ("NVLink peer-memory dispatch and combine kernels (libklcmoe klc_ep_*)" if self.exchange == "p2p"
+                              else "NCCL all_to_all_single dispatch and combine (split sizes read back to the host)")
         if backend is not None:
             self.backend = backend
             return
@@ -133,6 +145,8 @@ class ExpertParallelMoe:
         if share_local is not None:
             self.backend = CudaBackend(share_local.backend.local, as_bf16(router_w, dev), as_bf16(tensors[f"{p}.router.bias"], dev),
                                        self.top_k)
+            if self.exchange == "p2p":
+                self._ep = PeerExchange(self.backend, self.rank, self.world, self.epr, max_tokens, group)
             return
         e = f"{p}.experts"
         packed = PackedLayer.from_checkpoint_tensors(
@@ -142,6 +156,8 @@ class ExpertParallelMoe:
         local = MoeLayer(packed, router_w[lo:hi], tensors[f"{p}.router.bias"][lo:hi], tensors[f"{e}.gate_up_proj_bias"][lo:hi],
                          tensors[f"{e}.down_proj_bias"][lo:hi], top_k=1, path=path)
         self.backend = CudaBackend(local, as_bf16(router_w, dev), as_bf16(tensors[f"{p}.router.bias"], dev), self.top_k)
+        if self.exchange == "p2p":
+            self._ep = PeerExchange(self.backend, self.rank, self.world, self.epr, max_tokens, group)
 
     def _exchange(self, send: torch.Tensor, send_counts: list[int], recv_counts: list[int]) -> torch.Tensor:
         out = torch.empty((sum(recv_counts),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
@@ -150,15 +166,35 @@ class ExpertParallelMoe:
 
     def last_received_rows(self) -> int:
         """(token, expert) pairs this rank's experts processed in the last forward."""
+        if self._ep is not None:
+            return self._ep.received_rows()
         return int(self._received)
 
     def check_device_status(self) -> None:
-        """Raise if a kernel of the last local expert call recorded a device-side fault (synchronises)."""
+        """Raise if a kernel of the last forward recorded a device-side fault (synchronises)."""
+        if self._ep is not None:
+            self._ep.check_status()
+            return
         local = getattr(self.backend, "local", None)  # host backends have no device status
         if local is not None:
             local.check_device_status()
 
-    def forward(self, x: torch.Tensor, precision: str = "bf16", residual: torch.Tensor | None = None) -> tuple[torch.Tensor, RouteBatch]:
+    def close(self) -> None:
+        """Release the p2p exchange arena (collective: every rank calls it; the peers
+        must be done writing into it, so the ranks meet at a barrier first)."""
+        if self._ep is not None:
+            self._ep.close()
+            self._ep = None
+
+    def forward(self, x: torch.Tensor, precision: str = "bf16", residual: torch.Tensor | None = None,
+                next_norm: tuple[torch.Tensor, float] | None = None):
+        """This rank's tokens x bf16 [T, H] -> (y bf16 [T, H], routing); with
+        ``next_norm=(weight, eps)`` returns (y, routing, rms_norm(y)) computed by
+        the combine kernel (p2p exchange)."""
+        if self._ep is not None:
+            return self._ep.forward(x, precision, residual, next_norm)
+        if next_norm is not None:
+            raise ValueError("next_norm needs the p2p exchange")
         be = self.backend
         idx, w = be.router(x)
         send_rows, send_expert, send_counts, pair_pos = be.pack(idx, x, self.epr, self.world)
@@ -173,3 +209,85 @@ class ExpertParallelMoe:
         y_back = self._exchange(_rows_as_bytes(y_local), rc, sc).view(y_local.dtype).reshape(-1, y_local.shape[1])
         out = be.combine(y_back, pair_pos, w, residual)
         return out, RouteBatch(idx, w)
+
+
+class PeerExchange:
+    """One rank's side of the NVLink peer-memory exchange (libklcmoe ``klc_ep_*``)."""
+
+    def __init__(self, backend: CudaBackend, rank: int, world: int, experts_per_rank: int, max_tokens: int, group=None):
+        self.backend = backend
+        self.local = backend.local
+        self.device = backend.device
+        self.top_k = backend.top_k
+        self.group = group
+        self.max_tokens = int(max_tokens)
+        L = _lib.lib()
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(L.klc_ep_create(rank, world, self.max_tokens, self.top_k, self.local.hidden, experts_per_rank, ctypes.byref(h)))
+            self.handle = h
+            buf = (ctypes.c_char * 64)()
+            _lib.check(L.klc_ep_ipc_handle(h, buf))
+            # every rank's arena must have the same layout: same capacity, width, k and expert split
+            cfg = torch.tensor([self.max_tokens, self.local.hidden, self.top_k, experts_per_rank], dtype=torch.int64, device=self.device)
+            cfgs = torch.empty(world * 4, dtype=torch.int64, device=self.device)
+            dist.all_gather_into_tensor(cfgs, cfg, group=group)
+            if not bool((cfgs.view(world, 4) == cfg).all()):
+                _lib.lib().klc_ep_destroy(h)
+                raise ValueError(f"ranks disagree on (max_tokens, hidden, top_k, experts_per_rank): {cfgs.view(world, 4).tolist()}")
+            mine = torch.frombuffer(bytearray(bytes(buf)), dtype=torch.uint8).to(self.device)
+            everyone = torch.empty(world * 64, dtype=torch.uint8, device=self.device)
+            dist.all_gather_into_tensor(everyone, mine, group=group)
+            host = bytes(everyone.cpu().numpy().tobytes())
+            _lib.check(L.klc_ep_connect(h, host))
+            self.dims = _lib.KlcDims(0, self.local.hidden, self.local.intermediate, self.local.experts, 1,
+                                     _lib.PATH_CODE[self.local.path])
+            n = ctypes.c_size_t(0)
+            _lib.check(L.klc_ep_workspace_size(h, ctypes.byref(self.dims), ctypes.byref(n)))
+            self.ws = torch.empty(int(n.value), dtype=torch.uint8, device=self.device)
+        dist.barrier(group=group)  # every rank connected before any dispatch
+
+    def forward(self, x: torch.Tensor, precision: str = "bf16", residual=None, next_norm=None):
+        T, H = int(x.shape[0]), int(x.shape[1])
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the exchange capacity of {self.max_tokens} tokens per rank")
+        x = as_bf16(x, self.device)
+        dev, k = self.device, self.top_k
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        idx = torch.empty((T, k), dtype=torch.int32, device=dev)
+        w = torch.empty((T, k), dtype=torch.bfloat16, device=dev)
+        slot = torch.empty((T * k,), dtype=torch.int32, device=dev)
+        if residual is not None:
+            residual = as_bf16(residual, dev)
+        norm_w, eps, normed = None, 0.0, None
+        if next_norm is not None:
+            norm_w, eps = as_bf16(next_norm[0], dev), float(next_norm[1])
+            normed = torch.empty_like(out)
+        be = self.backend
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib().klc_ep_forward(
+                self.handle, ctypes.byref(self.dims), ctypes.byref(self.local.weights), be.router_w.data_ptr(), be.router_b.data_ptr(),
+                x.data_ptr(), T, _lib.PRECISION_CODE[precision], _lib.ptr(residual), _lib.ptr(norm_w), eps, out.data_ptr(),
+                _lib.ptr(normed), idx.data_ptr(), w.data_ptr(), slot.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                _lib.stream_ptr(dev)))
+        if next_norm is not None:
+            return out, RouteBatch(idx, w, normed=normed), normed
+        return out, RouteBatch(idx, w)
+
+    def received_rows(self) -> int:
+        n = ctypes.c_int64(0)
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().klc_ep_received_rows(self.handle, ctypes.byref(n), _lib.stream_ptr(self.device)))
+        return int(n.value)
+
+    def check_status(self) -> None:
+        with torch.cuda.device(self.device):
+            _lib.check(_lib.lib().klc_ep_status(self.handle, self.ws.data_ptr(), None, None, _lib.stream_ptr(self.device)))
+
+    def close(self) -> None:
+        if self.handle is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        _lib.check(_lib.lib().klc_ep_destroy(self.handle))
+        self.handle = None

@@ -1,9 +1,12 @@
-"""Expert-parallel layer on GPUs (NCCL), against the single-GPU layer.
+"""Expert-parallel layer on GPUs against the single-GPU layer, for both
+exchanges: the NVLink peer-memory kernels (``p2p``, libklcmoe klc_ep_*) and
+NCCL all_to_all_single (``nccl``).
 
 Each pair's expert output is computed by the same kernels in both layouts,
 and the combine order is the reference's, so the outputs agree (up to the
 tile shape the row count selects).  The two-rank test needs two GPUs and is
-skipped otherwise.
+skipped otherwise.  The exchange's bounded waits are checked on one GPU with
+a peer that never signals.
 """
 from __future__ import annotations
 
@@ -31,7 +34,8 @@ def _bits(t):
     return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
-def test_ep_single_rank_matches_layer():
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_ep_single_rank_matches_layer(exchange):
     from kcapw_klcquant_b200 import MoeLayer
     from kcapw_klcquant_b200 import synthetic as syn
     from kcapw_klcquant_b200.ep import ExpertParallelMoe
@@ -44,18 +48,80 @@ def test_ep_single_rank_matches_layer():
         layer = syn.make_layer(dims, seed=7, device=dev)
         x = syn.make_hidden(64, 2880, seed=7, device=dev)
         ref, rb_ref = MoeLayer.from_tensors(0, layer, dev, top_k=4).forward(x, precision="bf16")
-        ep = ExpertParallelMoe(0, layer, dev, top_k=4)
-        y, rb = ep.forward(x, precision="bf16")
+        ep = ExpertParallelMoe(0, layer, dev, top_k=4, exchange=exchange, max_tokens=64)
+        for _ in range(3):  # repeated steps reuse the exchange buffers
+            y, rb = ep.forward(x, precision="bf16")
         torch.cuda.synchronize()
         ep.check_device_status()
         assert torch.equal(rb.indices, rb_ref.indices)
-        m = parity.assert_output_close(_bits(y), _bits(ref), "ep1 vs layer")
+        m = parity.assert_output_close(_bits(y), _bits(ref), f"ep1 ({exchange}) vs layer")
         assert m["bit_equal_frac"] >= 0.99, m
+        if exchange == "p2p":
+            # residual + the next layer's RMSNorm fused into the exchange's combine
+            res = syn.make_hidden(64, 2880, seed=8, device=dev)
+            nw = syn.make_rms_weight(2880, seed=8, device=dev)
+            y2, _, normed = ep.forward(x, precision="bf16", residual=res, next_norm=(nw, 1e-5))
+            ref2, rb2 = MoeLayer.from_tensors(0, layer, dev, top_k=4).forward(x, precision="bf16", residual=res, next_norm=(nw, 1e-5))
+            parity.assert_output_close(_bits(y2), _bits(ref2), "ep1 residual")
+            parity.assert_output_close(_bits(normed), _bits(rb2.normed), "ep1 normed")
+            ep.check_device_status()
+        ep.close()
     finally:
         dist.destroy_process_group()
 
 
-def _worker(rank, world, port, q):
+def test_ep_wait_expires_without_peer():
+    """A rank whose peer never signals: the exchange's bounded waits give up,
+    record KLC_ERR_DEVICE_TIMEOUT (site 100 + the silent rank) and return; the
+    GPU keeps answering.  Both ranks' IPC handles are this process's own arena,
+    so every store stays inside it; nothing ever raises rank 1's flags."""
+    import ctypes
+
+    from kcapw_klcquant_b200 import MoeLayer, _lib
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    L = _lib.lib()
+    dev = torch.device("cuda", 0)
+    E, H, epr, T = 16, 256, 8, 24
+    layer = syn.make_layer(syn.LayerDims(E, H, H, 4), seed=9, device=dev)
+    p = "model.layers.0.mlp"
+    e = f"{p}.experts"
+    from kcapw_klcquant_b200.mxfp4_expert import PackedLayer
+
+    packed = PackedLayer.from_checkpoint_tensors(layer[f"{e}.gate_up_proj_blocks"][:epr], layer[f"{e}.gate_up_proj_scales"][:epr],
+                                                 layer[f"{e}.down_proj_blocks"][:epr], layer[f"{e}.down_proj_scales"][:epr], dev)
+    local = MoeLayer(packed, layer[f"{p}.router.weight"][:epr], layer[f"{p}.router.bias"][:epr], layer[f"{e}.gate_up_proj_bias"][:epr],
+                     layer[f"{e}.down_proj_bias"][:epr], top_k=1, path="simt")
+    h = ctypes.c_void_p()
+    _lib.check(L.klc_ep_create(0, 2, T, 4, H, epr, ctypes.byref(h)))
+    try:
+        _lib.check(L.klc_ep_set_wait_limit_ns(h, 50_000_000))  # 50 ms
+        buf = (ctypes.c_char * 64)()
+        _lib.check(L.klc_ep_ipc_handle(h, buf))
+        _lib.check(L.klc_ep_connect(h, bytes(buf) * 2))
+        dims = _lib.KlcDims(0, H, H, epr, 1, _lib.KLC_PATH_SIMT)
+        n = ctypes.c_size_t(0)
+        _lib.check(L.klc_ep_workspace_size(h, ctypes.byref(dims), ctypes.byref(n)))
+        ws = torch.empty(n.value, dtype=torch.uint8, device=dev)
+        x = syn.make_hidden(T, H, seed=9, device=dev)
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        idx = torch.empty((T, 4), dtype=torch.int32, device=dev)
+        w = torch.empty((T, 4), dtype=torch.bfloat16, device=dev)
+        slot = torch.empty((T * 4,), dtype=torch.int32, device=dev)
+        rw, rb = layer[f"{p}.router.weight"].contiguous(), layer[f"{p}.router.bias"].contiguous()
+        _lib.check(L.klc_ep_forward(h, ctypes.byref(dims), ctypes.byref(local.weights), rw.data_ptr(), rb.data_ptr(), x.data_ptr(), T,
+                                    _lib.KLC_PREC_BF16, None, None, 0.0, out.data_ptr(), None, idx.data_ptr(), w.data_ptr(),
+                                    slot.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr()))
+        code, where = ctypes.c_int(0), ctypes.c_int(0)
+        st = L.klc_ep_status(h, ws.data_ptr(), ctypes.byref(code), ctypes.byref(where), _lib.stream_ptr())
+        assert st == _lib.KLC_ERR_DEVICE_TIMEOUT and code.value == _lib.KLC_ERR_DEVICE_TIMEOUT, (st, code.value, where.value)
+        assert where.value in (101, 301), where.value
+        assert float(torch.ones(4, device=dev).sum()) == 4.0  # the context is still usable
+    finally:
+        L.klc_ep_destroy(h)
+
+
+def _worker(rank, world, port, q, exchange):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     dev = torch.device("cuda", rank)
     torch.cuda.set_device(dev)
@@ -68,22 +134,24 @@ def _worker(rank, world, port, q):
         layer = syn.make_layer(syn.GPT_OSS_120B, seed=3, device=dev)
         x = syn.make_hidden(96 + 32 * rank, 2880, seed=50 + rank, device=dev)
         ref, rb_ref = MoeLayer.from_tensors(0, layer, dev, top_k=4).forward(x, precision="bf16")
-        ep = ExpertParallelMoe(0, layer, dev, top_k=4)
-        for _ in range(2):  # repeated steps reuse the exchange buffers
+        ep = ExpertParallelMoe(0, layer, dev, top_k=4, exchange=exchange, max_tokens=256)
+        for _ in range(3):  # repeated steps reuse the exchange buffers
             y, rb = ep.forward(x, precision="bf16")
             ep.check_device_status()
         torch.cuda.synchronize()
         q.put((rank, bool(torch.equal(rb.indices, rb_ref.indices)), _bits(y), _bits(ref)))
+        ep.close()
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_ep_two_ranks_match_single_gpu():
+@pytest.mark.parametrize("exchange", ["p2p", "nccl"])
+def test_ep_two_ranks_match_single_gpu(exchange):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, exchange)) for r in range(2)]
     for p in procs:
         p.start()
     out = [q.get(timeout=600) for _ in procs]
