@@ -77,6 +77,9 @@ int klc_device_sm_count(int* out_sms);
  * devices; a launch that failed is counted too).  No reference counterpart:
  * measurement support, e.g. launches per step.                            */
 int klc_launch_count(uint64_t* out);
+/* sizeof(klc_moe_dims) and sizeof(klc_moe_weights) as this library was
+ * compiled, for bindings to check their own structure layouts against.    */
+int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes);
 
 /* ---- MXFP4 dequant ---------------------------------------------------- *
  * Replaces dequantize_mxfp4_matrix(blocks, scales, dtype)
@@ -101,6 +104,13 @@ int klc_mxfp4_transpose_scales(const uint8_t* scales, int64_t experts, int64_t r
  * ceil(groups/4) * 512 bytes.
  * No reference counterpart: layout preparation for the B200 kernel, like
  * the transpose above.                                                     */
+/* Expert blocks [E, rows, groups, 16] -> [E, rows, groups_pad, 16] with
+ * groups_pad = ceil(groups / 4) * 4 (each row's K padded to a multiple of 128
+ * values with zero bytes), once per layer: the layout the tensor-core path
+ * loads with TMA's 4-bit unpacking copy.  No reference counterpart (layout
+ * preparation for the B200 kernel).  out must hold E*rows*groups_pad*16 bytes. */
+int klc_mxfp4_pad_k128(const uint8_t* blocks, int64_t experts, int64_t rows, int64_t groups, uint8_t* out, void* stream);
+
 int klc_mxfp4_scales_mx_bytes(int64_t experts, int64_t rows, int64_t groups, size_t* out_bytes);
 int klc_mxfp4_scales_mx(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups, uint8_t* out,
                         void* stream);
@@ -176,6 +186,13 @@ typedef struct klc_moe_weights {
   float alpha;        /* 1.702 (streamed_moe_router.py:248) */
   const uint8_t* gu_scales_mx; /* klc_mxfp4_scales_mx of gate_up_proj_scales (tensor-core path) */
   const uint8_t* dn_scales_mx; /* klc_mxfp4_scales_mx of down_proj_scales */
+  /* gate_up / down blocks with every row's K padded to a multiple of 128
+   * values (klc_mxfp4_pad_k128): the tensor-core path then loads them
+   * straight into its MMA operand layout.  NULL: the blocks themselves when K
+   * is already a multiple of 128, else the tensor-core path stages them
+   * through its repack warps.                                               */
+  const uint8_t* gu_blocks_k128;
+  const uint8_t* dn_blocks_k128;
 } klc_moe_weights;
 
 /* Expert execution + combine for given routing (idx, weights), the body of

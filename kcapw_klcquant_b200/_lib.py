@@ -65,6 +65,8 @@ class KlcWeights(ctypes.Structure):
         ("alpha", c_float),
         ("gu_scales_mx", c_void_p),
         ("dn_scales_mx", c_void_p),
+        ("gu_blocks_k128", c_void_p),
+        ("dn_blocks_k128", c_void_p),
     ]
 
 
@@ -73,10 +75,12 @@ SIGNATURES: dict[str, list] = {
     "klc_version": [],
     "klc_device_sm_count": [POINTER(c_int)],
     "klc_launch_count": [POINTER(ctypes.c_uint64)],
+    "klc_struct_sizes": [POINTER(c_size_t), POINTER(c_size_t)],
     "klc_capabilities": [POINTER(c_int)],
     "klc_mxfp4_dequant": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p],
     "klc_mxfp4_transpose_scales": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "klc_mxfp4_scales_mx_bytes": [c_int64, c_int64, c_int64, POINTER(c_size_t)],
+    "klc_mxfp4_pad_k128": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "klc_mxfp4_scales_mx": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "klc_mx_quantize_rows": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     "klc_router_status": [POINTER(c_int), POINTER(c_int), c_void_p],
@@ -137,6 +141,12 @@ def lib() -> ctypes.CDLL:
         fn.restype = c_int
     h.klc_last_error.argtypes = []
     h.klc_last_error.restype = c_char_p
+    # the structures passed by pointer must have the library's layout
+    nd, nw = c_size_t(0), c_size_t(0)
+    if h.klc_struct_sizes(ctypes.byref(nd), ctypes.byref(nw)) != KLC_OK or (nd.value, nw.value) != (
+            ctypes.sizeof(KlcDims), ctypes.sizeof(KlcWeights)):
+        raise ImportError(f"{LIB_PATH} was built with other structure layouts (dims {nd.value} B, weights {nw.value} B) "
+                          f"than this binding ({ctypes.sizeof(KlcDims)} B, {ctypes.sizeof(KlcWeights)} B): rebuild it")
     _LIB = h
     return h
 

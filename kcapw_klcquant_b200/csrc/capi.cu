@@ -61,3 +61,10 @@ extern "C" int klc_launch_count(uint64_t* out) {
   *out = klc::g_launches.load(std::memory_order_relaxed);
   return KLC_OK;
 }
+
+extern "C" int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes) {
+  if (dims_bytes == nullptr || weights_bytes == nullptr) return klc::fail(KLC_ERR_INVALID, "klc_struct_sizes: null output");
+  *dims_bytes = sizeof(klc_moe_dims);
+  *weights_bytes = sizeof(klc_moe_weights);
+  return KLC_OK;
+}

@@ -549,6 +549,313 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Direct-operand variant: the weights are loaded by TMA with the
+// CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B element type, which writes each group
+// of 16 packed E2M1 values (8 bytes) into a 16-byte slot -- the operand layout
+// the MMA reads -- so the weight tile lands in shared memory ready to use and
+// no warp copies it.  This needs each weight row's K padded to a multiple of
+// 128 values (klc_mxfp4_pad_k128, once per layer).
+//
+// Warps: 0 weight TMA producer (+ L2 prefetch cursor), 1 activation TMA
+// producer, 2 the MMA issuer (one thread), 4-7 (and 12-15) epilogue, 8-11 the
+// scale warpgroup: each warp writes the stage's weight and activation E8M0
+// scales into its TMEM lane quarter (tcgen05.st) once both TMA copies of the
+// stage landed, then signals the issuer.  Per stage (SK = 128 or 256 K) the
+// issuer waits once, issues SK/32 MMAs and one commit, which frees the stage's
+// weight slot, activation slot and scale set together.
+// ---------------------------------------------------------------------------
+constexpr int kWarp2A = 0, kWarp2B = 1, kWarp2Mma = 2, kWarp2Epi0 = 4, kWarp2Sf0 = 8, kWarp2Epi2 = 12;
+
+//   BN  max token rows of a row-block (N2 = 2*BN hi/lo rows, <= 128)
+//   NS  pipeline stages (weight slot + activation slot + TMEM scale set each)
+//   ND  accumulator sets (the epilogue of one item overlaps the next)
+//   EPI epilogue warpgroups
+//   SK  K per stage: SK/128 TMA boxes of each operand
+//   PF  weight stages prefetched into L2 beyond the shared-memory ring
+template <int BN_, int NS_, int ND_, int EPI_, int SK_, int PF_>
+struct Mx2Cfg {
+  static constexpr int BN = BN_, NS = NS_, ND = ND_, EPI = EPI_, SK = SK_, PF = PF_;
+  static constexpr int N2 = 2 * BN;
+  static_assert(N2 <= 128, "one MMA N chunk");
+  static constexpr int SUB = SK / 128;  // 128-K boxes per stage
+  static_assert(SK == 128 || SK == 256, "stage K");
+  static constexpr int THREADS = (EPI == 2 ? 16 : 12) * 32;
+  static constexpr int ABOX = kBM * 128;      // one 128-K box of padded E2M1: 128 rows x 128 B in shared memory
+  static constexpr int ABOX_TX = ABOX / 2;    // ... whose TMA transaction counts the packed bytes it read (8 KB)
+  static constexpr int BBOX = N2 * kStageK;   // one 128-K box of hi/lo E4M3 rows
+  static constexpr int ASLOT = SUB * ABOX, BSLOT = SUB * BBOX;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + NS * ASLOT;
+  static constexpr int OFF_ASF = OFF_B + NS * BSLOT;       // NS x SUB x 512
+  static constexpr int OFF_BSF = OFF_ASF + NS * SUB * 512;  // NS x SUB x 512
+  static constexpr int OFF_BAR = OFF_BSF + NS * SUB * 512;
+  static constexpr int NUM_BARS = 4 * NS + 2 * ND + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ACC_COLS = ND * N2;
+  static constexpr int SF_COLS = 8 * SUB;  // per scale set: 4 columns per box for A, 4 for B
+  static_assert(ACC_COLS + NS * SF_COLS <= kTmemCols, "TMEM budget");
+  static_assert(BSLOT % 1024 == 0 && ASLOT % 1024 == 0, "slots stay 1024-byte aligned");
+  static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
+};
+
+template <int PHASE, class C>
+__global__ void __launch_bounds__(C::THREADS, 1)
+    mx2_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, MxParams p) {
+  constexpr int NS = C::NS, ND = C::ND, N2 = C::N2, SUB = C::SUB;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
+  auto afull = [&](int s) { return bar0 + 8u * s; };
+  auto bfull = [&](int s) { return bar0 + 8u * (NS + s); };
+  auto sready = [&](int s) { return bar0 + 8u * (2 * NS + s); };
+  auto sempty = [&](int s) { return bar0 + 8u * (3 * NS + s); };
+  auto dfull = [&](int d) { return bar0 + 8u * (4 * NS + d); };
+  auto dempty = [&](int d) { return bar0 + 8u * (4 * NS + ND + d); };
+  const uint32_t mma_done = bar0 + 8u * (4 * NS + 2 * ND);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const Ctl ctl{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(afull(s), 1);
+      mbar_init(bfull(s), 1);
+      mbar_init(sready(s), 4);  // the four scale warps
+      mbar_init(sempty(s), 1);  // the issuer's commit
+    }
+    for (int d = 0; d < ND; ++d) {
+      mbar_init(dfull(d), 1);
+      mbar_init(dempty(d), 4 * C::EPI);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kWarp2Mma) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int nrb = p.status->rowblocks;
+  const int total = nrb * p.n_mtiles;
+  const int kb128 = p.ksteps;                 // 128-K boxes per item
+  const int st_n = (kb128 + SUB - 1) / SUB;    // stages per item
+
+  if (warp == kWarp2A) {
+    // ------------------------------------------------------------ weights
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      int pf_item = blockIdx.x, pf_k = 0;
+      uint32_t pf_n = 0;
+      int4 pf_rb = pf_item < total ? p.rowblocks[pf_item / p.n_mtiles] : make_int4(0, 0, 0, 0);
+      auto prefetch_ahead = [&](uint32_t upto) {  // upto: in 128-K boxes issued so far
+        while (pf_n < upto && pf_item < total) {
+          tma_prefetch_3d(&map_a, pf_k * 128, (pf_item % p.n_mtiles) * kBM, pf_rb.x);
+          ++pf_n;
+          if (++pf_k == kb128) {
+            pf_k = 0;
+            pf_item += gridDim.x;
+            if (pf_item < total) pf_rb = p.rowblocks[pf_item / p.n_mtiles];
+          }
+        }
+      };
+      uint32_t boxes = 0;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int mt = item % p.n_mtiles;
+        const uint8_t* sfa_item = p.sfa + (int64_t(rb.x) * p.n_mtiles + mt) * int64_t(kb128) * 512;
+        for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
+          prefetch_ahead(boxes + uint32_t(NS * SUB + C::PF));
+          const int s = int(it % NS);
+          if (!(ok = wait_bar(sempty(s), ((it / NS) & 1) ^ 1, ctl, 50))) break;
+          const int nb = min(SUB, kb128 - ks * SUB);
+          mbar_arrive_expect_tx(afull(s), uint32_t(nb * (C::ABOX_TX + 512)));
+          for (int j = 0; j < nb; ++j)
+            tma_load_3d(smem_u32(smem + C::OFF_A + s * C::ASLOT + j * C::ABOX), &map_a, (ks * SUB + j) * 128, mt * kBM, rb.x,
+                        afull(s));
+          bulk_load(smem_u32(smem + C::OFF_ASF + s * SUB * 512), sfa_item + int64_t(ks * SUB) * 512, uint32_t(nb * 512),
+                    afull(s));
+          boxes += uint32_t(nb);
+        }
+      }
+      if (!ok) drain_ring(afull(0), NS, it);
+    }
+  } else if (warp == kWarp2B) {
+    // ------------------------------------------------------------ activations
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int rbi = item / p.n_mtiles;
+        const int4 rb = p.rowblocks[rbi];
+        const uint8_t* sfb_rb = p.sfb + int64_t(rbi) * kb128 * 512;
+        for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
+          const int s = int(it % NS);
+          if (!(ok = wait_bar(sempty(s), ((it / NS) & 1) ^ 1, ctl, 51))) break;
+          const int nb = min(SUB, kb128 - ks * SUB);
+          mbar_arrive_expect_tx(bfull(s), uint32_t(nb * (C::BBOX + 512)));
+          for (int j = 0; j < nb; ++j)
+            tma_load_2d(smem_u32(smem + C::OFF_B + s * C::BSLOT + j * C::BBOX), &map_b, (ks * SUB + j) * kStageK, 2 * rb.y,
+                        bfull(s));
+          bulk_load(smem_u32(smem + C::OFF_BSF + s * SUB * 512), sfb_rb + int64_t(ks * SUB) * 512, uint32_t(nb * 512),
+                    bfull(s));
+        }
+      }
+      if (!ok) drain_ring(bfull(0), NS, it);
+    }
+  } else if (warp >= kWarp2Sf0 && warp < kWarp2Sf0 + 4) {
+    // ------------------------------------------------------------ scales
+    const int q = warp & 3;  // this warp's TMEM lane quarter
+    uint32_t it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+      for (int ks = 0; ks < st_n; ++ks, ++it) {
+        const int s = int(it % NS);
+        const uint32_t ph = (it / NS) & 1;
+        ok = wait_bar(afull(s), ph, ctl, 52) && wait_bar(bfull(s), ph, ctl, 53);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        tc_fence_after();  // the set is rewritten after the MMAs of its previous use completed
+        const int nb = min(SUB, kb128 - ks * SUB);
+        const uint32_t sf_t = tmem + (uint32_t(q * 32) << 16) + uint32_t(C::ACC_COLS + s * C::SF_COLS);
+        for (int j = 0; j < nb; ++j) {
+          tmem_st4(sf_t + 4 * j, *reinterpret_cast<const uint4*>(smem + C::OFF_ASF + (s * SUB + j) * 512 + lane * 16));
+          tmem_st4(sf_t + 4 * SUB + 4 * j, *reinterpret_cast<const uint4*>(smem + C::OFF_BSF + (s * SUB + j) * 512 + lane * 16));
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sready(s));
+      }
+    }
+  } else if (warp == kWarp2Mma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, ic = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int n2 = 2 * ((rb.z + 7) & ~7);  // hi/lo rows the MMA reads
+        const uint32_t idesc = mx_idesc(n2, 0, 0);
+        const int d = ic % ND;
+        const uint32_t d_tmem = tmem + uint32_t(d * N2);
+        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 60))) break;
+        tc_fence_after();
+        for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
+          const int s = int(it % NS);
+          if (!(ok = wait_bar(sready(s), (it / NS) & 1, ctl, 61))) break;
+          tc_fence_after();
+          const uint32_t sfa_t = tmem + uint32_t(C::ACC_COLS + s * C::SF_COLS);
+          const uint32_t sfb_t = sfa_t + 4 * SUB;
+          const uint64_t adesc0 = sw128_desc(smem_u32(smem + C::OFF_A + s * C::ASLOT));
+          const uint64_t bdesc0 = sw128_desc(smem_u32(smem + C::OFF_B + s * C::BSLOT));
+          const int kk_n = min(C::SK, p.k_in - ks * C::SK) / 32;  // 32-K blocks in this stage
+#pragma unroll
+          for (int kk = 0; kk < 4 * SUB; ++kk) {
+            if (kk < kk_n) {
+              const int j = kk >> 2, kb = kk & 3;
+              // descriptor start addresses advance by 32 B per K block and by one box per 128 K
+              mx_mma(d_tmem, adesc0 + uint64_t(j * (C::ABOX >> 4) + kb * 2), bdesc0 + uint64_t(j * (C::BBOX >> 4) + kb * 2),
+                     idesc | (uint32_t(kb) << 4) | (uint32_t(kb) << 29), (sfa_t + 4 * j) | (uint32_t(kb) << 30),
+                     (sfb_t + 4 * j) | (uint32_t(kb) << 30), (ks == 0 && kk == 0) ? 0u : 1u);
+            }
+          }
+          tc_commit(sempty(s));  // frees the weight slot, the activation slot and the scale set
+        }
+        if (ok) tc_commit(dfull(d));
+      }
+      tc_commit(mma_done);
+      drain_wait(mma_done, 0);
+    }
+  } else if ((warp >= kWarp2Epi0 && warp < kWarp2Epi0 + 4) || (C::EPI == 2 && warp >= kWarp2Epi2 && warp < kWarp2Epi2 + 4)) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int m = q * 32 + lane;
+    const int eg = warp >= kWarp2Epi2 ? 1 : 0;
+    uint32_t ic = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+      const int4 rb = p.rowblocks[item / p.n_mtiles];
+      const int mt = item % p.n_mtiles;
+      const int e = rb.x, r0 = rb.y, nrows = rb.z;
+      const int npad = (nrows + 7) & ~7;
+      const int d = ic % ND;
+      const int j = mt * kBM + m;
+      const bool jok = j < p.n_out;
+      const float bias = jok ? bf16_to_f32(p.bias[int64_t(e) * p.n_out + j]) : 0.f;
+      ok = wait_bar_backoff(dfull(d), (ic / ND) & 1, ctl, 70);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16) + uint32_t(d * N2);
+      if (8 * eg >= npad) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dempty(d));
+      }
+      for (int t0 = 8 * eg; t0 < npad; t0 += 8 * C::EPI) {
+        uint32_t raw[16];
+        tmem_ld16(lane_base + uint32_t(2 * t0), raw);
+        tmem_wait_ld();
+        if (t0 + 8 * C::EPI >= npad) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(dempty(d));
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int n = t0 + i;
+          float v = __uint_as_float(raw[2 * i]) + __uint_as_float(raw[2 * i + 1]);
+          if (p.precision == KLC_PREC_BF16) v = round_bf16(v);
+          v += bias;
+          const bool nok = n < nrows;
+          if (PHASE == 1) {
+            const float up_raw = __shfl_xor_sync(0xffffffffu, v, 1);
+            float g2 = 0.f;
+            if ((lane & 1) == 0 && jok && nok) {
+              const float gate = fminf(v, p.limit);
+              const float up = fminf(fmaxf(up_raw, -p.limit), p.limit);
+              const float glu = gate * (1.0f / (1.0f + expf(-(gate * p.alpha))));
+              const float gated = (up + 1.0f) * glu;
+              const uint16_t gb = f32_to_bf16(gated);
+              p.out[int64_t(r0 + n) * p.out_ld + (j >> 1)] = gb;
+              const float gr = bf16_to_f32(gb);
+              g2 = (p.precision == KLC_PREC_BF16) ? gr * gr : gated * gated;
+            }
+            if (p.normsq != nullptr) {
+              g2 = warp_sum(g2);
+              if (lane == 0 && nok) atomicAdd(&p.normsq[int64_t(p.rows[r0 + n]) * 2 + 0], g2);
+            }
+          } else {
+            float o2 = 0.f;
+            if (jok && nok) {
+              p.out[int64_t(r0 + n) * p.out_ld + j] = f32_to_bf16(v);
+              o2 = v * v;
+            }
+            if (p.normsq != nullptr) {
+              o2 = warp_sum(o2);
+              if (lane == 0 && nok) atomicAdd(&p.normsq[int64_t(p.rows[r0 + n]) * 2 + 1], o2);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kWarp2Mma)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 template <int PHASE, class C>
@@ -582,6 +889,84 @@ int launch_mx_phase(const uint8_t* blocks, const uint8_t* act_q, int64_t rows_ca
   mx_expert_kernel<PHASE, C><<<grid, C::THREADS, smem, stream>>>(ma, mb, p);
   KLC_LAUNCH_CHECK("tcgen05 expert launch");
   return KLC_OK;
+}
+
+template <int PHASE, class C>
+int launch_mx2_phase(const uint8_t* blocks_k128, const uint8_t* act_q, int64_t rows_cap, int experts, MxParams p,
+                     int max_rowblocks, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out);
+  const uint64_t Kp = (K + 127) / 128 * 128;  // padded row length in E2M1 values
+  p.ksteps = int(Kp / 128);
+  KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(blocks_k128) & 31) == 0, "tensor-core path: padded weight blocks must be 32-byte aligned");
+  {
+    // packed E2M1 [E][N][Kp] values (Kp/2 bytes per row); box = 128 values x 128 rows; each
+    // 16-value group lands in a 16-byte shared-memory slot (16U4_ALIGN16B), 128B swizzle
+    const uint64_t dims[3] = {Kp, N, uint64_t(experts)};
+    const uint64_t strides[2] = {Kp / 2, N * Kp / 2};
+    const uint32_t box[3] = {128, kBM, 1};
+    int st = make_map(&ma, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, blocks_k128, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  {
+    // hi/lo E4M3 rows [2 rows_cap][K] bytes; box = N2 rows x 128 bytes, 128B swizzle
+    const uint64_t dims[2] = {K, 2 * uint64_t(rows_cap)};
+    const uint64_t strides[1] = {K};
+    const uint32_t box[2] = {kStageK, uint32_t(C::N2)};
+    int st = make_map(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, act_q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  const int smem = (C::BYTES + 1024 > 118 * 1024) ? C::BYTES + 1024 : 118 * 1024;  // one CTA per SM
+  KLC_CUDA(cudaFuncSetAttribute(mx2_expert_kernel<PHASE, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
+  const int grid = int(items < sm_count() ? items : sm_count());
+  if (grid <= 0) return KLC_OK;
+  mx2_expert_kernel<PHASE, C><<<grid, C::THREADS, smem, stream>>>(ma, mb, p);
+  KLC_LAUNCH_CHECK("tcgen05 expert launch");
+  return KLC_OK;
+}
+
+template <class C>
+int launch_mx2_both(const ExpertArgs& a, const uint8_t* gu_k128, const uint8_t* dn_k128, cudaStream_t stream) {
+  const klc_moe_weights& w = *a.wts;
+  KLC_CHECK_ARG(w.gu_scales_mx != nullptr && w.dn_scales_mx != nullptr,
+                "tensor-core path: gu_scales_mx / dn_scales_mx are required (klc_mxfp4_scales_mx)");
+  MxParams p1{};
+  p1.n_out = int(2 * a.inter);
+  p1.k_in = int(a.hidden);
+  p1.n_mtiles = (p1.n_out + kBM - 1) / kBM;
+  p1.rowblocks = a.rowblocks;
+  p1.status = a.status_rw;
+  p1.rows = a.rows;
+  p1.sfa = w.gu_scales_mx;
+  p1.sfb = a.sfb1;
+  p1.bias = w.gu_bias;
+  p1.out = static_cast<uint16_t*>(a.gated);
+  p1.out_ld = int(a.inter);
+  p1.normsq = a.normsq;
+  p1.precision = a.precision;
+  p1.limit = w.swiglu_limit;
+  p1.alpha = w.alpha;
+  int st = launch_quantize_rows(a.x, a.hidden, a.rows, a.k, a.rowblocks, a.status, a.max_rowblocks, 1, a.xq, a.sfb1, stream);
+  if (st != KLC_OK) return st;
+  st = launch_mx2_phase<1, C>(gu_k128, a.xq, a.rows_cap, int(a.experts), p1, a.max_rowblocks, stream);
+  if (st != KLC_OK) return st;
+  stage_mark(kStageGateUp, stream);
+  st = launch_quantize_rows(static_cast<const uint16_t*>(a.gated), a.inter, nullptr, 1, a.rowblocks, a.status,
+                            a.max_rowblocks, 1, a.gq, a.sfb2, stream);
+  if (st != KLC_OK) return st;
+  MxParams p2 = p1;
+  p2.n_out = int(a.hidden);
+  p2.k_in = int(a.inter);
+  p2.n_mtiles = (p2.n_out + kBM - 1) / kBM;
+  p2.sfa = w.dn_scales_mx;
+  p2.sfb = a.sfb2;
+  p2.bias = w.dn_bias;
+  p2.out = a.y;
+  p2.out_ld = int(a.hidden);
+  st = launch_mx2_phase<2, C>(dn_k128, a.gq, a.rows_cap, int(a.experts), p2, a.max_rowblocks, stream);
+  stage_mark(kStageDown, stream);
+  return st;
 }
 
 template <class C>
@@ -645,6 +1030,16 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 //                BN  NA NS NB NP ND PF EPI
 using MxN16  = MxCfg<16, 4, 6, 6, 1, 2, 8, 1>;
 using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0, 2>;
+// Direct-operand kernels (weights padded to K % 128 == 0):
+//                 BN  NS ND EPI  SK  PF
+#ifndef KLC_MX2_N16
+#define KLC_MX2_N16 16, 4, 2, 1, 256, 8
+#endif
+#ifndef KLC_MX2_N64
+#define KLC_MX2_N64 64, 3, 2, 2, 256, 0
+#endif
+using Mx2N16 = Mx2Cfg<KLC_MX2_N16>;
+using Mx2N64 = Mx2Cfg<KLC_MX2_N64>;
 
 }  // namespace
 
@@ -703,6 +1098,17 @@ int mx_sfb_chunks(int block_n) { return (2 * block_n + 127) / 128; }
 int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   KLC_CHECK_ARG(a.hidden % 64 == 0 && a.inter % 64 == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
   KLC_CHECK_ARG(2 * a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
+  // direct-operand kernels when the weights are available with K padded to a multiple of 128
+  const klc_moe_weights& w = *a.wts;
+  const uint8_t* gu = w.gu_blocks_k128 != nullptr ? w.gu_blocks_k128 : (a.hidden % 128 == 0 ? w.gu_blocks : nullptr);
+  const uint8_t* dn = w.dn_blocks_k128 != nullptr ? w.dn_blocks_k128 : (a.inter % 128 == 0 ? w.dn_blocks : nullptr);
+  if (gu != nullptr && dn != nullptr) {
+    switch (a.block_n) {
+      case 16: return launch_mx2_both<Mx2N16>(a, gu, dn, stream);
+      case 64: return launch_mx2_both<Mx2N64>(a, gu, dn, stream);
+      default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 16 or 64");
+    }
+  }
   switch (a.block_n) {
     case 16: return launch_mx_both<MxN16>(a, stream);
     case 64: return launch_mx_both<MxN64>(a, stream);

@@ -39,6 +39,16 @@ __global__ void scales_mx_kernel(const uint8_t* __restrict__ scales, int64_t row
   }
 }
 
+// Rows of 16-byte groups [E*rows][groups] -> [E*rows][groups_pad], zero groups past the row.
+__global__ void pad_k128_kernel(const uint4* __restrict__ src, int64_t nrows, int64_t groups, int64_t groups_pad,
+                                uint4* __restrict__ dst) {
+  const int64_t n = nrows * groups_pad;
+  for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / groups_pad, g = i - r * groups_pad;
+    dst[i] = g < groups ? src[r * groups + g] : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
 __device__ __forceinline__ uint32_t e4m3x2(float lo_elem, float hi_elem) {
   // first operand -> upper byte, second -> lower byte
   uint16_t r;
@@ -184,5 +194,24 @@ extern "C" int klc_mxfp4_scales_mx(const uint8_t* scales, int64_t experts, int64
   scales_mx_kernel<<<dim3(unsigned(stages), unsigned(mtiles), unsigned(experts)), 128, 0, as_stream(stream)>>>(
       scales, rows, groups, int(mtiles), int(stages), out);
   KLC_LAUNCH_CHECK("klc_mxfp4_scales_mx launch");
+  return KLC_OK;
+}
+
+extern "C" int klc_mxfp4_pad_k128(const uint8_t* blocks, int64_t experts, int64_t rows, int64_t groups, uint8_t* out,
+                                  void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(experts >= 0 && rows >= 0 && groups >= 0, "klc_mxfp4_pad_k128: negative size");
+  const int64_t nrows = experts * rows;
+  if (nrows == 0 || groups == 0) return KLC_OK;
+  KLC_CHECK_ARG(blocks && out, "klc_mxfp4_pad_k128: null pointer");
+  KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(blocks) & 15) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0,
+                "klc_mxfp4_pad_k128: blocks and out must be 16-byte aligned");
+  const int64_t gp = (groups + 3) / 4 * 4;
+  const int64_t n = nrows * gp;
+  const int64_t want = (n + 255) / 256;
+  const int blocks_n = int(want < 8192 ? want : 8192);
+  pad_k128_kernel<<<blocks_n, 256, 0, as_stream(stream)>>>(reinterpret_cast<const uint4*>(blocks), nrows, groups, gp,
+                                                            reinterpret_cast<uint4*>(out));
+  KLC_LAUNCH_CHECK("klc_mxfp4_pad_k128 launch");
   return KLC_OK;
 }

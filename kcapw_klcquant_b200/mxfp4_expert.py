@@ -74,6 +74,20 @@ def transpose_scales(scales: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def pad_k128(blocks: torch.Tensor) -> torch.Tensor | None:
+    """Expert blocks [E, rows, G, 16] with each row's K padded to a multiple of 128
+    values ([E, rows, ceil(G/4)*4, 16], zero bytes appended; klc_mxfp4_pad_k128), or
+    None when G is already a multiple of 4."""
+    E, rows, G, _ = blocks.shape
+    if G % 4 == 0:
+        return None
+    _lib.require_cuda(blocks)
+    out = torch.empty((E, rows, (G + 3) // 4 * 4, 16), dtype=torch.uint8, device=blocks.device)
+    with torch.cuda.device(blocks.device):
+        _lib.check(_lib.lib().klc_mxfp4_pad_k128(blocks.data_ptr(), E, rows, G, out.data_ptr(), _lib.stream_ptr()))
+    return out
+
+
 def scales_mx(scales: torch.Tensor) -> torch.Tensor:
     """E8M0 scales [E, rows, groups] -> the tensor-core path's 512-byte scale blocks
     [E, ceil(rows/128), ceil(groups/4), 512] (klc_mxfp4_scales_mx)."""
@@ -101,6 +115,10 @@ class PackedLayer:
     dn_scales: torch.Tensor | None = None
     gu_scales_mx: torch.Tensor | None = None  # tensor-core scale blocks (scales_mx)
     dn_scales_mx: torch.Tensor | None = None
+    # blocks with K padded to a multiple of 128 values (pad_k128), loaded by the tensor-core
+    # path straight into its operand layout; None where K already is a multiple of 128
+    gu_blocks_k128: torch.Tensor | None = None
+    dn_blocks_k128: torch.Tensor | None = None
 
     @property
     def experts(self) -> int:
@@ -116,7 +134,8 @@ class PackedLayer:
 
     @property
     def nbytes(self) -> int:
-        ts = (self.gu_blocks, self.gu_scales_t, self.dn_blocks, self.dn_scales_t, self.gu_scales_mx, self.dn_scales_mx)
+        ts = (self.gu_blocks, self.gu_scales_t, self.dn_blocks, self.dn_scales_t, self.gu_scales_mx, self.dn_scales_mx,
+              self.gu_blocks_k128, self.dn_blocks_k128)
         return sum(t.numel() for t in ts if t is not None)
 
     @classmethod
@@ -132,7 +151,7 @@ class PackedLayer:
             raise ValueError(f"inconsistent MXFP4 layer shapes {gb.shape} {gs.shape} {db.shape} {ds.shape}")
         if db.shape[1] != g_h * 32 or db.shape[2] * 64 != two_i:
             raise ValueError("down_proj must be [E, H, I/32, 16] with gate_up [E, 2I, H/32, 16]")
-        return cls(gb, transpose_scales(gs), db, transpose_scales(ds), gs, ds, scales_mx(gs), scales_mx(ds))
+        return cls(gb, transpose_scales(gs), db, transpose_scales(ds), gs, ds, scales_mx(gs), scales_mx(ds), pad_k128(gb), pad_k128(db))
 
 
 @dataclass

@@ -109,3 +109,16 @@ def test_split_matches_restatement_and_is_exact_near_block_max(case):
     far = ~near & (amax > np.ldexp(1.0, -120))
     if far.any():
         assert np.all(np.abs(recon[far] - xblk[far]) <= np.broadcast_to(amax, xblk.shape)[far] * 2.0**-16)
+
+
+def test_pad_k128_matches_numpy():
+    """klc_mxfp4_pad_k128: each row's 16-byte groups copied, zero groups appended up to a multiple of 4."""
+    from kcapw_klcquant_b200.mxfp4_expert import pad_k128
+
+    g = torch.Generator().manual_seed(4)
+    b = torch.randint(0, 256, (3, 40, 90, 16), generator=g, dtype=torch.uint8)
+    out = pad_k128(b.to(DEV)).cpu().numpy()
+    want = np.zeros((3, 40, 92, 16), np.uint8)
+    want[:, :, :90] = b.numpy()
+    np.testing.assert_array_equal(out, want)
+    assert pad_k128(torch.zeros((1, 4, 8, 16), dtype=torch.uint8, device=DEV)) is None
