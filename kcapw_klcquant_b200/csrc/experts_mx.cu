@@ -564,7 +564,13 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 // issuer waits once, issues SK/32 MMAs and one commit, which frees the stage's
 // weight slot, activation slot and scale set together.
 // ---------------------------------------------------------------------------
-constexpr int kWarp2A = 0, kWarp2B = 1, kWarp2Mma = 2, kWarp2Epi0 = 4, kWarp2Sf0 = 8, kWarp2Epi2 = 12;
+constexpr int kWarp2A = 0, kWarp2B = 1, kWarp2Mma = 2, kWarp2Epi0 = 4, kWarp2Sf0 = 8, kWarp2Epi2 = 12, kWarp2Sf1 = 16;
+
+// tcgen05.cp of one 512-byte scale block (32 rows x 16 bytes in shared memory)
+// into 4 TMEM columns of lanes 0-31, replicated to the four lane quarters
+__device__ __forceinline__ void tc_cp_scales(uint32_t taddr, uint32_t saddr) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(plain_desc(saddr)) : "memory");
+}
 
 //   BN  max token rows of a row-block (N2 = 2*BN hi/lo rows, <= 128)
 //   NS  pipeline stages (weight slot + activation slot + TMEM scale set each)
@@ -572,14 +578,17 @@ constexpr int kWarp2A = 0, kWarp2B = 1, kWarp2Mma = 2, kWarp2Epi0 = 4, kWarp2Sf0
 //   EPI epilogue warpgroups
 //   SK  K per stage: SK/128 TMA boxes of each operand
 //   PF  weight stages prefetched into L2 beyond the shared-memory ring
-template <int BN_, int NS_, int ND_, int EPI_, int SK_, int PF_>
+//   SFW scale writers: 1 or 2 scale warpgroups (tcgen05.st; stage parity picks
+//       the warpgroup), or 0: the issuer copies the scales itself (tcgen05.cp)
+template <int BN_, int NS_, int ND_, int EPI_, int SK_, int PF_, int SFW_ = 1>
 struct Mx2Cfg {
-  static constexpr int BN = BN_, NS = NS_, ND = ND_, EPI = EPI_, SK = SK_, PF = PF_;
+  static constexpr int BN = BN_, NS = NS_, ND = ND_, EPI = EPI_, SK = SK_, PF = PF_, SFW = SFW_;
   static constexpr int N2 = 2 * BN;
   static_assert(N2 <= 128, "one MMA N chunk");
   static constexpr int SUB = SK / 128;  // 128-K boxes per stage
   static_assert(SK == 128 || SK == 256, "stage K");
-  static constexpr int THREADS = (EPI == 2 ? 16 : 12) * 32;
+  static_assert(SFW >= 0 && SFW <= 2 && (SFW < 2 || NS % 2 == 0), "scale warpgroups own slots by parity");
+  static constexpr int THREADS = (SFW == 2 ? 20 : (EPI == 2 ? 16 : (SFW == 1 ? 12 : 8))) * 32;
   static constexpr int ABOX = kBM * 128;      // one 128-K box of padded E2M1: 128 rows x 128 B in shared memory
   static constexpr int ABOX_TX = ABOX / 2;    // ... whose TMA transaction counts the packed bytes it read (8 KB)
   static constexpr int BBOX = N2 * kStageK;   // one 128-K box of hi/lo E4M3 rows
@@ -623,7 +632,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     for (int s = 0; s < NS; ++s) {
       mbar_init(afull(s), 1);
       mbar_init(bfull(s), 1);
-      mbar_init(sready(s), 4);  // the four scale warps
+      mbar_init(sready(s), 4);  // the four warps of the slot's scale warpgroup
       mbar_init(sempty(s), 1);  // the issuer's commit
     }
     for (int d = 0; d < ND; ++d) {
@@ -711,16 +720,21 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       }
       if (!ok) drain_ring(bfull(0), NS, it);
     }
-  } else if (warp >= kWarp2Sf0 && warp < kWarp2Sf0 + 4) {
+  } else if (C::SFW > 0 && ((warp >= kWarp2Sf0 && warp < kWarp2Sf0 + 4) || (C::SFW == 2 && warp >= kWarp2Sf1 && warp < kWarp2Sf1 + 4))) {
     // ------------------------------------------------------------ scales
     const int q = warp & 3;  // this warp's TMEM lane quarter
+    const uint32_t wg = warp >= kWarp2Sf1 ? 1u : 0u;  // stages it with it % SFW == wg
     uint32_t it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
       for (int ks = 0; ks < st_n; ++ks, ++it) {
+        if (C::SFW == 2 && (it & 1u) != wg) continue;
         const int s = int(it % NS);
         const uint32_t ph = (it / NS) & 1;
-        ok = wait_bar(afull(s), ph, ctl, 52) && wait_bar(bfull(s), ph, ctl, 53);
+        // lane 0 polls; then every lane observes the completed phases (acquire) once
+        if (lane == 0) ok = wait_bar(afull(s), ph, ctl, 52) && wait_bar(bfull(s), ph, ctl, 53);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (ok && lane != 0) ok = mbar_try_wait(afull(s), ph) && mbar_try_wait(bfull(s), ph);
         if (!(ok = __all_sync(0xffffffffu, ok))) break;
         tc_fence_after();  // the set is rewritten after the MMAs of its previous use completed
         const int nb = min(SUB, kb128 - ks * SUB);
@@ -750,10 +764,22 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         tc_fence_after();
         for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
           const int s = int(it % NS);
-          if (!(ok = wait_bar(sready(s), (it / NS) & 1, ctl, 61))) break;
-          tc_fence_after();
           const uint32_t sfa_t = tmem + uint32_t(C::ACC_COLS + s * C::SF_COLS);
           const uint32_t sfb_t = sfa_t + 4 * SUB;
+          if (C::SFW > 0) {
+            if (!(ok = wait_bar(sready(s), (it / NS) & 1, ctl, 61))) break;
+            tc_fence_after();
+          } else {
+            // both operands and their scale blocks landed: copy the scales into the
+            // stage's set (ordered before this thread's MMAs that read them)
+            if (!(ok = wait_bar(afull(s), (it / NS) & 1, ctl, 62) && wait_bar(bfull(s), (it / NS) & 1, ctl, 63))) break;
+            tc_fence_after();
+            const int nbx = min(SUB, kb128 - ks * SUB);
+            for (int j = 0; j < nbx; ++j) {
+              tc_cp_scales(sfa_t + 4 * j, smem_u32(smem + C::OFF_ASF + (s * SUB + j) * 512));
+              tc_cp_scales(sfb_t + 4 * j, smem_u32(smem + C::OFF_BSF + (s * SUB + j) * 512));
+            }
+          }
           const uint64_t adesc0 = sw128_desc(smem_u32(smem + C::OFF_A + s * C::ASLOT));
           const uint64_t bdesc0 = sw128_desc(smem_u32(smem + C::OFF_B + s * C::BSLOT));
           const int kk_n = min(C::SK, p.k_in - ks * C::SK) / 32;  // 32-K blocks in this stage
@@ -1031,12 +1057,12 @@ int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
 using MxN16  = MxCfg<16, 4, 6, 6, 1, 2, 8, 1>;
 using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0, 2>;
 // Direct-operand kernels (weights padded to K % 128 == 0):
-//                 BN  NS ND EPI  SK  PF
+//                 BN  NS ND EPI  SK  PF SFW
 #ifndef KLC_MX2_N16
-#define KLC_MX2_N16 16, 4, 2, 1, 256, 8
+#define KLC_MX2_N16 16, 4, 2, 1, 256, 8, 1
 #endif
 #ifndef KLC_MX2_N64
-#define KLC_MX2_N64 64, 3, 2, 2, 256, 0
+#define KLC_MX2_N64 64, 3, 2, 2, 256, 0, 1
 #endif
 using Mx2N16 = Mx2Cfg<KLC_MX2_N16>;
 using Mx2N64 = Mx2Cfg<KLC_MX2_N64>;
