@@ -111,6 +111,16 @@ int klc_mxfp4_transpose_scales(const uint8_t* scales, int64_t experts, int64_t r
  * preparation for the B200 kernel).  out must hold E*rows*groups_pad*16 bytes. */
 int klc_mxfp4_pad_k128(const uint8_t* blocks, int64_t experts, int64_t rows, int64_t groups, uint8_t* out, void* stream);
 
+/* Scales [E, rows, groups] in tiles of tile_rows (<= 256) rows: block
+ * [e][t][stage][chunk] of 512 bytes per 128-K stage and 128-row chunk of the
+ * tile, byte (m % 32)*16 + (m / 32)*4 + kb = scale of tile row chunk*128 + m,
+ * 32-K block kb; zero past the matrix.  tile_rows 128 gives the
+ * klc_mxfp4_scales_mx layout; 192 the tiles of the weights-as-N kernels.
+ * No reference counterpart (layout preparation for the B200 kernel).     */
+int klc_mxfp4_scales_tile_bytes(int64_t experts, int64_t rows, int64_t groups, int tile_rows, size_t* out_bytes);
+int klc_mxfp4_scales_tile(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups, int tile_rows, uint8_t* out,
+                          void* stream);
+
 int klc_mxfp4_scales_mx_bytes(int64_t experts, int64_t rows, int64_t groups, size_t* out_bytes);
 int klc_mxfp4_scales_mx(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups, uint8_t* out,
                         void* stream);
@@ -193,6 +203,11 @@ typedef struct klc_moe_weights {
    * through its repack warps.                                               */
   const uint8_t* gu_blocks_k128;
   const uint8_t* dn_blocks_k128;
+  /* gate_up / down scales in 192-row tiles (klc_mxfp4_scales_tile with
+   * tile_rows 192): with the padded blocks above (and 16-byte aligned
+   * biases) the tensor-core path runs its weights-as-N = 192 kernels.      */
+  const uint8_t* gu_scales_t192;
+  const uint8_t* dn_scales_t192;
 } klc_moe_weights;
 
 /* Expert execution + combine for given routing (idx, weights), the body of

@@ -67,6 +67,8 @@ class KlcWeights(ctypes.Structure):
         ("dn_scales_mx", c_void_p),
         ("gu_blocks_k128", c_void_p),
         ("dn_blocks_k128", c_void_p),
+        ("gu_scales_t192", c_void_p),
+        ("dn_scales_t192", c_void_p),
     ]
 
 
@@ -81,6 +83,8 @@ SIGNATURES: dict[str, list] = {
     "klc_mxfp4_transpose_scales": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "klc_mxfp4_scales_mx_bytes": [c_int64, c_int64, c_int64, POINTER(c_size_t)],
     "klc_mxfp4_pad_k128": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
+    "klc_mxfp4_scales_tile_bytes": [c_int64, c_int64, c_int64, c_int, POINTER(c_size_t)],
+    "klc_mxfp4_scales_tile": [c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p, c_void_p],
     "klc_mxfp4_scales_mx": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p],
     "klc_mx_quantize_rows": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p],
     "klc_router_status": [POINTER(c_int), POINTER(c_int), c_void_p],

@@ -882,6 +882,324 @@ __global__ void __launch_bounds__(C::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Swapped-operand variant: A = the row-block's hi/lo E4M3 activation rows (the
+// MMA's M = 128 TMEM lanes; 2*BN rows are loaded and lanes past them are never
+// read), B = kWN = 192 weight rows (N = 192) loaded by TMA's 4-bit unpacking
+// copy.  One instruction then covers 192 weight rows x 32 K (3 KB of packed
+// weights), 1.5x what the weights-as-A form covers with M = 128, so a stage needs
+// fewer MMA issues per weight byte -- the limit of the decode kernel.  In D the
+// lanes are activation rows (hi and lo of a token in lanes 2n, 2n+1) and the
+// columns weight rows (gate and up of a feature in columns 2f, 2f+1): the
+// epilogue adds hi + lo across a lane pair and applies the clamped SwiGLU across
+// a column pair, both inside a thread's registers or one shuffle.
+// Weight scales come in 192-row tiles (klc_mxfp4_scales_tile, two 512-byte
+// blocks per 128-K stage: rows 0-127 and 128-191 of the tile).
+// ---------------------------------------------------------------------------
+constexpr int kWN = 192;
+
+//   BN  max tokens of a row-block (2*BN <= 128 activation rows)
+//   NS  pipeline stages, ND accumulator sets, SK K per stage, PF L2 prefetch depth (boxes)
+template <int BN_, int NS_, int ND_, int SK_, int PF_>
+struct Mx3Cfg {
+  static constexpr int BN = BN_, NS = NS_, ND = ND_, SK = SK_, PF = PF_;
+  static constexpr int N2 = 2 * BN;
+  static_assert(N2 <= 128, "activation rows fit the MMA's 128 lanes");
+  static constexpr int SUB = SK / 128;
+  static_assert(SK == 128 || SK == 256, "stage K");
+  static constexpr int THREADS = 12 * 32;
+  static constexpr int ABOX = N2 * 128;              // activation box (= its transaction bytes)
+  static constexpr int BBOX = kWN * 128;             // weight box in shared memory (16-byte groups)
+  static constexpr int BBOX_TX = BBOX / 2;           // ... counted as the packed bytes read
+  static constexpr int ASLOT = SUB * ABOX, BSLOT = SUB * BBOX;
+  static constexpr int OFF_B = 0;
+  static constexpr int OFF_A = OFF_B + NS * BSLOT;
+  // the MMA reads 128 rows (16 KB) from every activation box start: keep 16 KB of
+  // shared memory after the last box
+  static constexpr int APAD = 16384 > ABOX ? 16384 - ABOX : 0;
+  static constexpr int OFF_ASF = OFF_A + NS * ASLOT + APAD;   // NS x SUB x 512 (activation scales)
+  static constexpr int OFF_BSF = OFF_ASF + NS * SUB * 512;    // NS x SUB x 1024 (weight scales, 2 chunks)
+  static constexpr int OFF_BAR = OFF_BSF + NS * SUB * 1024;
+  static constexpr int NUM_BARS = 4 * NS + 2 * ND + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ACC_COLS = ND * kWN;
+  static constexpr int SF_COLS = 12 * SUB;  // per box: 4 columns of activation scales, 8 of weight scales
+  static_assert(ACC_COLS + NS * SF_COLS <= kTmemCols, "TMEM budget");
+  static_assert(ABOX % 1024 == 0 && BBOX % 1024 == 0, "boxes stay 1024-byte aligned");
+  static_assert(BYTES + 1024 <= 227 * 1024, "shared memory budget");
+};
+
+// kind::mxf8f6f4 instruction descriptor: A E4M3 (activations), B E2M1 (weights),
+// fp32 accumulate, both K-major, E8M0 scales, M = 128, N = kWN; scale byte ids.
+__device__ __forceinline__ uint32_t mx3_idesc(uint32_t a_id, uint32_t b_id) {
+  return (b_id << 4) | (0u << 7) | (5u << 10) | (uint32_t(kWN >> 3) << 17) | (1u << 23) | (uint32_t(kBM >> 4) << 24) |
+         (a_id << 29);
+}
+
+template <int PHASE, class C>
+__global__ void __launch_bounds__(C::THREADS, 1)
+    mx3_expert_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, MxParams p) {
+  constexpr int NS = C::NS, ND = C::ND, SUB = C::SUB;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const uint32_t bar0 = smem_u32(smem + C::OFF_BAR);
+  auto wfull = [&](int s) { return bar0 + 8u * s; };
+  auto xfull = [&](int s) { return bar0 + 8u * (NS + s); };
+  auto sready = [&](int s) { return bar0 + 8u * (2 * NS + s); };
+  auto sempty = [&](int s) { return bar0 + 8u * (3 * NS + s); };
+  auto dfull = [&](int d) { return bar0 + 8u * (4 * NS + d); };
+  auto dempty = [&](int d) { return bar0 + 8u * (4 * NS + ND + d); };
+  const uint32_t mma_done = bar0 + 8u * (4 * NS + 2 * ND);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  const Ctl ctl{abort_flag, p.status};
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(wfull(s), 1);
+      mbar_init(xfull(s), 1);
+      mbar_init(sready(s), 4);
+      mbar_init(sempty(s), 1);
+    }
+    for (int d = 0; d < ND; ++d) {
+      mbar_init(dfull(d), 1);
+      mbar_init(dempty(d), 4);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kWarp2Mma) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  const int nrb = p.status->rowblocks;
+  const int total = nrb * p.n_mtiles;  // items: (row-block, 192-row weight tile)
+  const int kb128 = p.ksteps;
+  const int st_n = (kb128 + SUB - 1) / SUB;
+
+  if (warp == kWarp2A) {
+    // ------------------------------------------------------------ weights (operand B)
+    if (lane == 0) {
+      uint32_t it = 0, boxes = 0;
+      bool ok = true;
+      int pf_item = blockIdx.x, pf_k = 0;
+      uint32_t pf_n = 0;
+      int4 pf_rb = pf_item < total ? p.rowblocks[pf_item / p.n_mtiles] : make_int4(0, 0, 0, 0);
+      auto prefetch_ahead = [&](uint32_t upto) {
+        while (pf_n < upto && pf_item < total) {
+          tma_prefetch_3d(&map_w, pf_k * 128, (pf_item % p.n_mtiles) * kWN, pf_rb.x);
+          ++pf_n;
+          if (++pf_k == kb128) {
+            pf_k = 0;
+            pf_item += gridDim.x;
+            if (pf_item < total) pf_rb = p.rowblocks[pf_item / p.n_mtiles];
+          }
+        }
+      };
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int4 rb = p.rowblocks[item / p.n_mtiles];
+        const int nt = item % p.n_mtiles;
+        const uint8_t* sfw_item = p.sfa + (int64_t(rb.x) * p.n_mtiles + nt) * int64_t(kb128) * 1024;
+        for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
+          prefetch_ahead(boxes + uint32_t(NS * SUB + C::PF));
+          const int s = int(it % NS);
+          if (!(ok = wait_bar(sempty(s), ((it / NS) & 1) ^ 1, ctl, 80))) break;
+          const int nb = min(SUB, kb128 - ks * SUB);
+          mbar_arrive_expect_tx(wfull(s), uint32_t(nb * (C::BBOX_TX + 1024)));
+          for (int j = 0; j < nb; ++j)
+            tma_load_3d(smem_u32(smem + C::OFF_B + s * C::BSLOT + j * C::BBOX), &map_w, (ks * SUB + j) * 128, nt * kWN, rb.x,
+                        wfull(s));
+          bulk_load(smem_u32(smem + C::OFF_BSF + s * SUB * 1024), sfw_item + int64_t(ks * SUB) * 1024, uint32_t(nb * 1024),
+                    wfull(s));
+          boxes += uint32_t(nb);
+        }
+      }
+      if (!ok) drain_ring(wfull(0), NS, it);
+    }
+  } else if (warp == kWarp2B) {
+    // ------------------------------------------------------------ activations (operand A)
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        const int rbi = item / p.n_mtiles;
+        const int4 rb = p.rowblocks[rbi];
+        const uint8_t* sfx_rb = p.sfb + int64_t(rbi) * kb128 * 512;
+        for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
+          const int s = int(it % NS);
+          if (!(ok = wait_bar(sempty(s), ((it / NS) & 1) ^ 1, ctl, 81))) break;
+          const int nb = min(SUB, kb128 - ks * SUB);
+          mbar_arrive_expect_tx(xfull(s), uint32_t(nb * (C::ABOX + 512)));
+          for (int j = 0; j < nb; ++j)
+            tma_load_2d(smem_u32(smem + C::OFF_A + s * C::ASLOT + j * C::ABOX), &map_x, (ks * SUB + j) * kStageK, 2 * rb.y,
+                        xfull(s));
+          bulk_load(smem_u32(smem + C::OFF_ASF + s * SUB * 512), sfx_rb + int64_t(ks * SUB) * 512, uint32_t(nb * 512),
+                    xfull(s));
+        }
+      }
+      if (!ok) drain_ring(xfull(0), NS, it);
+    }
+  } else if (warp >= kWarp2Sf0 && warp < kWarp2Sf0 + 4) {
+    // ------------------------------------------------------------ scales into TMEM
+    const int q = warp & 3;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+      for (int ks = 0; ks < st_n; ++ks, ++it) {
+        const int s = int(it % NS);
+        const uint32_t ph = (it / NS) & 1;
+        if (lane == 0) ok = wait_bar(wfull(s), ph, ctl, 82) && wait_bar(xfull(s), ph, ctl, 83);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (ok && lane != 0) ok = mbar_try_wait(wfull(s), ph) && mbar_try_wait(xfull(s), ph);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        tc_fence_after();  // the set is rewritten after the MMAs of its previous use completed
+        const int nb = min(SUB, kb128 - ks * SUB);
+        const uint32_t sf_t = tmem + (uint32_t(q * 32) << 16) + uint32_t(C::ACC_COLS + s * C::SF_COLS);
+        for (int j = 0; j < nb; ++j) {
+          tmem_st4(sf_t + 12 * j, *reinterpret_cast<const uint4*>(smem + C::OFF_ASF + (s * SUB + j) * 512 + lane * 16));
+          tmem_st4(sf_t + 12 * j + 4, *reinterpret_cast<const uint4*>(smem + C::OFF_BSF + (s * SUB + j) * 1024 + lane * 16));
+          tmem_st4(sf_t + 12 * j + 8, *reinterpret_cast<const uint4*>(smem + C::OFF_BSF + (s * SUB + j) * 1024 + 512 + lane * 16));
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sready(s));
+      }
+    }
+  } else if (warp == kWarp2Mma) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0, ic = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+        const int d = ic % ND;
+        const uint32_t d_tmem = tmem + uint32_t(d * kWN);
+        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 90))) break;
+        tc_fence_after();
+        for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
+          const int s = int(it % NS);
+          if (!(ok = wait_bar(sready(s), (it / NS) & 1, ctl, 91))) break;
+          tc_fence_after();
+          const uint32_t sf_t = tmem + uint32_t(C::ACC_COLS + s * C::SF_COLS);
+          const uint64_t xdesc0 = sw128_desc(smem_u32(smem + C::OFF_A + s * C::ASLOT));
+          const uint64_t wdesc0 = sw128_desc(smem_u32(smem + C::OFF_B + s * C::BSLOT));
+          const int kk_n = min(C::SK, p.k_in - ks * C::SK) / 32;
+#pragma unroll
+          for (int kk = 0; kk < 4 * SUB; ++kk) {
+            if (kk < kk_n) {
+              const int j = kk >> 2, kb = kk & 3;
+              mx_mma(d_tmem, xdesc0 + uint64_t(j * (C::ABOX >> 4) + kb * 2), wdesc0 + uint64_t(j * (C::BBOX >> 4) + kb * 2),
+                     mx3_idesc(uint32_t(kb), uint32_t(kb)), (sf_t + 12 * j) | (uint32_t(kb) << 30),
+                     (sf_t + 12 * j + 4) | (uint32_t(kb) << 30), (ks == 0 && kk == 0) ? 0u : 1u);
+            }
+          }
+          tc_commit(sempty(s));
+        }
+        if (ok) tc_commit(dfull(d));
+      }
+      tc_commit(mma_done);
+      drain_wait(mma_done, 0);
+    }
+  } else if (warp >= kWarp2Epi0 && warp < kWarp2Epi0 + 4) {
+    // ------------------------------------------------------------ epilogue
+    // warp q reads TMEM lanes 32q..32q+31 = activation rows of tokens 16q..16q+15
+    const int q = warp & 3;
+    uint32_t ic = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+      const int4 rb = p.rowblocks[item / p.n_mtiles];
+      const int nt = item % p.n_mtiles;
+      const int e = rb.x, r0 = rb.y, nrows = rb.z;
+      const int d = ic % ND;
+      ok = wait_bar_backoff(dfull(d), (ic / ND) & 1, ctl, 92);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      const int n = 16 * q + (lane >> 1);     // this lane's token within the row-block
+      const bool tok = n < nrows;
+      const bool hi_lane = (lane & 1) == 0;   // even lane: hi row, holds the sum
+      if (16 * q < nrows) {
+        const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16) + uint32_t(d * kWN);
+        float sq = 0.f;
+        for (int c0 = 0; c0 < kWN; c0 += 16) {
+          uint32_t raw[16];
+          tmem_ld16(lane_base + uint32_t(c0), raw);
+          tmem_wait_ld();
+          const int j0 = nt * kWN + c0;  // first weight row of this chunk
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float mine = __uint_as_float(raw[i]);
+            v[i] = mine + __shfl_xor_sync(0xffffffffu, mine, 1);  // hi + lo
+          }
+          if (j0 < p.n_out) {
+            // 16 bias values of this chunk (j0 is a multiple of 16; n_out a multiple of 64)
+            const uint4 b0 = *reinterpret_cast<const uint4*>(p.bias + int64_t(e) * p.n_out + j0);
+            const uint4 b1 = *reinterpret_cast<const uint4*>(p.bias + int64_t(e) * p.n_out + j0 + 8);
+            const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float x = v[i];
+              if (p.precision == KLC_PREC_BF16) x = round_bf16(x);
+              v[i] = x + bf16_to_f32(uint16_t((i & 1) ? (bw[i >> 1] >> 16) : (bw[i >> 1] & 0xFFFFu)));
+            }
+            if (tok && hi_lane) {
+              uint16_t* orow = p.out + int64_t(r0 + n) * p.out_ld;
+              if (PHASE == 1) {
+                // columns 2f, 2f+1: gate and up of feature j0/2 + f
+                uint32_t pk[4];
+#pragma unroll
+                for (int f = 0; f < 8; ++f) {
+                  const float gate = fminf(v[2 * f], p.limit);
+                  const float up = fminf(fmaxf(v[2 * f + 1], -p.limit), p.limit);
+                  const float glu = gate * (1.0f / (1.0f + expf(-(gate * p.alpha))));
+                  const float gated = (up + 1.0f) * glu;
+                  const uint16_t gb = f32_to_bf16(gated);
+                  const float gr = bf16_to_f32(gb);
+                  sq += (p.precision == KLC_PREC_BF16) ? gr * gr : gated * gated;
+                  if (f & 1) pk[f >> 1] |= uint32_t(gb) << 16;
+                  else pk[f >> 1] = gb;
+                }
+                *reinterpret_cast<uint4*>(orow + (j0 >> 1)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              } else {
+                uint32_t pk[8];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const uint16_t ob = f32_to_bf16(v[i]);
+                  sq += v[i] * v[i];
+                  if (i & 1) pk[i >> 1] |= uint32_t(ob) << 16;
+                  else pk[i >> 1] = ob;
+                }
+                *reinterpret_cast<uint4*>(orow + j0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                *reinterpret_cast<uint4*>(orow + j0 + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+              }
+            }
+          }
+        }
+        if (p.normsq != nullptr && tok && hi_lane)
+          atomicAdd(&p.normsq[int64_t(p.rows[r0 + n]) * 2 + (PHASE == 1 ? 0 : 1)], sq);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dempty(d));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == kWarp2Mma)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 template <int PHASE, class C>
@@ -995,6 +1313,78 @@ int launch_mx2_both(const ExpertArgs& a, const uint8_t* gu_k128, const uint8_t* 
   return st;
 }
 
+template <int PHASE, class C>
+int launch_mx3_phase(const uint8_t* blocks_k128, const uint8_t* act_q, int64_t rows_cap, int experts, MxParams p,
+                     int max_rowblocks, cudaStream_t stream) {
+  CUtensorMap mw, mx;
+  const uint64_t K = uint64_t(p.k_in), N = uint64_t(p.n_out);
+  const uint64_t Kp = (K + 127) / 128 * 128;
+  p.ksteps = int(Kp / 128);
+  p.n_mtiles = int((N + kWN - 1) / kWN);  // 192-row weight tiles
+  KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(blocks_k128) & 31) == 0, "tensor-core path: padded weight blocks must be 32-byte aligned");
+  {
+    const uint64_t dims[3] = {Kp, N, uint64_t(experts)};
+    const uint64_t strides[2] = {Kp / 2, N * Kp / 2};
+    const uint32_t box[3] = {128, uint32_t(kWN), 1};
+    int st = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, blocks_k128, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  {
+    const uint64_t dims[2] = {K, 2 * uint64_t(rows_cap)};
+    const uint64_t strides[1] = {K};
+    const uint32_t box[2] = {kStageK, uint32_t(C::N2)};
+    int st = make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, act_q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  const int smem = (C::BYTES + 1024 > 118 * 1024) ? C::BYTES + 1024 : 118 * 1024;
+  KLC_CUDA(cudaFuncSetAttribute(mx3_expert_kernel<PHASE, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
+  const int grid = int(items < sm_count() ? items : sm_count());
+  if (grid <= 0) return KLC_OK;
+  mx3_expert_kernel<PHASE, C><<<grid, C::THREADS, smem, stream>>>(mw, mx, p);
+  KLC_LAUNCH_CHECK("tcgen05 expert launch");
+  return KLC_OK;
+}
+
+template <class C>
+int launch_mx3_both(const ExpertArgs& a, const uint8_t* gu_k128, const uint8_t* dn_k128, cudaStream_t stream) {
+  const klc_moe_weights& w = *a.wts;
+  MxParams p1{};
+  p1.n_out = int(2 * a.inter);
+  p1.k_in = int(a.hidden);
+  p1.rowblocks = a.rowblocks;
+  p1.status = a.status_rw;
+  p1.rows = a.rows;
+  p1.sfa = w.gu_scales_t192;
+  p1.sfb = a.sfb1;
+  p1.bias = w.gu_bias;
+  p1.out = static_cast<uint16_t*>(a.gated);
+  p1.out_ld = int(a.inter);
+  p1.normsq = a.normsq;
+  p1.precision = a.precision;
+  p1.limit = w.swiglu_limit;
+  p1.alpha = w.alpha;
+  int st = launch_quantize_rows(a.x, a.hidden, a.rows, a.k, a.rowblocks, a.status, a.max_rowblocks, 1, a.xq, a.sfb1, stream);
+  if (st != KLC_OK) return st;
+  st = launch_mx3_phase<1, C>(gu_k128, a.xq, a.rows_cap, int(a.experts), p1, a.max_rowblocks, stream);
+  if (st != KLC_OK) return st;
+  stage_mark(kStageGateUp, stream);
+  st = launch_quantize_rows(static_cast<const uint16_t*>(a.gated), a.inter, nullptr, 1, a.rowblocks, a.status,
+                            a.max_rowblocks, 1, a.gq, a.sfb2, stream);
+  if (st != KLC_OK) return st;
+  MxParams p2 = p1;
+  p2.n_out = int(a.hidden);
+  p2.k_in = int(a.inter);
+  p2.sfa = w.dn_scales_t192;
+  p2.sfb = a.sfb2;
+  p2.bias = w.dn_bias;
+  p2.out = a.y;
+  p2.out_ld = int(a.hidden);
+  st = launch_mx3_phase<2, C>(dn_k128, a.gq, a.rows_cap, int(a.experts), p2, a.max_rowblocks, stream);
+  stage_mark(kStageDown, stream);
+  return st;
+}
+
 template <class C>
 int launch_mx_both(const ExpertArgs& a, cudaStream_t stream) {
   const klc_moe_weights& w = *a.wts;
@@ -1066,6 +1456,16 @@ using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0, 2>;
 #endif
 using Mx2N16 = Mx2Cfg<KLC_MX2_N16>;
 using Mx2N64 = Mx2Cfg<KLC_MX2_N64>;
+// Swapped-operand kernels (weights as N = 192, scales in 192-row tiles):
+//                 BN  NS ND  SK  PF
+#ifndef KLC_MX3_N16
+#define KLC_MX3_N16 16, 3, 2, 256, 8
+#endif
+#ifndef KLC_MX3_N64
+#define KLC_MX3_N64 64, 2, 2, 256, 0
+#endif
+using Mx3N16 = Mx3Cfg<KLC_MX3_N16>;
+using Mx3N64 = Mx3Cfg<KLC_MX3_N64>;
 
 }  // namespace
 
@@ -1128,6 +1528,14 @@ int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   const klc_moe_weights& w = *a.wts;
   const uint8_t* gu = w.gu_blocks_k128 != nullptr ? w.gu_blocks_k128 : (a.hidden % 128 == 0 ? w.gu_blocks : nullptr);
   const uint8_t* dn = w.dn_blocks_k128 != nullptr ? w.dn_blocks_k128 : (a.inter % 128 == 0 ? w.dn_blocks : nullptr);
+  const bool bias16 = ((reinterpret_cast<uintptr_t>(w.gu_bias) | reinterpret_cast<uintptr_t>(w.dn_bias)) & 15) == 0;
+  if (gu != nullptr && dn != nullptr && w.gu_scales_t192 != nullptr && w.dn_scales_t192 != nullptr && bias16) {
+    switch (a.block_n) {
+      case 16: return launch_mx3_both<Mx3N16>(a, gu, dn, stream);
+      case 64: return launch_mx3_both<Mx3N64>(a, gu, dn, stream);
+      default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 16 or 64");
+    }
+  }
   if (gu != nullptr && dn != nullptr) {
     switch (a.block_n) {
       case 16: return launch_mx2_both<Mx2N16>(a, gu, dn, stream);

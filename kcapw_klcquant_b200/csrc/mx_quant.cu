@@ -39,6 +39,25 @@ __global__ void scales_mx_kernel(const uint8_t* __restrict__ scales, int64_t row
   }
 }
 
+// Weight scales in tiles of `tile` rows: block [e][t][stage][chunk] (512 bytes) holds,
+// for row m = chunk*128 + mm of tile t, byte (mm % 32)*16 + (mm / 32)*4 + kb = the
+// scale of 32-K block 4*stage + kb; rows past the matrix or the tile are zero.
+__global__ void scales_tile_kernel(const uint8_t* __restrict__ scales, int64_t rows, int64_t groups, int tile, int ntiles,
+                                   int stages, int chunks, uint8_t* __restrict__ out) {
+  const int stage = blockIdx.x, t = blockIdx.y;
+  const int64_t e = blockIdx.z;
+  const int m = threadIdx.x;  // row within the tile, blockDim.x = chunks * 128
+  const int64_t row = int64_t(t) * tile + m;
+  const int chunk = m >> 7, mm = m & 127;
+  uint8_t* blk = out + (((e * ntiles + t) * stages + stage) * chunks + chunk) * 512;
+#pragma unroll
+  for (int kb = 0; kb < 4; ++kb) {
+    const int64_t g = int64_t(stage) * 4 + kb;
+    const uint8_t v = (m < tile && row < rows && g < groups) ? scales[(e * rows + row) * groups + g] : uint8_t(0);
+    blk[(mm & 31) * 16 + (mm >> 5) * 4 + kb] = v;
+  }
+}
+
 // Rows of 16-byte groups [E*rows][groups] -> [E*rows][groups_pad], zero groups past the row.
 __global__ void pad_k128_kernel(const uint4* __restrict__ src, int64_t nrows, int64_t groups, int64_t groups_pad,
                                 uint4* __restrict__ dst) {
@@ -213,5 +232,31 @@ extern "C" int klc_mxfp4_pad_k128(const uint8_t* blocks, int64_t experts, int64_
   pad_k128_kernel<<<blocks_n, 256, 0, as_stream(stream)>>>(reinterpret_cast<const uint4*>(blocks), nrows, groups, gp,
                                                             reinterpret_cast<uint4*>(out));
   KLC_LAUNCH_CHECK("klc_mxfp4_pad_k128 launch");
+  return KLC_OK;
+}
+
+extern "C" int klc_mxfp4_scales_tile_bytes(int64_t experts, int64_t rows, int64_t groups, int tile_rows, size_t* out_bytes) {
+  using namespace klc;
+  KLC_CHECK_ARG(experts >= 0 && rows >= 0 && groups >= 0 && tile_rows >= 1 && tile_rows <= 256,
+                "klc_mxfp4_scales_tile_bytes: bad sizes");
+  KLC_CHECK_ARG(out_bytes != nullptr, "klc_mxfp4_scales_tile_bytes: null output");
+  *out_bytes = size_t(experts) * size_t((rows + tile_rows - 1) / tile_rows) * size_t((groups + 3) / 4) *
+               size_t((tile_rows + 127) / 128) * 512;
+  return KLC_OK;
+}
+
+extern "C" int klc_mxfp4_scales_tile(const uint8_t* scales, int64_t experts, int64_t rows, int64_t groups, int tile_rows,
+                                     uint8_t* out, void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(experts >= 0 && rows >= 0 && groups >= 0 && tile_rows >= 1 && tile_rows <= 256,
+                "klc_mxfp4_scales_tile: bad sizes");
+  if (experts == 0 || rows == 0 || groups == 0) return KLC_OK;
+  KLC_CHECK_ARG(scales && out, "klc_mxfp4_scales_tile: null pointer");
+  const int64_t ntiles = (rows + tile_rows - 1) / tile_rows, stages = (groups + 3) / 4;
+  const int chunks = (tile_rows + 127) / 128;
+  KLC_CHECK_ARG(experts <= 65535 && ntiles <= 65535 && stages <= 0x7fffffff, "klc_mxfp4_scales_tile: too large");
+  scales_tile_kernel<<<dim3(unsigned(stages), unsigned(ntiles), unsigned(experts)), chunks * 128, 0, as_stream(stream)>>>(
+      scales, rows, groups, tile_rows, int(ntiles), int(stages), chunks, out);
+  KLC_LAUNCH_CHECK("klc_mxfp4_scales_tile launch");
   return KLC_OK;
 }

@@ -101,6 +101,7 @@ class MoeLayer:
             self.router_weight.data_ptr(), self.router_bias.data_ptr(), float(swiglu_limit), float(alpha),
             _lib.ptr(packed.gu_scales_mx), _lib.ptr(packed.dn_scales_mx),
             _lib.ptr(packed.gu_blocks_k128), _lib.ptr(packed.dn_blocks_k128),
+            _lib.ptr(packed.gu_scales_t192), _lib.ptr(packed.dn_scales_t192),
         )
 
     @classmethod

@@ -88,6 +88,19 @@ def pad_k128(blocks: torch.Tensor) -> torch.Tensor | None:
     return out
 
 
+def scales_tile(scales: torch.Tensor, tile_rows: int) -> torch.Tensor:
+    """E8M0 scales [E, rows, groups] -> 512-byte blocks in tiles of ``tile_rows`` rows
+    [E, ceil(rows/tile), ceil(groups/4), ceil(tile/128), 512] (klc_mxfp4_scales_tile)."""
+    scales = scales.to(torch.uint8).contiguous()
+    _lib.require_cuda(scales)
+    E, rows, groups = scales.shape
+    t = (rows + tile_rows - 1) // tile_rows
+    out = torch.empty((E, t, (groups + 3) // 4, (tile_rows + 127) // 128, 512), dtype=torch.uint8, device=scales.device)
+    with torch.cuda.device(scales.device):
+        _lib.check(_lib.lib().klc_mxfp4_scales_tile(scales.data_ptr(), E, rows, groups, int(tile_rows), out.data_ptr(), _lib.stream_ptr()))
+    return out
+
+
 def scales_mx(scales: torch.Tensor) -> torch.Tensor:
     """E8M0 scales [E, rows, groups] -> the tensor-core path's 512-byte scale blocks
     [E, ceil(rows/128), ceil(groups/4), 512] (klc_mxfp4_scales_mx)."""
@@ -119,6 +132,9 @@ class PackedLayer:
     # path straight into its operand layout; None where K already is a multiple of 128
     gu_blocks_k128: torch.Tensor | None = None
     dn_blocks_k128: torch.Tensor | None = None
+    # scales in 192-row tiles (scales_tile): the tensor-core path's weights-as-N kernels
+    gu_scales_t192: torch.Tensor | None = None
+    dn_scales_t192: torch.Tensor | None = None
 
     @property
     def experts(self) -> int:
@@ -135,7 +151,7 @@ class PackedLayer:
     @property
     def nbytes(self) -> int:
         ts = (self.gu_blocks, self.gu_scales_t, self.dn_blocks, self.dn_scales_t, self.gu_scales_mx, self.dn_scales_mx,
-              self.gu_blocks_k128, self.dn_blocks_k128)
+              self.gu_blocks_k128, self.dn_blocks_k128, self.gu_scales_t192, self.dn_scales_t192)
         return sum(t.numel() for t in ts if t is not None)
 
     @classmethod
@@ -151,7 +167,8 @@ class PackedLayer:
             raise ValueError(f"inconsistent MXFP4 layer shapes {gb.shape} {gs.shape} {db.shape} {ds.shape}")
         if db.shape[1] != g_h * 32 or db.shape[2] * 64 != two_i:
             raise ValueError("down_proj must be [E, H, I/32, 16] with gate_up [E, 2I, H/32, 16]")
-        return cls(gb, transpose_scales(gs), db, transpose_scales(ds), gs, ds, scales_mx(gs), scales_mx(ds), pad_k128(gb), pad_k128(db))
+        return cls(gb, transpose_scales(gs), db, transpose_scales(ds), gs, ds, scales_mx(gs), scales_mx(ds), pad_k128(gb), pad_k128(db),
+                   scales_tile(gs, 192), scales_tile(ds, 192))
 
 
 @dataclass

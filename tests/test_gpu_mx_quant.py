@@ -122,3 +122,27 @@ def test_pad_k128_matches_numpy():
     want[:, :, :90] = b.numpy()
     np.testing.assert_array_equal(out, want)
     assert pad_k128(torch.zeros((1, 4, 8, 16), dtype=torch.uint8, device=DEV)) is None
+
+
+def test_scales_tile_layouts():
+    """klc_mxfp4_scales_tile: tile 128 equals klc_mxfp4_scales_mx; tile 192 against numpy."""
+    from kcapw_klcquant_b200.mxfp4_expert import scales_mx, scales_tile
+
+    g = torch.Generator().manual_seed(6)
+    s = torch.randint(0, 256, (2, 400, 90), generator=g, dtype=torch.uint8)
+    sd = s.to(DEV)
+    np.testing.assert_array_equal(scales_tile(sd, 128).cpu().numpy().reshape(-1), scales_mx(sd).cpu().numpy().reshape(-1))
+    got = scales_tile(sd, 192).cpu().numpy()  # [E, tiles, stages, 2, 512]
+    E, rows, G = s.shape
+    want = np.zeros_like(got)
+    sn = s.numpy()
+    for t in range(got.shape[1]):
+        for m in range(192):
+            r = t * 192 + m
+            if r >= rows:
+                continue
+            for g4 in range(G):
+                st, kb = divmod(g4, 4)
+                c, mm = divmod(m, 128)
+                want[:, t, st, c, (mm % 32) * 16 + (mm // 32) * 4 + kb] = sn[:, r, g4]
+    np.testing.assert_array_equal(got, want)

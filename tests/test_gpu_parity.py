@@ -518,3 +518,32 @@ def test_bench_configs_subsample_vs_oracle(T, zipf, seed, path):
     m = parity.assert_output_close(bits_of(y[sample]), want, f"T={T} zipf={zipf} {path}")
     if path == "simt":
         assert m["bit_equal_frac"] >= 0.99, m
+
+
+@pytest.mark.parametrize("kernel", ["weights_as_n192", "direct_operand", "repack"])
+@pytest.mark.parametrize("name", ["c1_e128_h2880_t8", "mid_zipf_e16_h2880_t64"])
+def test_tensor_core_kernel_forms_vs_reference(case_cache, name, kernel):
+    """Each tensor-core kernel form against the reference's outputs (replayed routing):
+    weights as N = 192 (the default), weights as A with TMA-unpacked operands (no
+    192-row scale tiles), and the repack form (no K-padded blocks either).  The
+    mid case runs the 64-row tiles, the c1 case the 16-row tiles."""
+    import dataclasses
+
+    from kcapw_klcquant_b200 import MoeLayer
+
+    if "tc" not in PATHS:
+        pytest.skip("tensor-core path not available")
+    fx, dims, layer, x, ml = load(case_cache, name)
+    packed = ml.packed
+    if kernel != "weights_as_n192":
+        packed = dataclasses.replace(packed, gu_scales_t192=None, dn_scales_t192=None)
+    if kernel == "repack":
+        packed = dataclasses.replace(packed, gu_blocks_k128=None, dn_blocks_k128=None)
+    m = MoeLayer(packed, ml.router_weight, ml.router_bias, ml.gate_up_bias, ml.down_bias, top_k=dims.top_k, path="tc")
+    for precision in ("bf16", "fp32"):
+        idx = torch.from_numpy(fx[f"experts_{precision}"].astype(np.int32))
+        w = torch.from_numpy(fx[f"weights_{precision}"].view(np.int16)).view(torch.bfloat16)
+        y, norms = m.experts_forward(x.to(DEV), idx, w, precision=precision, return_norms=True)
+        m.check_device_status()
+        parity.assert_output_close(bits_of(y), fx[f"out_{precision}"], f"{name}/{kernel}/{precision}")
+        np.testing.assert_allclose(norms.cpu().numpy(), fx[f"norms_{precision}"], rtol=5e-3)
