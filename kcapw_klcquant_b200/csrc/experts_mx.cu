@@ -899,14 +899,18 @@ constexpr int kWN = 192;
 
 //   BN  max tokens of a row-block (2*BN <= 128 activation rows)
 //   NS  pipeline stages, ND accumulator sets, SK K per stage, PF L2 prefetch depth (boxes)
-template <int BN_, int NS_, int ND_, int SK_, int PF_>
+//   EPI epilogue warpgroups (warps 4-7, 12-15): warpgroup g takes the 16-column
+//       chunks c with c % EPI == g, so a decode tile (all tokens in lane quarter 0)
+//       is still read by EPI warps at once
+template <int BN_, int NS_, int ND_, int SK_, int PF_, int EPI_ = 2>
 struct Mx3Cfg {
-  static constexpr int BN = BN_, NS = NS_, ND = ND_, SK = SK_, PF = PF_;
+  static constexpr int BN = BN_, NS = NS_, ND = ND_, SK = SK_, PF = PF_, EPI = EPI_;
   static constexpr int N2 = 2 * BN;
   static_assert(N2 <= 128, "activation rows fit the MMA's 128 lanes");
+  static_assert(EPI == 1 || EPI == 2, "epilogue warpgroups");
   static constexpr int SUB = SK / 128;
   static_assert(SK == 128 || SK == 256, "stage K");
-  static constexpr int THREADS = 12 * 32;
+  static constexpr int THREADS = (EPI == 2 ? 16 : 12) * 32;
   static constexpr int ABOX = N2 * 128;              // activation box (= its transaction bytes)
   static constexpr int BBOX = kWN * 128;             // weight box in shared memory (16-byte groups)
   static constexpr int BBOX_TX = BBOX / 2;           // ... counted as the packed bytes read
@@ -965,7 +969,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     }
     for (int d = 0; d < ND; ++d) {
       mbar_init(dfull(d), 1);
-      mbar_init(dempty(d), 4);
+      mbar_init(dempty(d), 4 * C::EPI);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -1108,10 +1112,12 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       tc_commit(mma_done);
       drain_wait(mma_done, 0);
     }
-  } else if (warp >= kWarp2Epi0 && warp < kWarp2Epi0 + 4) {
+  } else if ((warp >= kWarp2Epi0 && warp < kWarp2Epi0 + 4) || (C::EPI == 2 && warp >= kWarp2Epi2 && warp < kWarp2Epi2 + 4)) {
     // ------------------------------------------------------------ epilogue
-    // warp q reads TMEM lanes 32q..32q+31 = activation rows of tokens 16q..16q+15
+    // warp q reads TMEM lanes 32q..32q+31 = activation rows of tokens 16q..16q+15;
+    // warpgroup eg takes the column chunks c with c % EPI == eg
     const int q = warp & 3;
+    const int eg = warp >= kWarp2Epi2 ? 1 : 0;
     uint32_t ic = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
@@ -1128,9 +1134,23 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       if (16 * q < nrows) {
         const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16) + uint32_t(d * kWN);
         float sq = 0.f;
-        for (int c0 = 0; c0 < kWN; c0 += 16) {
+        // bias of the first chunk, loaded before the accumulators are read; each
+        // chunk then loads the next chunk's bias ahead of its own work
+        const uint16_t* brow = p.bias + int64_t(e) * p.n_out;
+        auto load_bias = [&](int c0, uint4& b0, uint4& b1) {
+          const int j = nt * kWN + c0;
+          if (c0 < kWN && j < p.n_out) {  // j is a multiple of 16; n_out a multiple of 64
+            b0 = *reinterpret_cast<const uint4*>(brow + j);
+            b1 = *reinterpret_cast<const uint4*>(brow + j + 8);
+          }
+        };
+        uint4 nb0 = make_uint4(0, 0, 0, 0), nb1 = nb0;
+        load_bias(16 * eg, nb0, nb1);
+        for (int c0 = 16 * eg; c0 < kWN; c0 += 16 * C::EPI) {
           uint32_t raw[16];
           tmem_ld16(lane_base + uint32_t(c0), raw);
+          const uint4 b0 = nb0, b1 = nb1;
+          load_bias(c0 + 16 * C::EPI, nb0, nb1);
           tmem_wait_ld();
           const int j0 = nt * kWN + c0;  // first weight row of this chunk
           float v[16];
@@ -1140,9 +1160,6 @@ __global__ void __launch_bounds__(C::THREADS, 1)
             v[i] = mine + __shfl_xor_sync(0xffffffffu, mine, 1);  // hi + lo
           }
           if (j0 < p.n_out) {
-            // 16 bias values of this chunk (j0 is a multiple of 16; n_out a multiple of 64)
-            const uint4 b0 = *reinterpret_cast<const uint4*>(p.bias + int64_t(e) * p.n_out + j0);
-            const uint4 b1 = *reinterpret_cast<const uint4*>(p.bias + int64_t(e) * p.n_out + j0 + 8);
             const uint32_t bw[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
@@ -1457,12 +1474,14 @@ using MxN64  = MxCfg<64, 4, 4, 4, 1, 2, 0, 2>;
 using Mx2N16 = Mx2Cfg<KLC_MX2_N16>;
 using Mx2N64 = Mx2Cfg<KLC_MX2_N64>;
 // Swapped-operand kernels (weights as N = 192, scales in 192-row tiles):
-//                 BN  NS ND  SK  PF
+//                 BN  NS ND  SK  PF EPI
+// (measured on B200, gate_up + down ms: decode T=256 0.290 + 0.146, config 3
+// T=16384 2.76 + 1.35; 128-K stages win for 64-row tiles, 256-K stages for 16-row)
 #ifndef KLC_MX3_N16
-#define KLC_MX3_N16 16, 3, 2, 256, 8
+#define KLC_MX3_N16 16, 3, 2, 256, 0, 2
 #endif
 #ifndef KLC_MX3_N64
-#define KLC_MX3_N64 64, 2, 2, 256, 0
+#define KLC_MX3_N64 64, 4, 2, 128, 0, 2
 #endif
 using Mx3N16 = Mx3Cfg<KLC_MX3_N16>;
 using Mx3N64 = Mx3Cfg<KLC_MX3_N64>;
