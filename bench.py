@@ -674,6 +674,101 @@ def run_layer(args, world, rank, local):
         print(json.dumps(line))
 
 
+def run_stack(args, world, rank, local):
+    """Config 4: a 36-layer MoE-only stack (RMSNorm + residual between the blocks), 32
+    sequences x 128 decode steps, experts sharded over the ranks (N=1: one GPU).  One
+    decode step of all layers is captured as a CUDA graph and replayed per step."""
+    from kcapw_klcquant_b200 import synthetic as syn
+    from kcapw_klcquant_b200.ep import ExpertParallelMoe
+    from kcapw_klcquant_b200.stack import MoeStack
+
+    device = torch.device("cuda", local)
+    n_layers, seqs, steps = args.layers, args.tokens, args.decode_steps
+    if seqs % world:
+        raise SystemExit(f"{seqs} sequences cannot be split over {world} ranks")
+    T = seqs // world
+    layers, norms = [], []
+    for li in range(n_layers):  # independent seeded weights per layer (seed 1000 + layer)
+        t = make_tensors(1000 + li, device)
+        if world == 1:
+            layers.append(layer_from(t, device))
+        else:
+            layers.append(ExpertParallelMoe(0, t, device, top_k=TOP_K, path=args.path, exchange="p2p", max_tokens=T))
+        norms.append(syn.make_rms_weight(GPT_OSS_H, seed=1000 + li, device=device))
+        del t
+        torch.cuda.empty_cache()
+    stack = MoeStack(layers, norms)
+    inputs = syn.make_hidden(steps * seqs, GPT_OSS_H, seed=args.seed, device=device).view(steps, seqs, GPT_OSS_H)
+    inputs = inputs[:, rank * T : (rank + 1) * T].contiguous()
+    n0 = launch_count()
+    eager = stack.step(inputs[0]).clone()  # also sizes every workspace before the capture
+    launches = launch_count() - n0
+    stack.capture(inputs[0])
+    replayed = stack.replay(inputs[0]).clone()
+    graph_equal = bool(torch.equal(replayed, eager))
+    for s in range(args.warmup):
+        stack.replay(inputs[s % steps])
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    clk = ClockSampler(local)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk.start()
+    a.record()
+    for s in range(steps):
+        stack.replay(inputs[s])
+    b.record()
+    torch.cuda.synchronize()
+    clk.stop()
+    barrier(world)
+    ms = reduce_over_ranks(a.elapsed_time(b), world, "max")
+    # end to end: every step's input uploaded from pinned host memory, its output read back
+    host_in = inputs.cpu().pin_memory()
+    host_out = torch.empty((T, GPT_OSS_H), dtype=torch.bfloat16).pin_memory()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        y = stack.replay(host_in[s].to(device, non_blocking=True))
+        host_out.copy_(y, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = reduce_over_ranks(e0.elapsed_time(e1), world, "max")
+    for layer in layers:
+        if hasattr(layer, "check_device_status"):
+            layer.check_device_status()
+    # parity: N>1, the first two layers of the stack against the single-GPU layers on this rank's tokens
+    parity = {"graph_replay_equals_eager": bool(reduce_over_ranks(1.0 if graph_equal else 0.0, world, "min") == 1.0)}
+    if world > 1:
+        sub = MoeStack(layers[:2], norms[:2])
+        y_ep = sub.step(inputs[1])
+        full = [layer_from(make_tensors(1000 + li, device), device) for li in range(2)]
+        y_ref = MoeStack(full, norms[:2]).step(inputs[1])
+        m = compare(y_ep, y_ref)
+        parity["two_layers_vs_single_gpu"] = {"cosine_min": reduce_over_ranks(m["cosine"], world, "min"),
+                                              "bit_equal_frac_min": reduce_over_ranks(m["bit_equal_frac"], world, "min")}
+        del full
+    stack.release()
+    for layer in layers:
+        if hasattr(layer, "close"):
+            layer.close()
+    tok = seqs * steps
+    line = base_line(args, world, tok / (ms / 1e3), ms / steps, launches,
+                     f"config 4: {n_layers}-layer MoE stack (RMSNorm + residual between blocks), {seqs} sequences x {steps} decode steps, "
+                     f"E=128 ({GPT_OSS_E // world} per GPU), H=I=2880, top-4, independent seeded weights per layer",
+                     "weak", f"ep{world}: NVLink peer-memory exchange, one CUDA graph per decode step" if world > 1 else "1 GPU, one CUDA graph per decode step",
+                     {"l2": "each layer's weights exceed L2", "sequences": seqs, "decode_steps": steps, "layers": n_layers})
+    line.update({"steps": steps, "gpu_launches": launches * steps, "gpu_launches_per_step": launches,
+                 "ms_per_step_note": "ms_per_step is one decode step of all layers (one graph replay)",
+                 "e2e": {"value": tok / (e2e_ms / 1e3), "unit": "tokens/s", "mode": "per step: input uploaded from pinned host memory, output read back",
+                         "h2d_bytes_per_step": seqs * GPT_OSS_H * 2, "d2h_bytes_per_step": seqs * GPT_OSS_H * 2},
+                 "parity": parity, "clocks": clk.summary()})
+    if rank == 0:
+        print(json.dumps(line))
+
+
 def run_reference(args, world, rank):
     """Reference arm: the reference algorithm (CPU restatement) on the host cores, rank 0
     only, on the same workload's layer; each step a bounded sample of tokens."""
@@ -692,6 +787,8 @@ def run_reference(args, world, rank):
         if i >= args.warmup:
             vals.append(v)
     v = statistics.median(vals)
+    if args.workload == "stack":
+        v /= args.layers  # a stack token passes every layer: the per-layer rate over the layer count
     wl = {"ep": f"config 3: MoE layer over {args.tokens} tokens, E=128, H=I=2880, top-4, uniform routing",
           "decode": f"config 1: decode MoE layer, T={args.tokens}, E=128, H=I=2880, top-4",
           "prefill": f"config 2: prefill MoE layer, T={args.tokens}, Zipf(1.1), E=128, H=I=2880, top-4",
@@ -715,7 +812,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["ep", "decode", "prefill"], default="ep")
+    ap.add_argument("--workload", choices=["ep", "decode", "prefill", "stack"], default="ep")
+    ap.add_argument("--layers", type=int, default=36, help="stack: MoE layers")
+    ap.add_argument("--decode-steps", type=int, default=128, help="stack: decode steps (the timed steps)")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--path", choices=["auto", "simt", "tc"], default="auto")
@@ -735,6 +834,8 @@ def main():
             run_reference(args, world, rank)
         elif args.workload == "ep":
             run_ep(args, world, rank, local)
+        elif args.workload == "stack":
+            run_stack(args, world, rank, local)
         else:
             run_layer(args, world, rank, local)
     finally:

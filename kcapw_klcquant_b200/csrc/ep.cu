@@ -12,7 +12,12 @@
 //   recv_rows     bf16 [world][cap][H] token rows, one segment per source
 //   back_rows     bf16 [world][cap][H] expert outputs, one segment per destination
 //   --- local only ---
-//   status, done counters, recv_expert i32 [world][cap] (expert id or -1 = empty slot)
+//   status, done counters, epoch (u32: forwards dispatched so far), recv_expert
+//   i32 [world][cap] (expert id or -1 = empty slot)
+//
+// The epoch lives in device memory and every kernel reads it there (the send
+// kernel's last CTA advances it), so a captured CUDA graph of forwards replays
+// with fresh epochs.
 //
 // One layer forward on every rank, all stream-ordered, no host synchronisation:
 //   1. dispatch: stable counting sort of the rank's (token, slot) pairs by
@@ -54,7 +59,7 @@ constexpr uint64_t kDefaultWaitNs = 10ull * 1000000000ull;  // 10 s
 
 struct ArenaLayout {
   size_t flag_dispatch, flag_combine, counts, recv_meta, recv_rows, back_rows;  // written by peers
-  size_t status, done, recv_expert, ones;                                     // local
+  size_t status, done, epoch, recv_expert, ones;                              // local
   size_t total;
 };
 
@@ -75,6 +80,7 @@ ArenaLayout arena_layout(int world, int64_t cap, int64_t hidden) {
   L.back_rows = take(slots * size_t(hidden) * 2);
   L.status = take(sizeof(DeviceStatus));
   L.done = take(2 * sizeof(unsigned int));
+  L.epoch = take(sizeof(uint32_t));
   L.recv_expert = take(slots * 4);
   L.ones = take(slots * 2);
   L.total = off;
@@ -115,13 +121,13 @@ __device__ bool wait_flag(const uint32_t* flag, uint32_t epoch, uint64_t limit_n
 // Last-CTA signal: every CTA makes its peer stores visible system-wide and
 // counts itself done; the last one writes the counts (dispatch) and the flag
 // of this rank into every peer's arena, then rearms the counter.
-__device__ void signal_peers(const PeerBases& peers, int world, int rank, unsigned int* done, size_t flag_off,
+__device__ bool signal_peers(const PeerBases& peers, int world, int rank, unsigned int* done, size_t flag_off,
                              size_t counts_off, const int32_t* counts, uint32_t epoch) {
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x != 0) return;
+  if (threadIdx.x != 0) return false;
   const unsigned int prev = atomicAdd(done, 1u);
-  if (prev != gridDim.x - 1) return;
+  if (prev != gridDim.x - 1) return false;
   __threadfence_system();
   for (int d = 0; d < world; ++d) {
     char* b = peers.base[d];
@@ -130,6 +136,7 @@ __device__ void signal_peers(const PeerBases& peers, int world, int rank, unsign
   __threadfence_system();
   for (int d = 0; d < world; ++d) st_release_sys(reinterpret_cast<uint32_t*>(peers.base[d] + flag_off) + rank, epoch);
   *done = 0u;  // the next launch using this counter starts after this kernel ends
+  return true;
 }
 
 // 1. token rows of every (token, slot) pair into the owner rank's arena
@@ -137,10 +144,14 @@ __global__ void __launch_bounds__(256)
     ep_send_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ pair_pos, const int32_t* __restrict__ offsets,
                    const int32_t* __restrict__ counts, int64_t pairs, int k, int epr, int world, int rank, int64_t cap,
                    const uint16_t* __restrict__ x, int64_t hidden, int32_t* __restrict__ pair_slot, PeerBases peers,
-                   ArenaLayout L, unsigned int* done, uint32_t epoch) {
+                   ArenaLayout L, char* arena) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
   const int chunks = int(hidden / 8);
+  // this forward's epoch; the last CTA advances the stored one after every CTA read it
+  uint32_t* epoch_p = reinterpret_cast<uint32_t*>(arena + L.epoch);
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(epoch_p) + 1u;
+  unsigned int* done = reinterpret_cast<unsigned int*>(arena + L.done);
   for (int64_t p = int64_t(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); p < pairs; p += warps) {
     const int v = idx[p];
     const int d = v / epr;  // validated by the permute (faults recorded, pair_pos -1)
@@ -160,13 +171,14 @@ __global__ void __launch_bounds__(256)
       pair_slot[p] = int32_t(int64_t(d) * cap + pos);
     }
   }
-  signal_peers(peers, world, rank, done, L.flag_dispatch, L.counts, counts, epoch);
+  if (signal_peers(peers, world, rank, done, L.flag_dispatch, L.counts, counts, epoch)) *epoch_p = epoch;
 }
 
 // 2a. wait for every source's rows, mark the received slots
 __global__ void __launch_bounds__(256)
-    ep_fill_kernel(char* arena, ArenaLayout L, int64_t cap, uint32_t epoch, uint64_t limit_ns) {
+    ep_fill_kernel(char* arena, ArenaLayout L, int64_t cap, uint64_t limit_ns) {
   const int s = blockIdx.y;
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(arena + L.epoch);
   __shared__ int count;
   if (threadIdx.x == 0) {
     const uint32_t* flag = reinterpret_cast<const uint32_t*>(arena + L.flag_dispatch) + s;
@@ -194,8 +206,10 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     ep_return_kernel(const int32_t* __restrict__ recv_expert, const int32_t* __restrict__ pair_pos,
                      const uint16_t* __restrict__ y, int64_t hidden, int world, int rank, int64_t cap, PeerBases peers,
-                     ArenaLayout L, unsigned int* done, uint32_t epoch) {
+                     ArenaLayout L, char* arena) {
   const int lane = threadIdx.x & 31;
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(arena + L.epoch);
+  unsigned int* done = reinterpret_cast<unsigned int*>(arena + L.done) + 1;
   const int64_t slots = int64_t(world) * cap;
   const int64_t warps = int64_t(gridDim.x) * (blockDim.x >> 5);
   const int chunks = int(hidden / 8);
@@ -213,9 +227,10 @@ __global__ void __launch_bounds__(256)
 }
 
 // 3. wait for every destination's returned rows
-__global__ void ep_wait_kernel(char* arena, ArenaLayout L, int world, uint32_t epoch, uint64_t limit_ns) {
+__global__ void ep_wait_kernel(char* arena, ArenaLayout L, int world, uint64_t limit_ns) {
   const int d = threadIdx.x;
   if (d >= world) return;
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(arena + L.epoch);
   const uint32_t* flag = reinterpret_cast<const uint32_t*>(arena + L.flag_combine) + d;
   if (!wait_flag(flag, epoch, limit_ns))
     record_fault(reinterpret_cast<DeviceStatus*>(arena + L.status), KLC_ERR_DEVICE_TIMEOUT, 300 + d, int(epoch));
@@ -238,7 +253,7 @@ struct klc_ep {
   char* peer[klc::kMaxRanks] = {};
   bool opened[klc::kMaxRanks] = {};
   bool connected = false;
-  uint32_t epoch = 0;
+  uint64_t dispatches = 0;  // host count (the epoch itself lives in the arena)
   uint64_t wait_ns = klc::kDefaultWaitNs;
 };
 
@@ -399,7 +414,7 @@ extern "C" int klc_ep_dispatch(klc_ep* h, const int32_t* idx, int64_t tokens, co
   if (workspace == nullptr || workspace_bytes < need)
     return fail(KLC_ERR_WORKSPACE, "klc_ep_dispatch: workspace too small (need " + std::to_string(need) + " bytes)");
   cudaStream_t s = as_stream(stream);
-  h->epoch += 1;  // every rank dispatches once per forward, so epochs agree
+  h->dispatches += 1;  // every rank dispatches once per forward, so the device epochs agree
   klc_moe_dims d{tokens, 64, 64, h->world, h->top_k, KLC_PATH_SIMT};
   const WorkspaceLayout W = workspace_layout(d, false);
   char* ws = static_cast<char*>(workspace);
@@ -435,7 +450,7 @@ extern "C" int klc_ep_dispatch(klc_ep* h, const int32_t* idx, int64_t tokens, co
   ep_send_kernel<<<unsigned(blocks), 256, 0, s>>>(
       idx, reinterpret_cast<const int32_t*>(ws + W.pair_pos), reinterpret_cast<const int32_t*>(ws + W.offsets),
       reinterpret_cast<const int32_t*>(ws + W.counts), pairs, h->top_k, int(h->epr), h->world, h->rank, h->cap, x,
-      h->hidden, pair_slot, bases_of(h), h->L, reinterpret_cast<unsigned int*>(h->arena + h->L.done), h->epoch);
+      h->hidden, pair_slot, bases_of(h), h->L, h->arena);
   KLC_LAUNCH_CHECK("ep_send_kernel launch");
   return KLC_OK;
 }
@@ -450,7 +465,7 @@ extern "C" int klc_ep_experts(klc_ep* h, const klc_moe_dims* local, const klc_mo
   if ((st = validate_weights(wts)) != KLC_OK) return st;
   KLC_CHECK_ARG(ld.experts == h->epr, "klc_ep_experts: local experts must equal experts_per_rank");
   KLC_CHECK_ARG(precision == KLC_PREC_FP32 || precision == KLC_PREC_BF16, "klc_ep_experts: bad precision");
-  KLC_CHECK_ARG(h->epoch > 0, "klc_ep_experts: no dispatch before");
+  KLC_CHECK_ARG(h->dispatches > 0, "klc_ep_experts: no dispatch before");
   const WorkspaceLayout W = workspace_layout(ld, false);
   size_t need = W.total;
   if (need < dispatch_ws_bytes(h)) need = dispatch_ws_bytes(h);
@@ -459,7 +474,7 @@ extern "C" int klc_ep_experts(klc_ep* h, const klc_moe_dims* local, const klc_mo
   KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(workspace) & 255) == 0, "klc_ep_experts: workspace must be 256-byte aligned");
   cudaStream_t s = as_stream(stream);
   const int64_t fill_x = (h->cap + 255) / 256 < 64 ? (h->cap + 255) / 256 : 64;
-  ep_fill_kernel<<<dim3(unsigned(fill_x), unsigned(h->world)), 256, 0, s>>>(h->arena, h->L, h->cap, h->epoch, h->wait_ns);
+  ep_fill_kernel<<<dim3(unsigned(fill_x), unsigned(h->world)), 256, 0, s>>>(h->arena, h->L, h->cap, h->wait_ns);
   KLC_LAUNCH_CHECK("ep_fill_kernel launch");
   char* ws = static_cast<char*>(workspace);
   const int32_t* recv_expert = reinterpret_cast<const int32_t*>(h->arena + h->L.recv_expert);
@@ -472,8 +487,7 @@ extern "C" int klc_ep_experts(klc_ep* h, const klc_moe_dims* local, const klc_mo
   if (blocks > max_blocks) blocks = max_blocks;
   ep_return_kernel<<<unsigned(blocks), 256, 0, s>>>(recv_expert, reinterpret_cast<const int32_t*>(ws + W.pair_pos),
                                                     reinterpret_cast<const uint16_t*>(ws + W.y), h->hidden, h->world, h->rank,
-                                                    h->cap, bases_of(h), h->L,
-                                                    reinterpret_cast<unsigned int*>(h->arena + h->L.done) + 1, h->epoch);
+                                                    h->cap, bases_of(h), h->L, h->arena);
   KLC_LAUNCH_CHECK("ep_return_kernel launch");
   return KLC_OK;
 }
@@ -487,7 +501,7 @@ extern "C" int klc_ep_combine(klc_ep* h, const int32_t* pair_slot, const uint16_
   KLC_CHECK_ARG(tokens == 0 || (pair_slot && w && out), "klc_ep_combine: null pointer");
   KLC_CHECK_ARG((norm_w == nullptr) == (normed == nullptr), "klc_ep_combine: norm_w and normed go together");
   cudaStream_t s = as_stream(stream);
-  ep_wait_kernel<<<1, ((h->world + 31) / 32) * 32, 0, s>>>(h->arena, h->L, h->world, h->epoch, h->wait_ns);
+  ep_wait_kernel<<<1, ((h->world + 31) / 32) * 32, 0, s>>>(h->arena, h->L, h->world, h->wait_ns);
   KLC_LAUNCH_CHECK("ep_wait_kernel launch");
   if (tokens == 0) return KLC_OK;
   PostNorm post{norm_w, eps, normed};

@@ -113,11 +113,14 @@ class ExpertParallelMoe:
 
     def __init__(self, layer_idx: int, tensors: dict[str, torch.Tensor], device, group=None, top_k: int = 4,
                  path: str = "auto", backend=None, share_local: "ExpertParallelMoe | None" = None,
-                 exchange: str = "auto", max_tokens: int = 4096):
-        """``share_local``: reuse another instance's resident local experts (same expert
-        weights, e.g. the same layer with another router bias).  ``exchange``: "p2p",
-        "nccl" or "auto" (p2p for the CUDA backend); ``max_tokens``: the most tokens a
-        rank passes to one forward (sizes the p2p exchange arenas)."""
+                 exchange: str = "auto", max_tokens: int = 4096, store=None):
+        """``tensors`` holds the layer's checkpoint-named tensors: the router and bias
+        tensors always, the expert blocks/scales unless ``store`` (an
+        :class:`Mxfp4ExpertStore` over the checkpoint) supplies this rank's expert
+        shard.  ``share_local``: reuse another instance's resident local experts (same
+        expert weights, e.g. the same layer with another router bias).  ``exchange``:
+        "p2p", "nccl" or "auto" (p2p for the CUDA backend); ``max_tokens``: the most
+        tokens a rank passes to one forward (sizes the p2p exchange arenas)."""
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -149,10 +152,14 @@ class ExpertParallelMoe:
                 self._ep = PeerExchange(self.backend, self.rank, self.world, self.epr, max_tokens, group)
             return
         e = f"{p}.experts"
-        packed = PackedLayer.from_checkpoint_tensors(
-            tensors[f"{e}.gate_up_proj_blocks"][lo:hi], tensors[f"{e}.gate_up_proj_scales"][lo:hi],
-            tensors[f"{e}.down_proj_blocks"][lo:hi], tensors[f"{e}.down_proj_scales"][lo:hi], dev,
-        )
+        if store is not None:
+            # this rank's shard read straight from the checkpoint (safetensors slices)
+            packed = store.layer(layer_idx, (lo, hi))
+        else:
+            packed = PackedLayer.from_checkpoint_tensors(
+                tensors[f"{e}.gate_up_proj_blocks"][lo:hi], tensors[f"{e}.gate_up_proj_scales"][lo:hi],
+                tensors[f"{e}.down_proj_blocks"][lo:hi], tensors[f"{e}.down_proj_scales"][lo:hi], dev,
+            )
         local = MoeLayer(packed, router_w[lo:hi], tensors[f"{p}.router.bias"][lo:hi], tensors[f"{e}.gate_up_proj_bias"][lo:hi],
                          tensors[f"{e}.down_proj_bias"][lo:hi], top_k=1, path=path)
         self.backend = CudaBackend(local, as_bf16(router_w, dev), as_bf16(tensors[f"{p}.router.bias"], dev), self.top_k)

@@ -390,14 +390,21 @@ class Mxfp4ExpertStore:
         return packed
 
     # -- packed access used by the fused path --
-    def layer(self, layer_idx: int) -> PackedLayer:
+    def layer(self, layer_idx: int, expert_range: tuple[int, int] | None = None) -> PackedLayer:
+        """The packed experts of a layer, loaded to the device on first use.
+
+        ``expert_range=(lo, hi)`` loads only experts [lo, hi) -- one rank's shard
+        under expert parallelism -- reading just those slices of the checkpoint
+        tensors (safetensors ``get_slice``), as the reference's per-expert loads
+        do (mxfp4_expert.py:515-525)."""
+        key = int(layer_idx) if expert_range is None else (int(layer_idx), int(expert_range[0]), int(expert_range[1]))
         with self._lock:
-            packed = self.layers.get(int(layer_idx))
+            packed = self.layers.get(key)
         if packed is not None:
             return packed
         start = time.perf_counter()
         names = {k: f"model.layers.{layer_idx}.mlp.experts.{k}" for k in ("gate_up_proj_blocks", "gate_up_proj_scales", "down_proj_blocks", "down_proj_scales")}
-        loaded = {k: self._load_tensor(n) for k, n in names.items()}
+        loaded = {k: self._load_tensor(n, expert_range) for k, n in names.items()}
         nbytes = sum(t.numel() for t in loaded.values())
         self.cache.stats.loaded_bytes += nbytes
         self.cache.stats.miss_loaded_bytes += nbytes
@@ -408,12 +415,17 @@ class Mxfp4ExpertStore:
         self.cache.stats.transfer_time_s += time.perf_counter() - t0
         self.cache.stats.materialization_time_s += time.perf_counter() - start
         with self._lock:
-            self.layers[int(layer_idx)] = packed
+            self.layers[key] = packed
         return packed
 
-    def _load_tensor(self, name: str) -> torch.Tensor:
+    def _load_tensor(self, name: str, expert_range: tuple[int, int] | None = None) -> torch.Tensor:
+        """One checkpoint tensor (or its experts [lo, hi)) on the host, with the
+        reference's quantized-override branch (mxfp4_expert.py:516-522)."""
         if self.quant_loader is not None and name in self.quant_loader.tensor_index:
             full, meta = self.quant_loader.load_tensor(name, dtype=self.dtype)
+            if expert_range is not None:
+                full = full[int(expert_range[0]) : int(expert_range[1])]
+            full = full.detach().cpu()
             if meta.dtype == "torch.uint8":
                 return torch.clamp(torch.round(full.float()), 0, 255).to(torch.uint8)
             return full
@@ -423,7 +435,9 @@ class Mxfp4ExpertStore:
 
         shard = self.weight_map[name]
         with safe_open(str(self.model_dir / shard), framework="pt", device="cpu") as handle:
-            return handle.get_tensor(name)
+            if expert_range is None:
+                return handle.get_tensor(name)
+            return handle.get_slice(name)[int(expert_range[0]) : int(expert_range[1])]
 
     # -- reference API --
     def load_expert_matrix(self, layer_idx: int, expert_idx: int, proj: str) -> torch.Tensor:
@@ -476,9 +490,15 @@ class Mxfp4ExpertStore:
         self.cache.stats.prefetch_completed += 1
 
     def resident_experts(self, layer_idx: int) -> set[int]:
-        """Experts whose weights are in device memory (all of a loaded layer)."""
-        packed = self.layers.get(int(layer_idx))
-        return set(range(packed.experts)) if packed is not None else set()
+        """Experts whose weights are in device memory: all of a loaded layer, or the
+        experts of the loaded shards of it."""
+        out: set[int] = set()
+        for key, packed in self.layers.items():
+            if key == int(layer_idx):
+                out |= set(range(packed.experts))
+            elif isinstance(key, tuple) and key[0] == int(layer_idx):
+                out |= set(range(key[1], key[2]))
+        return out
 
     def pin_experts(self, keys: list[tuple[int, int, str]]) -> None:
         for layer_idx, expert_idx, proj in keys:
@@ -488,6 +508,6 @@ class Mxfp4ExpertStore:
     def to_json(self) -> dict:
         payload = self.cache.to_json()
         payload["pending_prefetches"] = 0
-        payload["packed_layers"] = sorted(self.layers)
+        payload["packed_layers"] = sorted(self.layers, key=lambda k: (k, 0, 0) if isinstance(k, int) else k)
         payload["packed_resident_bytes"] = sum(p.nbytes for p in self.layers.values())
         return payload

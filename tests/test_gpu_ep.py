@@ -162,3 +162,52 @@ def test_ep_two_ranks_match_single_gpu(exchange):
         assert same_route
         m = parity.assert_output_close(y, ref, f"ep2 rank {rank}")
         assert m["bit_equal_frac"] >= 0.99, m
+
+
+def test_ep_from_checkpoint_store_and_stack(tmp_path):
+    """The rank's expert shard read from a safetensors checkpoint (Mxfp4ExpertStore
+    with expert_range) gives the same layer as the in-memory tensors; a two-layer
+    MoeStack (RMSNorm + residual between the blocks) over it, eager and as a
+    captured CUDA graph, equals the single-GPU layers."""
+    import json
+
+    from safetensors.torch import save_file
+
+    from kcapw_klcquant_b200 import MoeLayer, Mxfp4ExpertStore
+    from kcapw_klcquant_b200 import synthetic as syn
+    from kcapw_klcquant_b200.ep import ExpertParallelMoe
+    from kcapw_klcquant_b200.stack import MoeStack
+
+    dev = torch.device("cuda", 0)
+    dims = syn.LayerDims(16, 2880, 2880, 4)
+    layers = {li: syn.make_layer(dims, seed=60 + li, layer_idx=li) for li in range(2)}
+    experts = {k: v.contiguous() for t in layers.values() for k, v in t.items() if ".experts." in k and (k.endswith("_blocks") or k.endswith("_scales"))}
+    save_file(experts, str(tmp_path / "model-00000.safetensors"))
+    (tmp_path / "model.safetensors.index.json").write_text(json.dumps({"weight_map": {k: "model-00000.safetensors" for k in experts}}))
+    store = Mxfp4ExpertStore(tmp_path, tmp_path, dev, dtype=torch.bfloat16)
+    port = _free_port()
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1, device_id=dev)
+    try:
+        dense = {li: {k: v.to(dev) for k, v in syn.dense_tensors(t, li).items()} for li, t in layers.items()}
+        eps = [ExpertParallelMoe(li, dense[li], dev, top_k=4, store=store, max_tokens=16) for li in range(2)]
+        assert store.resident_experts(0) == set(range(16))
+        singles = [MoeLayer.from_tensors(li, {k: v.to(dev) for k, v in layers[li].items()}, dev, top_k=4) for li in range(2)]
+        norms = [syn.make_rms_weight(2880, seed=70 + li, device=dev) for li in range(2)]
+        x = syn.make_hidden(16, 2880, seed=61, device=dev)
+        ref = MoeStack(singles, norms).step(x)
+        st = MoeStack(eps, norms)
+        y = st.step(x)
+        parity.assert_output_close(_bits(y), _bits(ref), "stack from store")
+        assert float(torch.mean((y.view(torch.int16) == ref.view(torch.int16)).float())) >= 0.99
+        st.capture(x)
+        for _ in range(2):  # replays advance the exchange epochs on the device
+            yg = st.replay(x).clone()
+            torch.cuda.synchronize()
+            assert torch.equal(yg, y)
+        for ep in eps:
+            ep.check_device_status()
+        st.release()
+        for ep in eps:
+            ep.close()
+    finally:
+        dist.destroy_process_group()
