@@ -136,3 +136,67 @@ def test_expert_partition_rejects_uneven_split():
     with um.patch("torch.distributed.get_world_size", return_value=3), um.patch("torch.distributed.get_rank", return_value=0):
         with pytest.raises(ValueError):
             ExpertParallelMoe(0, {"model.layers.0.mlp.router.weight": torch.zeros(16, 64)}, "cpu", group=G(), backend=object())
+
+
+# ---------------------------------------------------------------------------
+# failure detection: a rank that dies or stalls must not hang the others
+# ---------------------------------------------------------------------------
+
+
+def _failing_worker(rank, world, port, mode, results):
+    """Rank 1 fails (exits, or stalls past the process-group timeout) right before
+    the exchange of a forward; the other ranks must get an error, not hang."""
+    import datetime
+    import time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    from kcapw_klcquant_b200 import synthetic as syn
+    from kcapw_klcquant_b200.ep import ExpertParallelMoe
+
+    layer = syn.make_layer(syn.LayerDims(E, H, I, K), seed=5)
+    epr = E // world
+    moe = ExpertParallelMoe(0, layer, "cpu", top_k=K, backend=OracleBackend(layer, rank * epr, (rank + 1) * epr, K))
+    x = syn.make_hidden(4, H, seed=100 + rank)
+    moe.forward(x, precision="bf16")  # one healthy step on every rank
+    if rank == 1:
+        results[rank] = "failing"
+        if mode == "exit":
+            os._exit(3)
+        time.sleep(40)  # stalls past the peers' timeout; killed by the test afterwards
+        os._exit(4)
+    t0 = time.monotonic()
+    try:
+        moe.forward(x, precision="bf16")
+        results[rank] = "no error"
+    except Exception as e:  # the exchange's collective gives up with an error
+        results[rank] = f"error after {time.monotonic() - t0:.1f}s: {type(e).__name__}"
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "stall"])
+def test_exchange_survivors_get_an_error(mode):
+    import time
+
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    results = mgr.dict()
+    port = _free_port()
+    world = 4
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, mode, results)) for r in range(world)]
+    for p in procs:
+        p.start()
+    t0 = time.monotonic()
+    survivors = [r for r in range(world) if r != 1]
+    for r in survivors:
+        procs[r].join(timeout=90)
+        assert procs[r].exitcode == 0, f"survivor {r} did not finish cleanly ({procs[r].exitcode})"
+    assert time.monotonic() - t0 < 90
+    procs[1].join(timeout=1 if mode == "stall" else 30)
+    if procs[1].is_alive():
+        procs[1].kill()  # the stalled rank (this test's own child process)
+        procs[1].join(timeout=10)
+    assert results[1] == "failing"
+    for r in survivors:
+        assert results[r].startswith("error after"), results[r]
