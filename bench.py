@@ -564,11 +564,14 @@ def run_ep(args, world, rank, local):
         e2e_fwd = lambda xd, yd: moe.forward(xd, precision=args.precision)[0]  # noqa: E731
         parallelism = f"ep{world}: experts sharded {GPT_OSS_E // world} per GPU, {moe.exchange_name}"
 
+    # clocks sampled over the timed legs (headline, Zipf and end-to-end), all of them under load
     clk = ClockSampler(local)
-    ms_local, launches = time_window(fwd, args.steps, args.warmup, world, clk)
+    clk.start()
+    ms_local, launches = time_window(fwd, args.steps, args.warmup, world)
     ms = reduce_over_ranks(ms_local, world, "max")
     ms_zipf = reduce_over_ranks(time_window(fwd_zipf, args.steps, args.warmup, world)[0], world, "max")
     e2e_ms = reduce_over_ranks(time_e2e(e2e_fwd, x.cpu().pin_memory(), args.steps, args.warmup, world), world, "max")
+    clk.stop()
 
     # roofline of the dominant kernel: the gate_up grouped GEMM (tensor-bound at these sizes)
     stage = stage_pass(fwd)

@@ -77,6 +77,12 @@ int klc_device_sm_count(int* out_sms);
  * devices; a launch that failed is counted too).  No reference counterpart:
  * measurement support, e.g. launches per step.                            */
 int klc_launch_count(uint64_t* out);
+/* Self-test of the bounded device waits (no reference counterpart): a
+ * kernel waits on an mbarrier nothing arrives on, gives up after
+ * limit_cycles SM cycles and records KLC_ERR_DEVICE_TIMEOUT (site 999);
+ * *code / *where receive the recorded status (synchronises `stream`).
+ * Returns KLC_OK when the self-test ran; the GPU stays usable.             */
+int klc_selftest_wait_timeout(int64_t limit_cycles, int* code, int* where, void* stream);
 /* sizeof(klc_moe_dims) and sizeof(klc_moe_weights) as this library was
  * compiled, for bindings to check their own structure layouts against.    */
 int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes);

@@ -40,6 +40,10 @@ constexpr int kTok = 8;       // tokens per CTA
 constexpr int kWarps = 8;     // warps per CTA
 constexpr int kMaxK = 8;
 constexpr int kMaxCluster = 8;  // portable cluster size
+#ifndef KLC_ROUTER_GEMM_MIN_TOKENS
+#define KLC_ROUTER_GEMM_MIN_TOKENS 1024
+#endif
+constexpr int64_t kRouterGemmMinTokens = KLC_ROUTER_GEMM_MIN_TOKENS;  // whole-K tiles of 128 tokens from here on
 
 // k rounds of a warp-wide arg-max over `row` (value descending, lower index
 // on ties), then softmax over the k selected fp32 scores (max-subtracted,
@@ -360,6 +364,180 @@ int launch_router_tc(const uint16_t* x, int64_t tokens, int64_t hidden, const ui
   return KLC_OK;
 }
 
+// Router for large batches: one CTA per 128 tokens computes all E logits over the
+// whole hidden dimension on the tensor cores (tcgen05 kind::f16, M = 128 tokens,
+// N = E experts, K streamed through a TMA ring), so each TMEM lane holds one
+// token's logits and a thread selects that token's top-k alone.  The split-K
+// cluster form above serves small batches, where 128-token tiles would leave
+// most SMs idle.
+constexpr int kRgStages = 4;
+constexpr int kRgThreads = 256;  // warp 0 TMA, warp 1 MMA, warps 4-7 epilogue
+
+template <int EP>  // experts padded to a multiple of 16 (the MMA's N)
+__global__ void __launch_bounds__(kRgThreads, 1)
+    router_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, int64_t tokens,
+                       int64_t hidden, const uint16_t* __restrict__ b, int experts, int k, const float* __restrict__ adjust,
+                       int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  using namespace tc;
+  constexpr int XBOX = 128 * 128, WBOX = EP * 128;  // bytes of one 64-K box of each operand
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  unsigned char* xs = smem;
+  unsigned char* wsm = smem + kRgStages * XBOX;
+  __shared__ __align__(8) uint64_t bars[2 * kRgStages + 1];
+  __shared__ uint32_t tmem_holder;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t0 = int64_t(blockIdx.x) * 128;
+  const int nk = int(hidden / 64);
+  auto full = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty = [&](int s) { return smem_u32(&bars[kRgStages + s]); };
+  const uint32_t done = smem_u32(&bars[2 * kRgStages]);
+  const Ctl ctl{reinterpret_cast<volatile int*>(&abort_flag), &g_router_status};
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kRgStages; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    mbar_init(done, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_holder)),
+                 "r"(EP <= 32 ? 32 : (EP <= 64 ? 64 : (EP <= 128 ? 128 : 256))));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_holder;
+  if (warp == 0 && lane == 0) {
+    bool ok = true;
+    uint32_t issued = 0;
+    for (int kc = 0; kc < nk && ok; ++kc) {
+      const int s = kc % kRgStages;
+      if (!(ok = wait_bar(empty(s), ((kc / kRgStages) & 1) ^ 1, ctl, 60))) break;
+      mbar_arrive_expect_tx(full(s), uint32_t(XBOX + WBOX));
+      tma_load_2d(smem_u32(xs + s * XBOX), &map_x, kc * 64, int(t0), full(s));
+      tma_load_2d(smem_u32(wsm + s * WBOX), &map_w, kc * 64, 0, full(s));
+      ++issued;
+    }
+    if (!ok) drain_ring(full(0), kRgStages, issued);
+  } else if (warp == 1 && lane == 0) {
+    // kind::f16: bf16 A (tokens) and B (router rows), fp32 accumulate, K-major, M = 128, N = EP
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(EP >> 3) << 17) | (uint32_t(128 >> 4) << 24);
+    bool ok = true;
+    for (int kc = 0; kc < nk && ok; ++kc) {
+      const int s = kc % kRgStages;
+      if (!(ok = wait_bar(full(s), (kc / kRgStages) & 1, ctl, 61))) break;
+      tc_fence_after();
+      const uint64_t ad = sw128_desc(smem_u32(xs + s * XBOX)), bd = sw128_desc(smem_u32(wsm + s * WBOX));
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t acc = (kc | kk) ? 1u : 0u;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+            "l"(ad + uint64_t(kk * 2)), "l"(bd + uint64_t(kk * 2)), "r"(idesc), "r"(acc));
+      }
+      tc_commit(empty(s));
+    }
+    tc_commit(done);
+  } else if (warp >= 4) {
+    // one thread per token: its logits from its TMEM lane, bias, one bf16 rounding,
+    // top-k (value descending, lower index first) and the softmax of the selected
+    const int q = warp & 3;
+    const int tl = q * 32 + lane;
+    const int64_t t = t0 + tl;
+    bool ok = wait_bar_backoff(done, 0, ctl, 62);
+    tc_fence_after();
+    float sv[kMaxK];
+    int si[kMaxK];
+#pragma unroll
+    for (int r = 0; r < kMaxK; ++r) {
+      sv[r] = -INFINITY;
+      si[r] = -1;
+    }
+    for (int c0 = 0; c0 < EP; c0 += 16) {
+      uint32_t raw[16];
+      tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), raw);
+      tmem_wait_ld();
+      uint32_t packed[8];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int e = c0 + j;
+        uint16_t lb = 0;
+        if (e < experts) {
+          lb = f32_to_bf16(__uint_as_float(raw[j]) + bf16_to_f32(b[e]));
+          const float v = bf16_to_f32(lb) + (adjust ? adjust[e] : 0.f);
+          if (v == v) {  // NaN only fills slots nothing else takes (below)
+            // insertion into the sorted selection; an equal value keeps the earlier (lower) index first
+            float cv = v;
+            int ci = e;
+#pragma unroll
+            for (int r = 0; r < kMaxK; ++r) {
+              if (r < k && ci >= 0 && (si[r] < 0 || cv > sv[r])) {
+                const float tv = sv[r];
+                const int ti = si[r];
+                sv[r] = cv;
+                si[r] = ci;
+                cv = tv;
+                ci = ti;
+              }
+            }
+          }
+        }
+        if (j & 1) packed[j >> 1] |= uint32_t(lb) << 16;
+        else packed[j >> 1] = lb;
+      }
+      // 16-byte stores when the row and chunk start are 16-byte aligned (E a multiple of 8)
+      if (out_logits != nullptr && t < tokens && c0 + 16 <= experts && (experts & 7) == 0 &&
+          (reinterpret_cast<uintptr_t>(out_logits) & 15) == 0) {
+        uint4* dst = reinterpret_cast<uint4*>(out_logits + t * experts + c0);
+        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+      } else if (out_logits != nullptr && t < tokens) {
+        for (int j = 0; j < 16 && c0 + j < experts; ++j)
+          out_logits[t * experts + c0 + j] = uint16_t((j & 1) ? (packed[j >> 1] >> 16) : (packed[j >> 1] & 0xFFFFu));
+      }
+    }
+    // slots still empty: the lowest-index experts not taken (their scores NaN)
+    for (int r = 0; r < k; ++r) {
+      if (si[r] >= 0) continue;
+      for (int e = 0; e < experts; ++e) {
+        bool taken = false;
+        for (int qq = 0; qq < r; ++qq) taken |= (si[qq] == e);
+        if (!taken) {
+          si[r] = e;
+          sv[r] = __uint_as_float(0x7fc00000u);
+          break;
+        }
+      }
+    }
+    if (ok && t < tokens) {
+      float m = sv[0];
+      for (int r = 1; r < k; ++r) m = fmaxf(m, sv[r]);
+      float ex[kMaxK];
+      float sum = 0.f;
+      for (int r = 0; r < k; ++r) {
+        ex[r] = expf(sv[r] - m);
+        sum += ex[r];
+      }
+      for (int r = 0; r < k; ++r) {
+        out_idx[t * k + r] = si[r];
+        out_w[t * k + r] = f32_to_bf16(ex[r] / sum);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(EP <= 32 ? 32 : (EP <= 64 ? 64 : (EP <= 128 ? 128 : 256))));
+}
+
 __global__ void select_kernel(const float* __restrict__ scores, int64_t tokens, int experts, int k, int keep_order,
                               int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w) {
   const int lane = threadIdx.x & 31;
@@ -367,6 +545,44 @@ __global__ void select_kernel(const float* __restrict__ scores, int64_t tokens, 
   if (t >= tokens) return;
   (void)lane;
   select_softmax_warp(scores + t * experts, experts, k, keep_order != 0, out_idx + t * k, out_w + t * k);
+}
+
+template <int EP>
+int launch_router_gemm_ep(const CUtensorMap& mx, const CUtensorMap& mw, int64_t tokens, int64_t hidden, const uint16_t* b,
+                          int experts, int k, const float* adjust, int32_t* out_idx, uint16_t* out_w, uint16_t* out_logits,
+                          cudaStream_t stream) {
+  const int smem = kRgStages * (128 * 128 + EP * 128) + 1024;
+  KLC_CUDA(cudaFuncSetAttribute(router_gemm_kernel<EP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int64_t grid = (tokens + 127) / 128;
+  KLC_CHECK_ARG(grid <= 0x7fffffff, "klc_router_topk: too many tokens");
+  router_gemm_kernel<EP><<<unsigned(grid), kRgThreads, smem, stream>>>(mx, mw, tokens, hidden, b, experts, k, adjust, out_idx,
+                                                                       out_w, out_logits);
+  KLC_LAUNCH_CHECK("klc_router_topk launch");
+  return KLC_OK;
+}
+
+int launch_router_gemm(const uint16_t* x, int64_t tokens, int64_t hidden, const uint16_t* w, const uint16_t* b, int experts,
+                       int k, const float* adjust, int32_t* out_idx, uint16_t* out_w, uint16_t* out_logits,
+                       cudaStream_t stream) {
+  const int ep = (experts + 15) / 16 * 16;
+  CUtensorMap mx, mw;
+  {
+    const uint64_t dims[2] = {uint64_t(hidden), uint64_t(tokens)};
+    const uint64_t strides[1] = {uint64_t(hidden) * 2};
+    const uint32_t box[2] = {64, 128};
+    int st = tc::make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  {
+    const uint64_t dims[2] = {uint64_t(hidden), uint64_t(experts)};
+    const uint64_t strides[1] = {uint64_t(hidden) * 2};
+    const uint32_t box[2] = {64, uint32_t(ep)};
+    int st = tc::make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != KLC_OK) return st;
+  }
+  if (ep <= 64) return launch_router_gemm_ep<64>(mx, mw, tokens, hidden, b, experts, k, adjust, out_idx, out_w, out_logits, stream);
+  if (ep <= 128) return launch_router_gemm_ep<128>(mx, mw, tokens, hidden, b, experts, k, adjust, out_idx, out_w, out_logits, stream);
+  return launch_router_gemm_ep<256>(mx, mw, tokens, hidden, b, experts, k, adjust, out_idx, out_w, out_logits, stream);
 }
 
 }  // namespace
@@ -382,6 +598,8 @@ int launch_router(const uint16_t* x, int64_t tokens, int64_t hidden, const uint1
   KLC_CHECK_ARG(x && w && b && out_idx && out_w, "klc_router_topk: null pointer");
   KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
                 "klc_router_topk: x and w must be 16-byte aligned");
+  if (tokens >= kRouterGemmMinTokens && experts <= 256 && hidden % 64 == 0 && tc_path_supported(hidden, 64))
+    return launch_router_gemm(x, tokens, hidden, w, b, int(experts), k, adjust, out_idx, out_w, out_logits, stream);
   if (experts <= 128 && hidden % 64 == 0 && hidden <= 8 * kRtK && tc_path_supported(hidden, 64)) {
     // token tile: as few router-weight passes as keep every SM busy
     const int C = int((hidden + kRtK - 1) / kRtK);

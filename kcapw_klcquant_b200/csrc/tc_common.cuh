@@ -76,6 +76,20 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, const Ct
   }
 }
 
+// Bounded wait with an explicit cycle limit (the wait self-test uses a short one).
+__device__ __forceinline__ bool wait_bar_limit(uint32_t bar, uint32_t parity, const Ctl& c, int site, long long limit) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*c.abort) return false;
+    if (clock64() - t0 > limit) {
+      *c.abort = 1;
+      record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Bounded wait for roles that wait long and are not on the critical path:
 // sleeping between polls leaves issue slots to the warps that share the
 // scheduler (the MMA issuer above all).

@@ -146,3 +146,17 @@ def test_scales_tile_layouts():
                 c, mm = divmod(m, 128)
                 want[:, t, st, c, (mm % 32) * 16 + (mm // 32) * 4 + kb] = sn[:, r, g4]
     np.testing.assert_array_equal(got, want)
+
+
+def test_bounded_wait_reports_timeout_and_gpu_answers():
+    """The bounded mbarrier wait of the tensor-core kernels gives up on a barrier
+    nothing arrives on, records KLC_ERR_DEVICE_TIMEOUT at its site, and the GPU
+    keeps answering (klc_selftest_wait_timeout, 2e6 cycles ~ 1 ms)."""
+    import ctypes
+
+    from kcapw_klcquant_b200 import _lib
+
+    code, where = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.lib().klc_selftest_wait_timeout(2_000_000, ctypes.byref(code), ctypes.byref(where), _lib.stream_ptr()))
+    assert code.value == _lib.KLC_ERR_DEVICE_TIMEOUT and where.value == 999
+    assert float(torch.arange(8, device=DEV, dtype=torch.float32).sum()) == 28.0
