@@ -41,9 +41,11 @@ constexpr int kWarps = 8;     // warps per CTA
 constexpr int kMaxK = 8;
 constexpr int kMaxCluster = 8;  // portable cluster size
 #ifndef KLC_ROUTER_GEMM_MIN_TOKENS
-#define KLC_ROUTER_GEMM_MIN_TOKENS 1024
+#define KLC_ROUTER_GEMM_MIN_TOKENS 2048
 #endif
-constexpr int64_t kRouterGemmMinTokens = KLC_ROUTER_GEMM_MIN_TOKENS;  // whole-K tiles of 128 tokens from here on
+// whole-K tiles of 128 tokens from here on (B200, T = 2048 / 4096 / 16384: 71 / 72 / 78 us
+// against 82 / 131 / 434 us for the split-K cluster form, which wins below: 18 us at T = 1)
+constexpr int64_t kRouterGemmMinTokens = KLC_ROUTER_GEMM_MIN_TOKENS;
 
 // k rounds of a warp-wide arg-max over `row` (value descending, lower index
 // on ties), then softmax over the k selected fp32 scores (max-subtracted,
@@ -472,12 +474,13 @@ __global__ void __launch_bounds__(kRgThreads, 1)
           lb = f32_to_bf16(__uint_as_float(raw[j]) + bf16_to_f32(b[e]));
           const float v = bf16_to_f32(lb) + (adjust ? adjust[e] : 0.f);
           if (v == v) {  // NaN only fills slots nothing else takes (below)
-            // insertion into the sorted selection; an equal value keeps the earlier (lower) index first
+            // insertion into the selection kept in (value descending, index ascending) order;
+            // an element pushed down by the insertion keeps that order against equal values too
             float cv = v;
             int ci = e;
 #pragma unroll
             for (int r = 0; r < kMaxK; ++r) {
-              if (r < k && ci >= 0 && (si[r] < 0 || cv > sv[r])) {
+              if (r < k && ci >= 0 && (si[r] < 0 || cv > sv[r] || (cv == sv[r] && ci < si[r]))) {
                 const float tv = sv[r];
                 const int ti = si[r];
                 sv[r] = cv;

@@ -173,6 +173,32 @@ def test_router_shapes_vs_oracle(T, E, H, k):
     assert wdist.max() <= 1 and np.mean(wdist > 0) <= 0.02
 
 
+@pytest.mark.parametrize("T", [100, 4096])
+def test_router_exact_ties_lower_index_first(T):
+    """Router rows duplicated in pairs: every token has exact ties at every rank of
+    its top-k.  Both router forms (the cluster form at T = 100, the whole-K GEMM
+    form at T = 4096) must order equal values by the lower expert index."""
+    from kcapw_klcquant_b200 import _lib
+
+    E, H, k = 64, 256, 5
+    rng = np.random.default_rng(T)
+    half = (rng.standard_normal((E // 2, H)) * 0.05).astype(np.float32)
+    wr = torch.from_numpy(np.repeat(half, 2, axis=0)[rng.permutation(E)].copy()).to(torch.bfloat16)
+    br = torch.zeros(E, dtype=torch.bfloat16)
+    x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(torch.bfloat16)
+    idx = torch.empty((T, k), dtype=torch.int32, device=DEV)
+    w = torch.empty((T, k), dtype=torch.bfloat16, device=DEV)
+    lg = torch.empty((T, E), dtype=torch.bfloat16, device=DEV)
+    xd, wd, bd = x.to(DEV), wr.to(DEV), br.to(DEV)
+    _lib.check(_lib.lib().klc_router_topk(xd.data_ptr(), T, H, wd.data_ptr(), bd.data_ptr(), E, k, None, idx.data_ptr(),
+                                          w.data_ptr(), lg.data_ptr(), _lib.stream_ptr()))
+    got = bits_of(lg)
+    ties = parity.check_selection(got, idx.cpu().numpy(), k)
+    assert ties > 0
+    scores = np.take_along_axis(orc.bf16_bits_to_f32(got), idx.cpu().numpy().astype(np.int64), axis=1)
+    assert parity.ulp_distance_bf16(bits_of(w), orc.softmax_weights_bits(scores)).max() <= 1
+
+
 # ---------------------------------------------------------------------------
 # permutation (bit-exact vs the stable-sort oracle)
 # ---------------------------------------------------------------------------
