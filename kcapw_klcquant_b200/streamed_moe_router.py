@@ -213,7 +213,10 @@ class StreamedMoERouter:
         self.experts_per_token = experts_per_token
         self.swiglu_limit = swiglu_limit
         self.alpha = 1.702
-        self.stats = RouterStats()
+        self._stats = RouterStats()
+        # route_batch() routings on their way to the host: (copy-done event, layer, first position, k,
+        # pinned expert ids, pinned weights); recorded, in call order, whenever the stats are read
+        self._pending: list[tuple] = []
         self.locality_config = locality_config or RoutingLocalityConfig()
         self.matmul_precision = matmul_precision
         self.expert_path = expert_path
@@ -222,6 +225,21 @@ class StreamedMoERouter:
         self.recent_history: dict[int, deque[int]] = {}
         self.dynamic_caps: dict[int, int] = {}
         self._layers: dict[tuple, MoeLayer] = {}
+
+    @property
+    def stats(self) -> RouterStats:
+        """The routing telemetry (reference ``RouterStats``), with every pending
+        route_batch() routing recorded first."""
+        self._flush_pending()
+        return self._stats
+
+    def _flush_pending(self) -> None:
+        while self._pending:
+            done, layer_idx, position, k, ids_h, ws_h = self._pending.pop(0)
+            done.synchronize()
+            ids, ws = ids_h.tolist(), ws_h.float().tolist()
+            for t, (e, w) in enumerate(zip(ids, ws)):
+                self._stats.record_route(layer_idx, position + t, e, w, e, False, active_cap=k)
 
     # ------------------------------------------------------------------
     # device layer cache
@@ -244,6 +262,7 @@ class StreamedMoERouter:
     def route(self, layer_idx: int, hidden: torch.Tensor, tensors: dict[str, torch.Tensor], expert_store: Mxfp4ExpertStore | None = None,
               execute_experts: bool = True, position: int = 0, predicted_experts: list[int] | None = None,
               resident_experts: set[int] | None = None) -> tuple[torch.Tensor, dict]:
+        self._flush_pending()  # earlier route_batch() routings are recorded before this token
         p = f"model.layers.{layer_idx}.mlp"
         w_r, b_r = tensors[f"{p}.router.weight"], tensors[f"{p}.router.bias"]
         if not hidden.is_cuda:
@@ -330,8 +349,10 @@ class StreamedMoERouter:
 
         Equivalent to calling ``route()`` per token with locality disabled
         (the batched path does not apply the per-token sticky policy).  With
-        ``record_stats`` the routing is copied to the host and recorded as
-        positions ``position .. position+T-1``.  ``next_norm=(weight, eps)``
+        ``record_stats`` the routing is copied asynchronously into pinned host
+        buffers on the call's stream (no synchronisation here) and recorded as
+        positions ``position .. position+T-1`` when the statistics are next
+        read (``router.stats``) or ``route()`` runs.  ``next_norm=(weight, eps)``
         fuses the next layer's input RMSNorm of the output into the combine
         (``RouteBatch.normed``).
         """
@@ -344,9 +365,13 @@ class StreamedMoERouter:
         y, rb = layer.forward(hidden, precision=self.matmul_precision, return_logits=return_logits, return_norms=return_norms,
                               residual=residual, next_norm=next_norm)
         if record_stats:
-            ids, ws = rb.indices.tolist(), rb.weights.float().tolist()
-            for t, (e, w) in enumerate(zip(ids, ws)):
-                self.stats.record_route(layer_idx, position + t, e, w, e, False, active_cap=k)
+            ids_h = torch.empty(tuple(rb.indices.shape), dtype=rb.indices.dtype, pin_memory=True)
+            ws_h = torch.empty(tuple(rb.weights.shape), dtype=rb.weights.dtype, pin_memory=True)
+            ids_h.copy_(rb.indices, non_blocking=True)
+            ws_h.copy_(rb.weights, non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(torch.cuda.current_stream(rb.indices.device))
+            self._pending.append((done, layer_idx, position, k, ids_h, ws_h))
         return y, rb
 
     # ------------------------------------------------------------------
@@ -371,7 +396,7 @@ class StreamedMoERouter:
         adjusted_flag = experts != raw_experts
         predicted = predicted_experts if predicted_experts is not None else self.predict_experts(layer_idx, k)
         resident = sorted(int(v) for v in (resident_experts or set()))
-        self.stats.record_route(layer_idx, position, experts, weights, raw_experts, adjusted_flag,
+        self._stats.record_route(layer_idx, position, experts, weights, raw_experts, adjusted_flag,
                                 predicted_experts=[int(v) for v in predicted], resident_experts=resident, active_cap=k,
                                 blocked_adjustment=blocked)
         self._update_sticky_scores(layer_idx, experts, weights)
@@ -380,7 +405,7 @@ class StreamedMoERouter:
 
     def _after_execution(self, layer_idx: int, position: int, experts: list[int], before: dict, after: dict) -> None:
         """Cache-delta statistics and the dynamic active-expert cap (:307-309)."""
-        self.stats.record_cache_delta(layer_idx, position, experts, before, after)
+        self._stats.record_cache_delta(layer_idx, position, experts, before, after)
         self._adapt_active_cap(layer_idx, position, before, after)
 
     # ------------------------------------------------------------------
@@ -516,7 +541,7 @@ class StreamedMoERouter:
             new, reason = old + 1, "stable_high_hit_rate"
         if new != old:
             self.dynamic_caps[layer_idx] = new
-            self.stats.record_cap_event(layer_idx, position, old, new, reason, hits, misses, evictions)
+            self._stats.record_cap_event(layer_idx, position, old, new, reason, hits, misses, evictions)
 
     @staticmethod
     def _cache_snapshot(expert_store) -> dict:

@@ -336,6 +336,31 @@ def test_route_dropin(case_cache, precision):
     assert parity.ulp_distance_bf16(bits_of(y.reshape(1, -1)), fx["out_bias_only"][:1]).max() <= 1
 
 
+def test_route_batch_matches_route_and_records_stats(case_cache):
+    """route_batch() over T tokens equals route() per token (locality off), and its
+    statistics, copied asynchronously, appear in order once the stats are read."""
+    from kcapw_klcquant_b200 import Mxfp4ExpertStore, StreamedMoERouter
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    fx, dims, layer, x, ml = load(case_cache, "mini_e16_h256_t32")
+    store = Mxfp4ExpertStore.from_layers({0: layer}, DEV)
+    tensors = {k: v.to(DEV) for k, v in syn.dense_tensors(layer).items()}
+    rb_router = StreamedMoERouter(dims.top_k, 7.0, matmul_precision="bf16")
+    y, rb = rb_router.route_batch(0, x.to(DEV), tensors, store, record_stats=True, position=10)
+    y2, rb2 = rb_router.route_batch(0, x[:5].to(DEV), tensors, store, record_stats=True, position=100)
+    assert len(rb_router._pending) == 2  # nothing recorded (no host synchronisation) until the stats are read
+    js = rb_router.stats.to_json()
+    assert js["routed_tokens"] == x.shape[0] + 5 and not rb_router._pending
+    ev = js["route_events"]
+    assert [e["position"] for e in ev] == list(range(10, 10 + x.shape[0])) + list(range(100, 105))
+    assert [e["experts"] for e in ev[: x.shape[0]]] == rb.indices.tolist()
+    per_token = StreamedMoERouter(dims.top_k, 7.0, matmul_precision="bf16")
+    for t in range(x.shape[0]):
+        yt, route = per_token.route(0, x[t].to(DEV), tensors, store, True, t)
+        assert route["experts"] == rb.indices[t].tolist()
+        assert torch.equal(yt.reshape(-1), y[t])
+
+
 def test_store_load_expert_matrix_matches_dequant(case_cache):
     from kcapw_klcquant_b200 import Mxfp4ExpertStore
 
