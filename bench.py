@@ -59,7 +59,7 @@ FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H
 GATE_UP_FLOPS_PER_PAIR = 2 * GPT_OSS_H * 2 * GPT_OSS_I  # 33,177,600
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from ncu captures
 # (profiles/): decode T=256, prefill T=4096 Zipf.  None where no capture was taken.
-PROFILED_GATE_UP_TRAFFIC = {"decode": 1_145_114_000 + 8_942_592, "prefill": 1_024_244_000 + 95_751_424}
+PROFILED_GATE_UP_TRAFFIC = {"decode": 1_191_247_000 + 8_817_664, "prefill": 1_071_562_000 + 97_615_616}
 
 
 def peaks() -> dict:
@@ -593,9 +593,9 @@ def run_ep(args, world, rank, local):
     # output against the single-GPU layer on the same tokens
     if world == 1:
         y, rb = ml.forward(x, precision=args.precision, path=args.path)
-        ys, _ = ml.forward(x, precision=args.precision, path="simt")
+        ys, _ = ml.forward(x[:1024], precision=args.precision, path="simt")  # the CUDA-core path on the first 1024 tokens
         parity = {"vs_oracle": oracle_parity(tensors, x, y, rb.indices, rb.weights, 6) if not args.no_oracle else None,
-                  "vs_cuda_core_path": compare(y, ys)}
+                  "vs_cuda_core_path_1024_tokens": compare(y[:1024], ys)}
     else:
         y, _ = moe.forward(x, precision=args.precision)
         full = layer_from(tensors, device)
