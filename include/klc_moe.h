@@ -23,6 +23,11 @@
  *   klc_rms_norm             <- rms_norm                        streamed_attention.py:27-28
  *   klc_moe_combine_rmsnorm  <- combine, `hidden += moe_out` and the next layer's
  *   klc_moe_forward_rmsnorm     input rms_norm in one kernel    streamed_transformer_executor.py:235,260
+ *   klc_moe_*_rmsnorm_route  <- the above plus the next layer's router (F.linear + topk + softmax,
+ *                               streamed_moe_router.py:269-282) on the normalised rows
+ *   klc_locality_route       <- route()'s locality steps: _apply_locality_bias :331-363,
+ *                               _guarded_expert_selection :365-394, predict_experts :426-440,
+ *                               _update_sticky_scores / _update_workload_scores :396-424
  *   klc_runtime_dequant      <- RuntimeDequantizer.dequantize   runtime_dequantizer.py:30-52
  *                               (unpack_lowbit adaptive_quantizer.py:183-213,
  *                                reconstruct_pruned tensor_pruner.py:62-69)
@@ -291,6 +296,37 @@ int klc_moe_forward_rmsnorm(const klc_moe_dims* dims, const klc_moe_weights* wts
 int klc_moe_bias_only(const uint16_t* dn_bias, int64_t tokens, int64_t hidden, int k, const int32_t* idx,
                       const uint16_t* w, uint16_t* y, void* stream);
 
+/* The next layer's router fused into the combine (decode): after the
+ * residual add and the next layer's input RMSNorm (as klc_moe_forward_rmsnorm /
+ * klc_moe_combine_rmsnorm), the normalised rows are routed for the next layer
+ * (streamed_moe_router.py:269-282 on streamed_transformer_executor.py:247's
+ * `post`): router_w bf16 [E,H], router_b bf16 [E], k <= 8, E <= 1024;
+ * out_idx int32 [T,k], out_w bf16 [T,k], out_logits bf16 [T,E] or NULL.  Up to
+ * 64 tokens the router runs inside the combine kernel (one launch), above it
+ * the router kernels follow the combine.  No locality adjustment. */
+typedef struct klc_next_router {
+  const uint16_t* router_w;
+  const uint16_t* router_b;
+  int64_t experts;
+  int k;
+  int32_t* out_idx;
+  uint16_t* out_w;
+  uint16_t* out_logits;
+} klc_next_router;
+int klc_moe_forward_rmsnorm_route(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
+                                  const float* adjust, int precision, uint16_t* y, int32_t* out_idx, uint16_t* out_w,
+                                  uint16_t* out_logits, float* norms, const uint16_t* residual, const uint16_t* norm_w,
+                                  float eps, uint16_t* normed, const klc_next_router* next, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+/* Experts + combine for given routing (klc_moe_experts) + residual + RMSNorm + next router. */
+int klc_moe_experts_rmsnorm_route(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
+                                  const int32_t* idx, const uint16_t* w, int precision, uint16_t* y, float* norms,
+                                  const uint16_t* residual, const uint16_t* norm_w, float eps, uint16_t* normed,
+                                  const klc_next_router* next, void* workspace, size_t workspace_bytes, void* stream);
+int klc_moe_combine_rmsnorm_route(const uint16_t* y_rows, const int32_t* pair_pos, const uint16_t* w, int64_t tokens,
+                                  int k, int64_t hidden, const uint16_t* residual, const uint16_t* norm_w, float eps,
+                                  uint16_t* out, uint16_t* normed, const klc_next_router* next, void* stream);
+
 /* Stable counting-sort permutation of (token, slot) pairs by expert.
  * idx int32 [T,k]; writes pair_pos int32 [T*k] (padded row of each pair),
  * counts int32 [E], offsets int32 [E+1] (each group padded to `pad` rows)
@@ -331,6 +367,47 @@ int klc_ep_pack(const int32_t* idx, int64_t tokens, int k, int64_t experts_per_r
                 int64_t hidden, uint16_t* send_rows, int32_t* send_expert, int32_t* send_counts, int32_t* pair_pos,
                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* Locality-aware routing on the device (replaces the host steps of
+ * StreamedMoERouter.route when RoutingLocalityConfig.enabled,
+ * streamed_moe_router.py:270-302: raw top-k, _apply_locality_bias :331-363,
+ * adjusted top-k, _guarded_expert_selection :365-394, softmax, predict_experts
+ * :426-440, _update_sticky_scores / _update_workload_scores :396-424).  The
+ * fields are RoutingLocalityConfig's (:12-35) with experts_per_token the
+ * router's; Python bools as 0/1.  The policy state (sticky and workload scores,
+ * recent-expert history) lives in a caller-owned device buffer of
+ * klc_locality_state_bytes, zero-filled before first use, one per layer; each
+ * call continues it over `tokens` rows of bf16 logits [T,E] in order.  Per
+ * token t: resident (or NULL) is a 0/1 byte mask [E] of resident experts at
+ * resident + t*resident_stride (stride 0: one mask for all tokens); k the
+ * active expert count (the caller applies the dynamic cap).  Outputs:
+ * out_experts int32 [T,k] (guarded, in the reference's order), out_w bf16
+ * [T,k], out_raw int32 [T,k] (topk of the raw logits), out_pred int32 [T,k]
+ * with out_npred[t] valid entries (the prediction before token t's update;
+ * 0 when predictive_prefetch is off), out_flags uint8 [T] (bit 0: the guard
+ * replaced an expert, bit 1: experts != raw).  Exact ties resolve as
+ * torch.topk on the CPU does.  One warp walks the tokens in order (latency
+ * kernel, meant for decode batches). */
+typedef struct klc_locality_config {
+  double sticky_strength;
+  double sticky_candidate_margin;
+  double max_sticky_bonus;
+  double exploration_margin;
+  double cache_aware_strength;
+  double sticky_decay;
+  double workload_window;
+  int32_t semantic_guard;
+  int32_t min_raw_overlap;
+  int32_t max_hot_experts;
+  int32_t prediction_window;
+  int32_t predictive_prefetch;
+  int32_t experts_per_token;
+} klc_locality_config;
+int klc_locality_state_bytes(int64_t experts, int prediction_window, size_t* out_bytes);
+int klc_locality_route(const klc_locality_config* cfg, const uint16_t* logits, int64_t tokens, int64_t experts, int k,
+                       const uint8_t* resident, int64_t resident_stride, void* state, size_t state_bytes,
+                       int32_t* out_experts, uint16_t* out_w, int32_t* out_raw, int32_t* out_pred, int32_t* out_npred,
+                       uint8_t* out_flags, void* stream);
+
 /* ---- expert parallelism over NVLink peer memory ------------------------
  * No counterpart in the reference (one process, one device): the node-level
  * sharding of the MoE block, rank r owning experts [r*epr, (r+1)*epr).  One
@@ -366,6 +443,12 @@ int klc_ep_arena_bytes(const klc_ep* h, size_t* out_bytes);
 int klc_ep_ipc_handle(const klc_ep* h, void* out_64_bytes);
 int klc_ep_connect(klc_ep* h, const void* handles_world_x_64_bytes);
 int klc_ep_set_wait_limit_ns(klc_ep* h, uint64_t ns);
+/* enable != 0 (the default): with the weights-as-N tensor-core kernels and at most
+ * 8 ranks, the down-projection epilogue of klc_ep_experts stores every expert
+ * output row straight into its source rank's arena over NVLink, so the return
+ * transfer overlaps the GEMM; 0: the rows go through the workspace and a
+ * separate copy kernel.  Both give identical results. */
+int klc_ep_set_fused_return(klc_ep* h, int enable);
 int klc_ep_workspace_size(const klc_ep* h, const klc_moe_dims* local_dims, size_t* out_bytes);
 int klc_ep_dispatch(klc_ep* h, const int32_t* idx, int64_t tokens, const uint16_t* x, int32_t* pair_slot, void* workspace,
                     size_t workspace_bytes, void* stream);
@@ -373,6 +456,11 @@ int klc_ep_experts(klc_ep* h, const klc_moe_dims* local_dims, const klc_moe_weig
                    void* workspace, size_t workspace_bytes, void* stream);
 int klc_ep_combine(klc_ep* h, const int32_t* pair_slot, const uint16_t* w, int64_t tokens, const uint16_t* residual,
                    const uint16_t* norm_w, float eps, uint16_t* out, uint16_t* normed, void* stream);
+/* klc_ep_combine with the next layer's router on the normalised rows (see
+ * klc_next_router); norm_w / normed required. */
+int klc_ep_combine_route(klc_ep* h, const int32_t* pair_slot, const uint16_t* w, int64_t tokens, const uint16_t* residual,
+                         const uint16_t* norm_w, float eps, uint16_t* out, uint16_t* normed, const klc_next_router* next,
+                         void* stream);
 /* Router (klc_router_topk over all epr*world experts) + dispatch + experts +
  * combine: one expert-parallel MoE layer forward on this rank's tokens.     */
 int klc_ep_forward(klc_ep* h, const klc_moe_dims* local_dims, const klc_moe_weights* local_wts, const uint16_t* router_w,

@@ -51,6 +51,40 @@ class KlcDims(ctypes.Structure):
     ]
 
 
+class KlcLocalityConfig(ctypes.Structure):
+    """klc_locality_config: RoutingLocalityConfig's fields plus the router's experts_per_token."""
+
+    _fields_ = [
+        ("sticky_strength", ctypes.c_double),
+        ("sticky_candidate_margin", ctypes.c_double),
+        ("max_sticky_bonus", ctypes.c_double),
+        ("exploration_margin", ctypes.c_double),
+        ("cache_aware_strength", ctypes.c_double),
+        ("sticky_decay", ctypes.c_double),
+        ("workload_window", ctypes.c_double),
+        ("semantic_guard", c_int32),
+        ("min_raw_overlap", c_int32),
+        ("max_hot_experts", c_int32),
+        ("prediction_window", c_int32),
+        ("predictive_prefetch", c_int32),
+        ("experts_per_token", c_int32),
+    ]
+
+
+class KlcNextRouter(ctypes.Structure):
+    """klc_next_router: the next layer's router, run on the normalised rows by the combine."""
+
+    _fields_ = [
+        ("router_w", c_void_p),
+        ("router_b", c_void_p),
+        ("experts", c_int64),
+        ("k", c_int),
+        ("out_idx", c_void_p),
+        ("out_w", c_void_p),
+        ("out_logits", c_void_p),
+    ]
+
+
 class KlcWeights(ctypes.Structure):
     _fields_ = [
         ("gu_blocks", c_void_p),
@@ -91,6 +125,9 @@ SIGNATURES: dict[str, list] = {
     "klc_router_status": [POINTER(c_int), POINTER(c_int), c_void_p],
     "klc_router_topk": [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "klc_select_softmax": [c_void_p, c_int64, c_int64, c_int, c_int, c_void_p, c_void_p, c_void_p],
+    "klc_locality_state_bytes": [c_int64, c_int, POINTER(c_size_t)],
+    "klc_locality_route": [POINTER(KlcLocalityConfig), c_void_p, c_int64, c_int64, c_int, c_void_p, c_int64, c_void_p, c_size_t,
+                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "klc_moe_workspace_size": [POINTER(KlcDims), POINTER(c_size_t)],
     "klc_moe_experts": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "klc_moe_experts_noalloc": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
@@ -100,6 +137,13 @@ SIGNATURES: dict[str, list] = {
     "klc_moe_combine": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_void_p],
     "klc_moe_combine_rmsnorm": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p],
     "klc_moe_forward_rmsnorm": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_size_t, c_void_p],
+    "klc_moe_forward_rmsnorm_route": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, POINTER(KlcNextRouter), c_void_p,
+                                      c_size_t, c_void_p],
+    "klc_moe_experts_rmsnorm_route": [POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_float, c_void_p, POINTER(KlcNextRouter), c_void_p, c_size_t, c_void_p],
+    "klc_moe_combine_rmsnorm_route": [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int64, c_void_p, c_void_p, c_float, c_void_p,
+                                      c_void_p, POINTER(KlcNextRouter), c_void_p],
     "klc_moe_bias_only": [c_void_p, c_int64, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
     "klc_moe_permute": [c_void_p, c_int64, c_int, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_size_t, c_void_p],
     "klc_ep_pack": [c_void_p, c_int64, c_int, c_int64, c_int, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
@@ -111,10 +155,13 @@ SIGNATURES: dict[str, list] = {
     "klc_ep_ipc_handle": [c_void_p, c_void_p],
     "klc_ep_connect": [c_void_p, c_void_p],
     "klc_ep_set_wait_limit_ns": [c_void_p, ctypes.c_uint64],
+    "klc_ep_set_fused_return": [c_void_p, c_int],
     "klc_ep_workspace_size": [c_void_p, POINTER(KlcDims), POINTER(c_size_t)],
     "klc_ep_dispatch": [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "klc_ep_experts": [c_void_p, POINTER(KlcDims), POINTER(KlcWeights), c_int, c_void_p, c_size_t, c_void_p],
     "klc_ep_combine": [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p],
+    "klc_ep_combine_route": [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
+                             POINTER(KlcNextRouter), c_void_p],
     "klc_ep_forward": [c_void_p, POINTER(KlcDims), POINTER(KlcWeights), c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p,
                        c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "klc_ep_status": [c_void_p, c_void_p, POINTER(c_int), POINTER(c_int), c_void_p],

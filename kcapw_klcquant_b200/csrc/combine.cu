@@ -16,12 +16,15 @@
 // from the bf16 values as they are stored, and each thread re-reads only the
 // chunks it stored itself, so no second kernel re-reads the hidden state.
 #include "permute.cuh"
+#include "select.cuh"
 
 namespace klc {
 
 namespace {
 
 constexpr int kMaxTopK = 8;
+// up to this many tokens the next layer's router runs inside the combine
+constexpr int64_t kFusedRouterMaxTokens = 64;
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
@@ -120,6 +123,121 @@ __global__ void __launch_bounds__(256, 4) combine_kernel(const uint16_t* __restr
   }
 }
 
+// The fused form plus the next layer's router (decode batches): the CTA keeps
+// the token's normalised row in shared memory after storing it, computes its E
+// router logits on the CUDA cores (router rows read from L2 with 16-byte
+// loads, fp32 sums, the bias added in fp32, one bf16 rounding, as the router
+// kernels do) and one warp selects the top-k and the softmax.  Replaces the
+// separate router launch of the next layer (streamed_moe_router.py:269-282 on
+// streamed_transformer_executor.py:247's `post`).
+__global__ void __launch_bounds__(256) combine_norm_route_kernel(
+    const uint16_t* __restrict__ y, const int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ w, int k,
+    int64_t hidden, const uint16_t* __restrict__ residual, uint16_t* __restrict__ out, const float* __restrict__ normsq,
+    float* __restrict__ norms, const uint16_t* __restrict__ norm_w, float eps, uint16_t* __restrict__ normed,
+    const uint16_t* __restrict__ rw, const uint16_t* __restrict__ rb, int E, int kn, int32_t* __restrict__ nidx,
+    uint16_t* __restrict__ nw, uint16_t* __restrict__ nlogits) {
+  extern __shared__ __align__(16) unsigned char cr_smem[];
+  uint4* xs = reinterpret_cast<uint4*>(cr_smem);                             // normalised row [H/8]
+  float* row = reinterpret_cast<float*>(cr_smem + (hidden * 2 + 15) / 16 * 16);  // logits [E]
+  __shared__ float red[32];
+  const int64_t t = blockIdx.x;
+  const int chunks = int(hidden / 8);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = int(blockDim.x >> 5);
+  if (norms != nullptr && threadIdx.x < 2 * k) {
+    const int64_t q = t * k * 2 + threadIdx.x;
+    norms[q] = sqrtf(normsq[q]);
+  }
+  int pos[kMaxTopK];
+  float wsel[kMaxTopK];
+#pragma unroll
+  for (int s = 0; s < kMaxTopK; ++s) {
+    pos[s] = s < k ? pair_pos[t * k + s] : -1;
+    wsel[s] = s < k ? bf16_to_f32(w[t * k + s]) : 0.f;
+  }
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    uint4 v[kMaxTopK];
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s)
+      v[s] = pos[s] >= 0 ? reinterpret_cast<const uint4*>(y + int64_t(pos[s]) * hidden)[c] : make_uint4(0, 0, 0, 0);
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s) {
+      if (pos[s] < 0) continue;
+      const float ws = wsel[s];
+      const uint32_t vv[4] = {v[s].x, v[s].y, v[s].z, v[s].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
+        acc[2 * j] = round_bf16(acc[2 * j] + round_bf16(lo * ws));
+        acc[2 * j + 1] = round_bf16(acc[2 * j + 1] + round_bf16(hi * ws));
+      }
+    }
+    if (residual != nullptr) {
+      const uint4 r = reinterpret_cast<const uint4*>(residual + t * hidden)[c];
+      const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = round_bf16(__uint_as_float(rr[j] << 16) + acc[2 * j]);
+        acc[2 * j + 1] = round_bf16(__uint_as_float(rr[j] & 0xffff0000u) + acc[2 * j + 1]);
+      }
+    }
+    uint4 o;
+    o.x = uint32_t(f32_to_bf16(acc[0])) | (uint32_t(f32_to_bf16(acc[1])) << 16);
+    o.y = uint32_t(f32_to_bf16(acc[2])) | (uint32_t(f32_to_bf16(acc[3])) << 16);
+    o.z = uint32_t(f32_to_bf16(acc[4])) | (uint32_t(f32_to_bf16(acc[5])) << 16);
+    o.w = uint32_t(f32_to_bf16(acc[6])) | (uint32_t(f32_to_bf16(acc[7])) << 16);
+    reinterpret_cast<uint4*>(out + t * hidden)[c] = o;
+    xs[c] = o;  // the stored sum, normalised below in place
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(acc[j], acc[j], ss);
+  }
+  const float total = block_sum(ss, red);
+  const float inv = round_bf16(1.0f / sqrtf(total / float(hidden) + eps));
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    const uint4 o = xs[c];
+    const uint4 g = reinterpret_cast<const uint4*>(norm_w)[c];
+    const uint32_t oo[4] = {o.x, o.y, o.z, o.w}, gg[4] = {g.x, g.y, g.z, g.w};
+    uint32_t r[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float lo = round_bf16(__uint_as_float(oo[j] << 16) * inv) * __uint_as_float(gg[j] << 16);
+      const float hi = round_bf16(__uint_as_float(oo[j] & 0xffff0000u) * inv) * __uint_as_float(gg[j] & 0xffff0000u);
+      r[j] = uint32_t(f32_to_bf16(lo)) | (uint32_t(f32_to_bf16(hi)) << 16);
+    }
+    const uint4 nv = make_uint4(r[0], r[1], r[2], r[3]);
+    reinterpret_cast<uint4*>(normed + t * hidden)[c] = nv;
+    xs[c] = nv;
+  }
+  __syncthreads();
+  // router logits of the normalised row: warp w takes experts w, w + nwarps, ...
+  for (int e = warp; e < E; e += nwarps) {
+    const uint16_t* wr = rw + int64_t(e) * hidden;
+    float acc = 0.f;
+#pragma unroll 4
+    for (int c = lane; c < chunks; c += 32) {
+      const uint4 a = ldg_nc_v4(wr + int64_t(c) * 8);
+      const uint4 b = xs[c];
+      const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc = fmaf(__uint_as_float(aa[j] << 16), __uint_as_float(bb[j] << 16), acc);
+        acc = fmaf(__uint_as_float(aa[j] & 0xffff0000u), __uint_as_float(bb[j] & 0xffff0000u), acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) {
+      const uint16_t lb = f32_to_bf16(acc + bf16_to_f32(rb[e]));
+      if (nlogits != nullptr) nlogits[t * E + e] = lb;
+      row[e] = bf16_to_f32(lb);
+    }
+  }
+  __syncthreads();
+  if (warp == 0) select_softmax_warp(row, E, kn, false, nidx + t * kn, nw + t * kn);
+}
+
 // execute_experts=False (streamed_moe_router.py:317-329):
 //   contribution = sum(down_bias[experts].to(bf16) * weights[:, None], dim=0)
 // products rounded to bf16, the k-term sum accumulated in fp32, rounded once.
@@ -171,6 +289,29 @@ int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w
     KLC_CHECK_ARG(post->weight && post->normed, "combine: null RMSNorm weight or output");
     KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(post->weight) & 15) == 0 && (reinterpret_cast<uintptr_t>(post->normed) & 15) == 0,
                   "combine: RMSNorm weight and output must be 16-byte aligned");
+    if (post->router_w != nullptr) {
+      KLC_CHECK_ARG(post->router_b && post->out_idx && post->out_w, "combine: null next-layer router argument");
+      KLC_CHECK_ARG(post->experts >= 1 && post->experts <= 1024 && post->k >= 1 && post->k <= kSelMaxK && post->k <= post->experts,
+                    "combine: next-layer router needs 1 <= k <= min(8, experts), experts <= 1024");
+      KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(post->router_w) & 15) == 0, "combine: router weight must be 16-byte aligned");
+      const size_t smem = size_t((hidden * 2 + 15) / 16 * 16) + size_t(post->experts) * 4;
+      if (tokens <= kFusedRouterMaxTokens && smem <= 200 * 1024) {
+        // decode batches: the next router inside the combine (router rows from L2, one CTA per token)
+        if (smem > 48 * 1024)
+          KLC_CUDA(cudaFuncSetAttribute(combine_norm_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+        combine_norm_route_kernel<<<unsigned(tokens), threads, smem, stream>>>(
+            y, pair_pos, w, k, hidden, residual, out, normsq, norms, post->weight, post->eps, post->normed, post->router_w,
+            post->router_b, post->experts, post->k, post->out_idx, post->out_w, post->out_logits);
+        KLC_LAUNCH_CHECK("combine launch");
+        return KLC_OK;
+      }
+      // larger batches: the combine, then the router kernels on the normalised rows
+      combine_kernel<true><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
+                                                                      norms, post->weight, post->eps, post->normed);
+      KLC_LAUNCH_CHECK("combine launch");
+      return launch_router(post->normed, tokens, hidden, post->router_w, post->router_b, post->experts, post->k, nullptr,
+                           post->out_idx, post->out_w, post->out_logits, stream);
+    }
     combine_kernel<true><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
                                                                     norms, post->weight, post->eps, post->normed);
   } else {
@@ -228,4 +369,25 @@ extern "C" int klc_moe_combine_rmsnorm(const uint16_t* y_rows, const int32_t* pa
   const PostNorm post{norm_w, eps, normed};
   return launch_combine(y_rows, pair_pos, w, tokens, k, hidden, residual, out, nullptr, nullptr, &post,
                         as_stream(stream));
+}
+
+extern "C" int klc_moe_combine_rmsnorm_route(const uint16_t* y_rows, const int32_t* pair_pos, const uint16_t* w,
+                                             int64_t tokens, int k, int64_t hidden, const uint16_t* residual,
+                                             const uint16_t* norm_w, float eps, uint16_t* out, uint16_t* normed,
+                                             const klc_next_router* next, void* stream) {
+  using namespace klc;
+  KLC_CHECK_ARG(tokens >= 0 && k >= 1 && hidden > 0 && hidden % 8 == 0, "klc_moe_combine_rmsnorm_route: bad sizes");
+  KLC_CHECK_ARG(next != nullptr && next->experts >= 1 && next->experts <= 1024, "klc_moe_combine_rmsnorm_route: bad next router");
+  if (tokens == 0) return KLC_OK;
+  KLC_CHECK_ARG(y_rows && pair_pos && w && out && norm_w && normed, "klc_moe_combine_rmsnorm_route: null pointer");
+  PostNorm post{norm_w, eps, normed};
+  post.router_w = next->router_w;
+  post.router_b = next->router_b;
+  post.experts = int(next->experts);
+  post.k = next->k;
+  post.out_idx = next->out_idx;
+  post.out_w = next->out_w;
+  post.out_logits = next->out_logits;
+  KLC_CHECK_ARG(post.router_w != nullptr, "klc_moe_combine_rmsnorm_route: null router weight");
+  return launch_combine(y_rows, pair_pos, w, tokens, k, hidden, residual, out, nullptr, nullptr, &post, as_stream(stream));
 }

@@ -27,9 +27,12 @@
 //      writes the per-destination counts and then the dispatch flags.
 //   2. experts: ep_fill_kernel waits (bounded) for every source's dispatch flag
 //      and marks each received slot with its expert id or -1; the local expert
-//      GEMMs run on the received rows (k = 1, empty slots skipped);
-//      ep_return_kernel stores every expert output row into the source's
-//      back_rows segment of this destination and raises the combine flags.
+//      GEMMs run on the received rows (k = 1, empty slots skipped).  The down
+//      GEMM's epilogue stores every expert output row straight into the
+//      source's back_rows segment of this destination over NVLink, so the
+//      return overlaps the GEMM tiles (weights-as-N kernels, up to 8 ranks;
+//      otherwise ep_return_kernel copies the rows afterwards); then the
+//      combine flags are raised.
 //   3. combine: ep_wait_kernel waits (bounded) for every destination's combine
 //      flag; the weighted combine (combine.cu) reads back_rows by the slot the
 //      dispatch recorded for each pair, in top-k order: the reference's combine
@@ -226,6 +229,15 @@ __global__ void __launch_bounds__(256)
   signal_peers(peers, world, rank, done, L.flag_combine, 0, nullptr, epoch);
 }
 
+// 2b'. after a down kernel that stored the rows into the sources' arenas itself:
+// only the combine flags (the rows were made visible system-wide by that kernel)
+__global__ void ep_signal_kernel(int world, int rank, PeerBases peers, ArenaLayout L, char* arena) {
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(arena + L.epoch);
+  __threadfence_system();
+  for (int d = threadIdx.x; d < world; d += blockDim.x)
+    st_release_sys(reinterpret_cast<uint32_t*>(peers.base[d] + L.flag_combine) + rank, epoch);
+}
+
 // 3. wait for every destination's returned rows
 __global__ void ep_wait_kernel(char* arena, ArenaLayout L, int world, uint64_t limit_ns) {
   const int d = threadIdx.x;
@@ -255,6 +267,7 @@ struct klc_ep {
   bool connected = false;
   uint64_t dispatches = 0;  // host count (the epoch itself lives in the arena)
   uint64_t wait_ns = klc::kDefaultWaitNs;
+  bool fused_return = true;  // down epilogue stores rows to the sources (weights-as-N kernels)
 };
 
 namespace klc {
@@ -392,6 +405,12 @@ extern "C" int klc_ep_set_wait_limit_ns(klc_ep* h, uint64_t ns) {
   return KLC_OK;
 }
 
+extern "C" int klc_ep_set_fused_return(klc_ep* h, int enable) {
+  KLC_CHECK_ARG(h != nullptr, "klc_ep_set_fused_return: null handle");
+  h->fused_return = enable != 0;
+  return KLC_OK;
+}
+
 extern "C" int klc_ep_workspace_size(const klc_ep* h, const klc_moe_dims* local, size_t* out) {
   KLC_CHECK_ARG(h != nullptr && local != nullptr && out != nullptr, "klc_ep_workspace_size: null argument");
   const klc_moe_dims ld = local_dims(h, *local);
@@ -478,6 +497,23 @@ extern "C" int klc_ep_experts(klc_ep* h, const klc_moe_dims* local, const klc_mo
   KLC_LAUNCH_CHECK("ep_fill_kernel launch");
   char* ws = static_cast<char*>(workspace);
   const int32_t* recv_expert = reinterpret_cast<const int32_t*>(h->arena + h->L.recv_expert);
+  // weights-as-N kernels: the down epilogue stores every output row straight into its
+  // source's back_rows segment over NVLink, overlapping the transfer with the GEMM
+  if (h->fused_return && h->world <= kMaxScatterSegments && use_tc_path(ld) &&
+      experts_tc_can_scatter(*wts, ld.hidden, ld.intermediate, W.block_n)) {
+    RowScatter sc{};
+    const PeerBases pb = bases_of(h);
+    for (int d = 0; d < h->world; ++d) sc.base[d] = pb.base[d] + h->L.back_rows;
+    sc.seg_cap = h->cap;
+    sc.slot0 = int64_t(h->rank) * h->cap;
+    sc.world = h->world;
+    st = run_expert_stage(ld, *wts, reinterpret_cast<const uint16_t*>(h->arena + h->L.recv_rows), recv_expert, precision,
+                          nullptr, true, ws, W, s, &sc);
+    if (st != KLC_OK) return st;
+    ep_signal_kernel<<<1, ((h->world + 31) / 32) * 32, 0, s>>>(h->world, h->rank, pb, h->L, h->arena);
+    KLC_LAUNCH_CHECK("ep_signal_kernel launch");
+    return KLC_OK;
+  }
   st = run_expert_stage(ld, *wts, reinterpret_cast<const uint16_t*>(h->arena + h->L.recv_rows), recv_expert, precision,
                         nullptr, true, ws, W, s);
   if (st != KLC_OK) return st;
@@ -507,6 +543,33 @@ extern "C" int klc_ep_combine(klc_ep* h, const int32_t* pair_slot, const uint16_
   PostNorm post{norm_w, eps, normed};
   st = launch_combine(reinterpret_cast<const uint16_t*>(h->arena + h->L.back_rows), pair_slot, w, tokens, h->top_k,
                       h->hidden, residual, out, nullptr, nullptr, norm_w != nullptr ? &post : nullptr, s);
+  stage_mark(kStageCombined, s);
+  return st;
+}
+
+extern "C" int klc_ep_combine_route(klc_ep* h, const int32_t* pair_slot, const uint16_t* w, int64_t tokens,
+                                    const uint16_t* residual, const uint16_t* norm_w, float eps, uint16_t* out,
+                                    uint16_t* normed, const klc_next_router* next, void* stream) {
+  int st = check_handle(h, true);
+  if (st != KLC_OK) return st;
+  KLC_CHECK_ARG(tokens >= 0 && tokens <= h->max_tokens, "klc_ep_combine_route: tokens must be in [0, max_tokens]");
+  KLC_CHECK_ARG(tokens == 0 || (pair_slot && w && out && norm_w && normed), "klc_ep_combine_route: null pointer");
+  KLC_CHECK_ARG(next != nullptr && next->router_w && next->experts >= 1 && next->experts <= 1024,
+                "klc_ep_combine_route: bad next router");
+  cudaStream_t s = as_stream(stream);
+  ep_wait_kernel<<<1, ((h->world + 31) / 32) * 32, 0, s>>>(h->arena, h->L, h->world, h->wait_ns);
+  KLC_LAUNCH_CHECK("ep_wait_kernel launch");
+  if (tokens == 0) return KLC_OK;
+  PostNorm post{norm_w, eps, normed};
+  post.router_w = next->router_w;
+  post.router_b = next->router_b;
+  post.experts = int(next->experts);
+  post.k = next->k;
+  post.out_idx = next->out_idx;
+  post.out_w = next->out_w;
+  post.out_logits = next->out_logits;
+  st = launch_combine(reinterpret_cast<const uint16_t*>(h->arena + h->L.back_rows), pair_slot, w, tokens, h->top_k,
+                      h->hidden, residual, out, nullptr, nullptr, &post, s);
   stage_mark(kStageCombined, s);
   return st;
 }

@@ -173,6 +173,7 @@ struct MxParams {
   float* normsq;
   int precision;
   float limit, alpha;
+  RowScatter sc;        // phase 2 of the weights-as-N kernels: rows to other buffers (world 0: none)
 };
 
 template <int PHASE, class C>
@@ -1133,6 +1134,16 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       const bool hi_lane = (lane & 1) == 0;   // even lane: hi row, holds the sum
       if (16 * q < nrows) {
         const uint32_t lane_base = tmem + (uint32_t(q * 32) << 16) + uint32_t(d * kWN);
+        // destination row: dense, or (down pass with a scatter) its segment of another buffer
+        uint16_t* drow = p.out + int64_t(r0 + n) * p.out_ld;
+        if (PHASE == 2 && p.sc.world > 0 && tok) {
+          const int pq = p.rows[r0 + n];
+          const int seg = pq >= 0 ? int(pq / p.sc.seg_cap) : -1;
+          drow = (seg >= 0 && seg < p.sc.world)
+                     ? reinterpret_cast<uint16_t*>(p.sc.base[seg] +
+                                                   (p.sc.slot0 + pq % p.sc.seg_cap) * int64_t(p.out_ld) * 2)
+                     : nullptr;
+        }
         float sq = 0.f;
         // bias of the first chunk, loaded before the accumulators are read; each
         // chunk then loads the next chunk's bias ahead of its own work
@@ -1167,8 +1178,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
               if (p.precision == KLC_PREC_BF16) x = round_bf16(x);
               v[i] = x + bf16_to_f32(uint16_t((i & 1) ? (bw[i >> 1] >> 16) : (bw[i >> 1] & 0xFFFFu)));
             }
-            if (tok && hi_lane) {
-              uint16_t* orow = p.out + int64_t(r0 + n) * p.out_ld;
+            if (tok && hi_lane && drow != nullptr) {
+              uint16_t* orow = drow;
               if (PHASE == 1) {
                 // columns 2f, 2f+1: gate and up of feature j0/2 + f
                 uint32_t pk[4];
@@ -1207,6 +1218,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(dempty(d));
     }
+    // scattered rows (peer memory) visible system-wide before the kernel that raises the flags
+    if (PHASE == 2 && p.sc.world > 0) __threadfence_system();
   }
 
   tc_fence_before();
@@ -1397,6 +1410,7 @@ int launch_mx3_both(const ExpertArgs& a, const uint8_t* gu_k128, const uint8_t* 
   p2.bias = w.dn_bias;
   p2.out = a.y;
   p2.out_ld = int(a.hidden);
+  if (a.scatter != nullptr) p2.sc = *a.scatter;
   st = launch_mx3_phase<2, C>(dn_k128, a.gq, a.rows_cap, int(a.experts), p2, a.max_rowblocks, stream);
   stage_mark(kStageDown, stream);
   return st;
@@ -1540,15 +1554,35 @@ bool tc_path_supported(int64_t hidden, int64_t inter) {
 
 int mx_sfb_chunks(int block_n) { return (2 * block_n + 127) / 128; }
 
+namespace {
+// padded (K multiple of 128) weight blocks for the direct-operand kernels, or null
+const uint8_t* gu_k128_of(const klc_moe_weights& w, int64_t hidden) {
+  return w.gu_blocks_k128 != nullptr ? w.gu_blocks_k128 : (hidden % 128 == 0 ? w.gu_blocks : nullptr);
+}
+const uint8_t* dn_k128_of(const klc_moe_weights& w, int64_t inter) {
+  return w.dn_blocks_k128 != nullptr ? w.dn_blocks_k128 : (inter % 128 == 0 ? w.dn_blocks : nullptr);
+}
+bool mx3_usable(const klc_moe_weights& w, int64_t hidden, int64_t inter) {
+  const bool bias16 = ((reinterpret_cast<uintptr_t>(w.gu_bias) | reinterpret_cast<uintptr_t>(w.dn_bias)) & 15) == 0;
+  return gu_k128_of(w, hidden) != nullptr && dn_k128_of(w, inter) != nullptr && w.gu_scales_t192 != nullptr &&
+         w.dn_scales_t192 != nullptr && bias16;
+}
+}  // namespace
+
+bool experts_tc_can_scatter(const klc_moe_weights& w, int64_t hidden, int64_t inter, int block_n) {
+  return hidden % 64 == 0 && inter % 64 == 0 && (block_n == 16 || block_n == 64) && mx3_usable(w, hidden, inter);
+}
+
 int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   KLC_CHECK_ARG(a.hidden % 64 == 0 && a.inter % 64 == 0, "tensor-core path: hidden and intermediate must be multiples of 64");
   KLC_CHECK_ARG(2 * a.rows_cap < (int64_t(1) << 31), "tensor-core path: too many rows");
   // direct-operand kernels when the weights are available with K padded to a multiple of 128
   const klc_moe_weights& w = *a.wts;
-  const uint8_t* gu = w.gu_blocks_k128 != nullptr ? w.gu_blocks_k128 : (a.hidden % 128 == 0 ? w.gu_blocks : nullptr);
-  const uint8_t* dn = w.dn_blocks_k128 != nullptr ? w.dn_blocks_k128 : (a.inter % 128 == 0 ? w.dn_blocks : nullptr);
-  const bool bias16 = ((reinterpret_cast<uintptr_t>(w.gu_bias) | reinterpret_cast<uintptr_t>(w.dn_bias)) & 15) == 0;
-  if (gu != nullptr && dn != nullptr && w.gu_scales_t192 != nullptr && w.dn_scales_t192 != nullptr && bias16) {
+  const uint8_t* gu = gu_k128_of(w, a.hidden);
+  const uint8_t* dn = dn_k128_of(w, a.inter);
+  KLC_CHECK_ARG(a.scatter == nullptr || mx3_usable(w, a.hidden, a.inter),
+                "tensor-core path: row scatter needs the weights-as-N kernels");
+  if (mx3_usable(w, a.hidden, a.inter)) {
     switch (a.block_n) {
       case 16: return launch_mx3_both<Mx3N16>(a, gu, dn, stream);
       case 64: return launch_mx3_both<Mx3N64>(a, gu, dn, stream);

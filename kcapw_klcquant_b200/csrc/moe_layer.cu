@@ -110,8 +110,11 @@ int validate_weights(const klc_moe_weights* w) {
 }
 
 int run_expert_stage(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx, int precision,
-                     float* normsq, bool empty_ok, char* ws, const WorkspaceLayout& L, cudaStream_t stream) {
+                     float* normsq, bool empty_ok, char* ws, const WorkspaceLayout& L, cudaStream_t stream,
+                     const RowScatter* scatter) {
   const bool tc = use_tc_path(d);
+  KLC_CHECK_ARG(scatter == nullptr || (tc && experts_tc_can_scatter(wts, d.hidden, d.intermediate, L.block_n)),
+                "expert stage: row scatter needs the weights-as-N tensor-core kernels");
   DeviceStatus* status = reinterpret_cast<DeviceStatus*>(ws + L.status);
   KLC_CUDA(cudaMemsetAsync(status, 0, sizeof(DeviceStatus), stream));
   PermuteArgs pa{};
@@ -163,6 +166,7 @@ int run_expert_stage(const klc_moe_dims& d, const klc_moe_weights& wts, const ui
   ea.normsq = normsq;
   ea.rows_cap = L.rows_cap;
   ea.block_n = L.block_n;
+  ea.scatter = scatter;
   return tc ? launch_experts_tc(ea, stream) : launch_experts_simt(ea, stream);
 }
 
@@ -264,6 +268,46 @@ extern "C" int klc_moe_forward_rmsnorm(const klc_moe_dims* dims, const klc_moe_w
   const PostNorm post{norm_w, eps, normed};
   return forward_entry(dims, wts, x, adjust, precision, y, out_idx, out_w, out_logits, norms, residual, &post,
                        workspace, workspace_bytes, stream);
+}
+
+namespace {
+PostNorm post_with_router(const uint16_t* norm_w, float eps, uint16_t* normed, const klc_next_router* next) {
+  PostNorm post{norm_w, eps, normed};
+  if (next != nullptr) {
+    post.router_w = next->router_w;
+    post.router_b = next->router_b;
+    post.experts = int(next->experts);
+    post.k = next->k;
+    post.out_idx = next->out_idx;
+    post.out_w = next->out_w;
+    post.out_logits = next->out_logits;
+  }
+  return post;
+}
+}  // namespace
+
+extern "C" int klc_moe_forward_rmsnorm_route(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
+                                             const float* adjust, int precision, uint16_t* y, int32_t* out_idx,
+                                             uint16_t* out_w, uint16_t* out_logits, float* norms, const uint16_t* residual,
+                                             const uint16_t* norm_w, float eps, uint16_t* normed,
+                                             const klc_next_router* next, void* workspace, size_t workspace_bytes,
+                                             void* stream) {
+  KLC_CHECK_ARG(norm_w && normed && next && next->router_w, "klc_moe_forward_rmsnorm_route: null argument");
+  KLC_CHECK_ARG(next->experts >= 1 && next->experts <= 1024, "klc_moe_forward_rmsnorm_route: next experts out of range");
+  const PostNorm post = post_with_router(norm_w, eps, normed, next);
+  return forward_entry(dims, wts, x, adjust, precision, y, out_idx, out_w, out_logits, norms, residual, &post,
+                       workspace, workspace_bytes, stream);
+}
+
+extern "C" int klc_moe_experts_rmsnorm_route(const klc_moe_dims* dims, const klc_moe_weights* wts, const uint16_t* x,
+                                             const int32_t* idx, const uint16_t* w, int precision, uint16_t* y,
+                                             float* norms, const uint16_t* residual, const uint16_t* norm_w, float eps,
+                                             uint16_t* normed, const klc_next_router* next, void* workspace,
+                                             size_t workspace_bytes, void* stream) {
+  KLC_CHECK_ARG(norm_w && normed && next && next->router_w, "klc_moe_experts_rmsnorm_route: null argument");
+  KLC_CHECK_ARG(next->experts >= 1 && next->experts <= 1024, "klc_moe_experts_rmsnorm_route: next experts out of range");
+  const PostNorm post = post_with_router(norm_w, eps, normed, next);
+  return experts_entry(dims, wts, x, idx, w, precision, y, norms, residual, &post, workspace, workspace_bytes, stream);
 }
 
 extern "C" int klc_moe_permute(const int32_t* idx, int64_t tokens, int k, int64_t experts, int pad, int32_t* pair_pos,

@@ -49,12 +49,26 @@ struct WorkspaceLayout {
 
 WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffers);
 
+// Down-projection output rows stored into segments of other buffers instead of y
+// (expert parallelism: each row goes back to its source rank's arena over
+// NVLink).  Padded row r holding pair q is written to
+// base[q / seg_cap] + (slot0 + q % seg_cap) * hidden * 2 bytes.
+constexpr int kMaxScatterSegments = 8;
+struct RowScatter {
+  char* base[kMaxScatterSegments];
+  int64_t seg_cap;
+  int64_t slot0;
+  int world;  // 0: no scatter
+};
+
 // Permute + both expert GEMMs for given routing, without the combine: the
 // expert output of pair p is row pair_pos[p] of y (ws + L.pair_pos, ws + L.y;
 // -1 for an empty slot when empty_ok).  `normsq` (or null) accumulates the
-// per-pair squared norms.
+// per-pair squared norms.  With `scatter` the down rows go to its segments
+// instead of y (weights-as-N tensor-core kernels only).
 int run_expert_stage(const klc_moe_dims& d, const klc_moe_weights& wts, const uint16_t* x, const int32_t* idx, int precision,
-                     float* normsq, bool empty_ok, char* ws, const WorkspaceLayout& L, cudaStream_t stream);
+                     float* normsq, bool empty_ok, char* ws, const WorkspaceLayout& L, cudaStream_t stream,
+                     const RowScatter* scatter = nullptr);
 
 // Argument checks shared by every layer entry point (KLC_ERR_INVALID and a
 // message on failure): sizes, the expert path, and the expert weight pointers
@@ -86,11 +100,16 @@ struct ExpertArgs {
   float* normsq;               // [pairs, 2] or null
   int64_t rows_cap;
   int block_n;                 // max rows per row-block
+  const RowScatter* scatter;   // null: down rows into y
 };
 
 int launch_experts_simt(const ExpertArgs& a, cudaStream_t stream);
 int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream);
 bool tc_path_supported(int64_t hidden, int64_t inter);
+bool use_tc_path(const klc_moe_dims& d);  // the dims' path choice (auto: tc_path_supported)
+// true when launch_experts_tc runs these weights with the weights-as-N kernels,
+// the form whose down epilogue can scatter rows (RowScatter)
+bool experts_tc_can_scatter(const klc_moe_weights& w, int64_t hidden, int64_t inter, int block_n);
 // 512-byte activation-scale blocks per (row-block, 128-K stage) of the tensor-core path
 int mx_sfb_chunks(int block_n);
 // bf16 rows -> hi/lo E4M3 rows + scale blocks for every row-block (mx_quant.cu);
@@ -110,6 +129,13 @@ struct PostNorm {
   const uint16_t* weight;
   float eps;
   uint16_t* normed;
+  // optional: the next layer's router on the normalised rows (router_w null: none)
+  const uint16_t* router_w;   // bf16 [E, H]
+  const uint16_t* router_b;   // bf16 [E]
+  int experts, k;
+  int32_t* out_idx;           // int32 [T, k]
+  uint16_t* out_w;            // bf16 [T, k]
+  uint16_t* out_logits;       // bf16 [T, E] or null
 };
 
 int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w, int64_t tokens, int k,

@@ -30,6 +30,7 @@
 
 #include "klc_common.cuh"
 #include "permute.cuh"
+#include "select.cuh"
 #include "tc_common.cuh"
 
 namespace klc {
@@ -46,72 +47,6 @@ constexpr int kMaxCluster = 8;  // portable cluster size
 // whole-K tiles of 128 tokens from here on (B200, T = 2048 / 4096 / 16384: 71 / 72 / 78 us
 // against 82 / 131 / 434 us for the split-K cluster form, which wins below: 18 us at T = 1)
 constexpr int64_t kRouterGemmMinTokens = KLC_ROUTER_GEMM_MIN_TOKENS;
-
-// k rounds of a warp-wide arg-max over `row` (value descending, lower index
-// on ties), then softmax over the k selected fp32 scores (max-subtracted,
-// summed in selection order), each weight rounded once to bf16.  With
-// keep_order the row already holds exactly k scores in the wanted order.
-__device__ void select_softmax_warp(const float* row, int experts, int k, bool keep_order, int32_t* out_idx,
-                                    uint16_t* out_w) {
-  const int lane = threadIdx.x & 31;
-  float sel_v[kMaxK];
-  int sel_i[kMaxK];
-  for (int r = 0; r < k; ++r) {
-    if (keep_order) {
-      sel_v[r] = row[r];
-      sel_i[r] = r;
-      continue;
-    }
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int e = lane; e < experts; e += 32) {
-      bool taken = false;
-      for (int q = 0; q < r; ++q) taken |= (sel_i[q] == e);
-      const float v = row[e];
-      // -inf is still selectable; NaN compares false and is only taken when nothing else is left
-      if (!taken && (v > bv || (v == bv && e < bi))) {
-        bv = v;
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (bi == 0x7fffffff) {
-      for (int e = 0; e < experts; ++e) {
-        bool taken = false;
-        for (int q = 0; q < r; ++q) taken |= (sel_i[q] == e);
-        if (!taken) {
-          bi = e;
-          bv = row[e];
-          break;
-        }
-      }
-    }
-    sel_v[r] = bv;
-    sel_i[r] = bi;
-  }
-  if (lane == 0) {
-    float m = sel_v[0];
-    for (int r = 1; r < k; ++r) m = fmaxf(m, sel_v[r]);
-    float ex[kMaxK];
-    float sum = 0.f;
-    for (int r = 0; r < k; ++r) {
-      ex[r] = expf(sel_v[r] - m);
-      sum += ex[r];
-    }
-    for (int r = 0; r < k; ++r) {
-      if (!keep_order) out_idx[r] = sel_i[r];
-      out_w[r] = f32_to_bf16(ex[r] / sum);
-    }
-  }
-}
 
 // dot products of one router row with the kTok staged tokens; lanes split the
 // 16-byte chunks of the row, four loads in flight per lane
@@ -305,28 +240,41 @@ __global__ void __launch_bounds__(256, 1)
       }
     }
   }
+  tc_fence_before();
+  cluster.sync();  // every CTA's MMAs done: the operand space takes partial sums from the cluster
   tc_fence_after();
-  // partial logits [128 experts][NT tokens] fp32 into shared memory (the operand space is free now)
-  float* part = reinterpret_cast<float*>(ws);
-  // warps w and w + 4 share TMEM lane quarter w and split the token columns
-  for (int c0 = (warp >> 2) * 16; c0 < NT; c0 += 32) {
-    uint32_t v[16];
-    tmem_ld16(tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(c0), v);
-    tmem_wait_ld();
+  // CTA r finishes tokens r, r + C, ... of the tile; every CTA stores its partial logits of
+  // those tokens into that CTA's shared memory, slot (this rank, token / C): remote stores,
+  // local reads.  Warps w and w + 4 share TMEM lane quarter w and split the token columns.
+  const int tpc = (NT + C - 1) / C;  // tokens finished per CTA (at most)
+  float* recv = reinterpret_cast<float*>(ws);  // [C][tpc][128 experts]
+  {
+    const int e = (warp & 3) * 32 + lane;
+    for (int c0 = (warp >> 2) * 16; c0 < NT; c0 += 32) {
+      uint32_t v[16];
+      tmem_ld16(tmem + (uint32_t((warp & 3) * 32) << 16) + uint32_t(c0), v);
+      tmem_wait_ld();
 #pragma unroll
-    for (int j = 0; j < 16; ++j) part[((warp & 3) * 32 + lane) * NT + c0 + j] = __uint_as_float(v[j]);
+      for (int j = 0; j < 16; ++j) {
+        const int tok = c0 + j;
+        float* dst = C == 1 ? recv : cluster.map_shared_rank(recv, tok % C);
+        dst[(crank * tpc + tok / C) * 128 + e] = __uint_as_float(v[j]);
+      }
+    }
   }
   tc_fence_before();
   cluster.sync();
 
-  // tokens t = crank + C*j of the tile: sum the C partials in rank order, bias, one bf16 rounding,
-  // then top-k + softmax (one warp per token)
+  // local token j = tile token crank + C*j: the C partials summed in rank order, bias, one
+  // bf16 rounding, then top-k + softmax (one warp per token)
   float* rows = reinterpret_cast<float*>(xs);  // [8 warps][experts]
-  for (int t = crank + C * warp; t < ntok; t += C * 8) {
+  for (int j = warp; j < tpc; j += 8) {
+    const int t = crank + C * j;
+    if (t >= ntok || t >= NT) break;
     float* row = rows + warp * experts;
     for (int e = lane; e < experts; e += 32) {
       float acc = 0.f;
-      for (int r = 0; r < C; ++r) acc += cluster.map_shared_rank(part, r)[e * NT + t];
+      for (int r = 0; r < C; ++r) acc += recv[(r * tpc + j) * 128 + e];
       const uint16_t lb = f32_to_bf16(acc + bf16_to_f32(b[e]));
       if (out_logits) out_logits[(t0 + t) * experts + e] = lb;
       row[e] = bf16_to_f32(lb) + (adjust ? adjust[e] : 0.f);
@@ -335,7 +283,9 @@ __global__ void __launch_bounds__(256, 1)
     if (!failed) select_softmax_warp(row, experts, k, false, out_idx + (t0 + t) * k, out_w + (t0 + t) * k);
     __syncwarp();
   }
-  cluster.sync();  // no CTA leaves while its partials may still be read
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NT < 32 ? 32 : NT));
 }
 
@@ -366,32 +316,53 @@ int launch_router_tc(const uint16_t* x, int64_t tokens, int64_t hidden, const ui
   return KLC_OK;
 }
 
-// Router for large batches: one CTA per 128 tokens computes all E logits over the
-// whole hidden dimension on the tensor cores (tcgen05 kind::f16, M = 128 tokens,
-// N = E experts, K streamed through a TMA ring), so each TMEM lane holds one
-// token's logits and a thread selects that token's top-k alone.  The split-K
-// cluster form above serves small batches, where 128-token tiles would leave
-// most SMs idle.
+// Router for large batches: a tile of 128 tokens computes all E logits on the tensor
+// cores (tcgen05 kind::f16, M = 128 tokens, N = E experts, fp32 accumulators in
+// TMEM), the hidden dimension streamed through a TMA ring and split over a
+// thread-block cluster of C = 1, 2, 4 or 8 CTAs (as many as keep the SMs covered
+// once).  CTA r finishes tokens r, r + C, ... of the tile: once every CTA's MMAs are
+// done, each stores its partial logits of those tokens into that CTA's shared
+// memory (distributed shared memory stores; nobody waits on a remote load), and
+// after a cluster barrier one warp per token sums the C partials in rank order
+// (fixed, deterministic), adds the bias in fp32, rounds once to bf16 and runs the
+// warp-wide top-k + softmax.  The split-K cluster
+// form above, with tokens as N, serves small batches.
 constexpr int kRgStages = 4;
-constexpr int kRgThreads = 256;  // warp 0 TMA, warp 1 MMA, warps 4-7 epilogue
+constexpr int kRgThreads = 256;  // warp 0 TMA, warp 1 MMA, warps 4-7 TMEM -> shared; all 8 warps select
 
 template <int EP>  // experts padded to a multiple of 16 (the MMA's N)
+struct RgLayout {
+  static constexpr int XBOX = 128 * 128, WBOX = EP * 128;  // bytes of one 64-K box of each operand
+  static constexpr int RING = kRgStages * (XBOX + WBOX);
+  static constexpr int PS = EP + 4;                        // partial row stride (floats), 16-byte rows
+  static_assert(128 * PS * 4 <= RING, "partials fit in the drained ring");
+  static constexpr int ROWS = RING;                        // per-warp selection rows [8][EP] floats
+  static constexpr int BYTES = ROWS + 8 * EP * 4 + 1024;
+  static constexpr uint32_t TMEM_COLS = EP <= 32 ? 32 : (EP <= 64 ? 64 : (EP <= 128 ? 128 : 256));
+};
+
+template <int EP>
 __global__ void __launch_bounds__(kRgThreads, 1)
     router_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, int64_t tokens,
                        int64_t hidden, const uint16_t* __restrict__ b, int experts, int k, const float* __restrict__ adjust,
                        int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  namespace cg = cooperative_groups;
   using namespace tc;
-  constexpr int XBOX = 128 * 128, WBOX = EP * 128;  // bytes of one 64-K box of each operand
+  using Lay = RgLayout<EP>;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = int(cluster.num_blocks());
+  const int crank = int(cluster.block_rank());
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   unsigned char* xs = smem;
-  unsigned char* wsm = smem + kRgStages * XBOX;
+  unsigned char* wsm = smem + kRgStages * Lay::XBOX;
   __shared__ __align__(8) uint64_t bars[2 * kRgStages + 1];
   __shared__ uint32_t tmem_holder;
   __shared__ int abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t0 = int64_t(blockIdx.x) * 128;
+  const int64_t t0 = int64_t(blockIdx.x / C) * 128;
   const int nk = int(hidden / 64);
+  const int kb0 = int(int64_t(crank) * nk / C), kb1 = int(int64_t(crank + 1) * nk / C);  // this CTA's 64-K steps
   auto full = [&](int s) { return smem_u32(&bars[s]); };
   auto empty = [&](int s) { return smem_u32(&bars[kRgStages + s]); };
   const uint32_t done = smem_u32(&bars[2 * kRgStages]);
@@ -407,7 +378,7 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_holder)),
-                 "r"(EP <= 32 ? 32 : (EP <= 64 ? 64 : (EP <= 128 ? 128 : 256))));
+                 "r"(Lay::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -417,12 +388,12 @@ __global__ void __launch_bounds__(kRgThreads, 1)
   if (warp == 0 && lane == 0) {
     bool ok = true;
     uint32_t issued = 0;
-    for (int kc = 0; kc < nk && ok; ++kc) {
-      const int s = kc % kRgStages;
-      if (!(ok = wait_bar(empty(s), ((kc / kRgStages) & 1) ^ 1, ctl, 60))) break;
-      mbar_arrive_expect_tx(full(s), uint32_t(XBOX + WBOX));
-      tma_load_2d(smem_u32(xs + s * XBOX), &map_x, kc * 64, int(t0), full(s));
-      tma_load_2d(smem_u32(wsm + s * WBOX), &map_w, kc * 64, 0, full(s));
+    for (int kc = kb0; kc < kb1 && ok; ++kc) {
+      const int i = kc - kb0, s = i % kRgStages;
+      if (!(ok = wait_bar(empty(s), ((i / kRgStages) & 1) ^ 1, ctl, 60))) break;
+      mbar_arrive_expect_tx(full(s), uint32_t(Lay::XBOX + Lay::WBOX));
+      tma_load_2d(smem_u32(xs + s * Lay::XBOX), &map_x, kc * 64, int(t0), full(s));
+      tma_load_2d(smem_u32(wsm + s * Lay::WBOX), &map_w, kc * 64, 0, full(s));
       ++issued;
     }
     if (!ok) drain_ring(full(0), kRgStages, issued);
@@ -430,14 +401,14 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     // kind::f16: bf16 A (tokens) and B (router rows), fp32 accumulate, K-major, M = 128, N = EP
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(EP >> 3) << 17) | (uint32_t(128 >> 4) << 24);
     bool ok = true;
-    for (int kc = 0; kc < nk && ok; ++kc) {
-      const int s = kc % kRgStages;
-      if (!(ok = wait_bar(full(s), (kc / kRgStages) & 1, ctl, 61))) break;
+    for (int kc = kb0; kc < kb1 && ok; ++kc) {
+      const int i = kc - kb0, s = i % kRgStages;
+      if (!(ok = wait_bar(full(s), (i / kRgStages) & 1, ctl, 61))) break;
       tc_fence_after();
-      const uint64_t ad = sw128_desc(smem_u32(xs + s * XBOX)), bd = sw128_desc(smem_u32(wsm + s * WBOX));
+      const uint64_t ad = sw128_desc(smem_u32(xs + s * Lay::XBOX)), bd = sw128_desc(smem_u32(wsm + s * Lay::WBOX));
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const uint32_t acc = (kc | kk) ? 1u : 0u;
+        const uint32_t acc = (i | kk) ? 1u : 0u;
         asm volatile(
             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
@@ -446,99 +417,152 @@ __global__ void __launch_bounds__(kRgThreads, 1)
       tc_commit(empty(s));
     }
     tc_commit(done);
-  } else if (warp >= 4) {
-    // one thread per token: its logits from its TMEM lane, bias, one bf16 rounding,
-    // top-k (value descending, lower index first) and the softmax of the selected
-    const int q = warp & 3;
-    const int tl = q * 32 + lane;
-    const int64_t t = t0 + tl;
-    bool ok = wait_bar_backoff(done, 0, ctl, 62);
-    tc_fence_after();
-    float sv[kMaxK];
-    int si[kMaxK];
-#pragma unroll
-    for (int r = 0; r < kMaxK; ++r) {
-      sv[r] = -INFINITY;
-      si[r] = -1;
-    }
-    for (int c0 = 0; c0 < EP; c0 += 16) {
-      uint32_t raw[16];
-      tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), raw);
-      tmem_wait_ld();
-      uint32_t packed[8];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int e = c0 + j;
-        uint16_t lb = 0;
-        if (e < experts) {
-          lb = f32_to_bf16(__uint_as_float(raw[j]) + bf16_to_f32(b[e]));
-          const float v = bf16_to_f32(lb) + (adjust ? adjust[e] : 0.f);
-          if (v == v) {  // NaN only fills slots nothing else takes (below)
-            // insertion into the selection kept in (value descending, index ascending) order;
-            // an element pushed down by the insertion keeps that order against equal values too
-            float cv = v;
-            int ci = e;
-#pragma unroll
-            for (int r = 0; r < kMaxK; ++r) {
-              if (r < k && ci >= 0 && (si[r] < 0 || cv > sv[r] || (cv == sv[r] && ci < si[r]))) {
-                const float tv = sv[r];
-                const int ti = si[r];
-                sv[r] = cv;
-                si[r] = ci;
-                cv = tv;
-                ci = ti;
+  }
+  if (C == 1) {
+    if (warp >= 4) {
+      // one thread per token: its logits from its TMEM lane, bias, one bf16 rounding,
+      // top-k (value descending, lower index first) and the softmax of the selected
+      const int q = warp & 3;
+      const int tl = q * 32 + lane;
+      const int64_t t = t0 + tl;
+      bool ok = wait_bar_backoff(done, 0, ctl, 62);
+      tc_fence_after();
+      float sv[kMaxK];
+      int si[kMaxK];
+  #pragma unroll
+      for (int r = 0; r < kMaxK; ++r) {
+        sv[r] = -INFINITY;
+        si[r] = -1;
+      }
+      for (int c0 = 0; c0 < EP; c0 += 16) {
+        uint32_t raw[16];
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), raw);
+        tmem_wait_ld();
+        uint32_t packed[8];
+  #pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int e = c0 + j;
+          uint16_t lb = 0;
+          if (e < experts) {
+            lb = f32_to_bf16(__uint_as_float(raw[j]) + bf16_to_f32(b[e]));
+            const float v = bf16_to_f32(lb) + (adjust ? adjust[e] : 0.f);
+            if (v == v) {  // NaN only fills slots nothing else takes (below)
+              // insertion into the selection kept in (value descending, index ascending) order;
+              // an element pushed down by the insertion keeps that order against equal values too
+              float cv = v;
+              int ci = e;
+  #pragma unroll
+              for (int r = 0; r < kMaxK; ++r) {
+                if (r < k && ci >= 0 && (si[r] < 0 || cv > sv[r] || (cv == sv[r] && ci < si[r]))) {
+                  const float tv = sv[r];
+                  const int ti = si[r];
+                  sv[r] = cv;
+                  si[r] = ci;
+                  cv = tv;
+                  ci = ti;
+                }
               }
             }
           }
+          if (j & 1) packed[j >> 1] |= uint32_t(lb) << 16;
+          else packed[j >> 1] = lb;
         }
-        if (j & 1) packed[j >> 1] |= uint32_t(lb) << 16;
-        else packed[j >> 1] = lb;
-      }
-      // 16-byte stores when the row and chunk start are 16-byte aligned (E a multiple of 8)
-      if (out_logits != nullptr && t < tokens && c0 + 16 <= experts && (experts & 7) == 0 &&
-          (reinterpret_cast<uintptr_t>(out_logits) & 15) == 0) {
-        uint4* dst = reinterpret_cast<uint4*>(out_logits + t * experts + c0);
-        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-      } else if (out_logits != nullptr && t < tokens) {
-        for (int j = 0; j < 16 && c0 + j < experts; ++j)
-          out_logits[t * experts + c0 + j] = uint16_t((j & 1) ? (packed[j >> 1] >> 16) : (packed[j >> 1] & 0xFFFFu));
-      }
-    }
-    // slots still empty: the lowest-index experts not taken (their scores NaN)
-    for (int r = 0; r < k; ++r) {
-      if (si[r] >= 0) continue;
-      for (int e = 0; e < experts; ++e) {
-        bool taken = false;
-        for (int qq = 0; qq < r; ++qq) taken |= (si[qq] == e);
-        if (!taken) {
-          si[r] = e;
-          sv[r] = __uint_as_float(0x7fc00000u);
-          break;
+        // 16-byte stores when the row and chunk start are 16-byte aligned (E a multiple of 8)
+        if (out_logits != nullptr && t < tokens && c0 + 16 <= experts && (experts & 7) == 0 &&
+            (reinterpret_cast<uintptr_t>(out_logits) & 15) == 0) {
+          uint4* dst = reinterpret_cast<uint4*>(out_logits + t * experts + c0);
+          dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+        } else if (out_logits != nullptr && t < tokens) {
+          for (int j = 0; j < 16 && c0 + j < experts; ++j)
+            out_logits[t * experts + c0 + j] = uint16_t((j & 1) ? (packed[j >> 1] >> 16) : (packed[j >> 1] & 0xFFFFu));
         }
       }
+      // slots still empty: the lowest-index experts not taken (their scores NaN)
+      for (int r = 0; r < k; ++r) {
+        if (si[r] >= 0) continue;
+        for (int e = 0; e < experts; ++e) {
+          bool taken = false;
+          for (int qq = 0; qq < r; ++qq) taken |= (si[qq] == e);
+          if (!taken) {
+            si[r] = e;
+            sv[r] = __uint_as_float(0x7fc00000u);
+            break;
+          }
+        }
+      }
+      if (ok && t < tokens) {
+        float m = sv[0];
+        for (int r = 1; r < k; ++r) m = fmaxf(m, sv[r]);
+        float ex[kMaxK];
+        float sum = 0.f;
+        for (int r = 0; r < k; ++r) {
+          ex[r] = expf(sv[r] - m);
+          sum += ex[r];
+        }
+        for (int r = 0; r < k; ++r) {
+          out_idx[t * k + r] = si[r];
+          out_w[t * k + r] = f32_to_bf16(ex[r] / sum);
+        }
+      }
     }
-    if (ok && t < tokens) {
-      float m = sv[0];
-      for (int r = 1; r < k; ++r) m = fmaxf(m, sv[r]);
-      float ex[kMaxK];
-      float sum = 0.f;
-      for (int r = 0; r < k; ++r) {
-        ex[r] = expf(sv[r] - m);
-        sum += ex[r];
+  } else {
+    // every CTA's MMAs done (the ring may then take partial sums from the cluster)
+    const bool ok_done = warp < 4 ? true : wait_bar_backoff(done, 0, ctl, 62);
+    (void)ok_done;
+    __syncwarp();
+    tc_fence_before();
+    cluster.sync();
+    tc_fence_after();
+    // TMEM lane = token tl: its EP partial logits go to the CTA that finishes the token
+    // (tl % C), into slot (this rank, tl / C) of that CTA's shared memory: remote stores,
+    // local reads
+    constexpr int kTokPer = 128;  // tokens of a tile; CTA r finishes tokens r, r + C, ...
+    float* recv = reinterpret_cast<float*>(smem);
+    if (warp >= 4) {
+      const int q = warp & 3;
+      const int tl = q * 32 + lane;
+      const int owner = tl % C;
+      float* dst_base = C == 1 ? recv : cluster.map_shared_rank(recv, owner);
+      float* dst = dst_base + (crank * (kTokPer / C) + tl / C) * Lay::PS;
+      for (int c0 = 0; c0 < EP; c0 += 16) {
+        uint32_t raw[16];
+        tmem_ld16(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), raw);
+        tmem_wait_ld();
+  #pragma unroll
+        for (int j = 0; j < 16; j += 4)
+          *reinterpret_cast<float4*>(dst + c0 + j) =
+              make_float4(__uint_as_float(raw[j]), __uint_as_float(raw[j + 1]), __uint_as_float(raw[j + 2]), __uint_as_float(raw[j + 3]));
       }
-      for (int r = 0; r < k; ++r) {
-        out_idx[t * k + r] = si[r];
-        out_w[t * k + r] = f32_to_bf16(ex[r] / sum);
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster.sync();
+    const bool failed = abort_flag != 0;
+
+    // local token j = tile token crank + C*j: the C partials summed in rank order, bias,
+    // one bf16 rounding, locality adjustment, then top-k + softmax (one warp per token)
+    float* row = reinterpret_cast<float*>(smem + Lay::ROWS) + warp * EP;
+    for (int j = warp; j < kTokPer / C; j += kRgThreads / 32) {
+      const int t = crank + C * j;
+      const int64_t tg = t0 + t;
+      if (tg >= tokens) break;
+      for (int e = lane; e < experts; e += 32) {
+        float acc = 0.f;
+        for (int r = 0; r < C; ++r) acc += recv[(r * (kTokPer / C) + j) * Lay::PS + e];
+        const uint16_t lb = f32_to_bf16(acc + bf16_to_f32(b[e]));
+        if (out_logits) out_logits[tg * experts + e] = lb;
+        row[e] = bf16_to_f32(lb) + (adjust ? adjust[e] : 0.f);
       }
+      __syncwarp();
+      if (!failed) select_softmax_warp(row, experts, k, false, out_idx + tg * k, out_w + tg * k);
+      __syncwarp();
     }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // TMEM is freed once every warp is past its loads
   tc_fence_after();
-  if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(EP <= 32 ? 32 : (EP <= 64 ? 64 : (EP <= 128 ? 128 : 256))));
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(Lay::TMEM_COLS));
 }
 
 __global__ void select_kernel(const float* __restrict__ scores, int64_t tokens, int experts, int k, int keep_order,
@@ -554,12 +578,32 @@ template <int EP>
 int launch_router_gemm_ep(const CUtensorMap& mx, const CUtensorMap& mw, int64_t tokens, int64_t hidden, const uint16_t* b,
                           int experts, int k, const float* adjust, int32_t* out_idx, uint16_t* out_w, uint16_t* out_logits,
                           cudaStream_t stream) {
-  const int smem = kRgStages * (128 * 128 + EP * 128) + 1024;
+  const int smem = RgLayout<EP>::BYTES;
   KLC_CUDA(cudaFuncSetAttribute(router_gemm_kernel<EP>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int64_t grid = (tokens + 127) / 128;
-  KLC_CHECK_ARG(grid <= 0x7fffffff, "klc_router_topk: too many tokens");
-  router_gemm_kernel<EP><<<unsigned(grid), kRgThreads, smem, stream>>>(mx, mw, tokens, hidden, b, experts, k, adjust, out_idx,
-                                                                       out_w, out_logits);
+  const int64_t tiles = (tokens + 127) / 128;
+  const int nk = int(hidden / 64);
+  // split the hidden dimension over a cluster while the CTAs still run in one wave (one
+  // CTA per SM; B200 holds at most 15 clusters of 8 such CTAs at once)
+  const int64_t sms = sm_count();
+  int C = 1;
+  if (tiles * 8 <= 15 * 8 && tiles * 8 <= sms && nk >= 8) C = 8;
+  else if (tiles * 4 <= sms && nk >= 4) C = 4;
+  else if (tiles * 2 <= sms && nk >= 2) C = 2;
+  KLC_CHECK_ARG(tiles * C <= 0x7fffffff, "klc_router_topk: too many tokens");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(unsigned(tiles * C));
+  cfg.blockDim = dim3(kRgThreads);
+  cfg.dynamicSmemBytes = size_t(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = unsigned(C);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  KLC_CUDA(cudaLaunchKernelEx(&cfg, router_gemm_kernel<EP>, mx, mw, tokens, hidden, b, experts, k, adjust, out_idx, out_w,
+                              out_logits));
   KLC_LAUNCH_CHECK("klc_router_topk launch");
   return KLC_OK;
 }
@@ -576,10 +620,13 @@ int launch_router_gemm(const uint16_t* x, int64_t tokens, int64_t hidden, const 
     int st = tc::make_map(&mx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != KLC_OK) return st;
   }
+  // the router-row box spans the kernel's padded expert count (rows past E read as zeros),
+  // so every stage's transaction is XBOX + WBOX bytes
+  const int ep_t = ep <= 64 ? 64 : (ep <= 128 ? 128 : 256);
   {
     const uint64_t dims[2] = {uint64_t(hidden), uint64_t(experts)};
     const uint64_t strides[1] = {uint64_t(hidden) * 2};
-    const uint32_t box[2] = {64, uint32_t(ep)};
+    const uint32_t box[2] = {64, uint32_t(ep_t)};
     int st = tc::make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != KLC_OK) return st;
   }

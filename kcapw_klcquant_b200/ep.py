@@ -193,13 +193,42 @@ class ExpertParallelMoe:
             self._ep.close()
             self._ep = None
 
+    def next_router_args(self, T: int) -> tuple:
+        """This layer's (replicated) router as the previous layer's fused ``next_router``:
+        (klc_next_router, idx, w)."""
+        be = self.backend
+        dev = be.device
+        nidx = torch.empty((T, self.top_k), dtype=torch.int32, device=dev)
+        nw = torch.empty((T, self.top_k), dtype=torch.bfloat16, device=dev)
+        nr = _lib.KlcNextRouter(be.router_w.data_ptr(), be.router_b.data_ptr(), int(be.router_w.shape[0]), self.top_k,
+                                nidx.data_ptr(), nw.data_ptr(), None)
+        return nr, nidx, nw
+
+    def step_routed(self, x: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor, residual: torch.Tensor,
+                    next_norm: tuple[torch.Tensor, float] | None, next_router=None, precision: str = "bf16"):
+        """One stacked layer on routing the previous layer computed (p2p exchange):
+        dispatch, local experts, combine + residual + the next layer's input RMSNorm
+        and, with ``next_router``, its routing of the normalised rows -> (y, RouteBatch)."""
+        if self._ep is None:
+            raise ValueError("step_routed needs the p2p exchange")
+        return self._ep.forward_routed(x, indices, weights, precision, residual, next_norm, next_router)
+
     def forward(self, x: torch.Tensor, precision: str = "bf16", residual: torch.Tensor | None = None,
-                next_norm: tuple[torch.Tensor, float] | None = None):
+                next_norm: tuple[torch.Tensor, float] | None = None, next_router=None):
         """This rank's tokens x bf16 [T, H] -> (y bf16 [T, H], routing); with
         ``next_norm=(weight, eps)`` returns (y, routing, rms_norm(y)) computed by
-        the combine kernel (p2p exchange)."""
+        the combine kernel (p2p exchange); ``next_router`` (with next_norm) also
+        routes rms_norm(y) for the next layer (``routing.next_indices``)."""
         if self._ep is not None:
+            if next_router is not None:
+                if next_norm is None:
+                    raise ValueError("next_router needs next_norm")
+                idx, w = self.backend.router(as_bf16(x, self.backend.device))
+                y, rb = self._ep.forward_routed(x, idx, w, precision, residual, next_norm, next_router)
+                return y, rb, rb.normed
             return self._ep.forward(x, precision, residual, next_norm)
+        if next_router is not None:
+            raise ValueError("next_router needs the p2p exchange")
         if next_norm is not None:
             raise ValueError("next_norm needs the p2p exchange")
         be = self.backend
@@ -280,6 +309,44 @@ class PeerExchange:
         if next_norm is not None:
             return out, RouteBatch(idx, w, normed=normed), normed
         return out, RouteBatch(idx, w)
+
+    def set_fused_return(self, enabled: bool) -> None:
+        """Expert output rows stored to their sources by the down GEMM's epilogue (default) or by a copy kernel."""
+        _lib.check(_lib.lib().klc_ep_set_fused_return(self.handle, 1 if enabled else 0))
+
+    def forward_routed(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, precision: str, residual, next_norm,
+                       next_router=None):
+        """klc_ep_dispatch -> klc_ep_experts -> klc_ep_combine(_route) on given routing."""
+        T, H = int(x.shape[0]), int(x.shape[1])
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the exchange capacity of {self.max_tokens} tokens per rank")
+        dev = self.device
+        x = as_bf16(x, dev)
+        idx = idx.to(device=dev, dtype=torch.int32).contiguous()
+        w = w.to(device=dev, dtype=torch.bfloat16).contiguous()
+        residual = as_bf16(residual, dev) if residual is not None else None
+        if next_norm is None and next_router is not None:
+            raise ValueError("next_router needs next_norm")
+        norm_w, eps = (as_bf16(next_norm[0], dev), float(next_norm[1])) if next_norm is not None else (None, 0.0)
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        normed = torch.empty_like(out) if next_norm is not None else None
+        slot = torch.empty((T * self.top_k,), dtype=torch.int32, device=dev)
+        L = _lib.lib()
+        s = _lib.stream_ptr(dev)
+        nidx = nw = None
+        with torch.cuda.device(dev):
+            _lib.check(L.klc_ep_dispatch(self.handle, idx.data_ptr(), T, x.data_ptr(), slot.data_ptr(), self.ws.data_ptr(),
+                                         self.ws.numel(), s))
+            _lib.check(L.klc_ep_experts(self.handle, ctypes.byref(self.dims), ctypes.byref(self.local.weights),
+                                        _lib.PRECISION_CODE[precision], self.ws.data_ptr(), self.ws.numel(), s))
+            if next_router is not None:
+                nr, nidx, nw = next_router.next_router_args(T)
+                _lib.check(L.klc_ep_combine_route(self.handle, slot.data_ptr(), w.data_ptr(), T, _lib.ptr(residual),
+                                                  norm_w.data_ptr(), eps, out.data_ptr(), normed.data_ptr(), ctypes.byref(nr), s))
+            else:
+                _lib.check(L.klc_ep_combine(self.handle, slot.data_ptr(), w.data_ptr(), T, _lib.ptr(residual), _lib.ptr(norm_w),
+                                            eps, out.data_ptr(), _lib.ptr(normed), s))
+        return out, RouteBatch(idx, w, normed=normed, next_indices=nidx, next_weights=nw)
 
     def received_rows(self) -> int:
         n = ctypes.c_int64(0)

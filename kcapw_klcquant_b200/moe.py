@@ -59,6 +59,8 @@ class RouteBatch:
     logits: torch.Tensor | None = None
     norms: torch.Tensor | None = None  # fp32 [T,k,2]: (||gated||, ||out||) per selected expert
     normed: torch.Tensor | None = None  # bf16 [T,H]: the next layer's input RMSNorm of the output (next_norm)
+    next_indices: torch.Tensor | None = None  # int32 [T,k']: the next layer's routing of ``normed`` (next_router)
+    next_weights: torch.Tensor | None = None  # bf16 [T,k']
 
 
 class MoeLayer:
@@ -147,6 +149,7 @@ class MoeLayer:
         out: torch.Tensor | None = None,
         path: str | None = None,
         next_norm: tuple[torch.Tensor, float] | None = None,
+        next_router: "MoeLayer | None" = None,
     ) -> tuple[torch.Tensor, RouteBatch]:
         """Router + experts + combine for ``x`` bf16 [T, H] -> (y bf16 [T, H], routing).
 
@@ -154,7 +157,9 @@ class MoeLayer:
         ``rms_norm(y, weight, eps)`` -- the executor's ``hidden += moe_out``
         followed by the next layer's input norm
         (streamed_transformer_executor.py:235,260) -- computed by the combine
-        kernel itself.
+        kernel itself.  ``next_router`` (the next layer, with ``next_norm``)
+        routes ``normed`` for it as well (``routing.next_indices`` /
+        ``next_weights``), inside the combine kernel for decode batches.
         """
         T = int(x.shape[0])
         x = as_bf16(x, self.device)
@@ -188,15 +193,39 @@ class MoeLayer:
                 if norm_w.numel() != self.hidden:
                     raise ValueError(f"next_norm weight must have {self.hidden} elements")
                 normed = torch.empty_like(y)
-                _lib.check(
-                    _lib.lib().klc_moe_forward_rmsnorm(
-                        ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
-                        _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
-                        _lib.ptr(norms), _lib.ptr(residual), norm_w.data_ptr(), float(next_norm[1]), normed.data_ptr(),
-                        ws.data_ptr(), ws.numel(), stream,
+                if next_router is None:
+                    _lib.check(
+                        _lib.lib().klc_moe_forward_rmsnorm(
+                            ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
+                            _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
+                            _lib.ptr(norms), _lib.ptr(residual), norm_w.data_ptr(), float(next_norm[1]), normed.data_ptr(),
+                            ws.data_ptr(), ws.numel(), stream,
+                        )
                     )
-                )
+                else:
+                    nr, nidx, nw = next_router.next_router_args(T)
+                    _lib.check(
+                        _lib.lib().klc_moe_forward_rmsnorm_route(
+                            ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), _lib.ptr(adjust),
+                            _lib.PRECISION_CODE[precision], y.data_ptr(), idx.data_ptr(), w.data_ptr(), _lib.ptr(logits),
+                            _lib.ptr(norms), _lib.ptr(residual), norm_w.data_ptr(), float(next_norm[1]), normed.data_ptr(),
+                            ctypes.byref(nr), ws.data_ptr(), ws.numel(), stream,
+                        )
+                    )
+                    return y, RouteBatch(idx, w, logits, norms, normed, nidx, nw)
+        if next_router is not None:
+            raise ValueError("next_router needs next_norm")
         return y, RouteBatch(idx, w, logits, norms, normed)
+
+    def next_router_args(self, T: int) -> tuple:
+        """This layer's router as the previous layer's fused ``next_router``: (klc_next_router, idx, w)."""
+        if self.router_weight.device != self.device:
+            raise ValueError("router on another device")
+        nidx = torch.empty((T, self.top_k), dtype=torch.int32, device=self.device)
+        nw = torch.empty((T, self.top_k), dtype=torch.bfloat16, device=self.device)
+        nr = _lib.KlcNextRouter(self.router_weight.data_ptr(), self.router_bias.data_ptr(), self.experts, self.top_k,
+                                nidx.data_ptr(), nw.data_ptr(), None)
+        return nr, nidx, nw
 
     def experts_forward(
         self,
@@ -233,6 +262,50 @@ class MoeLayer:
                 )
             )
         return y, norms
+
+    def experts_step(
+        self,
+        x: torch.Tensor,
+        indices: torch.Tensor,
+        weights: torch.Tensor,
+        residual: torch.Tensor,
+        next_norm: tuple[torch.Tensor, float],
+        next_router: "MoeLayer | None" = None,
+        precision: str = "bf16",
+    ) -> tuple[torch.Tensor, RouteBatch]:
+        """One stacked layer on routing computed by the previous layer: experts + combine +
+        residual + the next layer's input RMSNorm (``routing.normed``) and, with
+        ``next_router``, the next layer's routing of it (``routing.next_indices`` /
+        ``next_weights``), all fused into the combine (klc_moe_experts_rmsnorm_route)."""
+        T = int(x.shape[0])
+        x = as_bf16(x, self.device)
+        idx = indices.to(device=self.device, dtype=torch.int32).contiguous()
+        w = weights.to(device=self.device, dtype=torch.bfloat16).contiguous()
+        if idx.shape != (T, self.top_k) or w.shape != (T, self.top_k):
+            raise ValueError(f"routing must be [{T},{self.top_k}]")
+        residual = as_bf16(residual, self.device)
+        norm_w = as_bf16(next_norm[0], self.device)
+        dims = self.dims(T, None)
+        y = torch.empty((T, self.hidden), dtype=torch.bfloat16, device=self.device)
+        normed = torch.empty_like(y)
+        nbytes = self.workspace_bytes(T, None)
+        stream = _lib.stream_ptr(self.device)
+        ws = workspace(self.device, nbytes, stream)
+        self._last.ws, self._last.stream = ws, stream
+        with torch.cuda.device(self.device):
+            if next_router is None:
+                _lib.check(_lib.lib().klc_moe_experts(
+                    ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), idx.data_ptr(), w.data_ptr(),
+                    _lib.PRECISION_CODE[precision], y.data_ptr(), None, residual.data_ptr(), ws.data_ptr(), ws.numel(), stream))
+                _lib.check(_lib.lib().klc_rms_norm(y.data_ptr(), norm_w.data_ptr(), T, self.hidden, float(next_norm[1]),
+                                                   normed.data_ptr(), stream))
+                return y, RouteBatch(idx, w, normed=normed)
+            nr, nidx, nw = next_router.next_router_args(T)
+            _lib.check(_lib.lib().klc_moe_experts_rmsnorm_route(
+                ctypes.byref(dims), ctypes.byref(self.weights), x.data_ptr(), idx.data_ptr(), w.data_ptr(),
+                _lib.PRECISION_CODE[precision], y.data_ptr(), None, residual.data_ptr(), norm_w.data_ptr(), float(next_norm[1]),
+                normed.data_ptr(), ctypes.byref(nr), ws.data_ptr(), ws.numel(), stream))
+        return y, RouteBatch(idx, w, normed=normed, next_indices=nidx, next_weights=nw)
 
     def check_device_status(self) -> None:
         """Raise if a kernel of this thread's last call recorded a device-side fault.

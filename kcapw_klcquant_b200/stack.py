@@ -11,8 +11,10 @@ layer loop over many layers and a whole batch of tokens at once:
         hidden = hidden + moe_L(normed)             # the combine adds the residual
         normed = rms_norm(hidden, norm[L + 1])      # ... and normalises for layer L+1
 
-with the residual add and the next layer's norm fused into each layer's combine
-kernel, so a layer is one MoE call.  Layers are :class:`MoeLayer` (one GPU) or
+with the residual add, the next layer's norm and (``fuse_router``, the
+default) the next layer's router fused into each layer's combine kernel, so a
+layer after the first is one experts-and-combine call on routing its
+predecessor already computed.  Layers are :class:`MoeLayer` (one GPU) or
 :class:`ExpertParallelMoe` with the peer-memory exchange (experts sharded over
 the GPUs of a node); both are free of host synchronisation, so
 :meth:`MoeStack.capture` records a whole decode step of all layers as one CUDA
@@ -28,7 +30,8 @@ from .moe import MoeLayer, as_bf16, rms_norm
 class MoeStack:
     """MoE layers with RMSNorm weights ``norm_weights[L]`` (bf16 [H]) applied to each layer's input."""
 
-    def __init__(self, layers: list, norm_weights: list[torch.Tensor], eps: float = 1e-5, precision: str = "bf16"):
+    def __init__(self, layers: list, norm_weights: list[torch.Tensor], eps: float = 1e-5, precision: str = "bf16",
+                 fuse_router: bool = True):
         if len(norm_weights) != len(layers):
             raise ValueError("one RMSNorm weight per layer")
         self.layers = list(layers)
@@ -36,6 +39,7 @@ class MoeStack:
         self.norm_weights = [as_bf16(w, dev) for w in norm_weights]
         self.eps = float(eps)
         self.precision = precision
+        self.fuse_router = bool(fuse_router)
         self._graph = None
         self._static_in = None
         self._static_out = None
@@ -48,15 +52,31 @@ class MoeStack:
         """One pass of this rank's tokens bf16 [T, H] through every layer."""
         normed = rms_norm(hidden, self.norm_weights[0], self.eps)
         n = len(self.layers)
+        idx = w = None  # routing of this layer, when the previous layer's combine computed it
         for li, layer in enumerate(self.layers):
-            nxt = (self.norm_weights[li + 1], self.eps) if li + 1 < n else None
-            if isinstance(layer, MoeLayer):
-                y, rb = layer.forward(normed, precision=self.precision, residual=hidden, next_norm=nxt)
-                normed = rb.normed
-            elif nxt is not None:
-                y, _, normed = layer.forward(normed, precision=self.precision, residual=hidden, next_norm=nxt)
+            last = li + 1 == n
+            nxt = None if last else (self.norm_weights[li + 1], self.eps)
+            nrouter = None if (last or not self.fuse_router) else self.layers[li + 1]
+            ep = not isinstance(layer, MoeLayer)
+            if idx is None:
+                if last:
+                    y, _ = layer.forward(normed, precision=self.precision, residual=hidden)
+                elif not ep:
+                    y, rb = layer.forward(normed, precision=self.precision, residual=hidden, next_norm=nxt, next_router=nrouter)
+                    normed, idx, w = rb.normed, rb.next_indices, rb.next_weights
+                else:
+                    y, rb, normed = layer.forward(normed, precision=self.precision, residual=hidden, next_norm=nxt,
+                                                  next_router=nrouter)
+                    idx, w = rb.next_indices, rb.next_weights
+            elif last:
+                if ep:
+                    y, _ = layer.step_routed(normed, idx, w, hidden, None, None, self.precision)
+                else:
+                    y, _ = layer.experts_forward(normed, idx, w, precision=self.precision, residual=hidden)
             else:
-                y, _ = layer.forward(normed, precision=self.precision, residual=hidden)
+                y, rb = (layer.step_routed(normed, idx, w, hidden, nxt, nrouter, self.precision) if ep
+                         else layer.experts_step(normed, idx, w, hidden, nxt, nrouter, self.precision))
+                normed, idx, w = rb.normed, rb.next_indices, rb.next_weights
             hidden = y
         return hidden
 

@@ -23,7 +23,9 @@ from dataclasses import dataclass, field
 import torch
 
 from . import _lib
-from .moe import MoeLayer, RouteBatch, as_bf16, workspace
+import ctypes
+
+from .moe import MoeLayer, RouteBatch, as_bf16, rms_norm, workspace
 from .mxfp4_expert import Mxfp4ExpertStore
 
 
@@ -207,7 +209,7 @@ class StreamedMoERouter:
     """MoE block with the reference's API (streamed_moe_router.py:238-529), executed by libklcmoe."""
 
     def __init__(self, experts_per_token: int = 4, swiglu_limit: float = 7.0, locality_config: RoutingLocalityConfig | None = None,
-                 matmul_precision: str = "fp32", expert_path: str = "auto") -> None:
+                 matmul_precision: str = "fp32", expert_path: str = "auto", locality_on_device: bool = True) -> None:
         if matmul_precision not in _lib.PRECISION_CODE:
             raise ValueError(f"matmul_precision must be one of {sorted(_lib.PRECISION_CODE)}")
         self.experts_per_token = experts_per_token
@@ -225,6 +227,10 @@ class StreamedMoERouter:
         self.recent_history: dict[int, deque[int]] = {}
         self.dynamic_caps: dict[int, int] = {}
         self._layers: dict[tuple, MoeLayer] = {}
+        # locality policy on the GPU (klc_locality_route): per-layer state buffers on the device; the
+        # host dicts above are then rebuilt from them only when predict_experts() is called
+        self.locality_on_device = bool(locality_on_device)
+        self._loc_states: dict[int, torch.Tensor] = {}
 
     @property
     def stats(self) -> RouterStats:
@@ -235,11 +241,18 @@ class StreamedMoERouter:
 
     def _flush_pending(self) -> None:
         while self._pending:
-            done, layer_idx, position, k, ids_h, ws_h = self._pending.pop(0)
+            done, layer_idx, position, k, ids_h, ws_h, loc = self._pending.pop(0)
             done.synchronize()
             ids, ws = ids_h.tolist(), ws_h.float().tolist()
+            if loc is None:
+                for t, (e, w) in enumerate(zip(ids, ws)):
+                    self._stats.record_route(layer_idx, position + t, e, w, e, False, active_cap=k)
+                continue
+            raw_h, pred_h, npred_h, flags_h, resident = loc
+            raws, preds, npreds, flags = raw_h.tolist(), pred_h.tolist(), npred_h.tolist(), flags_h.tolist()
             for t, (e, w) in enumerate(zip(ids, ws)):
-                self._stats.record_route(layer_idx, position + t, e, w, e, False, active_cap=k)
+                self._stats.record_route(layer_idx, position + t, e, w, raws[t], e != raws[t], predicted_experts=preds[t][: npreds[t]],
+                                         resident_experts=resident, active_cap=k, blocked_adjustment=bool(flags[t] & 1))
 
     # ------------------------------------------------------------------
     # device layer cache
@@ -279,19 +292,35 @@ class StreamedMoERouter:
         with torch.cuda.device(dev):
             _lib.check(_lib.lib().klc_router_topk(x.data_ptr(), 1, H, w_dev.data_ptr(), b_dev.data_ptr(), E, k, None,
                                                   idx.data_ptr(), wts.data_ptr(), logits.data_ptr(), _lib.stream_ptr()))
-        raw_experts = [int(v) for v in idx[0].tolist()]
         blocked = False
-        if cfg.enabled:
-            raw_experts, experts, scores, blocked = self._locality_select(layer_idx, logits[0].float().cpu(), k, resident_experts or set())
-            sc = torch.tensor(scores, dtype=torch.float32, device=dev).reshape(1, k)
-            idx = torch.tensor([experts], dtype=torch.int32, device=dev)
-            with torch.cuda.device(dev):
-                _lib.check(_lib.lib().klc_select_softmax(sc.data_ptr(), 1, k, k, 1, None, wts.data_ptr(), _lib.stream_ptr()))
+        update_state = True
+        if cfg.enabled and self.locality_on_device:
+            # the whole policy on the device: one readback of the token's decisions
+            pol = self._device_policy(layer_idx, logits, k, self._resident_mask(resident_experts, E, dev), 0)
+            idx, wts = pol["experts"], pol["weights"]
+            host = torch.cat([pol["experts"].reshape(-1).double(), pol["raw"].reshape(-1).double(), pol["pred"].reshape(-1).double(),
+                              pol["npred"].double(), pol["flags"].double(), pol["weights"].reshape(-1).double()]).cpu().tolist()
+            experts = [int(v) for v in host[:k]]
+            raw_experts = [int(v) for v in host[k:2 * k]]
+            npred = int(host[3 * k])
+            if predicted_experts is None:
+                predicted_experts = [int(v) for v in host[2 * k:2 * k + npred]]
+            blocked = bool(int(host[3 * k + 1]) & 1)
+            weights_list = [float(v) for v in host[3 * k + 2:]]
+            update_state = False  # the kernel already advanced the layer's policy state
         else:
-            experts = raw_experts
-        weights_list = [float(v) for v in wts[0].float().tolist()]
+            raw_experts = [int(v) for v in idx[0].tolist()]
+            if cfg.enabled:
+                raw_experts, experts, scores, blocked = self._locality_select(layer_idx, logits[0].float().cpu(), k, resident_experts or set())
+                sc = torch.tensor(scores, dtype=torch.float32, device=dev).reshape(1, k)
+                idx = torch.tensor([experts], dtype=torch.int32, device=dev)
+                with torch.cuda.device(dev):
+                    _lib.check(_lib.lib().klc_select_softmax(sc.data_ptr(), 1, k, k, 1, None, wts.data_ptr(), _lib.stream_ptr()))
+            else:
+                experts = raw_experts
+            weights_list = [float(v) for v in wts[0].float().tolist()]
         predicted, resident, adjusted_flag = self._record_route(layer_idx, position, experts, weights_list, raw_experts, blocked,
-                                                                predicted_experts, resident_experts, k)
+                                                                predicted_experts, resident_experts, k, update_state)
 
         if execute_experts and expert_store is not None:
             before = self._cache_snapshot(expert_store)
@@ -344,34 +373,63 @@ class StreamedMoERouter:
     def route_batch(self, layer_idx: int, hidden: torch.Tensor, tensors: dict[str, torch.Tensor], expert_store: Mxfp4ExpertStore,
                     *, return_logits: bool = False, return_norms: bool = False, residual: torch.Tensor | None = None,
                     record_stats: bool = False, position: int = 0,
-                    next_norm: tuple[torch.Tensor, float] | None = None) -> tuple[torch.Tensor, RouteBatch]:
+                    next_norm: tuple[torch.Tensor, float] | None = None,
+                    resident_experts: set[int] | None = None) -> tuple[torch.Tensor, RouteBatch]:
         """Route and execute T tokens at once: hidden bf16 [T, H] -> (output [T, H], RouteBatch).
 
-        Equivalent to calling ``route()`` per token with locality disabled
-        (the batched path does not apply the per-token sticky policy).  With
-        ``record_stats`` the routing is copied asynchronously into pinned host
-        buffers on the call's stream (no synchronisation here) and recorded as
-        positions ``position .. position+T-1`` when the statistics are next
-        read (``router.stats``) or ``route()`` runs.  ``next_norm=(weight, eps)``
-        fuses the next layer's input RMSNorm of the output into the combine
-        (``RouteBatch.normed``).
+        With locality disabled this equals calling ``route()`` per token.  With
+        locality enabled the policy runs on the device (klc_locality_route) over
+        the tokens in order, continuing the layer's sticky / workload state as
+        T consecutive route() calls would, with one active-expert count for the
+        whole batch (the dynamic cap adapts between calls) and one
+        ``resident_experts`` set for every token; the expert-cache deltas and
+        the cap are not updated per token.  With ``record_stats`` the routing is
+        copied asynchronously into pinned host buffers on the call's stream (no
+        synchronisation here) and recorded as positions ``position ..
+        position+T-1`` when the statistics are next read (``router.stats``) or
+        ``route()`` runs.  ``next_norm=(weight, eps)`` adds the next layer's input
+        RMSNorm of the output (``RouteBatch.normed``), fused into the combine
+        when locality is off.
         """
-        if self.locality_config.enabled:
-            raise ValueError("route_batch() routes without the per-token locality policy; use route() when locality is enabled")
         p = f"model.layers.{layer_idx}.mlp"
         E = int(tensors[f"{p}.router.weight"].shape[0])
         k = self._effective_expert_count(layer_idx, E)
         layer = self._moe_layer(layer_idx, tensors, expert_store, k)
-        y, rb = layer.forward(hidden, precision=self.matmul_precision, return_logits=return_logits, return_norms=return_norms,
-                              residual=residual, next_norm=next_norm)
+        loc = None
+        if self.locality_config.enabled:
+            if not self.locality_on_device:
+                raise ValueError("route_batch() with locality needs the device policy (locality_on_device=True); use route() otherwise")
+            x = as_bf16(hidden, layer.device)
+            T = int(x.shape[0])
+            logits = torch.empty((T, E), dtype=torch.bfloat16, device=layer.device)
+            ridx = torch.empty((T, k), dtype=torch.int32, device=layer.device)
+            rw = torch.empty((T, k), dtype=torch.bfloat16, device=layer.device)
+            with torch.cuda.device(layer.device):
+                _lib.check(_lib.lib().klc_router_topk(x.data_ptr(), T, int(x.shape[1]), layer.router_weight.data_ptr(),
+                                                      layer.router_bias.data_ptr(), E, k, None, ridx.data_ptr(), rw.data_ptr(),
+                                                      logits.data_ptr(), _lib.stream_ptr(layer.device)))
+            pol = self._device_policy(layer_idx, logits, k, self._resident_mask(resident_experts, E, layer.device), 0)
+            y, norms = layer.experts_forward(x, pol["experts"], pol["weights"], precision=self.matmul_precision,
+                                             return_norms=return_norms, residual=residual)
+            normed = rms_norm(y, next_norm[0], float(next_norm[1])) if next_norm is not None else None
+            rb = RouteBatch(pol["experts"], pol["weights"], logits=logits if return_logits else None, norms=norms, normed=normed)
+            if record_stats:
+                loc = [pol["raw"], pol["pred"], pol["npred"], pol["flags"]]
+        else:
+            y, rb = layer.forward(hidden, precision=self.matmul_precision, return_logits=return_logits, return_norms=return_norms,
+                                  residual=residual, next_norm=next_norm)
         if record_stats:
-            ids_h = torch.empty(tuple(rb.indices.shape), dtype=rb.indices.dtype, pin_memory=True)
-            ws_h = torch.empty(tuple(rb.weights.shape), dtype=rb.weights.dtype, pin_memory=True)
-            ids_h.copy_(rb.indices, non_blocking=True)
-            ws_h.copy_(rb.weights, non_blocking=True)
+            def pinned(t: torch.Tensor) -> torch.Tensor:
+                h = torch.empty(tuple(t.shape), dtype=t.dtype, pin_memory=True)
+                h.copy_(t, non_blocking=True)
+                return h
+
+            ids_h, ws_h = pinned(rb.indices), pinned(rb.weights)
+            if loc is not None:
+                loc = [pinned(t) for t in loc] + [sorted(int(v) for v in (resident_experts or set()))]
             done = torch.cuda.Event()
             done.record(torch.cuda.current_stream(rb.indices.device))
-            self._pending.append((done, layer_idx, position, k, ids_h, ws_h))
+            self._pending.append((done, layer_idx, position, k, ids_h, ws_h, loc))
         return y, rb
 
     # ------------------------------------------------------------------
@@ -390,18 +448,98 @@ class StreamedMoERouter:
         return raw_experts, experts, scores, blocked
 
     def _record_route(self, layer_idx: int, position: int, experts: list[int], weights: list[float], raw_experts: list[int],
-                      blocked: bool, predicted_experts: list[int] | None, resident_experts: set[int] | None, k: int):
+                      blocked: bool, predicted_experts: list[int] | None, resident_experts: set[int] | None, k: int,
+                      update_state: bool = True):
         """Statistics and sticky / workload state after a selection (:285-302):
-        returns (predicted experts, sorted resident experts, sticky_adjusted)."""
+        returns (predicted experts, sorted resident experts, sticky_adjusted).
+        ``update_state=False`` when the device policy already updated the state."""
         adjusted_flag = experts != raw_experts
         predicted = predicted_experts if predicted_experts is not None else self.predict_experts(layer_idx, k)
         resident = sorted(int(v) for v in (resident_experts or set()))
         self._stats.record_route(layer_idx, position, experts, weights, raw_experts, adjusted_flag,
                                 predicted_experts=[int(v) for v in predicted], resident_experts=resident, active_cap=k,
                                 blocked_adjustment=blocked)
-        self._update_sticky_scores(layer_idx, experts, weights)
-        self._update_workload_scores(layer_idx, experts, weights)
+        if update_state:
+            self._update_sticky_scores(layer_idx, experts, weights)
+            self._update_workload_scores(layer_idx, experts, weights)
         return predicted, resident, adjusted_flag
+
+    # ------------------------------------------------------------------
+    # locality policy on the device (klc_locality_route)
+    # ------------------------------------------------------------------
+    def _loc_config(self) -> "_lib.KlcLocalityConfig":
+        cfg = self.locality_config
+        return _lib.KlcLocalityConfig(
+            float(cfg.sticky_strength), float(cfg.sticky_candidate_margin), float(cfg.max_sticky_bonus), float(cfg.exploration_margin),
+            float(cfg.cache_aware_strength), float(cfg.sticky_decay), float(cfg.workload_window), int(bool(cfg.semantic_guard)),
+            int(cfg.min_raw_overlap), int(cfg.max_hot_experts_per_layer), int(cfg.prediction_window), int(bool(cfg.predictive_prefetch)),
+            int(self.experts_per_token))
+
+    def _loc_state(self, layer_idx: int, dev: torch.device, E: int) -> torch.Tensor:
+        """The layer's policy state on the device (zero = empty dicts), created on first use."""
+        st = self._loc_states.get(layer_idx)
+        n = ctypes.c_size_t(0)
+        _lib.check(_lib.lib().klc_locality_state_bytes(E, int(self.locality_config.prediction_window), ctypes.byref(n)))
+        if st is None:
+            st = torch.zeros(int(n.value), dtype=torch.uint8, device=dev)
+            self._loc_states[layer_idx] = st
+        elif st.device != dev or st.numel() != int(n.value):
+            raise ValueError(f"layer {layer_idx}: locality state was made for another device or expert count")
+        return st
+
+    @staticmethod
+    def _resident_mask(resident_experts: set[int] | None, E: int, dev: torch.device) -> torch.Tensor | None:
+        if not resident_experts:
+            return None
+        ids = sorted(int(v) for v in resident_experts)
+        if ids[0] < 0 or ids[-1] >= E:
+            raise IndexError(f"resident expert ids must be in [0, {E})")
+        mask = torch.zeros(E, dtype=torch.uint8)
+        mask[ids] = 1
+        return mask.to(dev, non_blocking=True)
+
+    def _device_policy(self, layer_idx: int, logits: torch.Tensor, k: int, resident: torch.Tensor | None,
+                       resident_stride: int) -> dict[str, torch.Tensor]:
+        """klc_locality_route over bf16 logits [T, E]: the raw / adjusted / guarded selections, weights,
+        predictions and flags of every token, the layer's state advanced token by token."""
+        dev = logits.device
+        T, E = int(logits.shape[0]), int(logits.shape[1])
+        st = self._loc_state(layer_idx, dev, E)
+        out = {
+            "experts": torch.empty((T, k), dtype=torch.int32, device=dev),
+            "weights": torch.empty((T, k), dtype=torch.bfloat16, device=dev),
+            "raw": torch.empty((T, k), dtype=torch.int32, device=dev),
+            "pred": torch.empty((T, k), dtype=torch.int32, device=dev),
+            "npred": torch.empty((T,), dtype=torch.int32, device=dev),
+            "flags": torch.empty((T,), dtype=torch.uint8, device=dev),
+        }
+        cfg = self._loc_config()
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib().klc_locality_route(
+                ctypes.byref(cfg), logits.contiguous().data_ptr(), T, E, k, _lib.ptr(resident), int(resident_stride), st.data_ptr(),
+                st.numel(), out["experts"].data_ptr(), out["weights"].data_ptr(), out["raw"].data_ptr(), out["pred"].data_ptr(),
+                out["npred"].data_ptr(), out["flags"].data_ptr(), _lib.stream_ptr(dev)))
+        return out
+
+    def _sync_host_state(self, layer_idx: int) -> None:
+        """Rebuild the host dicts (insertion order included) from the layer's device state."""
+        st = self._loc_states.get(layer_idx)
+        if st is None:
+            return
+        E = (st.numel() - 64 - 4 * max(int(self.locality_config.prediction_window), 1)) // 32
+        raw = st.cpu().numpy()
+        head = raw[:64].view("<i4")
+        hist_len, hist_head = int(head[4]), int(head[5])
+        body = raw[64:]
+        sticky = body[: 8 * E].view("<f8")
+        work = body[8 * E:16 * E].view("<f8")
+        s_at = body[16 * E:24 * E].view("<i8")
+        w_at = body[24 * E:32 * E].view("<i8")
+        W = max(int(self.locality_config.prediction_window), 1)
+        hist = body[32 * E:32 * E + 4 * W].view("<i4")
+        self.sticky_scores[layer_idx] = {int(e): float(sticky[e]) for e in sorted(range(E), key=lambda e: s_at[e]) if s_at[e] != 0}
+        self.workload_scores[layer_idx] = {int(e): float(work[e]) for e in sorted(range(E), key=lambda e: w_at[e]) if w_at[e] != 0}
+        self.recent_history[layer_idx] = deque((int(hist[(hist_head + i) % W]) for i in range(hist_len)), maxlen=W)
 
     def _after_execution(self, layer_idx: int, position: int, experts: list[int], before: dict, after: dict) -> None:
         """Cache-delta statistics and the dynamic active-expert cap (:307-309)."""
@@ -500,6 +638,8 @@ class StreamedMoERouter:
         cfg = self.locality_config
         if not cfg.enabled or not cfg.predictive_prefetch:
             return []
+        if self.locality_on_device and layer_idx in self._loc_states:
+            self._sync_host_state(layer_idx)
         scores: Counter[int] = Counter()
         for e, v in self.workload_scores.get(layer_idx, {}).items():
             scores[int(e)] += float(v)

@@ -54,6 +54,13 @@ def test_ep_single_rank_matches_layer(exchange):
         torch.cuda.synchronize()
         ep.check_device_status()
         assert torch.equal(rb.indices, rb_ref.indices)
+        if exchange == "p2p":
+            # rows returned by the copy kernel instead of the down epilogue: identical output
+            ep._ep.set_fused_return(False)
+            y_copy, _ = ep.forward(x, precision="bf16")
+            ep._ep.set_fused_return(True)
+            ep.check_device_status()
+            assert torch.equal(y_copy, y)
         m = parity.assert_output_close(_bits(y), _bits(ref), f"ep1 ({exchange}) vs layer")
         assert m["bit_equal_frac"] >= 0.99, m
         if exchange == "p2p":
@@ -138,8 +145,18 @@ def _worker(rank, world, port, q, exchange):
         for _ in range(3):  # repeated steps reuse the exchange buffers
             y, rb = ep.forward(x, precision="bf16")
             ep.check_device_status()
+        same_copy = True
+        if exchange == "p2p":
+            # rows returned by a copy kernel instead of the down epilogue's peer stores: same bits
+            ep._ep.set_fused_return(False)
+            y_copy, _ = ep.forward(x, precision="bf16")
+            ep.check_device_status()
+            ep._ep.set_fused_return(True)
+            y_again, _ = ep.forward(x, precision="bf16")
+            ep.check_device_status()
+            same_copy = bool(torch.equal(y_copy, y)) and bool(torch.equal(y_again, y))
         torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(rb.indices, rb_ref.indices)), _bits(y), _bits(ref)))
+        q.put((rank, bool(torch.equal(rb.indices, rb_ref.indices)) and same_copy, _bits(y), _bits(ref)))
         ep.close()
     finally:
         dist.destroy_process_group()

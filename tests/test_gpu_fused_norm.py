@@ -112,3 +112,73 @@ def test_ep_combine_next_norm():
     want = _residual_add_bits(orc.combine_bits(orc.bf16_bits_to_f32(y_bits)[pair_pos].reshape(T, k, H), w_bits), res_bits)
     assert np.array_equal(bits_of(out), want) and np.array_equal(bits_of(plain), want)
     _check_norm(bits_of(normed), orc.rms_norm_bits(want, g_bits, EPS))
+
+
+@pytest.mark.parametrize("T,k,H,E,kn", [(1, 4, 2880, 128, 4), (7, 4, 2880, 128, 4), (64, 4, 2880, 32, 2), (100, 4, 2880, 128, 4),
+                                        (5, 2, 256, 200, 8)])
+def test_combine_rmsnorm_next_router_vs_oracle(T, k, H, E, kn):
+    """klc_moe_combine_rmsnorm_route: the same residual sum and norm as
+    klc_moe_combine_rmsnorm, and the next layer's routing of the normalised rows
+    held to the router's bar (logits within 1 ulp or the fp32 summation bound of
+    the oracle's, a valid top-k of them, weights the softmax of the selected).
+    Up to 64 tokens the router runs inside the combine kernel, above it after it."""
+    from kcapw_klcquant_b200 import _lib
+
+    rng = np.random.default_rng(T * 17 + E)
+    R = T * k + 3
+    y_bits = _bf16_bits(rng.standard_normal((R, H)) * 2.0)
+    pair_pos = rng.permutation(R)[: T * k].astype(np.int32)
+    w_bits = _bf16_bits(rng.random((T, k)) / k)
+    res_bits = _bf16_bits(rng.standard_normal((T, H)) * 4.0)
+    g_bits = _bf16_bits(1.0 + 0.1 * rng.standard_normal(H))
+    rw_bits = _bf16_bits(rng.standard_normal((E, H)) * 0.05)
+    rb_bits = _bf16_bits(rng.standard_normal(E) * 0.1)
+    y, pp, w, g, res = _dev(y_bits), torch.from_numpy(pair_pos).to(DEV), _dev(w_bits), _dev(g_bits), _dev(res_bits)
+    rw, rb = _dev(rw_bits), _dev(rb_bits)
+    out, normed = torch.empty((T, H), dtype=torch.bfloat16, device=DEV), torch.empty((T, H), dtype=torch.bfloat16, device=DEV)
+    out0, normed0 = torch.empty_like(out), torch.empty_like(out)
+    nidx = torch.empty((T, kn), dtype=torch.int32, device=DEV)
+    nw = torch.empty((T, kn), dtype=torch.bfloat16, device=DEV)
+    nlg = torch.empty((T, E), dtype=torch.bfloat16, device=DEV)
+    nr = _lib.KlcNextRouter(rw.data_ptr(), rb.data_ptr(), E, kn, nidx.data_ptr(), nw.data_ptr(), nlg.data_ptr())
+    L = _lib.lib()
+    with torch.cuda.device(DEV):
+        _lib.check(L.klc_moe_combine_rmsnorm_route(y.data_ptr(), pp.data_ptr(), w.data_ptr(), T, k, H, res.data_ptr(), g.data_ptr(),
+                                                   EPS, out.data_ptr(), normed.data_ptr(), nr, _lib.stream_ptr()))
+        _lib.check(L.klc_moe_combine_rmsnorm(y.data_ptr(), pp.data_ptr(), w.data_ptr(), T, k, H, res.data_ptr(), g.data_ptr(), EPS,
+                                             out0.data_ptr(), normed0.data_ptr(), _lib.stream_ptr()))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits_of(out), bits_of(out0))
+    assert np.array_equal(bits_of(normed), bits_of(normed0))
+    n_bits = bits_of(normed)
+    ref = orc.router_logits_bits(n_bits, rw_bits, rb_bits)
+    got = bits_of(nlg)
+    d = parity.ulp_distance_bf16(got, ref)
+    xf, wf = orc.bf16_bits_to_f32(n_bits).astype(np.float64), orc.bf16_bits_to_f32(rw_bits).astype(np.float64)
+    mag = np.abs(xf) @ np.abs(wf).T + np.abs(orc.bf16_bits_to_f32(rb_bits))
+    err = np.abs(orc.bf16_bits_to_f32(got).astype(np.float64) - orc.bf16_bits_to_f32(ref))
+    assert ((d <= 1) | (err <= mag * 2.0**-18)).all(), int(d.max())
+    got_idx = nidx.cpu().numpy()
+    parity.check_selection(got, got_idx, kn)
+    scores = np.take_along_axis(orc.bf16_bits_to_f32(got), got_idx.astype(np.int64), axis=1)
+    wd = parity.ulp_distance_bf16(bits_of(nw), orc.softmax_weights_bits(scores))
+    assert wd.max() <= 1
+
+
+def test_stack_fused_router_matches_unfused():
+    """A 3-layer MoeStack with each layer's router fused into the previous combine
+    against the same stack routing every layer itself: same routing (up to exact
+    near-ties of the two router forms) and outputs."""
+    from kcapw_klcquant_b200 import MoeLayer
+    from kcapw_klcquant_b200.stack import MoeStack
+    from kcapw_klcquant_b200 import synthetic as syn
+
+    dims = syn.LayerDims(32, 2880, 2880, 4)
+    layers = [MoeLayer.from_tensors(0, syn.make_layer(dims, seed=90 + i, device=DEV), DEV, top_k=4) for i in range(3)]
+    norms = [syn.make_rms_weight(2880, seed=95 + i, device=DEV) for i in range(3)]
+    x = syn.make_hidden(24, 2880, seed=99, device=DEV)
+    fused = MoeStack(layers, norms, fuse_router=True).step(x)
+    plain = MoeStack(layers, norms, fuse_router=False).step(x)
+    torch.cuda.synchronize()
+    m = parity.assert_output_close(bits_of(fused), bits_of(plain), "stack fused router vs plain")
+    assert m["bit_equal_frac"] >= 0.99, m

@@ -135,12 +135,14 @@ def test_select_softmax_keep_order():
     np.testing.assert_array_equal(bits_of(w)[0], orc.softmax_weights_bits(s.cpu().numpy())[0])
 
 
-# Both router forms against the oracle's logits (fp32 accumulation, one bf16
+# Every router form against the oracle's logits (fp32 accumulation, one bf16
 # rounding): E <= 128 with H a multiple of 64 runs the tensor-core split-K
 # router, the other shapes the CUDA-core router; token counts cross the
-# 16 / 32 / 64-token tile choices.
+# 16 / 32 / 64-token tile choices; from 2048 tokens the large-batch router
+# (128-token tiles), also with expert counts below its padded width (32, 48, 200).
 @pytest.mark.parametrize("T,E,H,k", [(1, 128, 2880, 4), (37, 32, 2880, 4), (300, 128, 2880, 4), (5000, 128, 2880, 4),
-                                     (20, 8, 64, 2), (33, 128, 3072, 4), (40, 192, 256, 4), (24, 64, 200, 3)])
+                                     (20, 8, 64, 2), (33, 128, 3072, 4), (40, 192, 256, 4), (24, 64, 200, 3),
+                                     (2100, 32, 2880, 4), (2048, 48, 1024, 2), (2300, 200, 512, 8)])
 def test_router_shapes_vs_oracle(T, E, H, k):
     from kcapw_klcquant_b200 import _lib
 
