@@ -2,7 +2,8 @@
 and HBM GB/s or tensor-pipe % of peak at 1/2/4/8 B200).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ep|decode|prefill|stack]
-                    [--impl ours|reference] [--zipf]
+                    [--impl ours|reference] [--exchange p2p|nccl] [--layers L] [--decode-steps S]
+                    [--no-extras] [--no-cpu-baseline] [--no-oracle]
 
 Workloads (synthetic, seeded, GPT-OSS-120B MoE layout: E=128, H=I=2880, top-4):
   ep       (default) config 3: one MoE layer over 16 384 tokens shared evenly by
@@ -13,7 +14,8 @@ Workloads (synthetic, seeded, GPT-OSS-120B MoE layout: E=128, H=I=2880, top-4):
   decode   config 1: T=256 decode tokens per GPU, plus a sweep over T=1,8,64,256
   prefill  config 2: T=4096 tokens, router biased to a Zipf(1.1) expert popularity
   stack    config 4: a 36-layer MoE-only stack (RMSNorm + residual between the
-           blocks), 32 sequences x 128 decode steps, experts sharded over the ranks
+           blocks, each layer's router fused into the previous combine), 32
+           sequences x 128 decode steps, experts sharded over the ranks
 
 A step is one MoE-layer forward (router -> dispatch -> MXFP4 SwiGLU experts ->
 combine) over the step's tokens with the weights resident in HBM.  Timing: W

@@ -42,10 +42,10 @@ constexpr int kWarps = 8;     // warps per CTA
 constexpr int kMaxK = 8;
 constexpr int kMaxCluster = 8;  // portable cluster size
 #ifndef KLC_ROUTER_GEMM_MIN_TOKENS
-#define KLC_ROUTER_GEMM_MIN_TOKENS 2048
+#define KLC_ROUTER_GEMM_MIN_TOKENS 1024
 #endif
-// whole-K tiles of 128 tokens from here on (B200, T = 2048 / 4096 / 16384: 71 / 72 / 78 us
-// against 82 / 131 / 434 us for the split-K cluster form, which wins below: 18 us at T = 1)
+// 128-token tiles from here on (B200: 29 / 48 / 49 / 70 / 72 us at T = 1024 / 2048 / 4096 /
+// 8192 / 16384); the tokens-as-N cluster form wins below (10 us at T = 1, 21 at 256, 29 at 512)
 constexpr int64_t kRouterGemmMinTokens = KLC_ROUTER_GEMM_MIN_TOKENS;
 
 // dot products of one router row with the kTok staged tokens; lanes split the
@@ -587,8 +587,7 @@ int launch_router_gemm_ep(const CUtensorMap& mx, const CUtensorMap& mw, int64_t 
   const int64_t sms = sm_count();
   int C = 1;
   if (tiles * 8 <= 15 * 8 && tiles * 8 <= sms && nk >= 8) C = 8;
-  else if (tiles * 4 <= sms && nk >= 4) C = 4;
-  else if (tiles * 2 <= sms && nk >= 2) C = 2;
+  else if (tiles * 4 <= sms && nk >= 4) C = 4;  // pairs measured slower than whole tiles (86 against ~72 us at 64 tiles)
   KLC_CHECK_ARG(tiles * C <= 0x7fffffff, "klc_router_topk: too many tokens");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(unsigned(tiles * C));
