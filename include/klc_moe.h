@@ -91,6 +91,9 @@ int klc_selftest_wait_timeout(int64_t limit_cycles, int* code, int* where, void*
 /* sizeof(klc_moe_dims) and sizeof(klc_moe_weights) as this library was
  * compiled, for bindings to check their own structure layouts against.    */
 int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes);
+/* sizeof one structure of this header: 0 klc_moe_dims, 1 klc_moe_weights,
+ * 2 klc_locality_config, 3 klc_next_router (KLC_ERR_INVALID for others). */
+int klc_struct_size(int which, size_t* out_bytes);
 
 /* ---- MXFP4 dequant ---------------------------------------------------- *
  * Replaces dequantize_mxfp4_matrix(blocks, scales, dtype)

@@ -112,6 +112,7 @@ SIGNATURES: dict[str, list] = {
     "klc_device_sm_count": [POINTER(c_int)],
     "klc_launch_count": [POINTER(ctypes.c_uint64)],
     "klc_struct_sizes": [POINTER(c_size_t), POINTER(c_size_t)],
+    "klc_struct_size": [c_int, POINTER(c_size_t)],
     "klc_selftest_wait_timeout": [c_int64, POINTER(c_int), POINTER(c_int), c_void_p],
     "klc_capabilities": [POINTER(c_int)],
     "klc_mxfp4_dequant": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p],
@@ -194,11 +195,11 @@ def lib() -> ctypes.CDLL:
     h.klc_last_error.argtypes = []
     h.klc_last_error.restype = c_char_p
     # the structures passed by pointer must have the library's layout
-    nd, nw = c_size_t(0), c_size_t(0)
-    if h.klc_struct_sizes(ctypes.byref(nd), ctypes.byref(nw)) != KLC_OK or (nd.value, nw.value) != (
-            ctypes.sizeof(KlcDims), ctypes.sizeof(KlcWeights)):
-        raise ImportError(f"{LIB_PATH} was built with other structure layouts (dims {nd.value} B, weights {nw.value} B) "
-                          f"than this binding ({ctypes.sizeof(KlcDims)} B, {ctypes.sizeof(KlcWeights)} B): rebuild it")
+    for which, struct in enumerate((KlcDims, KlcWeights, KlcLocalityConfig, KlcNextRouter)):
+        n = c_size_t(0)
+        if h.klc_struct_size(which, ctypes.byref(n)) != KLC_OK or n.value != ctypes.sizeof(struct):
+            raise ImportError(f"{LIB_PATH} was built with another {struct.__name__} layout ({n.value} B) than this "
+                              f"binding ({ctypes.sizeof(struct)} B): rebuild it")
     _LIB = h
     return h
 

@@ -68,3 +68,14 @@ extern "C" int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes) {
   *weights_bytes = sizeof(klc_moe_weights);
   return KLC_OK;
 }
+
+extern "C" int klc_struct_size(int which, size_t* out_bytes) {
+  if (out_bytes == nullptr) return klc::fail(KLC_ERR_INVALID, "klc_struct_size: null output");
+  switch (which) {
+    case 0: *out_bytes = sizeof(klc_moe_dims); return KLC_OK;
+    case 1: *out_bytes = sizeof(klc_moe_weights); return KLC_OK;
+    case 2: *out_bytes = sizeof(klc_locality_config); return KLC_OK;
+    case 3: *out_bytes = sizeof(klc_next_router); return KLC_OK;
+    default: return klc::fail(KLC_ERR_INVALID, "klc_struct_size: unknown structure");
+  }
+}

@@ -212,26 +212,44 @@ __global__ void __launch_bounds__(256) combine_norm_route_kernel(
     xs[c] = nv;
   }
   __syncthreads();
-  // router logits of the normalised row: warp w takes experts w, w + nwarps, ...
-  for (int e = warp; e < E; e += nwarps) {
-    const uint16_t* wr = rw + int64_t(e) * hidden;
-    float acc = 0.f;
-#pragma unroll 4
-    for (int c = lane; c < chunks; c += 32) {
-      const uint4 a = ldg_nc_v4(wr + int64_t(c) * 8);
-      const uint4 b = xs[c];
-      const uint32_t aa[4] = {a.x, a.y, a.z, a.w}, bb[4] = {b.x, b.y, b.z, b.w};
+  // router logits of the normalised row: warp w takes experts w, w + nwarps, ..., four at a
+  // time, so each lane keeps the four rows' chunk loads (L2) in flight together
+  for (int e0 = warp; e0 < E; e0 += 4 * nwarps) {
+    const uint16_t* wr[4];
+    bool valid[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc = fmaf(__uint_as_float(aa[j] << 16), __uint_as_float(bb[j] << 16), acc);
-        acc = fmaf(__uint_as_float(aa[j] & 0xffff0000u), __uint_as_float(bb[j] & 0xffff0000u), acc);
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * nwarps;
+      valid[u] = e < E;
+      wr[u] = rw + int64_t(valid[u] ? e : 0) * hidden;
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 2
+    for (int c = lane; c < chunks; c += 32) {
+      uint4 a[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) a[u] = valid[u] ? ldg_nc_v4(wr[u] + int64_t(c) * 8) : make_uint4(0, 0, 0, 0);
+      const uint4 b = xs[c];
+      const uint32_t bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint32_t aa[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[u] = fmaf(__uint_as_float(aa[j] << 16), __uint_as_float(bb[j] << 16), acc[u]);
+          acc[u] = fmaf(__uint_as_float(aa[j] & 0xffff0000u), __uint_as_float(bb[j] & 0xffff0000u), acc[u]);
+        }
       }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) {
-      const uint16_t lb = f32_to_bf16(acc + bf16_to_f32(rb[e]));
-      if (nlogits != nullptr) nlogits[t * E + e] = lb;
-      row[e] = bf16_to_f32(lb);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float sum = warp_sum(acc[u]);
+      const int e = e0 + u * nwarps;
+      if (lane == 0 && valid[u]) {
+        const uint16_t lb = f32_to_bf16(sum + bf16_to_f32(rb[e]));
+        if (nlogits != nullptr) nlogits[t * E + e] = lb;
+        row[e] = bf16_to_f32(lb);
+      }
     }
   }
   __syncthreads();
