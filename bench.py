@@ -14,7 +14,7 @@ Workloads (synthetic, seeded, GPT-OSS-120B MoE layout: E=128, H=I=2880, top-4):
   decode   config 1: T=256 decode tokens per GPU, plus a sweep over T=1,8,64,256
   prefill  config 2: T=4096 tokens, router biased to a Zipf(1.1) expert popularity
   stack    config 4: a 36-layer MoE-only stack (RMSNorm + residual between the
-           blocks, each layer's router fused into the previous combine), 32
+           blocks, each layer routed by the previous layer's call), 32
            sequences x 128 decode steps, experts sharded over the ranks
 
 A step is one MoE-layer forward (router -> dispatch -> MXFP4 SwiGLU experts ->
@@ -561,10 +561,15 @@ def run_ep(args, world, rank, local):
         moe = ExpertParallelMoe(0, tensors, device, top_k=TOP_K, path=args.path, exchange=args.exchange, max_tokens=T)
         moe_zipf = ExpertParallelMoe(0, zipf_tensors, device, top_k=TOP_K, path=args.path, share_local=moe, exchange=args.exchange,
                                      max_tokens=T)
+        if args.fused_return != "auto" and moe._ep is not None:
+            for m in (moe, moe_zipf):
+                m._ep.set_fused_return(args.fused_return == "on")
         fwd = lambda: moe.forward(x, precision=args.precision)  # noqa: E731
         fwd_zipf = lambda: moe_zipf.forward(x, precision=args.precision)  # noqa: E731
         e2e_fwd = lambda xd, yd: moe.forward(xd, precision=args.precision)[0]  # noqa: E731
-        parallelism = f"ep{world}: experts sharded {GPT_OSS_E // world} per GPU, {moe.exchange_name}"
+        ret = {"auto": "fused into the down epilogue" if world <= 2 else "copy kernel", "on": "fused into the down epilogue",
+               "off": "copy kernel"}[args.fused_return] if args.exchange == "p2p" else "all_to_all"
+        parallelism = f"ep{world}: experts sharded {GPT_OSS_E // world} per GPU, {moe.exchange_name}; expert outputs returned by {ret}"
 
     # clocks sampled over the timed legs (headline, Zipf and end-to-end), all of them under load
     clk = ClockSampler(local)
@@ -828,6 +833,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-oracle", action="store_true", help="skip the CPU oracle parity subsample")
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p", help="N>1: the expert-parallel exchange")
+    ap.add_argument("--fused-return", choices=["auto", "on", "off"], default="auto",
+                    help="N>1 p2p: expert outputs stored to the source ranks by the down epilogue (auto: 2 ranks)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -304,9 +304,10 @@ int klc_moe_bias_only(const uint16_t* dn_bias, int64_t tokens, int64_t hidden, i
  * klc_moe_combine_rmsnorm), the normalised rows are routed for the next layer
  * (streamed_moe_router.py:269-282 on streamed_transformer_executor.py:247's
  * `post`): router_w bf16 [E,H], router_b bf16 [E], k <= 8, E <= 1024;
- * out_idx int32 [T,k], out_w bf16 [T,k], out_logits bf16 [T,E] or NULL.  Up to
- * 64 tokens the router runs inside the combine kernel (one launch), above it
- * the router kernels follow the combine.  No locality adjustment. */
+ * out_idx int32 [T,k], out_w bf16 [T,k], out_logits bf16 [T,E] or NULL.  The
+ * router kernels follow the combine in the same call (logits computed inside the
+ * combine, one CTA per token streaming all router rows, measured slower).  No
+ * locality adjustment. */
 typedef struct klc_next_router {
   const uint16_t* router_w;
   const uint16_t* router_b;
@@ -446,11 +447,12 @@ int klc_ep_arena_bytes(const klc_ep* h, size_t* out_bytes);
 int klc_ep_ipc_handle(const klc_ep* h, void* out_64_bytes);
 int klc_ep_connect(klc_ep* h, const void* handles_world_x_64_bytes);
 int klc_ep_set_wait_limit_ns(klc_ep* h, uint64_t ns);
-/* enable != 0 (the default): with the weights-as-N tensor-core kernels and at most
- * 8 ranks, the down-projection epilogue of klc_ep_experts stores every expert
- * output row straight into its source rank's arena over NVLink, so the return
- * transfer overlaps the GEMM; 0: the rows go through the workspace and a
- * separate copy kernel.  Both give identical results. */
+/* enable != 0: with the weights-as-N tensor-core kernels and at most 8 ranks,
+ * the down-projection epilogue of klc_ep_experts stores every expert output row
+ * straight into its source rank's arena over NVLink, so the return transfer
+ * overlaps the GEMM; 0: the rows go through the workspace and a separate copy
+ * kernel.  Both give identical results.  Default: on for 2 ranks, off above
+ * (where the epilogue's peer stores measured slower than the copy). */
 int klc_ep_set_fused_return(klc_ep* h, int enable);
 int klc_ep_workspace_size(const klc_ep* h, const klc_moe_dims* local_dims, size_t* out_bytes);
 int klc_ep_dispatch(klc_ep* h, const int32_t* idx, int64_t tokens, const uint16_t* x, int32_t* pair_slot, void* workspace,

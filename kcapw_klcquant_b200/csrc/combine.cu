@@ -23,8 +23,6 @@ namespace klc {
 namespace {
 
 constexpr int kMaxTopK = 8;
-// up to this many tokens the next layer's router runs inside the combine
-constexpr int64_t kFusedRouterMaxTokens = 64;
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
   v = warp_sum(v);
@@ -123,139 +121,6 @@ __global__ void __launch_bounds__(256, 4) combine_kernel(const uint16_t* __restr
   }
 }
 
-// The fused form plus the next layer's router (decode batches): the CTA keeps
-// the token's normalised row in shared memory after storing it, computes its E
-// router logits on the CUDA cores (router rows read from L2 with 16-byte
-// loads, fp32 sums, the bias added in fp32, one bf16 rounding, as the router
-// kernels do) and one warp selects the top-k and the softmax.  Replaces the
-// separate router launch of the next layer (streamed_moe_router.py:269-282 on
-// streamed_transformer_executor.py:247's `post`).
-__global__ void __launch_bounds__(256) combine_norm_route_kernel(
-    const uint16_t* __restrict__ y, const int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ w, int k,
-    int64_t hidden, const uint16_t* __restrict__ residual, uint16_t* __restrict__ out, const float* __restrict__ normsq,
-    float* __restrict__ norms, const uint16_t* __restrict__ norm_w, float eps, uint16_t* __restrict__ normed,
-    const uint16_t* __restrict__ rw, const uint16_t* __restrict__ rb, int E, int kn, int32_t* __restrict__ nidx,
-    uint16_t* __restrict__ nw, uint16_t* __restrict__ nlogits) {
-  extern __shared__ __align__(16) unsigned char cr_smem[];
-  uint4* xs = reinterpret_cast<uint4*>(cr_smem);                             // normalised row [H/8]
-  float* row = reinterpret_cast<float*>(cr_smem + (hidden * 2 + 15) / 16 * 16);  // logits [E]
-  __shared__ float red[32];
-  const int64_t t = blockIdx.x;
-  const int chunks = int(hidden / 8);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = int(blockDim.x >> 5);
-  if (norms != nullptr && threadIdx.x < 2 * k) {
-    const int64_t q = t * k * 2 + threadIdx.x;
-    norms[q] = sqrtf(normsq[q]);
-  }
-  int pos[kMaxTopK];
-  float wsel[kMaxTopK];
-#pragma unroll
-  for (int s = 0; s < kMaxTopK; ++s) {
-    pos[s] = s < k ? pair_pos[t * k + s] : -1;
-    wsel[s] = s < k ? bf16_to_f32(w[t * k + s]) : 0.f;
-  }
-  float ss = 0.f;
-  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-    uint4 v[kMaxTopK];
-#pragma unroll
-    for (int s = 0; s < kMaxTopK; ++s)
-      v[s] = pos[s] >= 0 ? reinterpret_cast<const uint4*>(y + int64_t(pos[s]) * hidden)[c] : make_uint4(0, 0, 0, 0);
-    float acc[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-#pragma unroll
-    for (int s = 0; s < kMaxTopK; ++s) {
-      if (pos[s] < 0) continue;
-      const float ws = wsel[s];
-      const uint32_t vv[4] = {v[s].x, v[s].y, v[s].z, v[s].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
-        acc[2 * j] = round_bf16(acc[2 * j] + round_bf16(lo * ws));
-        acc[2 * j + 1] = round_bf16(acc[2 * j + 1] + round_bf16(hi * ws));
-      }
-    }
-    if (residual != nullptr) {
-      const uint4 r = reinterpret_cast<const uint4*>(residual + t * hidden)[c];
-      const uint32_t rr[4] = {r.x, r.y, r.z, r.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc[2 * j] = round_bf16(__uint_as_float(rr[j] << 16) + acc[2 * j]);
-        acc[2 * j + 1] = round_bf16(__uint_as_float(rr[j] & 0xffff0000u) + acc[2 * j + 1]);
-      }
-    }
-    uint4 o;
-    o.x = uint32_t(f32_to_bf16(acc[0])) | (uint32_t(f32_to_bf16(acc[1])) << 16);
-    o.y = uint32_t(f32_to_bf16(acc[2])) | (uint32_t(f32_to_bf16(acc[3])) << 16);
-    o.z = uint32_t(f32_to_bf16(acc[4])) | (uint32_t(f32_to_bf16(acc[5])) << 16);
-    o.w = uint32_t(f32_to_bf16(acc[6])) | (uint32_t(f32_to_bf16(acc[7])) << 16);
-    reinterpret_cast<uint4*>(out + t * hidden)[c] = o;
-    xs[c] = o;  // the stored sum, normalised below in place
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(acc[j], acc[j], ss);
-  }
-  const float total = block_sum(ss, red);
-  const float inv = round_bf16(1.0f / sqrtf(total / float(hidden) + eps));
-  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-    const uint4 o = xs[c];
-    const uint4 g = reinterpret_cast<const uint4*>(norm_w)[c];
-    const uint32_t oo[4] = {o.x, o.y, o.z, o.w}, gg[4] = {g.x, g.y, g.z, g.w};
-    uint32_t r[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float lo = round_bf16(__uint_as_float(oo[j] << 16) * inv) * __uint_as_float(gg[j] << 16);
-      const float hi = round_bf16(__uint_as_float(oo[j] & 0xffff0000u) * inv) * __uint_as_float(gg[j] & 0xffff0000u);
-      r[j] = uint32_t(f32_to_bf16(lo)) | (uint32_t(f32_to_bf16(hi)) << 16);
-    }
-    const uint4 nv = make_uint4(r[0], r[1], r[2], r[3]);
-    reinterpret_cast<uint4*>(normed + t * hidden)[c] = nv;
-    xs[c] = nv;
-  }
-  __syncthreads();
-  // router logits of the normalised row: warp w takes experts w, w + nwarps, ..., four at a
-  // time, so each lane keeps the four rows' chunk loads (L2) in flight together
-  for (int e0 = warp; e0 < E; e0 += 4 * nwarps) {
-    const uint16_t* wr[4];
-    bool valid[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e = e0 + u * nwarps;
-      valid[u] = e < E;
-      wr[u] = rw + int64_t(valid[u] ? e : 0) * hidden;
-    }
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 2
-    for (int c = lane; c < chunks; c += 32) {
-      uint4 a[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) a[u] = valid[u] ? ldg_nc_v4(wr[u] + int64_t(c) * 8) : make_uint4(0, 0, 0, 0);
-      const uint4 b = xs[c];
-      const uint32_t bb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint32_t aa[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc[u] = fmaf(__uint_as_float(aa[j] << 16), __uint_as_float(bb[j] << 16), acc[u]);
-          acc[u] = fmaf(__uint_as_float(aa[j] & 0xffff0000u), __uint_as_float(bb[j] & 0xffff0000u), acc[u]);
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float sum = warp_sum(acc[u]);
-      const int e = e0 + u * nwarps;
-      if (lane == 0 && valid[u]) {
-        const uint16_t lb = f32_to_bf16(sum + bf16_to_f32(rb[e]));
-        if (nlogits != nullptr) nlogits[t * E + e] = lb;
-        row[e] = bf16_to_f32(lb);
-      }
-    }
-  }
-  __syncthreads();
-  if (warp == 0) select_softmax_warp(row, E, kn, false, nidx + t * kn, nw + t * kn);
-}
-
 // execute_experts=False (streamed_moe_router.py:317-329):
 //   contribution = sum(down_bias[experts].to(bf16) * weights[:, None], dim=0)
 // products rounded to bf16, the k-term sum accumulated in fp32, rounded once.
@@ -308,22 +173,13 @@ int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w
     KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(post->weight) & 15) == 0 && (reinterpret_cast<uintptr_t>(post->normed) & 15) == 0,
                   "combine: RMSNorm weight and output must be 16-byte aligned");
     if (post->router_w != nullptr) {
+      // the next layer's router on the normalised rows, right behind the combine in the same
+      // call (computing the logits inside the combine, one CTA per token streaming all E router
+      // rows from L2, measured slower than the router kernels: 84 against 73 us per layer at
+      // T = 1, 336 against 309 at T = 32, B200, GPT-OSS-120B layers)
       KLC_CHECK_ARG(post->router_b && post->out_idx && post->out_w, "combine: null next-layer router argument");
       KLC_CHECK_ARG(post->experts >= 1 && post->experts <= 1024 && post->k >= 1 && post->k <= kSelMaxK && post->k <= post->experts,
                     "combine: next-layer router needs 1 <= k <= min(8, experts), experts <= 1024");
-      KLC_CHECK_ARG((reinterpret_cast<uintptr_t>(post->router_w) & 15) == 0, "combine: router weight must be 16-byte aligned");
-      const size_t smem = size_t((hidden * 2 + 15) / 16 * 16) + size_t(post->experts) * 4;
-      if (tokens <= kFusedRouterMaxTokens && smem <= 200 * 1024) {
-        // decode batches: the next router inside the combine (router rows from L2, one CTA per token)
-        if (smem > 48 * 1024)
-          KLC_CUDA(cudaFuncSetAttribute(combine_norm_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-        combine_norm_route_kernel<<<unsigned(tokens), threads, smem, stream>>>(
-            y, pair_pos, w, k, hidden, residual, out, normsq, norms, post->weight, post->eps, post->normed, post->router_w,
-            post->router_b, post->experts, post->k, post->out_idx, post->out_w, post->out_logits);
-        KLC_LAUNCH_CHECK("combine launch");
-        return KLC_OK;
-      }
-      // larger batches: the combine, then the router kernels on the normalised rows
       combine_kernel<true><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
                                                                       norms, post->weight, post->eps, post->normed);
       KLC_LAUNCH_CHECK("combine launch");

@@ -159,7 +159,7 @@ class MoeLayer:
         (streamed_transformer_executor.py:235,260) -- computed by the combine
         kernel itself.  ``next_router`` (the next layer, with ``next_norm``)
         routes ``normed`` for it as well (``routing.next_indices`` /
-        ``next_weights``), inside the combine kernel for decode batches.
+        ``next_weights``) in the same library call.
         """
         T = int(x.shape[0])
         x = as_bf16(x, self.device)

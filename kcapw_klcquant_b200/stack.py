@@ -11,10 +11,10 @@ layer loop over many layers and a whole batch of tokens at once:
         hidden = hidden + moe_L(normed)             # the combine adds the residual
         normed = rms_norm(hidden, norm[L + 1])      # ... and normalises for layer L+1
 
-with the residual add, the next layer's norm and (``fuse_router``, the
-default) the next layer's router fused into each layer's combine kernel, so a
-layer after the first is one experts-and-combine call on routing its
-predecessor already computed.  Layers are :class:`MoeLayer` (one GPU) or
+with the residual add and the next layer's norm fused into each layer's
+combine kernel and (``fuse_router``, the default) the next layer's router run
+by the same library call, so a layer after the first is one experts-and-combine
+call on routing its predecessor already computed.  Layers are :class:`MoeLayer` (one GPU) or
 :class:`ExpertParallelMoe` with the peer-memory exchange (experts sharded over
 the GPUs of a node); both are free of host synchronisation, so
 :meth:`MoeStack.capture` records a whole decode step of all layers as one CUDA

@@ -120,8 +120,7 @@ def test_combine_rmsnorm_next_router_vs_oracle(T, k, H, E, kn):
     """klc_moe_combine_rmsnorm_route: the same residual sum and norm as
     klc_moe_combine_rmsnorm, and the next layer's routing of the normalised rows
     held to the router's bar (logits within 1 ulp or the fp32 summation bound of
-    the oracle's, a valid top-k of them, weights the softmax of the selected).
-    Up to 64 tokens the router runs inside the combine kernel, above it after it."""
+    the oracle's, a valid top-k of them, weights the softmax of the selected)."""
     from kcapw_klcquant_b200 import _lib
 
     rng = np.random.default_rng(T * 17 + E)
