@@ -14,7 +14,7 @@ Workloads (synthetic, seeded, GPT-OSS-120B MoE layout: E=128, H=I=2880, top-4):
   decode   config 1: T=256 decode tokens per GPU, plus a sweep over T=1,8,64,256
   prefill  config 2: T=4096 tokens, router biased to a Zipf(1.1) expert popularity
   stack    config 4: a 36-layer MoE-only stack (RMSNorm + residual between the
-           blocks, each layer routed by the previous layer's call), 32
+           blocks), 32
            sequences x 128 decode steps, experts sharded over the ranks
 
 A step is one MoE-layer forward (router -> dispatch -> MXFP4 SwiGLU experts ->

@@ -12,9 +12,10 @@ layer loop over many layers and a whole batch of tokens at once:
         normed = rms_norm(hidden, norm[L + 1])      # ... and normalises for layer L+1
 
 with the residual add and the next layer's norm fused into each layer's
-combine kernel and (``fuse_router``, the default) the next layer's router run
-by the same library call, so a layer after the first is one experts-and-combine
-call on routing its predecessor already computed.  Layers are :class:`MoeLayer` (one GPU) or
+combine kernel, so a layer is one MoE call.  With ``fuse_router`` the next
+layer's router also runs in that call (the same kernels; a layer after the
+first is then one experts-and-combine call on routing its predecessor already
+computed).  Layers are :class:`MoeLayer` (one GPU) or
 :class:`ExpertParallelMoe` with the peer-memory exchange (experts sharded over
 the GPUs of a node); both are free of host synchronisation, so
 :meth:`MoeStack.capture` records a whole decode step of all layers as one CUDA
@@ -31,7 +32,7 @@ class MoeStack:
     """MoE layers with RMSNorm weights ``norm_weights[L]`` (bf16 [H]) applied to each layer's input."""
 
     def __init__(self, layers: list, norm_weights: list[torch.Tensor], eps: float = 1e-5, precision: str = "bf16",
-                 fuse_router: bool = True):
+                 fuse_router: bool = False):
         if len(norm_weights) != len(layers):
             raise ValueError("one RMSNorm weight per layer")
         self.layers = list(layers)
