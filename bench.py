@@ -61,7 +61,8 @@ FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H
 GATE_UP_FLOPS_PER_PAIR = 2 * GPT_OSS_H * 2 * GPT_OSS_I  # 33,177,600
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from ncu captures
 # (profiles/): decode T=256, prefill T=4096 Zipf.  None where no capture was taken.
-PROFILED_GATE_UP_TRAFFIC = {"decode": 1_191_247_000 + 8_817_664, "prefill": 1_071_562_000 + 97_615_616}
+PROFILED_GATE_UP_TRAFFIC = {"decode": 1_191_247_000 + 8_817_664, "prefill": 1_071_562_000 + 97_615_616,
+                           "config3": 1_689_441_000 + 369_047_552}
 
 
 def peaks() -> dict:
@@ -594,7 +595,7 @@ def run_ep(args, world, rank, local):
     roof = {"bound": "tensor", "kernel": "gate_up grouped GEMM (block-scaled tcgen05 MMA, SwiGLU epilogue)" + (" of rank 0" if world > 1 else ""),
             "achieved": ach, "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / pk["bf16_tflops"],
             "frac_of_sustained": ach / pk["bf16_tflops_sustained"], "peak_source": pk["source"], "algorithmic_flops": flops_gu,
-            "rows": pairs, "traffic": None}
+            "rows": pairs, "traffic": PROFILED_GATE_UP_TRAFFIC["config3"] if world == 1 and T == 16384 else None}
 
     # parity: N=1 against the CPU oracle on a token subsample; N>1 every rank's EP
     # output against the single-GPU layer on the same tokens
