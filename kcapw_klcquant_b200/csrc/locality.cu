@@ -224,17 +224,35 @@ __device__ void topk_cpu(const float* v, int n, int k, VI* scratch, int* out_idx
   }
 }
 
-// entries of a stamped score table ordered like a stable sort of the dict by
-// value descending: value first, then insertion stamp; `skip` marks chosen ones
-__device__ int best_entry(const double* score, const long long* at, int E, const unsigned char* skip) {
-  int best = -1;
-  for (int e = 0; e < E; ++e) {
-    if (at[e] == 0 || (skip && skip[e])) continue;
-    if (best < 0 || score[e] > score[best] || (score[e] == score[best] && at[e] < at[best])) best = e;
+// The warp's best entry of a stamped score table, as a stable sort of the dict by
+// value descending would put it first: larger value, then earlier insertion.
+// Entries with at == 0 are absent; `skip` marks entries already taken.
+__device__ int warp_best_entry(const double* score, const long long* at, int E, const unsigned char* skip) {
+  const int lane = threadIdx.x & 31;
+  double bv = 0.0;
+  long long ba = 0;
+  int be = -1;
+  for (int e = lane; e < E; e += 32) {
+    if (at[e] == 0 || (skip != nullptr && skip[e])) continue;
+    if (be < 0 || score[e] > bv || (score[e] == bv && at[e] < ba)) {
+      bv = score[e];
+      ba = at[e];
+      be = e;
+    }
   }
-  return best;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const double ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const long long oa = __shfl_xor_sync(0xffffffffu, ba, o);
+    const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+    if (oe >= 0 && (be < 0 || ov > bv || (ov == bv && oa < ba))) {
+      bv = ov;
+      ba = oa;
+      be = oe;
+    }
+  }
+  return be;
 }
-
 
 // Python floats as the reference uses them: fp32 where they meet fp32 tensors,
 // fp64 in the dict arithmetic, and the Python-side comparisons done on the host
@@ -245,13 +263,43 @@ struct LocCfg {
   int sticky_positive, max_bonus_positive, cache_positive;
 };
 
-__device__ __forceinline__ void st_remove(double* val, long long* at, int e) {
-  val[e] = 0.0;
-  at[e] = 0;
+// Shared-memory copy of one layer's state plus the per-token work arrays.
+struct LocSmem {
+  double *sticky, *workload, *cnt;
+  long long *sticky_at, *workload_at, *rank1;
+  float *lg, *adj;
+  VI* scratch;
+  int *hist, *rank0;
+  unsigned char *allowed, *chosen;
+};
+
+__host__ __device__ inline size_t loc_smem_bytes(int E, int window) {
+  return size_t(E) * (8 + 8 + 8 + 8 + 8 + 8 + 4 + 4 + 8 + 4 + 1 + 1) + size_t(window) * 4 + 64;
 }
 
-// One warp; lane 0 walks the tokens (each token's steps depend on the state the
-// previous one left).
+__device__ LocSmem loc_smem_view(unsigned char* p, int E, int window) {
+  LocSmem m;
+  m.sticky = reinterpret_cast<double*>(p);
+  m.workload = m.sticky + E;
+  m.cnt = m.workload + E;
+  m.sticky_at = reinterpret_cast<long long*>(m.cnt + E);
+  m.workload_at = m.sticky_at + E;
+  m.rank1 = m.workload_at + E;
+  m.lg = reinterpret_cast<float*>(m.rank1 + E);
+  m.adj = m.lg + E;
+  m.scratch = reinterpret_cast<VI*>(m.adj + E);
+  m.hist = reinterpret_cast<int*>(m.scratch + E);
+  m.rank0 = m.hist + window;
+  m.allowed = reinterpret_cast<unsigned char*>(m.rank0 + E);
+  m.chosen = m.allowed + E;
+  return m;
+}
+
+// One warp runs the call and walks the tokens in order (each token's steps depend
+// on the state the previous one left).  The state lives in shared memory for the
+// call; the passes over the experts are spread over the lanes, the order-sensitive
+// steps (the torch.topk restatement, the guard, insertions into the dicts) run on
+// lane 0.
 __global__ void __launch_bounds__(32) locality_route_kernel(LocCfg c, const uint16_t* __restrict__ logits, int64_t T, int E,
                                                             int k, const uint8_t* __restrict__ resident, int64_t res_stride,
                                                             char* state, int32_t* __restrict__ out_exp,
@@ -259,250 +307,338 @@ __global__ void __launch_bounds__(32) locality_route_kernel(LocCfg c, const uint
                                                             int32_t* __restrict__ out_pred, int32_t* __restrict__ out_npred,
                                                             uint8_t* __restrict__ out_flags) {
   extern __shared__ __align__(16) unsigned char loc_smem[];
-  if (threadIdx.x != 0) return;
-  double* cnt = reinterpret_cast<double*>(loc_smem);           // [E] Counter values (predictions)
-  long long* rank1 = reinterpret_cast<long long*>(cnt + E);     // [E] Counter insertion order (minor)
-  float* lg = reinterpret_cast<float*>(rank1 + E);              // [E] logits
-  float* adj = lg + E;                                          // [E] adjusted logits
-  VI* scratch = reinterpret_cast<VI*>(adj + E);                 // [E] top-k work space
-  int* rank0 = reinterpret_cast<int*>(scratch + E);             // [E] Counter insertion order (major), -1 absent
-  unsigned char* allowed = reinterpret_cast<unsigned char*>(rank0 + E);  // [E]
-  unsigned char* chosen = allowed + E;                                   // [E]
-
+  __shared__ int raw_s[kLocMaxK], rt_idx_s[kLocMaxK], sel_s[kLocMaxK];
+  __shared__ float rt_val_s[kLocMaxK];
+  __shared__ uint16_t wb_s[kLocMaxK];
+  __shared__ long long sticky_clock, workload_clock;
+  __shared__ int hist_len, hist_head;
+  const int lane = threadIdx.x & 31;
+  const unsigned full = 0xffffffffu;
   LocState S = loc_view(state, E, c.window);
+  LocSmem M = loc_smem_view(loc_smem, E, c.window);
+  for (int e = lane; e < E; e += 32) {
+    M.sticky[e] = S.sticky[e];
+    M.workload[e] = S.workload[e];
+    M.sticky_at[e] = S.sticky_at[e];
+    M.workload_at[e] = S.workload_at[e];
+  }
+  for (int i = lane; i < c.window; i += 32) M.hist[i] = S.hist[i];
+  if (lane == 0) {
+    sticky_clock = S.h->sticky_clock;
+    workload_clock = S.h->workload_clock;
+    hist_len = S.h->hist_len;
+    hist_head = S.h->hist_head;
+  }
+  __syncwarp();
   const int raw_k = c.experts_per_token < E ? c.experts_per_token : E;
   for (int64_t t = 0; t < T; ++t) {
     const uint16_t* lrow = logits + t * E;
-    for (int e = 0; e < E; ++e) {
-      lg[e] = bf16_to_f32(lrow[e]);
-      adj[e] = lg[e];
+    for (int e = lane; e < E; e += 32) {
+      M.lg[e] = bf16_to_f32(lrow[e]);
+      M.adj[e] = M.lg[e];
     }
-    int raw[kLocMaxK], rt_idx[kLocMaxK];
-    float rt_val[kLocMaxK];
-    topk_cpu(lg, E, k, scratch, raw, nullptr);            // route(): topk(logits, k)          :271
-    topk_cpu(lg, E, raw_k, scratch, rt_idx, rt_val);     // _apply_locality_bias: raw_k top    :336
-
+    __syncwarp();
+    if (lane == 0) {
+      // route(): topk(logits, k) :271; _apply_locality_bias: topk(logits, raw_k) :336 (the same call when k == raw_k)
+      topk_cpu(M.lg, E, raw_k, M.scratch, rt_idx_s, rt_val_s);
+      if (raw_k == k) {
+        for (int r = 0; r < k; ++r) raw_s[r] = rt_idx_s[r];
+      } else {
+        topk_cpu(M.lg, E, k, M.scratch, raw_s, nullptr);
+      }
+    }
+    __syncwarp();
     int sticky_n = 0;
-    for (int e = 0; e < E; ++e) sticky_n += S.sticky_at[e] != 0;
+    for (int e = lane; e < E; e += 32) sticky_n += M.sticky_at[e] != 0;
+    sticky_n = __reduce_add_sync(full, sticky_n);
     // sticky bonus for remembered experts within the candidate margin of the raw top-k   :337-344
     if (sticky_n > 0 && c.sticky_positive) {
-      const float floor_v = __fsub_rn(rt_val[raw_k - 1], c.sticky_margin);
-      for (int e = 0; e < E; ++e) {
-        if (S.sticky_at[e] == 0 || !(lg[e] >= floor_v)) continue;
-        float bonus = __fmul_rn(__double2float_rn(S.sticky[e]), c.sticky_strength);
+      const float floor_v = __fsub_rn(rt_val_s[raw_k - 1], c.sticky_margin);
+      for (int e = lane; e < E; e += 32) {
+        if (M.sticky_at[e] == 0 || !(M.lg[e] >= floor_v)) continue;
+        float bonus = __fmul_rn(__double2float_rn(M.sticky[e]), c.sticky_strength);
         if (c.semantic_guard && c.max_bonus_positive && bonus > c.max_bonus) bonus = c.max_bonus;
-        adj[e] = __fadd_rn(adj[e], bonus);
+        M.adj[e] = __fadd_rn(M.adj[e], bonus);
       }
     }
     // experts outside the hot set and the leading raw picks lose the exploration margin  :345-351
     if (c.max_hot > 0 && sticky_n >= c.max_hot) {
-      for (int e = 0; e < E; ++e) allowed[e] = chosen[e] = 0;
+      for (int e = lane; e < E; e += 32) M.allowed[e] = M.chosen[e] = 0;
+      __syncwarp();
       for (int h = 0; h < c.max_hot; ++h) {
-        const int b = best_entry(S.sticky, S.sticky_at, E, chosen);
+        const int b = warp_best_entry(M.sticky, M.sticky_at, E, M.chosen);
         if (b < 0) break;
-        chosen[b] = 1;
-        allowed[b] = 1;
+        if (lane == 0) M.chosen[b] = M.allowed[b] = 1;
+        __syncwarp();
       }
-      int lead = c.experts_per_token / 2;
-      if (lead < 1) lead = 1;
-      if (lead > raw_k) lead = raw_k;
-      for (int r = 0; r < lead; ++r) allowed[rt_idx[r]] = 1;
-      for (int e = 0; e < E; ++e)
-        if (!allowed[e]) adj[e] = __fsub_rn(adj[e], c.explore_margin);
+      if (lane == 0) {
+        int lead = c.experts_per_token / 2;
+        if (lead < 1) lead = 1;
+        if (lead > raw_k) lead = raw_k;
+        for (int r = 0; r < lead; ++r) M.allowed[rt_idx_s[r]] = 1;
+      }
+      __syncwarp();
+      for (int e = lane; e < E; e += 32)
+        if (!M.allowed[e]) M.adj[e] = __fsub_rn(M.adj[e], c.explore_margin);
     }
     // resident experts close to the best raw logit gain the cache-aware bonus           :352-357
     if (resident != nullptr && c.cache_positive) {
       const uint8_t* res = resident + t * res_stride;
-      bool any = false;
-      for (int e = 0; e < E; ++e) any |= res[e] != 0;
+      bool any = false, nan = false;
+      float mx = -INFINITY;
+      for (int e = lane; e < E; e += 32) {
+        any |= res[e] != 0;
+        const float v = M.lg[e];
+        if (v != v) nan = true;
+        else mx = fmaxf(mx, v);
+      }
+      any = __any_sync(full, any);
+      nan = __any_sync(full, nan);
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(full, mx, o));
       if (any) {
-        float mx = lg[0];
-        for (int e = 0; e < E; ++e) {
-          if (lg[e] != lg[e]) {
-            mx = lg[e];
-            break;
+        const float thr = __fsub_rn(nan ? __int_as_float(0x7fc00000) : mx, c.explore_margin);
+        for (int e = lane; e < E; e += 32)
+          if (res[e] && M.lg[e] >= thr) M.adj[e] = __fadd_rn(M.adj[e], c.cache_strength);
+      }
+    }
+    __syncwarp();
+    bool blocked = false, adjusted = false;
+    if (lane == 0) {
+      int sel[kLocMaxK];
+      float sc[kLocMaxK];
+      topk_cpu(M.adj, E, k, M.scratch, sel, nullptr);  // topk(adjusted, k)                  :273
+      int raw[kLocMaxK];
+      for (int r = 0; r < k; ++r) raw[r] = raw_s[r];
+      if (c.semantic_guard) {
+        // keep at least min_raw_overlap raw experts: swap the weakest non-raw pick for the
+        // first missing raw expert, then order by adjusted logit (stable)                  :376-394
+        int need = c.min_raw_overlap < 0 ? 0 : c.min_raw_overlap;
+        if (need > k) need = k;
+        while (true) {
+          int overlap = 0;
+          for (int i = 0; i < k; ++i)
+            for (int j = 0; j < k; ++j) overlap += sel[i] == raw[j];
+          if (overlap >= need) break;
+          int missing = -1;
+          for (int j = 0; j < k && missing < 0; ++j) {
+            bool in_sel = false;
+            for (int i = 0; i < k; ++i) in_sel |= sel[i] == raw[j];
+            if (!in_sel) missing = raw[j];
           }
-          if (lg[e] > mx) mx = lg[e];
+          int evict_pos = -1;
+          for (int i = 0; i < k; ++i) {
+            bool in_raw = false;
+            for (int j = 0; j < k; ++j) in_raw |= sel[i] == raw[j];
+            if (in_raw) continue;
+            if (evict_pos < 0 || M.adj[sel[i]] < M.adj[sel[evict_pos]]) evict_pos = i;
+          }
+          if (missing < 0 || evict_pos < 0) break;
+          sel[evict_pos] = missing;
+          blocked = true;
         }
-        const float thr = __fsub_rn(mx, c.explore_margin);
-        for (int e = 0; e < E; ++e)
-          if (res[e] && lg[e] >= thr) adj[e] = __fadd_rn(adj[e], c.cache_strength);
+        for (int i = 1; i < k; ++i) {  // stable: a pick moves ahead only past strictly smaller ones
+          const int v = sel[i];
+          int j = i;
+          while (j > 0 && M.adj[sel[j - 1]] < M.adj[v]) {
+            sel[j] = sel[j - 1];
+            --j;
+          }
+          sel[j] = v;
+        }
+        for (int i = 0; i < k; ++i) sc[i] = M.lg[sel[i]];
+      } else {
+        for (int i = 0; i < k; ++i) sc[i] = M.adj[sel[i]];
       }
-    }
-    int sel[kLocMaxK];
-    float sc[kLocMaxK];
-    topk_cpu(adj, E, k, scratch, sel, nullptr);          // topk(adjusted, k)                  :273
-    bool blocked = false;
-    if (c.semantic_guard) {
-      // keep at least min_raw_overlap raw experts: swap the weakest non-raw pick for the
-      // first missing raw expert, then order by adjusted logit (stable)                  :376-394
-      int need = c.min_raw_overlap < 0 ? 0 : c.min_raw_overlap;
-      if (need > k) need = k;
-      while (true) {
-        int overlap = 0;
-        for (int i = 0; i < k; ++i)
-          for (int j = 0; j < k; ++j) overlap += sel[i] == raw[j];
-        if (overlap >= need) break;
-        int missing = -1;
-        for (int j = 0; j < k && missing < 0; ++j) {
-          bool in_sel = false;
-          for (int i = 0; i < k; ++i) in_sel |= sel[i] == raw[j];
-          if (!in_sel) missing = raw[j];
-        }
-        int evict_pos = -1;
-        for (int i = 0; i < k; ++i) {
-          bool in_raw = false;
-          for (int j = 0; j < k; ++j) in_raw |= sel[i] == raw[j];
-          if (in_raw) continue;
-          if (evict_pos < 0 || adj[sel[i]] < adj[sel[evict_pos]]) evict_pos = i;
-        }
-        if (missing < 0 || evict_pos < 0) break;
-        sel[evict_pos] = missing;
-        blocked = true;
+      // softmax of the selected scores, rounded once to bf16                               :281-282
+      float m = sc[0];
+      for (int r = 1; r < k; ++r) m = fmaxf(m, sc[r]);
+      float ex[kLocMaxK];
+      float sum = 0.f;
+      for (int r = 0; r < k; ++r) {
+        ex[r] = expf(sc[r] - m);
+        sum += ex[r];
       }
-      for (int i = 1; i < k; ++i) {  // stable: a pick moves ahead only past strictly smaller ones
-        const int v = sel[i];
-        int j = i;
-        while (j > 0 && adj[sel[j - 1]] < adj[v]) {
-          sel[j] = sel[j - 1];
-          --j;
-        }
-        sel[j] = v;
+      for (int r = 0; r < k; ++r) {
+        wb_s[r] = f32_to_bf16(ex[r] / sum);
+        sel_s[r] = sel[r];
+        adjusted |= sel[r] != raw[r];
+        out_exp[t * k + r] = sel[r];
+        out_w[t * k + r] = wb_s[r];
+        out_raw[t * k + r] = raw[r];
       }
-      for (int i = 0; i < k; ++i) sc[i] = lg[sel[i]];
-    } else {
-      for (int i = 0; i < k; ++i) sc[i] = adj[sel[i]];
+      out_flags[t] = uint8_t((blocked ? 1 : 0) | (adjusted ? 2 : 0));
     }
-    // softmax of the selected scores, rounded once to bf16                               :281-282
-    float m = sc[0];
-    for (int r = 1; r < k; ++r) m = fmaxf(m, sc[r]);
-    float ex[kLocMaxK];
-    float sum = 0.f;
-    for (int r = 0; r < k; ++r) {
-      ex[r] = expf(sc[r] - m);
-      sum += ex[r];
-    }
-    uint16_t wb[kLocMaxK];
-    for (int r = 0; r < k; ++r) wb[r] = f32_to_bf16(ex[r] / sum);
+    __syncwarp();
 
     // predicted experts from the state before this token's update                       :426-440
     int npred = 0;
     if (c.predictive) {
       bool any = false;
-      for (int e = 0; e < E; ++e) {
-        cnt[e] = 0.0;
-        rank0[e] = -1;
-        rank1[e] = 0;
-        if (S.workload_at[e] != 0) {
-          cnt[e] = __dadd_rn(cnt[e], S.workload[e]);
-          rank0[e] = 0;
-          rank1[e] = S.workload_at[e];
+      for (int e = lane; e < E; e += 32) {
+        double v = 0.0;
+        int r0 = -1;
+        long long r1 = 0;
+        if (M.workload_at[e] != 0) {
+          v = __dadd_rn(v, M.workload[e]);
+          r0 = 0;
+          r1 = M.workload_at[e];
         }
-        if (S.sticky_at[e] != 0) {
-          cnt[e] = __dadd_rn(cnt[e], __dmul_rn(S.sticky[e], 0.75));
-          if (rank0[e] < 0) {
-            rank0[e] = 1;
-            rank1[e] = S.sticky_at[e];
+        if (M.sticky_at[e] != 0) {
+          v = __dadd_rn(v, __dmul_rn(M.sticky[e], 0.75));
+          if (r0 < 0) {
+            r0 = 1;
+            r1 = M.sticky_at[e];
           }
         }
-      }
-      for (int i = 0; i < S.h->hist_len; ++i) {
-        const int e = S.hist[(S.h->hist_head + i) % c.window];
-        cnt[e] = __dadd_rn(cnt[e], 0.5);
-        if (rank0[e] < 0) {
-          rank0[e] = 2;
-          rank1[e] = i;
+        for (int i = 0; i < hist_len; ++i) {
+          if (M.hist[(hist_head + i) % c.window] != e) continue;
+          v = __dadd_rn(v, 0.5);
+          if (r0 < 0) {
+            r0 = 2;
+            r1 = i;
+          }
         }
+        M.cnt[e] = v;
+        M.rank0[e] = r0;
+        M.rank1[e] = r1;
+        M.chosen[e] = 0;
+        any |= r0 >= 0;
       }
-      for (int e = 0; e < E; ++e) {
-        chosen[e] = 0;
-        any |= rank0[e] >= 0;
-      }
+      any = __any_sync(full, any);
+      __syncwarp();
       if (any) {
-        for (int r = 0; r < k; ++r) {  // Counter.most_common(k): value desc, insertion order
-          int b = -1;
-          for (int e = 0; e < E; ++e) {
-            if (rank0[e] < 0 || chosen[e]) continue;
-            if (b < 0 || cnt[e] > cnt[b] ||
-                (cnt[e] == cnt[b] && (rank0[e] < rank0[b] || (rank0[e] == rank0[b] && rank1[e] < rank1[b]))))
-              b = e;
+        for (int r = 0; r < k; ++r) {  // Counter.most_common(k): value desc, then insertion order
+          double bv = 0.0;
+          int b0 = 0, be = -1;
+          long long b1 = 0;
+          for (int e = lane; e < E; e += 32) {
+            if (M.rank0[e] < 0 || M.chosen[e]) continue;
+            const double v = M.cnt[e];
+            if (be < 0 || v > bv || (v == bv && (M.rank0[e] < b0 || (M.rank0[e] == b0 && M.rank1[e] < b1)))) {
+              bv = v;
+              b0 = M.rank0[e];
+              b1 = M.rank1[e];
+              be = e;
+            }
           }
-          if (b < 0) break;
-          chosen[b] = 1;
-          out_pred[t * k + npred++] = b;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            const double ov = __shfl_xor_sync(full, bv, o);
+            const int o0 = __shfl_xor_sync(full, b0, o);
+            const long long o1 = __shfl_xor_sync(full, b1, o);
+            const int oe = __shfl_xor_sync(full, be, o);
+            if (oe >= 0 && (be < 0 || ov > bv || (ov == bv && (o0 < b0 || (o0 == b0 && o1 < b1))))) {
+              bv = ov;
+              b0 = o0;
+              b1 = o1;
+              be = oe;
+            }
+          }
+          if (be < 0) break;
+          if (lane == 0) {
+            M.chosen[be] = 1;
+            out_pred[t * k + npred] = be;
+          }
+          ++npred;
+          __syncwarp();
         }
       }
     }
+    if (lane == 0) out_npred[t] = npred;
 
     // sticky scores: decay, drop the faded, add this token's weights, trim to the hot set   :396-411
-    for (int e = 0; e < E; ++e) {
-      if (S.sticky_at[e] == 0) continue;
-      const double v = __dmul_rn(S.sticky[e], c.sticky_decay);
-      if (v < 1e-4) st_remove(S.sticky, S.sticky_at, e);
-      else S.sticky[e] = v;
-    }
-    for (int r = 0; r < k; ++r) {
-      const int e = sel[r];
-      const double w = double(bf16_to_f32(wb[r]));
-      if (S.sticky_at[e] != 0) {
-        S.sticky[e] = __dadd_rn(S.sticky[e], w);
+    for (int e = lane; e < E; e += 32) {
+      if (M.sticky_at[e] == 0) continue;
+      const double v = __dmul_rn(M.sticky[e], c.sticky_decay);
+      if (v < 1e-4) {
+        M.sticky[e] = 0.0;
+        M.sticky_at[e] = 0;
       } else {
-        S.sticky[e] = __dadd_rn(0.0, w);
-        S.sticky_at[e] = ++S.h->sticky_clock;
+        M.sticky[e] = v;
       }
     }
+    __syncwarp();
+    if (lane == 0) {
+      for (int r = 0; r < k; ++r) {
+        const int e = sel_s[r];
+        const double w = double(bf16_to_f32(wb_s[r]));
+        if (M.sticky_at[e] != 0) {
+          M.sticky[e] = __dadd_rn(M.sticky[e], w);
+        } else {
+          M.sticky[e] = __dadd_rn(0.0, w);
+          M.sticky_at[e] = ++sticky_clock;
+        }
+      }
+    }
+    __syncwarp();
     if (c.max_hot > 0) {
       int n = 0;
-      for (int e = 0; e < E; ++e) n += S.sticky_at[e] != 0;
+      for (int e = lane; e < E; e += 32) n += M.sticky_at[e] != 0;
+      n = __reduce_add_sync(full, n);
       if (n > 2 * c.max_hot) {
-        for (int e = 0; e < E; ++e) chosen[e] = 0;
+        for (int e = lane; e < E; e += 32) M.chosen[e] = 0;
+        __syncwarp();
         for (int h = 0; h < c.max_hot; ++h) {
-          const int b = best_entry(S.sticky, S.sticky_at, E, chosen);
+          const int b = warp_best_entry(M.sticky, M.sticky_at, E, M.chosen);
           if (b < 0) break;
-          chosen[b] = 1;
+          if (lane == 0) M.chosen[b] = 1;
+          __syncwarp();
         }
-        for (int e = 0; e < E; ++e)
-          if (S.sticky_at[e] != 0 && !chosen[e]) st_remove(S.sticky, S.sticky_at, e);
+        for (int e = lane; e < E; e += 32)
+          if (M.sticky_at[e] != 0 && !M.chosen[e]) {
+            M.sticky[e] = 0.0;
+            M.sticky_at[e] = 0;
+          }
       }
     }
     // workload scores and the recent-expert history                                       :413-424
-    for (int e = 0; e < E; ++e) {
-      if (S.workload_at[e] == 0) continue;
-      const double v = __dmul_rn(S.workload[e], c.workload_decay);
-      if (v < 1e-4) st_remove(S.workload, S.workload_at, e);
-      else S.workload[e] = v;
-    }
-    for (int r = 0; r < k; ++r) {
-      const int e = sel[r];
-      const double w = double(bf16_to_f32(wb[r]));
-      if (S.workload_at[e] != 0) {
-        S.workload[e] = __dadd_rn(S.workload[e], w);
+    for (int e = lane; e < E; e += 32) {
+      if (M.workload_at[e] == 0) continue;
+      const double v = __dmul_rn(M.workload[e], c.workload_decay);
+      if (v < 1e-4) {
+        M.workload[e] = 0.0;
+        M.workload_at[e] = 0;
       } else {
-        S.workload[e] = __dadd_rn(0.0, w);
-        S.workload_at[e] = ++S.h->workload_clock;
-      }
-      if (S.h->hist_len < c.window) {
-        S.hist[(S.h->hist_head + S.h->hist_len) % c.window] = e;
-        ++S.h->hist_len;
-      } else {
-        S.hist[S.h->hist_head] = e;
-        S.h->hist_head = (S.h->hist_head + 1) % c.window;
+        M.workload[e] = v;
       }
     }
-
-    bool adjusted = false;
-    for (int r = 0; r < k; ++r) {
-      adjusted |= sel[r] != raw[r];
-      out_exp[t * k + r] = sel[r];
-      out_w[t * k + r] = wb[r];
-      out_raw[t * k + r] = raw[r];
+    __syncwarp();
+    if (lane == 0) {
+      for (int r = 0; r < k; ++r) {
+        const int e = sel_s[r];
+        const double w = double(bf16_to_f32(wb_s[r]));
+        if (M.workload_at[e] != 0) {
+          M.workload[e] = __dadd_rn(M.workload[e], w);
+        } else {
+          M.workload[e] = __dadd_rn(0.0, w);
+          M.workload_at[e] = ++workload_clock;
+        }
+        if (hist_len < c.window) {
+          M.hist[(hist_head + hist_len) % c.window] = e;
+          ++hist_len;
+        } else {
+          M.hist[hist_head] = e;
+          hist_head = (hist_head + 1) % c.window;
+        }
+      }
     }
-    out_npred[t] = npred;
-    out_flags[t] = uint8_t((blocked ? 1 : 0) | (adjusted ? 2 : 0));
+    __syncwarp();
+  }
+  // the state back to its buffer for the next call
+  for (int e = lane; e < E; e += 32) {
+    S.sticky[e] = M.sticky[e];
+    S.workload[e] = M.workload[e];
+    S.sticky_at[e] = M.sticky_at[e];
+    S.workload_at[e] = M.workload_at[e];
+  }
+  for (int i = lane; i < c.window; i += 32) S.hist[i] = M.hist[i];
+  if (lane == 0) {
+    S.h->sticky_clock = sticky_clock;
+    S.h->workload_clock = workload_clock;
+    S.h->hist_len = hist_len;
+    S.h->hist_head = hist_head;
   }
 }
-
-size_t loc_smem_bytes(int E) { return size_t(E) * (8 + 8 + 4 + 4 + 8 + 4 + 1 + 1) + 16; }
 
 }  // namespace
 }  // namespace klc
@@ -551,7 +687,9 @@ extern "C" int klc_locality_route(const klc_locality_config* cfg, const uint16_t
   c.sticky_positive = cfg->sticky_strength > 0;
   c.max_bonus_positive = cfg->max_sticky_bonus > 0;
   c.cache_positive = cfg->cache_aware_strength > 0;
-  const size_t smem = loc_smem_bytes(int(experts));
+  const size_t smem = loc_smem_bytes(int(experts), window);
+  if (smem > 48 * 1024)
+    KLC_CUDA(cudaFuncSetAttribute(locality_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   locality_route_kernel<<<1, 32, smem, as_stream(stream)>>>(c, logits, tokens, int(experts), k, resident, resident_stride,
                                                            static_cast<char*>(state), out_experts, out_w, out_raw, out_pred,
                                                            out_npred, out_flags);
