@@ -224,6 +224,49 @@ __device__ void topk_cpu(const float* v, int n, int k, VI* scratch, int* out_idx
   }
 }
 
+// Fast path of topk_cpu for one warp: when the row has no NaN and its k + 1 largest
+// values are all different, torch.topk's result is simply the k largest in
+// descending order, whatever its algorithm; returns false (the outputs may then hold
+// a partial result) when a tie or a NaN makes the order depend on the algorithm.
+// Lane l owns l, l + 32, ...
+__device__ bool warp_topk_distinct(const float* v, int n, int k, int* out_idx, float* out_val) {
+  const int lane = threadIdx.x & 31;
+  bool nan = false;
+  for (int e = lane; e < n; e += 32) nan |= v[e] != v[e];
+  if (__any_sync(0xffffffffu, nan)) return false;
+  const int rounds = k < n ? k + 1 : k;
+  uint32_t taken = 0;
+  float prev = 0.f;
+  bool ok = true;
+  for (int r = 0; r < rounds && ok; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = 0, e = lane; e < n; ++j, e += 32)
+      if (!((taken >> j) & 1u) && (bi == 0x7fffffff || v[e] > bv || (v[e] == bv && e < bi))) {
+        bv = v[e];
+        bi = e;
+      }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (r > 0 && !(bv < prev)) ok = false;  // a tie (or a repeat of the k-th value just below)
+    prev = bv;
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if (r < k && lane == 0) {
+      out_idx[r] = bi;
+      if (out_val) out_val[r] = bv;
+    }
+  }
+  __syncwarp();
+  return ok;
+}
+
 // The warp's best entry of a stamped score table, as a stable sort of the dict by
 // value descending would put it first: larger value, then earlier insertion.
 // Entries with at == 0 are absent; `skip` marks entries already taken.
@@ -338,9 +381,11 @@ __global__ void __launch_bounds__(32) locality_route_kernel(LocCfg c, const uint
       M.adj[e] = M.lg[e];
     }
     __syncwarp();
+    // route(): topk(logits, k) :271; _apply_locality_bias: topk(logits, raw_k) :336 (the same
+    // selection when k == raw_k); the restated algorithm only where ties make it matter
+    const bool raw_fast = warp_topk_distinct(M.lg, E, raw_k, rt_idx_s, rt_val_s);
     if (lane == 0) {
-      // route(): topk(logits, k) :271; _apply_locality_bias: topk(logits, raw_k) :336 (the same call when k == raw_k)
-      topk_cpu(M.lg, E, raw_k, M.scratch, rt_idx_s, rt_val_s);
+      if (!raw_fast) topk_cpu(M.lg, E, raw_k, M.scratch, rt_idx_s, rt_val_s);
       if (raw_k == k) {
         for (int r = 0; r < k; ++r) raw_s[r] = rt_idx_s[r];
       } else {
@@ -402,11 +447,16 @@ __global__ void __launch_bounds__(32) locality_route_kernel(LocCfg c, const uint
       }
     }
     __syncwarp();
+    const bool adj_fast = warp_topk_distinct(M.adj, E, k, sel_s, nullptr);  // topk(adjusted, k)  :273
     bool blocked = false, adjusted = false;
     if (lane == 0) {
       int sel[kLocMaxK];
       float sc[kLocMaxK];
-      topk_cpu(M.adj, E, k, M.scratch, sel, nullptr);  // topk(adjusted, k)                  :273
+      if (adj_fast) {
+        for (int r = 0; r < k; ++r) sel[r] = sel_s[r];
+      } else {
+        topk_cpu(M.adj, E, k, M.scratch, sel, nullptr);
+      }
       int raw[kLocMaxK];
       for (int r = 0; r < k; ++r) raw[r] = raw_s[r];
       if (c.semantic_guard) {
