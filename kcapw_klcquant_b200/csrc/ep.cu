@@ -110,6 +110,20 @@ __device__ __forceinline__ uint64_t gtimer() {
   return t;
 }
 
+// One warp copies a row of 16-byte chunks to (peer) memory with four loads in flight
+// per lane before their stores, so the local reads do not serialise the remote writes.
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int chunks, int lane) {
+  int c = lane;
+  for (; c + 96 < chunks; c += 128) {
+    const uint4 v0 = src[c], v1 = src[c + 32], v2 = src[c + 64], v3 = src[c + 96];
+    dst[c] = v0;
+    dst[c + 32] = v1;
+    dst[c + 64] = v2;
+    dst[c + 96] = v3;
+  }
+  for (; c < chunks; c += 32) dst[c] = src[c];
+}
+
 // Bounded wait until *flag >= epoch (wrap-aware); false on expiry.
 __device__ bool wait_flag(const uint32_t* flag, uint32_t epoch, uint64_t limit_ns) {
   if (int32_t(ld_acquire_sys(flag) - epoch) >= 0) return true;
@@ -168,7 +182,7 @@ __global__ void __launch_bounds__(256)
     char* b = peers.base[d];
     const uint4* src = reinterpret_cast<const uint4*>(x + (p / k) * hidden);
     uint4* dst = reinterpret_cast<uint4*>(b + L.recv_rows + size_t(slot) * size_t(hidden) * 2);
-    for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
+    copy_row(dst, src, chunks, lane);
     if (lane == 0) {
       reinterpret_cast<int32_t*>(b + L.recv_meta)[slot] = v - d * epr;
       pair_slot[p] = int32_t(int64_t(d) * cap + pos);
@@ -224,7 +238,7 @@ __global__ void __launch_bounds__(256)
     const int64_t pos = q - int64_t(s) * cap;
     const uint4* src = reinterpret_cast<const uint4*>(y + int64_t(row) * hidden);
     uint4* dst = reinterpret_cast<uint4*>(peers.base[s] + L.back_rows + size_t(int64_t(rank) * cap + pos) * size_t(hidden) * 2);
-    for (int c = lane; c < chunks; c += 32) dst[c] = src[c];
+    copy_row(dst, src, chunks, lane);
   }
   signal_peers(peers, world, rank, done, L.flag_combine, 0, nullptr, epoch);
 }
