@@ -138,11 +138,13 @@ def test_select_softmax_keep_order():
 # Every router form against the oracle's logits (fp32 accumulation, one bf16
 # rounding): E <= 128 with H a multiple of 64 runs the tensor-core split-K
 # router, the other shapes the CUDA-core router; token counts cross the
-# 16 / 32 / 64-token tile choices; from 2048 tokens the large-batch router
-# (128-token tiles), also with expert counts below its padded width (32, 48, 200).
+# 16 / 32 / 64-token tile choices; from 1024 tokens the large-batch router
+# (128-token tiles, the hidden dimension split over a cluster of 8 or 4 CTAs
+# or whole), also with expert counts below its padded width (32, 48, 100, 200).
 @pytest.mark.parametrize("T,E,H,k", [(1, 128, 2880, 4), (37, 32, 2880, 4), (300, 128, 2880, 4), (5000, 128, 2880, 4),
                                      (20, 8, 64, 2), (33, 128, 3072, 4), (40, 192, 256, 4), (24, 64, 200, 3),
-                                     (2100, 32, 2880, 4), (2048, 48, 1024, 2), (2300, 200, 512, 8)])
+                                     (2100, 32, 2880, 4), (2048, 48, 1024, 2), (2300, 200, 512, 8), (1500, 128, 2880, 4),
+                                     (1100, 100, 1536, 3)])
 def test_router_shapes_vs_oracle(T, E, H, k):
     from kcapw_klcquant_b200 import _lib
 
