@@ -94,6 +94,11 @@ int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes);
 /* sizeof one structure of this header: 0 klc_moe_dims, 1 klc_moe_weights,
  * 2 klc_locality_config, 3 klc_next_router (KLC_ERR_INVALID for others). */
 int klc_struct_size(int which, size_t* out_bytes);
+/* enable != 0 (the default): the kernels of a layer call (router, permute,
+ * quantize, expert GEMMs, combine) are launched with programmatic dependent
+ * launch, so each launches while its predecessor finishes; 0: plain stream
+ * order.  Results are identical either way; process-wide. */
+int klc_set_pdl(int enable);
 
 /* ---- MXFP4 dequant ---------------------------------------------------- *
  * Replaces dequantize_mxfp4_matrix(blocks, scales, dtype)

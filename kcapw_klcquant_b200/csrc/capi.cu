@@ -69,6 +69,18 @@ extern "C" int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes) {
   return KLC_OK;
 }
 
+namespace klc {
+namespace {
+std::atomic<bool> g_pdl{true};
+}  // namespace
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+}  // namespace klc
+
+extern "C" int klc_set_pdl(int enable) {
+  klc::g_pdl.store(enable != 0, std::memory_order_relaxed);
+  return KLC_OK;
+}
+
 extern "C" int klc_struct_size(int which, size_t* out_bytes) {
   if (out_bytes == nullptr) return klc::fail(KLC_ERR_INVALID, "klc_struct_size: null output");
   switch (which) {

@@ -46,6 +46,8 @@ __global__ void __launch_bounds__(256, 4) combine_kernel(const uint16_t* __restr
                                const uint16_t* __restrict__ residual, uint16_t* __restrict__ out,
                                const float* __restrict__ normsq, float* __restrict__ norms,
                                const uint16_t* __restrict__ norm_w, float eps, uint16_t* __restrict__ normed) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   const int64_t t = blockIdx.x;
   float ss = 0.f;  // sum of squares of the stored row (kNorm)
   const int chunks = int(hidden / 8);
@@ -142,6 +144,8 @@ __global__ void bias_only_kernel(const uint16_t* __restrict__ bias, int64_t hidd
 //   x * rsqrt(mean(x.float()^2) + eps).to(bf16) * weight   (bf16 products)
 __global__ void rms_norm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wt, int64_t hidden,
                                 float eps, uint16_t* __restrict__ y) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   __shared__ float red[32];
   const int64_t r = blockIdx.x;
   const uint16_t* xr = x + r * hidden;
@@ -180,17 +184,17 @@ int launch_combine(const uint16_t* y, const int32_t* pair_pos, const uint16_t* w
       KLC_CHECK_ARG(post->router_b && post->out_idx && post->out_w, "combine: null next-layer router argument");
       KLC_CHECK_ARG(post->experts >= 1 && post->experts <= 1024 && post->k >= 1 && post->k <= kSelMaxK && post->k <= post->experts,
                     "combine: next-layer router needs 1 <= k <= min(8, experts), experts <= 1024");
-      combine_kernel<true><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
-                                                                      norms, post->weight, post->eps, post->normed);
+      KLC_CUDA(launch_chain(combine_kernel<true>, dim3(unsigned(tokens)), dim3(threads), size_t(0), stream, 0u, y, pair_pos, w, k, hidden, residual, out, normsq,
+                                                                      norms, post->weight, post->eps, post->normed));
       KLC_LAUNCH_CHECK("combine launch");
       return launch_router(post->normed, tokens, hidden, post->router_w, post->router_b, post->experts, post->k, nullptr,
                            post->out_idx, post->out_w, post->out_logits, stream);
     }
-    combine_kernel<true><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
-                                                                    norms, post->weight, post->eps, post->normed);
+    KLC_CUDA(launch_chain(combine_kernel<true>, dim3(unsigned(tokens)), dim3(threads), size_t(0), stream, 0u, y, pair_pos, w, k, hidden, residual, out, normsq,
+                                                                    norms, post->weight, post->eps, post->normed));
   } else {
-    combine_kernel<false><<<unsigned(tokens), threads, 0, stream>>>(y, pair_pos, w, k, hidden, residual, out, normsq,
-                                                                     norms, nullptr, 0.f, nullptr);
+    KLC_CUDA(launch_chain(combine_kernel<false>, dim3(unsigned(tokens)), dim3(threads), size_t(0), stream, 0u, y, pair_pos, w, k, hidden, residual, out, normsq,
+                                                                     norms, nullptr, 0.f, nullptr));
   }
   KLC_LAUNCH_CHECK("combine launch");
   return KLC_OK;
@@ -217,7 +221,7 @@ extern "C" int klc_rms_norm(const uint16_t* x, const uint16_t* w, int64_t rows, 
   if (rows == 0) return KLC_OK;
   KLC_CHECK_ARG(x && w && y, "klc_rms_norm: null pointer");
   KLC_CHECK_ARG(rows <= 0x7fffffff, "klc_rms_norm: too many rows");
-  rms_norm_kernel<<<unsigned(rows), 256, 0, as_stream(stream)>>>(x, w, hidden, eps, y);
+  KLC_CUDA(launch_chain(rms_norm_kernel, dim3(unsigned(rows)), dim3(256), size_t(0), as_stream(stream), 0u, x, w, hidden, eps, y));
   KLC_LAUNCH_CHECK("klc_rms_norm launch");
   return KLC_OK;
 }

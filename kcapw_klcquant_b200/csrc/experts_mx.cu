@@ -179,6 +179,8 @@ struct MxParams {
 template <int PHASE, class C>
 __global__ void __launch_bounds__(C::THREADS, 1)
     mx_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, MxParams p) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   constexpr int NA = C::NA, NS = C::NS, NB = C::NB, NP = C::NP, ND = C::ND, N2 = C::N2, NCH = C::NCH;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -612,6 +614,8 @@ struct Mx2Cfg {
 template <int PHASE, class C>
 __global__ void __launch_bounds__(C::THREADS, 1)
     mx2_expert_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, MxParams p) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   constexpr int NS = C::NS, ND = C::ND, N2 = C::N2, SUB = C::SUB;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -944,6 +948,8 @@ __device__ __forceinline__ uint32_t mx3_idesc(uint32_t a_id, uint32_t b_id) {
 template <int PHASE, class C>
 __global__ void __launch_bounds__(C::THREADS, 1)
     mx3_expert_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x, MxParams p) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   constexpr int NS = C::NS, ND = C::ND, SUB = C::SUB;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1260,7 +1266,7 @@ int launch_mx_phase(const uint8_t* blocks, const uint8_t* act_q, int64_t rows_ca
   const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
   const int grid = int(items < sm_count() ? items : sm_count());
   if (grid <= 0) return KLC_OK;
-  mx_expert_kernel<PHASE, C><<<grid, C::THREADS, smem, stream>>>(ma, mb, p);
+  KLC_CUDA(launch_chain(mx_expert_kernel<PHASE, C>, dim3(grid), dim3(C::THREADS), size_t(smem), stream, 0u, ma, mb, p));
   KLC_LAUNCH_CHECK("tcgen05 expert launch");
   return KLC_OK;
 }
@@ -1295,7 +1301,7 @@ int launch_mx2_phase(const uint8_t* blocks_k128, const uint8_t* act_q, int64_t r
   const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
   const int grid = int(items < sm_count() ? items : sm_count());
   if (grid <= 0) return KLC_OK;
-  mx2_expert_kernel<PHASE, C><<<grid, C::THREADS, smem, stream>>>(ma, mb, p);
+  KLC_CUDA(launch_chain(mx2_expert_kernel<PHASE, C>, dim3(grid), dim3(C::THREADS), size_t(smem), stream, 0u, ma, mb, p));
   KLC_LAUNCH_CHECK("tcgen05 expert launch");
   return KLC_OK;
 }
@@ -1371,7 +1377,7 @@ int launch_mx3_phase(const uint8_t* blocks_k128, const uint8_t* act_q, int64_t r
   const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
   const int grid = int(items < sm_count() ? items : sm_count());
   if (grid <= 0) return KLC_OK;
-  mx3_expert_kernel<PHASE, C><<<grid, C::THREADS, smem, stream>>>(mw, mx, p);
+  KLC_CUDA(launch_chain(mx3_expert_kernel<PHASE, C>, dim3(grid), dim3(C::THREADS), size_t(smem), stream, 0u, mw, mx, p));
   KLC_LAUNCH_CHECK("tcgen05 expert launch");
   return KLC_OK;
 }

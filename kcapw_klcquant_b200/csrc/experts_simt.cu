@@ -39,6 +39,8 @@ struct SimtParams {
 
 template <int PHASE>
 __global__ void __launch_bounds__(kRows) simt_expert_kernel(SimtParams p) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   extern __shared__ __align__(16) float xs[];  // [kTok][K]
   const int rb_index = blockIdx.y;
   if (rb_index >= p.status->rowblocks) return;
@@ -152,7 +154,7 @@ int launch_phase(const SimtParams& p, int max_rowblocks, cudaStream_t stream) {
   KLC_CUDA(cudaFuncSetAttribute(simt_expert_kernel<PHASE>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   dim3 grid(unsigned((p.n_out + kRows - 1) / kRows), unsigned(max_rowblocks));
   KLC_CHECK_ARG(max_rowblocks <= 65535, "SIMT expert path: too many row-blocks");
-  simt_expert_kernel<PHASE><<<grid, kRows, smem, stream>>>(p);
+  KLC_CUDA(launch_chain(simt_expert_kernel<PHASE>, dim3(grid), dim3(kRows), size_t(smem), stream, 0u, p));
   KLC_LAUNCH_CHECK("SIMT expert launch");
   return KLC_OK;
 }

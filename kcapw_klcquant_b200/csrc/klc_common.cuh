@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "klc_moe.h"
 
@@ -46,6 +47,47 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 int sm_count();
+
+// ---------------------------------------------------------------------------
+// programmatic dependent launch: the kernels of a layer's chain may be launched
+// while their predecessor still runs (launch latency and set-up overlap its
+// tail); each of them calls pdl_wait() before it reads anything the
+// predecessor wrote, and pdl_trigger() to let its own successor launch early.
+// Both are no-ops for a kernel launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();  // klc_set_pdl, default on
+
+// cudaLaunchKernelEx with the programmatic-serialization attribute (when enabled)
+// plus, for cluster_x >= 1, a cluster of cluster_x CTAs (0: no cluster launch)
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_chain(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                unsigned cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x >= 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = n > 0 ? attr : nullptr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // device status word (lives at the start of every workspace)

@@ -130,6 +130,8 @@ __global__ void __launch_bounds__(256)
     quantize_rows_kernel(const uint16_t* __restrict__ src, int64_t K, const int32_t* __restrict__ rows_map, int k,
                          const int4* __restrict__ rowblocks, const DeviceStatus* __restrict__ st, int nch,
                          uint8_t* __restrict__ q, uint8_t* __restrict__ sfb) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   const int rbi = blockIdx.x;
   if (rbi >= st->rowblocks) return;
   const int4 rb = rowblocks[rbi];
@@ -172,7 +174,7 @@ int launch_quantize_rows(const uint16_t* src, int64_t K, const int32_t* rows_map
                          cudaStream_t stream) {
   KLC_CHECK_ARG(K % 32 == 0, "quantize: K must be a multiple of 32");
   if (max_rowblocks <= 0) return KLC_OK;
-  quantize_rows_kernel<<<max_rowblocks, 256, 0, stream>>>(src, K, rows_map, k, rowblocks, status, nch, q, sfb);
+  KLC_CUDA(launch_chain(quantize_rows_kernel, dim3(max_rowblocks), dim3(256), size_t(0), stream, 0u, src, K, rows_map, k, rowblocks, status, nch, q, sfb));
   KLC_LAUNCH_CHECK("activation quantize launch");
   return KLC_OK;
 }

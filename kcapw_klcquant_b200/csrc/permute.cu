@@ -31,6 +31,8 @@ constexpr int kChunk = 1024;
 
 __global__ void __launch_bounds__(kChunk)
     hist_kernel(const int32_t* __restrict__ idx, int64_t pairs, int experts, int div, int32_t* __restrict__ chunk_hist) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   extern __shared__ int32_t hist[];
   for (int e = threadIdx.x; e < experts; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -77,6 +79,8 @@ __global__ void __launch_bounds__(1024)
     scan_kernel(int32_t* __restrict__ chunk_hist, int nchunks, int experts, int pad, int block_n,
                 int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
                 int4* __restrict__ rowblocks, DeviceStatus* st) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   __shared__ int tmp[33];
   const int e = threadIdx.x;
   int cnt = 0;
@@ -113,6 +117,8 @@ __global__ void __launch_bounds__(kChunk)
                           int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x, int64_t hidden,
                           uint16_t* __restrict__ xp, int div, int32_t* __restrict__ aux_out,
                           int split, int empty_ok, DeviceStatus* st) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                      // [32][experts]
   int32_t* s_pos = sm + 32 * experts;          // [kChunk]
@@ -189,6 +195,8 @@ __global__ void __launch_bounds__(kChunk)
                          int4* __restrict__ rowblocks, int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x,
                          int64_t hidden, uint16_t* __restrict__ xp, int div, int32_t* __restrict__ aux_out,
                          int split, int empty_ok, DeviceStatus* st) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   extern __shared__ int32_t sm[];
   int32_t* warp_cnt = sm;                    // [32][experts]
   int32_t* total = warp_cnt + 32 * experts;  // [experts]
@@ -321,22 +329,22 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
   if (pairs <= kFusedPairs) {
     const size_t smem = (size_t(32) * E + 2 * E + 2 * kChunk) * sizeof(int32_t);
     KLC_CUDA(cudaFuncSetAttribute(fused_permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-    fused_permute_kernel<<<unsigned(int64_t(nchunks) * split), kChunk, smem, stream>>>(
+    KLC_CUDA(launch_chain(fused_permute_kernel, dim3(unsigned(int64_t(nchunks) * split)), dim3(kChunk), size_t(smem), stream, 0u, 
         a.idx, pairs, a.k, E, a.pad, a.block_n, a.counts, a.offsets, a.rows, a.rowblocks, a.pair_pos, a.x, a.hidden,
-        a.xp, div, a.aux_out, split, a.empty_ok ? 1 : 0, a.status);
+        a.xp, div, a.aux_out, split, a.empty_ok ? 1 : 0, a.status));
     KLC_LAUNCH_CHECK("permute (fused) launch");
     return KLC_OK;
   }
-  hist_kernel<<<nchunks, kChunk, E * sizeof(int32_t), stream>>>(a.idx, pairs, E, div, a.chunk_hist);
+  KLC_CUDA(launch_chain(hist_kernel, dim3(nchunks), dim3(kChunk), size_t(E * sizeof(int32_t)), stream, 0u, a.idx, pairs, E, div, a.chunk_hist));
   KLC_LAUNCH_CHECK("permute hist launch");
-  scan_kernel<<<1, 1024, 0, stream>>>(a.chunk_hist, nchunks, E, a.pad, a.block_n, a.counts, a.offsets, a.rows,
-                                      a.rowblocks, a.status);
+  KLC_CUDA(launch_chain(scan_kernel, dim3(1), dim3(1024), size_t(0), stream, 0u, a.chunk_hist, nchunks, E, a.pad, a.block_n, a.counts, a.offsets, a.rows,
+                                      a.rowblocks, a.status));
   KLC_LAUNCH_CHECK("permute scan launch");
   const size_t smem = (size_t(32) * E + 2 * kChunk) * sizeof(int32_t);
   KLC_CUDA(cudaFuncSetAttribute(scatter_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  scatter_gather_kernel<<<unsigned(int64_t(nchunks) * split), kChunk, smem, stream>>>(
+  KLC_CUDA(launch_chain(scatter_gather_kernel, dim3(unsigned(int64_t(nchunks) * split)), dim3(kChunk), size_t(smem), stream, 0u, 
       a.idx, pairs, a.k, E, a.chunk_hist, a.rows, a.pair_pos, a.x, a.hidden, a.xp, div, a.aux_out, split,
-      a.empty_ok ? 1 : 0, a.status);
+      a.empty_ok ? 1 : 0, a.status));
   KLC_LAUNCH_CHECK("permute scatter launch");
   return KLC_OK;
 }

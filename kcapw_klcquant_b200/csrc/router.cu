@@ -91,6 +91,8 @@ __global__ void __launch_bounds__(kWarps * 32)
     router_kernel(const uint16_t* __restrict__ x, int64_t tokens, int64_t hidden, const uint16_t* __restrict__ w,
                   const uint16_t* __restrict__ b, int experts, int k, int epc, const float* __restrict__ adjust,
                   int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int C = int(cluster.num_blocks());
@@ -160,6 +162,8 @@ __global__ void __launch_bounds__(256, 1)
     router_tc_kernel(const uint16_t* __restrict__ x, int64_t tokens, int64_t hidden, const uint16_t* __restrict__ w,
                      const uint16_t* __restrict__ b, int experts, int k, const float* __restrict__ adjust,
                      int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   namespace cg = cooperative_groups;
   using namespace tc;
   cg::cluster_group cluster = cg::this_cluster();
@@ -298,19 +302,7 @@ int launch_router_tc(const uint16_t* x, int64_t tokens, int64_t hidden, const ui
   KLC_CHECK_ARG(tiles * C <= 0x7fffffff, "klc_router_topk: too many tokens");
   const size_t smem = 6 * 16384 + 6 * NT * 128 + 1024;
   KLC_CUDA(cudaFuncSetAttribute(router_tc_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(tiles * C));
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(C);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  KLC_CUDA(cudaLaunchKernelEx(&cfg, router_tc_kernel<NT>, x, tokens, hidden, w, b, experts, k, adjust, out_idx, out_w,
+  KLC_CUDA(launch_chain(router_tc_kernel<NT>, dim3(unsigned(tiles * C)), dim3(256), size_t(smem), stream, unsigned(C), x, tokens, hidden, w, b, experts, k, adjust, out_idx, out_w,
                               out_logits));
   KLC_LAUNCH_CHECK("klc_router_topk launch");
   return KLC_OK;
@@ -346,6 +338,8 @@ __global__ void __launch_bounds__(kRgThreads, 1)
     router_gemm_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w, int64_t tokens,
                        int64_t hidden, const uint16_t* __restrict__ b, int experts, int k, const float* __restrict__ adjust,
                        int32_t* __restrict__ out_idx, uint16_t* __restrict__ out_w, uint16_t* __restrict__ out_logits) {
+  pdl_wait();     // inputs written by the previous kernel of the chain
+  pdl_trigger();  // the next kernel may launch and set up meanwhile
   namespace cg = cooperative_groups;
   using namespace tc;
   using Lay = RgLayout<EP>;
@@ -589,19 +583,7 @@ int launch_router_gemm_ep(const CUtensorMap& mx, const CUtensorMap& mw, int64_t 
   if (tiles * 8 <= 15 * 8 && tiles * 8 <= sms && nk >= 8) C = 8;
   else if (tiles * 4 <= sms && nk >= 4) C = 4;  // pairs measured slower than whole tiles (86 against ~72 us at 64 tiles)
   KLC_CHECK_ARG(tiles * C <= 0x7fffffff, "klc_router_topk: too many tokens");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(tiles * C));
-  cfg.blockDim = dim3(kRgThreads);
-  cfg.dynamicSmemBytes = size_t(smem);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(C);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  KLC_CUDA(cudaLaunchKernelEx(&cfg, router_gemm_kernel<EP>, mx, mw, tokens, hidden, b, experts, k, adjust, out_idx, out_w,
+  KLC_CUDA(launch_chain(router_gemm_kernel<EP>, dim3(unsigned(tiles * C)), dim3(kRgThreads), size_t(size_t(smem)), stream, unsigned(C), mx, mw, tokens, hidden, b, experts, k, adjust, out_idx, out_w,
                               out_logits));
   KLC_LAUNCH_CHECK("klc_router_topk launch");
   return KLC_OK;
@@ -668,19 +650,7 @@ int launch_router(const uint16_t* x, int64_t tokens, int64_t hidden, const uint1
   KLC_CHECK_ARG(smem <= 200 * 1024, "klc_router_topk: hidden size too large for one CTA tile");
   KLC_CUDA(cudaFuncSetAttribute(router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   KLC_CHECK_ARG(nblocks * C <= 0x7fffffff, "klc_router_topk: too many tokens");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(nblocks * C));
-  cfg.blockDim = dim3(kWarps * 32);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = unsigned(C);
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  KLC_CUDA(cudaLaunchKernelEx(&cfg, router_kernel, x, tokens, hidden, w, b, int(experts), k, epc, adjust, out_idx,
+  KLC_CUDA(launch_chain(router_kernel, dim3(unsigned(nblocks * C)), dim3(kWarps * 32), size_t(smem), stream, unsigned(C), x, tokens, hidden, w, b, int(experts), k, epc, adjust, out_idx,
                               out_w, out_logits));
   KLC_LAUNCH_CHECK("klc_router_topk launch");
   return KLC_OK;
