@@ -292,55 +292,110 @@ class StreamedMoERouter:
         with torch.cuda.device(dev):
             _lib.check(_lib.lib().klc_router_topk(x.data_ptr(), 1, H, w_dev.data_ptr(), b_dev.data_ptr(), E, k, None,
                                                   idx.data_ptr(), wts.data_ptr(), logits.data_ptr(), _lib.stream_ptr()))
-        blocked = False
-        update_state = True
-        if cfg.enabled and self.locality_on_device:
-            # the whole policy on the device: one readback of the token's decisions
+        gu_b = tensors.get(f"{p}.experts.gate_up_proj_bias")
+        dn_b = tensors.get(f"{p}.experts.down_proj_bias")
+        if not cfg.enabled or self.locality_on_device:
+            return self._route_on_device(layer_idx, hidden, x, tensors, expert_store, execute_experts, position, predicted_experts,
+                                         resident_experts, logits, idx, wts, k, gu_b, dn_b)
+        # host locality policy (locality_on_device=False): the logits come to the host first
+        raw_experts, experts, scores, blocked = self._locality_select(layer_idx, logits[0].float().cpu(), k, resident_experts or set())
+        sc = torch.tensor(scores, dtype=torch.float32, device=dev).reshape(1, k)
+        idx = torch.tensor([experts], dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib().klc_select_softmax(sc.data_ptr(), 1, k, k, 1, None, wts.data_ptr(), _lib.stream_ptr()))
+        weights_list = [float(v) for v in wts[0].float().tolist()]
+        predicted, resident, adjusted_flag = self._record_route(layer_idx, position, experts, weights_list, raw_experts, blocked,
+                                                                predicted_experts, resident_experts, k)
+        norms_list = None
+        y = None
+        store_path = execute_experts and expert_store is not None
+        if store_path and gu_b is not None and dn_b is not None:
+            layer = self._moe_layer(layer_idx, tensors, expert_store, k)
+            y, norms = layer.experts_forward(x, idx, wts, precision=self.matmul_precision, return_norms=True)
+            norms_list = norms[0].tolist()
+        elif not store_path and dn_b is not None:
+            y = self._bias_only(x, tensors, p, idx, wts, k)
+        return self._finish_route(layer_idx, hidden, expert_store, execute_experts, position, experts, weights_list, raw_experts,
+                                  predicted, resident, adjusted_flag, k, y, norms_list, gu_b, dn_b, tensors, p)
+
+    def _bias_only(self, x: torch.Tensor, tensors, p: str, idx: torch.Tensor, wts: torch.Tensor, k: int) -> torch.Tensor:
+        dev = x.device
+        H = int(x.shape[-1])
+        db = as_bf16(tensors[f"{p}.experts.down_proj_bias"], dev)
+        y = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.lib().klc_moe_bias_only(db.data_ptr(), 1, H, k, idx.data_ptr(), wts.data_ptr(), y.data_ptr(), _lib.stream_ptr()))
+        return y
+
+    def _route_on_device(self, layer_idx, hidden, x, tensors, expert_store, execute_experts, position, predicted_experts,
+                         resident_experts, logits, idx, wts, k, gu_b, dn_b):
+        """route() with the selection on the device (plain top-k, or the locality kernel): the
+        experts (or the bias-only path) are launched on the device routing right away, and the
+        routing, the locality outputs and the expert norms come back in one copy; the host-side
+        steps (statistics, policy bookkeeping, expert-cache accounting) then run in the
+        reference's order on those values."""
+        p = f"model.layers.{layer_idx}.mlp"
+        dev = x.device
+        E = int(logits.shape[1])
+        loc = self.locality_config.enabled
+        pol = None
+        if loc:
             pol = self._device_policy(layer_idx, logits, k, self._resident_mask(resident_experts, E, dev), 0)
             idx, wts = pol["experts"], pol["weights"]
-            host = torch.cat([pol["experts"].reshape(-1).double(), pol["raw"].reshape(-1).double(), pol["pred"].reshape(-1).double(),
-                              pol["npred"].double(), pol["flags"].double(), pol["weights"].reshape(-1).double()]).cpu().tolist()
-            experts = [int(v) for v in host[:k]]
-            raw_experts = [int(v) for v in host[k:2 * k]]
-            npred = int(host[3 * k])
+        store_path = execute_experts and expert_store is not None
+        y, norms = None, None
+        if store_path and gu_b is not None and dn_b is not None:
+            layer = self._moe_layer(layer_idx, tensors, expert_store, k)
+            y, norms = layer.experts_forward(x, idx, wts, precision=self.matmul_precision, return_norms=True)
+        elif not store_path and dn_b is not None:
+            y = self._bias_only(x, tensors, p, idx, wts, k)
+        parts = [idx.reshape(-1).double(), wts.reshape(-1).double()]
+        if loc:
+            parts += [pol["raw"].reshape(-1).double(), pol["pred"].reshape(-1).double(), pol["npred"].double(), pol["flags"].double()]
+        if norms is not None:
+            parts.append(norms.reshape(-1).double())
+        host = torch.cat(parts).cpu().tolist()  # the one synchronisation of the call
+        experts = [int(v) for v in host[:k]]
+        weights_list = [float(v) for v in host[k:2 * k]]
+        at = 2 * k
+        blocked = False
+        if loc:
+            raw_experts = [int(v) for v in host[at:at + k]]
+            npred = int(host[at + 2 * k])
             if predicted_experts is None:
-                predicted_experts = [int(v) for v in host[2 * k:2 * k + npred]]
-            blocked = bool(int(host[3 * k + 1]) & 1)
-            weights_list = [float(v) for v in host[3 * k + 2:]]
-            update_state = False  # the kernel already advanced the layer's policy state
+                predicted_experts = [int(v) for v in host[at + k:at + k + npred]]
+            blocked = bool(int(host[at + 2 * k + 1]) & 1)
+            at += 2 * k + 2
         else:
-            raw_experts = [int(v) for v in idx[0].tolist()]
-            if cfg.enabled:
-                raw_experts, experts, scores, blocked = self._locality_select(layer_idx, logits[0].float().cpu(), k, resident_experts or set())
-                sc = torch.tensor(scores, dtype=torch.float32, device=dev).reshape(1, k)
-                idx = torch.tensor([experts], dtype=torch.int32, device=dev)
-                with torch.cuda.device(dev):
-                    _lib.check(_lib.lib().klc_select_softmax(sc.data_ptr(), 1, k, k, 1, None, wts.data_ptr(), _lib.stream_ptr()))
-            else:
-                experts = raw_experts
-            weights_list = [float(v) for v in wts[0].float().tolist()]
+            raw_experts = list(experts)
+        norms_list = None
+        if norms is not None:
+            flat = host[at:at + 2 * k]
+            norms_list = [[flat[2 * i], flat[2 * i + 1]] for i in range(k)]
+        # the device kernel already advanced the layer's locality state
         predicted, resident, adjusted_flag = self._record_route(layer_idx, position, experts, weights_list, raw_experts, blocked,
-                                                                predicted_experts, resident_experts, k, update_state)
+                                                                predicted_experts, resident_experts, k, update_state=not loc)
+        return self._finish_route(layer_idx, hidden, expert_store, execute_experts, position, experts, weights_list, raw_experts,
+                                  predicted, resident, adjusted_flag, k, y, norms_list, gu_b, dn_b, tensors, p)
 
+    def _finish_route(self, layer_idx, hidden, expert_store, execute_experts, position, experts, weights_list, raw_experts,
+                      predicted, resident, adjusted_flag, k, y, norms_list, gu_b, dn_b, tensors, p):
+        """The route() dict and the expert-store bookkeeping, in the reference's order (:303-329)."""
         if execute_experts and expert_store is not None:
             before = self._cache_snapshot(expert_store)
             expert_store.protect_experts(layer_idx, experts)
-            gu_b = tensors.get(f"{p}.experts.gate_up_proj_bias")
-            dn_b = tensors.get(f"{p}.experts.down_proj_bias")
             if gu_b is None or dn_b is None:
                 output, route = torch.zeros_like(hidden), {"experts": experts, "weights": weights_list, "mode": "mxfp4_missing_bias"}
             else:
                 expert_store.note_expert_use(layer_idx, experts)  # the reference's two load_expert_matrix calls per expert
-                layer = self._moe_layer(layer_idx, tensors, expert_store, k)
-                y, norms = layer.experts_forward(x, idx, wts, precision=self.matmul_precision, return_norms=True)
                 output = y.reshape(hidden.shape).to(hidden.dtype)
-                nl = norms[0].tolist()
                 route = {
                     "experts": experts,
                     "weights": weights_list,
                     "mode": "mxfp4_expert_matmul",
                     "expert_logs": [
-                        {"expert": int(e), "routing_weight": weights_list[i], "gate_up_norm": float(nl[i][0]), "output_norm": float(nl[i][1])}
+                        {"expert": int(e), "routing_weight": weights_list[i], "gate_up_norm": float(norms_list[i][0]),
+                         "output_norm": float(norms_list[i][1])}
                         for i, e in enumerate(experts)
                     ],
                 }
@@ -351,14 +406,8 @@ class StreamedMoERouter:
             route["sticky_adjusted"] = adjusted_flag
             route["active_expert_cap"] = k
             return output, route
-
-        down_bias = tensors.get(f"{p}.experts.down_proj_bias")
-        if down_bias is None:
+        if dn_b is None:
             return torch.zeros_like(hidden), {"experts": experts, "weights": weights_list, "mode": "router_only"}
-        db = as_bf16(down_bias, dev)
-        y = torch.empty((1, H), dtype=torch.bfloat16, device=dev)
-        with torch.cuda.device(dev):
-            _lib.check(_lib.lib().klc_moe_bias_only(db.data_ptr(), 1, H, k, idx.data_ptr(), wts.data_ptr(), y.data_ptr(), _lib.stream_ptr()))
         return y.reshape(hidden.shape).to(hidden.dtype), {
             "experts": experts,
             "raw_experts": raw_experts,
