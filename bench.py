@@ -836,12 +836,18 @@ def main():
     ap.add_argument("--exchange", choices=["p2p", "nccl"], default="p2p", help="N>1: the expert-parallel exchange")
     ap.add_argument("--fused-return", choices=["auto", "on", "off"], default="auto",
                     help="N>1 p2p: expert outputs stored to the source ranks by the down epilogue (auto: 2 ranks)")
+    ap.add_argument("--pair-tiles", type=int, choices=[0, 1, 2], default=1,
+                    help="two-SM expert tiles: 0 never, 1 from 192 rows per expert (default), 2 always")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.tokens is None:
         args.tokens = {"decode": 256, "prefill": 4096, "ep": 16384, "stack": 32}[args.workload]
     world, rank, local = dist_setup(use_gpu=args.impl != "reference")
+    if args.impl != "reference":
+        from kcapw_klcquant_b200 import _lib
+
+        _lib.check(_lib.lib().klc_set_pair_tiles(args.pair_tiles))
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)

@@ -99,6 +99,13 @@ int klc_struct_size(int which, size_t* out_bytes);
  * launch, so each launches while its predecessor finishes; 0: plain stream
  * order.  Results are identical either way; process-wide. */
 int klc_set_pdl(int enable);
+/* Two-SM expert tiles (tensor-core path, weights-as-N kernels, 64-row
+ * blocks): a pair of SMs computes two consecutive row-blocks of one expert
+ * with one 256-row block-scaled MMA, each SM loading half of the weight
+ * tile.  mode 0: never; 1 (the default): when the layer averages at least
+ * 192 rows per expert; 2: whenever the 64-row kernels run.  The layer
+ * output is identical in every mode; process-wide. */
+int klc_set_pair_tiles(int mode);
 
 /* ---- MXFP4 dequant ---------------------------------------------------- *
  * Replaces dequantize_mxfp4_matrix(blocks, scales, dtype)

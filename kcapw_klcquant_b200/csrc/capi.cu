@@ -72,12 +72,20 @@ extern "C" int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes) {
 namespace klc {
 namespace {
 std::atomic<bool> g_pdl{true};
+std::atomic<int> g_pair_tiles{0};
 }  // namespace
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+int pair_tiles_mode() { return g_pair_tiles.load(std::memory_order_relaxed); }
 }  // namespace klc
 
 extern "C" int klc_set_pdl(int enable) {
   klc::g_pdl.store(enable != 0, std::memory_order_relaxed);
+  return KLC_OK;
+}
+
+extern "C" int klc_set_pair_tiles(int mode) {
+  if (mode < 0 || mode > 2) return klc::fail(KLC_ERR_INVALID, "klc_set_pair_tiles: mode must be 0, 1 or 2");
+  klc::g_pair_tiles.store(mode, std::memory_order_relaxed);
   return KLC_OK;
 }
 

@@ -907,9 +907,20 @@ constexpr int kWN = 192;
 //   EPI epilogue warpgroups (warps 4-7, 12-15): warpgroup g takes the 16-column
 //       chunks c with c % EPI == g, so a decode tile (all tokens in lane quarter 0)
 //       is still read by EPI warps at once
-template <int BN_, int NS_, int ND_, int SK_, int PF_, int EPI_ = 2>
+//   PAIR two-SM tiles: a cluster of two CTAs computes a paired row-block (two
+//       consecutive 64-row blocks of one expert) with one M = 256 MMA
+//       (cta_group::2) issued by the even CTA: each CTA loads its own 64 tokens
+//       (A rows 0-127 / 128-255) and half of the weight tile (B rows 0-95 /
+//       96-191), so every weight byte an SM loads feeds twice the rows; both
+//       CTAs hold the full 128 x 192 accumulator of their own rows and all
+//       weight scales, and each runs its own epilogue
+template <int BN_, int NS_, int ND_, int SK_, int PF_, int EPI_ = 2, int PAIR_ = 0>
 struct Mx3Cfg {
   static constexpr int BN = BN_, NS = NS_, ND = ND_, SK = SK_, PF = PF_, EPI = EPI_;
+  static constexpr bool PAIR = PAIR_ != 0;
+  static_assert(!PAIR || BN == 64, "two-SM tiles take 64 tokens per CTA");
+  static constexpr int CTAS = PAIR ? 2 : 1;
+  static constexpr int WNB = kWN / CTAS;             // weight rows one CTA loads per tile
   static constexpr int N2 = 2 * BN;
   static_assert(N2 <= 128, "activation rows fit the MMA's 128 lanes");
   static_assert(EPI == 1 || EPI == 2, "epilogue warpgroups");
@@ -917,7 +928,7 @@ struct Mx3Cfg {
   static_assert(SK == 128 || SK == 256, "stage K");
   static constexpr int THREADS = (EPI == 2 ? 16 : 12) * 32;
   static constexpr int ABOX = N2 * 128;              // activation box (= its transaction bytes)
-  static constexpr int BBOX = kWN * 128;             // weight box in shared memory (16-byte groups)
+  static constexpr int BBOX = WNB * 128;             // weight box in shared memory (16-byte groups)
   static constexpr int BBOX_TX = BBOX / 2;           // ... counted as the packed bytes read
   static constexpr int ASLOT = SUB * ABOX, BSLOT = SUB * BBOX;
   static constexpr int OFF_B = 0;
@@ -939,10 +950,73 @@ struct Mx3Cfg {
 };
 
 // kind::mxf8f6f4 instruction descriptor: A E4M3 (activations), B E2M1 (weights),
-// fp32 accumulate, both K-major, E8M0 scales, M = 128, N = kWN; scale byte ids.
+// fp32 accumulate, both K-major, E8M0 scales, M = 128 (256 for a CTA pair),
+// N = kWN; scale byte ids.
+template <int M>
 __device__ __forceinline__ uint32_t mx3_idesc(uint32_t a_id, uint32_t b_id) {
-  return (b_id << 4) | (0u << 7) | (5u << 10) | (uint32_t(kWN >> 3) << 17) | (1u << 23) | (uint32_t(kBM >> 4) << 24) |
+  return (b_id << 4) | (0u << 7) | (5u << 10) | (uint32_t(kWN >> 3) << 17) | (1u << 23) | (uint32_t(M >> 4) << 24) |
          (a_id << 29);
+}
+
+// The two-SM forms of the MMA and of its commits (issued by the even CTA of
+// the pair; the commit arrives on the barrier at the same offset in every CTA
+// of `mask`).
+__device__ __forceinline__ void mx_mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb));
+}
+
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+               "h"(mask)
+               : "memory");
+}
+
+// Address of the same shared-memory variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+// Arrive on a barrier of another CTA of the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// wait_bar for barriers that CTAs of the cluster arrive on (acquire at cluster scope)
+__device__ __forceinline__ bool wait_bar_cluster(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 63) == 0) {
+      if (*c.abort) return false;
+      if (clock64() - t0 > kWaitCycles) {
+        *c.abort = 1;
+        record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 template <int PHASE, class C>
@@ -966,33 +1040,51 @@ __global__ void __launch_bounds__(C::THREADS, 1)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   const Ctl ctl{abort_flag, p.status};
+  // CTA pair: rank 0 issues the MMAs; sready and dempty of rank 0 count the
+  // arrivals of both CTAs, the other barriers are per CTA
+  uint32_t crank = 0;
+  if constexpr (C::PAIR) asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  const int cid = C::PAIR ? int(blockIdx.x >> 1) : int(blockIdx.x);
+  const int ncl = C::PAIR ? int(gridDim.x >> 1) : int(gridDim.x);
+  auto arrive_lead = [&](uint32_t bar) {
+    if constexpr (C::PAIR) mbar_arrive_cluster(cluster_addr(bar, 0));
+    else mbar_arrive(bar);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NS; ++s) {
       mbar_init(wfull(s), 1);
       mbar_init(xfull(s), 1);
-      mbar_init(sready(s), 4);
+      mbar_init(sready(s), 4 * C::CTAS);
       mbar_init(sempty(s), 1);
     }
     for (int d = 0; d < ND; ++d) {
       mbar_init(dfull(d), 1);
-      mbar_init(dempty(d), 4 * C::EPI);
+      mbar_init(dempty(d), 4 * C::EPI * C::CTAS);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == kWarp2Mma) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (C::PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (C::PAIR) cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
-  const int nrb = p.status->rowblocks;
-  const int total = nrb * p.n_mtiles;  // items: (row-block, 192-row weight tile)
+  // items: (row-block, 192-row weight tile); for a pair, (paired row-block, tile)
+  const int nrb = C::PAIR ? p.status->pairblocks : p.status->rowblocks;
+  const int total = nrb * p.n_mtiles;
   const int kb128 = p.ksteps;
   const int st_n = (kb128 + SUB - 1) / SUB;
 
@@ -1001,21 +1093,21 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0, boxes = 0;
       bool ok = true;
-      int pf_item = blockIdx.x, pf_k = 0;
+      int pf_item = cid, pf_k = 0;
       uint32_t pf_n = 0;
       int4 pf_rb = pf_item < total ? p.rowblocks[pf_item / p.n_mtiles] : make_int4(0, 0, 0, 0);
       auto prefetch_ahead = [&](uint32_t upto) {
         while (pf_n < upto && pf_item < total) {
-          tma_prefetch_3d(&map_w, pf_k * 128, (pf_item % p.n_mtiles) * kWN, pf_rb.x);
+          tma_prefetch_3d(&map_w, pf_k * 128, (pf_item % p.n_mtiles) * kWN + int(crank) * C::WNB, pf_rb.x);
           ++pf_n;
           if (++pf_k == kb128) {
             pf_k = 0;
-            pf_item += gridDim.x;
+            pf_item += ncl;
             if (pf_item < total) pf_rb = p.rowblocks[pf_item / p.n_mtiles];
           }
         }
       };
-      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+      for (int item = cid; item < total && ok; item += ncl) {
         const int4 rb = p.rowblocks[item / p.n_mtiles];
         const int nt = item % p.n_mtiles;
         const uint8_t* sfw_item = p.sfa + (int64_t(rb.x) * p.n_mtiles + nt) * int64_t(kb128) * 1024;
@@ -1026,8 +1118,8 @@ __global__ void __launch_bounds__(C::THREADS, 1)
           const int nb = min(SUB, kb128 - ks * SUB);
           mbar_arrive_expect_tx(wfull(s), uint32_t(nb * (C::BBOX_TX + 1024)));
           for (int j = 0; j < nb; ++j)
-            tma_load_3d(smem_u32(smem + C::OFF_B + s * C::BSLOT + j * C::BBOX), &map_w, (ks * SUB + j) * 128, nt * kWN, rb.x,
-                        wfull(s));
+            tma_load_3d(smem_u32(smem + C::OFF_B + s * C::BSLOT + j * C::BBOX), &map_w, (ks * SUB + j) * 128,
+                        nt * kWN + int(crank) * C::WNB, rb.x, wfull(s));
           bulk_load(smem_u32(smem + C::OFF_BSF + s * SUB * 1024), sfw_item + int64_t(ks * SUB) * 1024, uint32_t(nb * 1024),
                     wfull(s));
           boxes += uint32_t(nb);
@@ -1040,17 +1132,24 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     if (lane == 0) {
       uint32_t it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+      for (int item = cid; item < total && ok; item += ncl) {
         const int rbi = item / p.n_mtiles;
         const int4 rb = p.rowblocks[rbi];
-        const uint8_t* sfx_rb = p.sfb + int64_t(rbi) * kb128 * 512;
+        // a pair's CTA takes the pair's row-block rb.w + crank (64 rows), which may be empty
+        const int row0 = rb.y + int(crank) * 64;
+        const bool load = !C::PAIR || rb.z > int(crank) * 64;
+        const uint8_t* sfx_rb = p.sfb + int64_t(C::PAIR ? rb.w + int(crank) : rbi) * kb128 * 512;
         for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
           const int s = int(it % NS);
           if (!(ok = wait_bar(sempty(s), ((it / NS) & 1) ^ 1, ctl, 81))) break;
           const int nb = min(SUB, kb128 - ks * SUB);
+          if (!load) {  // no rows: the stage completes without data (its lanes are never read)
+            mbar_arrive(xfull(s));
+            continue;
+          }
           mbar_arrive_expect_tx(xfull(s), uint32_t(nb * (C::ABOX + 512)));
           for (int j = 0; j < nb; ++j)
-            tma_load_2d(smem_u32(smem + C::OFF_A + s * C::ASLOT + j * C::ABOX), &map_x, (ks * SUB + j) * kStageK, 2 * rb.y,
+            tma_load_2d(smem_u32(smem + C::OFF_A + s * C::ASLOT + j * C::ABOX), &map_x, (ks * SUB + j) * kStageK, 2 * row0,
                         xfull(s));
           bulk_load(smem_u32(smem + C::OFF_ASF + s * SUB * 512), sfx_rb + int64_t(ks * SUB) * 512, uint32_t(nb * 512),
                     xfull(s));
@@ -1063,7 +1162,7 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     const int q = warp & 3;
     uint32_t it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+    for (int item = cid; item < total && ok; item += ncl) {
       for (int ks = 0; ks < st_n; ++ks, ++it) {
         const int s = int(it % NS);
         const uint32_t ph = (it / NS) & 1;
@@ -1082,22 +1181,26 @@ __global__ void __launch_bounds__(C::THREADS, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(sready(s));
+        if (lane == 0) arrive_lead(sready(s));
       }
     }
   } else if (warp == kWarp2Mma) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (rank 0 of a pair)
+    if (lane == 0 && crank == 0) {
       uint32_t it = 0, ic = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+      for (int item = cid; item < total && ok; item += ncl, ++ic) {
         const int d = ic % ND;
         const uint32_t d_tmem = tmem + uint32_t(d * kWN);
-        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 90))) break;
+        if constexpr (C::PAIR) ok = wait_bar_cluster(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 90);
+        else ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 90);
+        if (!ok) break;
         tc_fence_after();
         for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
           const int s = int(it % NS);
-          if (!(ok = wait_bar(sready(s), (it / NS) & 1, ctl, 91))) break;
+          if constexpr (C::PAIR) ok = wait_bar_cluster(sready(s), (it / NS) & 1, ctl, 91);
+          else ok = wait_bar(sready(s), (it / NS) & 1, ctl, 91);
+          if (!ok) break;
           tc_fence_after();
           const uint32_t sf_t = tmem + uint32_t(C::ACC_COLS + s * C::SF_COLS);
           const uint64_t xdesc0 = sw128_desc(smem_u32(smem + C::OFF_A + s * C::ASLOT));
@@ -1107,16 +1210,24 @@ __global__ void __launch_bounds__(C::THREADS, 1)
           for (int kk = 0; kk < 4 * SUB; ++kk) {
             if (kk < kk_n) {
               const int j = kk >> 2, kb = kk & 3;
-              mx_mma(d_tmem, xdesc0 + uint64_t(j * (C::ABOX >> 4) + kb * 2), wdesc0 + uint64_t(j * (C::BBOX >> 4) + kb * 2),
-                     mx3_idesc(uint32_t(kb), uint32_t(kb)), (sf_t + 12 * j) | (uint32_t(kb) << 30),
-                     (sf_t + 12 * j + 4) | (uint32_t(kb) << 30), (ks == 0 && kk == 0) ? 0u : 1u);
+              const uint64_t xd = xdesc0 + uint64_t(j * (C::ABOX >> 4) + kb * 2);
+              const uint64_t wd = wdesc0 + uint64_t(j * (C::BBOX >> 4) + kb * 2);
+              const uint32_t sfa = (sf_t + 12 * j) | (uint32_t(kb) << 30), sfb = (sf_t + 12 * j + 4) | (uint32_t(kb) << 30);
+              const uint32_t acc = (ks == 0 && kk == 0) ? 0u : 1u;
+              if constexpr (C::PAIR) mx_mma_pair(d_tmem, xd, wd, mx3_idesc<256>(uint32_t(kb), uint32_t(kb)), sfa, sfb, acc);
+              else mx_mma(d_tmem, xd, wd, mx3_idesc<kBM>(uint32_t(kb), uint32_t(kb)), sfa, sfb, acc);
             }
           }
-          tc_commit(sempty(s));
+          if constexpr (C::PAIR) tc_commit_pair(sempty(s), 3);
+          else tc_commit(sempty(s));
         }
-        if (ok) tc_commit(dfull(d));
+        if (ok) {
+          if constexpr (C::PAIR) tc_commit_pair(dfull(d), 3);
+          else tc_commit(dfull(d));
+        }
       }
-      tc_commit(mma_done);
+      if constexpr (C::PAIR) tc_commit_pair(mma_done, 1);
+      else tc_commit(mma_done);
       drain_wait(mma_done, 0);
     }
   } else if ((warp >= kWarp2Epi0 && warp < kWarp2Epi0 + 4) || (C::EPI == 2 && warp >= kWarp2Epi2 && warp < kWarp2Epi2 + 4)) {
@@ -1127,10 +1238,12 @@ __global__ void __launch_bounds__(C::THREADS, 1)
     const int eg = warp >= kWarp2Epi2 ? 1 : 0;
     uint32_t ic = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++ic) {
+    for (int item = cid; item < total && ok; item += ncl, ++ic) {
       const int4 rb = p.rowblocks[item / p.n_mtiles];
       const int nt = item % p.n_mtiles;
-      const int e = rb.x, r0 = rb.y, nrows = rb.z;
+      // a pair's CTA holds the accumulators of its own 64 rows
+      const int e = rb.x, r0 = rb.y + int(crank) * 64;
+      const int nrows = C::PAIR ? max(0, min(64, rb.z - int(crank) * 64)) : rb.z;
       const int d = ic % ND;
       ok = wait_bar_backoff(dfull(d), (ic / ND) & 1, ctl, 92);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
@@ -1222,17 +1335,21 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(dempty(d));
+      if (lane == 0) arrive_lead(dempty(d));
     }
     // scattered rows (peer memory) visible system-wide before the kernel that raises the flags
     if (PHASE == 2 && p.sc.world > 0) __threadfence_system();
   }
 
   tc_fence_before();
-  __syncthreads();
+  // a pair: neither CTA leaves while the other's MMAs, arrivals or reads may still touch it
+  if constexpr (C::PAIR) cluster_sync_all();
+  else __syncthreads();
   tc_fence_after();
-  if (warp == kWarp2Mma)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  if (warp == kWarp2Mma) {
+    if constexpr (C::PAIR) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+    else asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -1361,7 +1478,7 @@ int launch_mx3_phase(const uint8_t* blocks_k128, const uint8_t* act_q, int64_t r
   {
     const uint64_t dims[3] = {Kp, N, uint64_t(experts)};
     const uint64_t strides[2] = {Kp / 2, N * Kp / 2};
-    const uint32_t box[3] = {128, uint32_t(kWN), 1};
+    const uint32_t box[3] = {128, uint32_t(C::WNB), 1};
     int st = make_map(&mw, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 3, blocks_k128, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (st != KLC_OK) return st;
   }
@@ -1374,7 +1491,37 @@ int launch_mx3_phase(const uint8_t* blocks_k128, const uint8_t* act_q, int64_t r
   }
   const int smem = (C::BYTES + 1024 > 118 * 1024) ? C::BYTES + 1024 : 118 * 1024;
   KLC_CUDA(cudaFuncSetAttribute(mx3_expert_kernel<PHASE, C>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;
+  const int64_t items = int64_t(max_rowblocks) * p.n_mtiles;  // an upper bound: the count is on the device
+  if constexpr (C::PAIR) {
+    // one persistent pair per two SMs, as many as can be resident at once
+    static int max_pairs = -1;
+    static std::once_flag once;
+    std::call_once(once, [&] {
+      cudaLaunchConfig_t cfg{};
+      cudaLaunchAttribute attr{};
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.gridDim = dim3(unsigned(2 * (sm_count() / 2)));
+      cfg.blockDim = dim3(C::THREADS);
+      cfg.dynamicSmemBytes = size_t(smem);
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, mx3_expert_kernel<PHASE, C>, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = sm_count() / 2;
+      }
+      max_pairs = n;
+    });
+    const int64_t pairs = items < max_pairs ? items : max_pairs;
+    if (pairs <= 0) return KLC_OK;
+    KLC_CUDA(launch_chain(mx3_expert_kernel<PHASE, C>, dim3(unsigned(2 * pairs)), dim3(C::THREADS), size_t(smem), stream, 2u,
+                          mw, mx, p));
+    KLC_LAUNCH_CHECK("tcgen05 expert launch (two-SM tiles)");
+    return KLC_OK;
+  }
   const int grid = int(items < sm_count() ? items : sm_count());
   if (grid <= 0) return KLC_OK;
   KLC_CUDA(launch_chain(mx3_expert_kernel<PHASE, C>, dim3(grid), dim3(C::THREADS), size_t(smem), stream, 0u, mw, mx, p));
@@ -1388,7 +1535,7 @@ int launch_mx3_both(const ExpertArgs& a, const uint8_t* gu_k128, const uint8_t* 
   MxParams p1{};
   p1.n_out = int(2 * a.inter);
   p1.k_in = int(a.hidden);
-  p1.rowblocks = a.rowblocks;
+  p1.rowblocks = C::PAIR ? a.pairblocks : a.rowblocks;
   p1.status = a.status_rw;
   p1.rows = a.rows;
   p1.sfa = w.gu_scales_t192;
@@ -1503,8 +1650,14 @@ using Mx2N64 = Mx2Cfg<KLC_MX2_N64>;
 #ifndef KLC_MX3_N64
 #define KLC_MX3_N64 64, 4, 2, 128, 0, 2
 #endif
+// Two-SM tiles (64 tokens per CTA, half of each weight tile per CTA):
+//                 BN  NS ND  SK  PF EPI PAIR
+#ifndef KLC_MX3_P64
+#define KLC_MX3_P64 64, 6, 2, 128, 0, 2, 1
+#endif
 using Mx3N16 = Mx3Cfg<KLC_MX3_N16>;
 using Mx3N64 = Mx3Cfg<KLC_MX3_N64>;
+using Mx3P64 = Mx3Cfg<KLC_MX3_P64>;
 
 }  // namespace
 
@@ -1591,7 +1744,9 @@ int launch_experts_tc(const ExpertArgs& a, cudaStream_t stream) {
   if (mx3_usable(w, a.hidden, a.inter)) {
     switch (a.block_n) {
       case 16: return launch_mx3_both<Mx3N16>(a, gu, dn, stream);
-      case 64: return launch_mx3_both<Mx3N64>(a, gu, dn, stream);
+      case 64:
+        if (a.pairblocks != nullptr) return launch_mx3_both<Mx3P64>(a, gu, dn, stream);
+        return launch_mx3_both<Mx3N64>(a, gu, dn, stream);
       default: return fail(KLC_ERR_INVALID, "tensor-core path: row-block size must be 16 or 64");
     }
   }

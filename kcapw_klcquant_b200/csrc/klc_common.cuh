@@ -59,6 +59,7 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 bool pdl_enabled();  // klc_set_pdl, default on
+int pair_tiles_mode();  // klc_set_pair_tiles: 0 never, 1 by rows per expert (default), 2 always
 
 // cudaLaunchKernelEx with the programmatic-serialization attribute (when enabled)
 // plus, for cluster_x >= 1, a cluster of cluster_x CTAs (0: no cluster launch)
@@ -97,6 +98,7 @@ struct DeviceStatus {
   int where;     // kernel-defined site id
   int detail;    // e.g. the bad index
   int rowblocks; // number of row-blocks the permute produced
+  int pairblocks; // number of paired row-blocks (two-SM tiles), when the permute built them
 };
 
 __device__ __forceinline__ void record_fault(DeviceStatus* st, int code, int where, int detail) {

@@ -28,6 +28,9 @@ void stage_mark(int stage, cudaStream_t stream) {
 namespace {
 
 constexpr int kPad = 16;  // rows of each expert group are padded to 16 (MMA N granularity)
+// two-SM tiles by default from this many routed rows per expert on average
+// (the row-block pairs of an expert then rarely have an empty half)
+constexpr int64_t kPairMinRows = 192;
 
 int pick_block_n(const klc_moe_dims& d, bool tc) {
   if (!tc) return 64;
@@ -78,6 +81,7 @@ WorkspaceLayout workspace_layout(const klc_moe_dims& d, bool need_routing_buffer
     L.gq = take(size_t(L.rows_cap) * 2 * d.intermediate);
     L.sfb1 = take(size_t(L.max_rowblocks) * size_t((d.hidden + 127) / 128) * nch * 512);
     L.sfb2 = take(size_t(L.max_rowblocks) * size_t((d.intermediate + 127) / 128) * nch * 512);
+    if (L.block_n == 64) L.pairblocks = take(size_t(L.max_rowblocks) * sizeof(int4));
   }
   if (need_routing_buffers) {
     L.idx = take(size_t(L.pairs) * 4);
@@ -136,6 +140,11 @@ int run_expert_stage(const klc_moe_dims& d, const klc_moe_weights& wts, const ui
   pa.empty_ok = empty_ok;
   // SIMT gathers bf16 rows here; the tensor-core path quantizes straight from x per row-block
   pa.xp = tc ? nullptr : reinterpret_cast<uint16_t*>(ws + L.xp);
+  // two-SM tiles: row-blocks paired by the permute (klc_set_pair_tiles)
+  const int pair_mode = pair_tiles_mode();
+  const int64_t rows_per_expert = d.tokens * d.top_k / std::max<int64_t>(d.experts, 1);
+  if (tc && L.pairblocks != 0 && (pair_mode == 2 || (pair_mode == 1 && rows_per_expert >= kPairMinRows)))
+    pa.pairblocks = reinterpret_cast<int4*>(ws + L.pairblocks);
   stage_mark(kStageRouted, stream);
   int st = launch_permute(pa, stream);
   if (st != KLC_OK) return st;
@@ -149,6 +158,7 @@ int run_expert_stage(const klc_moe_dims& d, const klc_moe_weights& wts, const ui
   ea.k = d.top_k;
   ea.precision = precision;
   ea.rowblocks = pa.rowblocks;
+  ea.pairblocks = pa.pairblocks;
   ea.max_rowblocks = int(L.max_rowblocks);
   ea.rows = pa.rows;
   ea.status = status;

@@ -78,7 +78,7 @@ __device__ int block_exclusive_scan(int v, int* tmp, int* total) {
 __global__ void __launch_bounds__(1024)
     scan_kernel(int32_t* __restrict__ chunk_hist, int nchunks, int experts, int pad, int block_n,
                 int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
-                int4* __restrict__ rowblocks, DeviceStatus* st) {
+                int4* __restrict__ rowblocks, int4* __restrict__ pairblocks, DeviceStatus* st) {
   pdl_wait();     // inputs written by the previous kernel of the chain
   pdl_trigger();  // the next kernel may launch and set up meanwhile
   __shared__ int tmp[33];
@@ -109,6 +109,16 @@ __global__ void __launch_bounds__(1024)
     rowblocks[base + j] = make_int4(e, off + r0, min(block_n, cnt - r0), 0);
   }
   if (e == 0) st->rowblocks = nblocks;
+  if (pairblocks != nullptr) {
+    const int np = (nb + 1) / 2;
+    int npairs = 0;
+    const int pbase = block_exclusive_scan(np, tmp, &npairs);
+    for (int j = 0; j < np; ++j) {
+      const int r0 = 2 * j * block_n;
+      pairblocks[pbase + j] = make_int4(e, off + r0, min(2 * block_n, cnt - r0), base + 2 * j);
+    }
+    if (e == 0) st->pairblocks = npairs;
+  }
 }
 
 __global__ void __launch_bounds__(kChunk)
@@ -192,7 +202,8 @@ constexpr int64_t kFusedPairs = 16 * kChunk;
 __global__ void __launch_bounds__(kChunk)
     fused_permute_kernel(const int32_t* __restrict__ idx, int64_t pairs, int k, int experts, int pad, int block_n,
                          int32_t* __restrict__ counts, int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
-                         int4* __restrict__ rowblocks, int32_t* __restrict__ pair_pos, const uint16_t* __restrict__ x,
+                         int4* __restrict__ rowblocks, int4* __restrict__ pairblocks, int32_t* __restrict__ pair_pos,
+                         const uint16_t* __restrict__ x,
                          int64_t hidden, uint16_t* __restrict__ xp, int div, int32_t* __restrict__ aux_out,
                          int split, int empty_ok, DeviceStatus* st) {
   pdl_wait();     // inputs written by the previous kernel of the chain
@@ -255,6 +266,16 @@ __global__ void __launch_bounds__(kChunk)
       rowblocks[rb_base + j] = make_int4(e_t, off + r0, min(block_n, cnt - r0), 0);
     }
     if (e_t == 0) st->rowblocks = nblocks;
+    if (pairblocks != nullptr) {  // uniform over the CTA: the scan's barriers are met by all threads
+      const int np = (nb + 1) / 2;
+      int npairs = 0;
+      const int pbase = block_exclusive_scan(np, tmp, &npairs);
+      for (int j = 0; j < np; ++j) {
+        const int r0 = 2 * j * block_n;
+        pairblocks[pbase + j] = make_int4(e_t, off + r0, min(2 * block_n, cnt - r0), rb_base + 2 * j);
+      }
+      if (e_t == 0) st->pairblocks = npairs;
+    }
   }
   if (e_t < experts) before[e_t] += off;  // chunk base per expert
   // stable rank inside this chunk
@@ -330,7 +351,7 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
     const size_t smem = (size_t(32) * E + 2 * E + 2 * kChunk) * sizeof(int32_t);
     KLC_CUDA(cudaFuncSetAttribute(fused_permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
     KLC_CUDA(launch_chain(fused_permute_kernel, dim3(unsigned(int64_t(nchunks) * split)), dim3(kChunk), size_t(smem), stream, 0u, 
-        a.idx, pairs, a.k, E, a.pad, a.block_n, a.counts, a.offsets, a.rows, a.rowblocks, a.pair_pos, a.x, a.hidden,
+        a.idx, pairs, a.k, E, a.pad, a.block_n, a.counts, a.offsets, a.rows, a.rowblocks, a.pairblocks, a.pair_pos, a.x, a.hidden,
         a.xp, div, a.aux_out, split, a.empty_ok ? 1 : 0, a.status));
     KLC_LAUNCH_CHECK("permute (fused) launch");
     return KLC_OK;
@@ -338,7 +359,7 @@ int launch_permute(const PermuteArgs& a, cudaStream_t stream) {
   KLC_CUDA(launch_chain(hist_kernel, dim3(nchunks), dim3(kChunk), size_t(E * sizeof(int32_t)), stream, 0u, a.idx, pairs, E, div, a.chunk_hist));
   KLC_LAUNCH_CHECK("permute hist launch");
   KLC_CUDA(launch_chain(scan_kernel, dim3(1), dim3(1024), size_t(0), stream, 0u, a.chunk_hist, nchunks, E, a.pad, a.block_n, a.counts, a.offsets, a.rows,
-                                      a.rowblocks, a.status));
+                                      a.rowblocks, a.pairblocks, a.status));
   KLC_LAUNCH_CHECK("permute scan launch");
   const size_t smem = (size_t(32) * E + 2 * kChunk) * sizeof(int32_t);
   KLC_CUDA(cudaFuncSetAttribute(scatter_gather_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));

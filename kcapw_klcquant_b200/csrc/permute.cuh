@@ -21,6 +21,8 @@ struct PermuteArgs {
   int32_t* pair_pos;   // [T*k]        pair id -> padded row
   int32_t* chunk_hist; // [nchunks*E]  scratch
   int4* rowblocks;     // [max_rowblocks] (expert, first row, rows, 0)
+  int4* pairblocks;    // null, or [max_rowblocks]: (expert, first row, rows <= 2*block_n, index of its
+                       // first row-block); two consecutive row-blocks of one expert per entry
   DeviceStatus* status;
   const uint16_t* x;   // [T, H] or null (no gather)
   int64_t hidden;
@@ -44,6 +46,7 @@ struct WorkspaceLayout {
   int pad, block_n;
   size_t status, counts, offsets, chunk_hist, rows, pair_pos, rowblocks, normsq, xp, gated, y, idx, w;
   size_t gq, sfb1, sfb2;  // tensor-core path: hi/lo E4M3 down-pass rows and activation scale blocks
+  size_t pairblocks;      // tensor-core path with 64-row blocks: the paired row-block list
   size_t total;
 };
 
@@ -85,6 +88,7 @@ struct ExpertArgs {
   int k;
   int precision;
   const int4* rowblocks;
+  const int4* pairblocks;      // null, or the paired list (two-SM tiles; count in status->pairblocks)
   int max_rowblocks;
   const int32_t* rows;
   const DeviceStatus* status;  // rowblocks count lives here
