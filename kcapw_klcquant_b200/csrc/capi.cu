@@ -72,7 +72,7 @@ extern "C" int klc_struct_sizes(size_t* dims_bytes, size_t* weights_bytes) {
 namespace klc {
 namespace {
 std::atomic<bool> g_pdl{true};
-std::atomic<int> g_pair_tiles{0};
+std::atomic<int> g_pair_tiles{1};
 }  // namespace
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
 int pair_tiles_mode() { return g_pair_tiles.load(std::memory_order_relaxed); }

@@ -982,37 +982,13 @@ __device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) 
   return r;
 }
 
-// Arrive on a barrier of another CTA of the cluster (release at cluster scope).
+// Arrive on a barrier of another CTA of the pair.  The plain form (release
+// at CTA scope) is the one two-SM tcgen05 pipelines use for their peer
+// arrivals: the tcgen05 fences around the arrive and the wait order the TMEM
+// accesses.  A cluster-scope release here costs a memory barrier per stage
+// (measured: the kernel ran at half speed, stalled on it).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// wait_bar for barriers that CTAs of the cluster arrive on (acquire at cluster scope)
-__device__ __forceinline__ bool wait_bar_cluster(uint32_t bar, uint32_t parity, const Ctl& c, int site) {
-  const long long t0 = clock64();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (*c.abort) return false;
-      if (clock64() - t0 > kWaitCycles) {
-        *c.abort = 1;
-        record_fault(c.status, KLC_ERR_DEVICE_TIMEOUT, site, 0);
-        return false;
-      }
-    }
-  }
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync_all() {
@@ -1192,15 +1168,11 @@ __global__ void __launch_bounds__(C::THREADS, 1)
       for (int item = cid; item < total && ok; item += ncl, ++ic) {
         const int d = ic % ND;
         const uint32_t d_tmem = tmem + uint32_t(d * kWN);
-        if constexpr (C::PAIR) ok = wait_bar_cluster(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 90);
-        else ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 90);
-        if (!ok) break;
+        if (!(ok = wait_bar(dempty(d), ((ic / ND) & 1) ^ 1, ctl, 90))) break;
         tc_fence_after();
         for (int ks = 0; ks < st_n && ok; ++ks, ++it) {
           const int s = int(it % NS);
-          if constexpr (C::PAIR) ok = wait_bar_cluster(sready(s), (it / NS) & 1, ctl, 91);
-          else ok = wait_bar(sready(s), (it / NS) & 1, ctl, 91);
-          if (!ok) break;
+          if (!(ok = wait_bar(sready(s), (it / NS) & 1, ctl, 91))) break;
           tc_fence_after();
           const uint32_t sf_t = tmem + uint32_t(C::ACC_COLS + s * C::SF_COLS);
           const uint64_t xdesc0 = sw128_desc(smem_u32(smem + C::OFF_A + s * C::ASLOT));
@@ -1650,10 +1622,14 @@ using Mx2N64 = Mx2Cfg<KLC_MX2_N64>;
 #ifndef KLC_MX3_N64
 #define KLC_MX3_N64 64, 4, 2, 128, 0, 2
 #endif
-// Two-SM tiles (64 tokens per CTA, half of each weight tile per CTA):
+// Two-SM tiles (64 tokens per CTA, half of each weight tile per CTA): the
+// half-size weight boxes leave room for three 256-K stages (one-SM tiles fit
+// only two), which halves the stage hops per item.  Measured on B200, config 3
+// (T = 16384, 512 rows per expert), gate_up + down ms: one-SM 128-K x 4 3.05 +
+// 1.50; pair 128-K x 6 3.18 + 1.56, 128-K x 7 3.15 + 1.56, 256-K x 3 2.86 + 1.36.
 //                 BN  NS ND  SK  PF EPI PAIR
 #ifndef KLC_MX3_P64
-#define KLC_MX3_P64 64, 6, 2, 128, 0, 2, 1
+#define KLC_MX3_P64 64, 3, 2, 256, 0, 2, 1
 #endif
 using Mx3N16 = Mx3Cfg<KLC_MX3_N16>;
 using Mx3N64 = Mx3Cfg<KLC_MX3_N64>;
