@@ -125,7 +125,37 @@ __device__ __forceinline__ uint8_t quantize_block(const uint4* __restrict__ src,
   return uint8_t(S + 127);
 }
 
-// One warp per row; lane l handles 32-K blocks l, l+32, ...
+// A quarter of a 32-value block per lane: the four lanes of a quad hold one
+// block (8 bf16 each, 16 contiguous bytes), agree on its exponent by two
+// shuffles and write 8 hi and 8 lo E4M3 bytes each, so a warp reads and writes
+// contiguous 512- and 256-byte spans.  The values are those of quantize_block.
+// All 32 lanes call it (the shuffles); `v` of a lane past the row is zero.
+__device__ __forceinline__ uint8_t quantize_quarter(const uint4 v, uint2& hi, uint2& lo) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t emax = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) emax = max(emax, max((w[i] >> 7) & 0xFFu, (w[i] >> 23) & 0xFFu));
+  emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, 1));
+  emax = max(emax, __shfl_xor_sync(0xffffffffu, emax, 2));
+  int S = emax == 0 ? 0 : int(emax) - 134;
+  S = S < -126 ? -126 : (S > 126 ? 126 : S);
+  const float inv = __uint_as_float(uint32_t(127 - S) << 23);  // 2^-S
+  uint32_t hp[4], lp[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t b0 = w[i] & 0xFFFFu, b1 = w[i] >> 16;
+    const float x0 = __uint_as_float(b0 << 16), x1 = __uint_as_float(b1 << 16);
+    const float h0 = __uint_as_float((b0 & 0xFFF0u) << 16), h1 = __uint_as_float((b1 & 0xFFF0u) << 16);
+    hp[i] = e4m3x2(h0 * inv, h1 * inv);
+    lp[i] = e4m3x2((x0 - h0) * inv, (x1 - h1) * inv);
+  }
+  hi = make_uint2(hp[0] | (hp[1] << 16), hp[2] | (hp[3] << 16));
+  lo = make_uint2(lp[0] | (lp[1] << 16), lp[2] | (lp[3] << 16));
+  return uint8_t(S + 127);
+}
+
+// One warp per row, 8 blocks of 32 K per pass (a quad per block), four passes'
+// loads issued before their conversions.
 __global__ void __launch_bounds__(256)
     quantize_rows_kernel(const uint16_t* __restrict__ src, int64_t K, const int32_t* __restrict__ rows_map, int k,
                          const int4* __restrict__ rowblocks, const DeviceStatus* __restrict__ st, int nch,
@@ -138,18 +168,35 @@ __global__ void __launch_bounds__(256)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = int(K / 32);
   const int stages = (G + 3) / 4;
+  const int part = lane & 3;
+  constexpr int kU = 4;  // passes in flight
   for (int n = warp; n < rb.z; n += blockDim.x >> 5) {
     const int64_t row = int64_t(rb.y) + n;
     const int64_t srow = rows_map != nullptr ? int64_t(rows_map[row] / k) : row;
     const uint4* s4 = reinterpret_cast<const uint4*>(src + srow * K);
     uint8_t* qh = q + row * 2 * K;
-    for (int kb = lane; kb < G; kb += 32) {
-      const uint8_t sb = quantize_block(s4 + kb * 4, qh + int64_t(kb) * 32, qh + K + int64_t(kb) * 32);
+    for (int b0 = 0; b0 < G; b0 += 8 * kU) {
+      uint4 v[kU];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n2 = 2 * n + h;
-        uint8_t* blk = sfb + ((int64_t(rbi) * stages + kb / 4) * nch + n2 / 128) * 512;
-        blk[(n2 & 31) * 16 + ((n2 & 127) >> 5) * 4 + (kb & 3)] = sb;
+      for (int u = 0; u < kU; ++u) {
+        const int kb = b0 + 8 * u + (lane >> 2);
+        v[u] = kb < G ? s4[kb * 4 + part] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int kb = b0 + 8 * u + (lane >> 2);
+        if (b0 + 8 * u >= G) break;  // uniform over the warp
+        uint2 hi, lo;
+        const uint8_t sb = quantize_quarter(v[u], hi, lo);
+        if (kb < G) {
+          *reinterpret_cast<uint2*>(qh + int64_t(kb) * 32 + part * 8) = hi;
+          *reinterpret_cast<uint2*>(qh + K + int64_t(kb) * 32 + part * 8) = lo;
+          if (part < 2) {  // the scale byte of the hi (part 0) and lo (part 1) row
+            const int n2 = 2 * n + part;
+            uint8_t* blk = sfb + ((int64_t(rbi) * stages + kb / 4) * nch + n2 / 128) * 512;
+            blk[(n2 & 31) * 16 + ((n2 & 127) >> 5) * 4 + (kb & 3)] = sb;
+          }
+        }
       }
     }
   }

@@ -96,3 +96,46 @@ def test_pair_tiles_chosen_by_rows_per_expert():
         torch.cuda.synchronize()
         ys.append(y.clone())
     assert torch.equal(ys[0], ys[1]) and torch.equal(ys[0], ys[2])
+
+
+@pytest.mark.parametrize("fused_return", [True, False])
+def test_pair_tiles_under_expert_parallel_exchange(fused_return):
+    """The expert-parallel path (one rank: dispatch into the arena, local expert
+    GEMMs on the received rows, return by the down epilogue or by the copy
+    kernel, combine) gives the same bits with and without pair tiles, and
+    matches the single-GPU layer."""
+    import socket
+
+    import torch.distributed as dist
+
+    from kcapw_klcquant_b200 import MoeLayer
+    from kcapw_klcquant_b200 import synthetic as syn
+    from kcapw_klcquant_b200.ep import ExpertParallelMoe
+    from tests import parity
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1, device_id=DEV)
+    try:
+        dims = syn.LayerDims(32, 2880, 2880, 4)
+        layer = syn.make_layer(dims, seed=91, device=DEV)
+        x = syn.make_hidden(2048, 2880, seed=92, device=DEV)  # 256 rows per expert on average
+        ref, _ = MoeLayer.from_tensors(0, layer, DEV, top_k=4).forward(x, precision="bf16")
+        ep = ExpertParallelMoe(0, layer, DEV, top_k=4, exchange="p2p", max_tokens=2048)
+        ep._ep.set_fused_return(fused_return)
+        ys = {}
+        for mode in (0, 2):
+            _set_mode(mode)
+            for _ in range(2):
+                y, _ = ep.forward(x, precision="bf16")
+            torch.cuda.synchronize()
+            ep.check_device_status()
+            ys[mode] = y.clone()
+        ep.close()
+        assert torch.equal(ys[0], ys[2]), "pair tiles changed the expert-parallel output"
+        bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        m = parity.assert_output_close(bits(ys[2]), bits(ref), "ep1 pair tiles vs layer")
+        assert m["bit_equal_frac"] >= 0.99, m
+    finally:
+        dist.destroy_process_group()
