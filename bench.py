@@ -838,6 +838,8 @@ def main():
                     help="N>1 p2p: expert outputs stored to the source ranks by the down epilogue (auto: 2 ranks)")
     ap.add_argument("--pair-tiles", type=int, choices=[0, 1, 2], default=1,
                     help="two-SM expert tiles: 0 never, 1 from 192 rows per expert (default), 2 always")
+    ap.add_argument("--fused-quantize", type=int, choices=[0, 1], default=1,
+                    help="1: the gate_up epilogue writes the down GEMM's E4M3 operand (default); 0: a separate pass")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -848,6 +850,7 @@ def main():
         from kcapw_klcquant_b200 import _lib
 
         _lib.check(_lib.lib().klc_set_pair_tiles(args.pair_tiles))
+        _lib.check(_lib.lib().klc_set_fused_quantize(args.fused_quantize))
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)

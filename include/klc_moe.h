@@ -106,6 +106,13 @@ int klc_set_pdl(int enable);
  * 192 rows per expert; 2: whenever the 64-row kernels run.  The layer
  * output is identical in every mode; process-wide. */
 int klc_set_pair_tiles(int mode);
+/* enable != 0 (the default): the tensor-core gate_up kernel (weights-as-N
+ * forms with 64-row or two-SM tiles) writes the down GEMM's operand, the
+ * hi/lo E4M3 rows and their scale blocks, straight from its SwiGLU epilogue,
+ * and the separate quantize pass over the gated rows is skipped; 0: bf16
+ * gated rows, then that pass (16-row decode tiles always take the pass).
+ * The layer output is identical either way; process-wide. */
+int klc_set_fused_quantize(int enable);
 
 /* ---- MXFP4 dequant ---------------------------------------------------- *
  * Replaces dequantize_mxfp4_matrix(blocks, scales, dtype)

@@ -115,6 +115,7 @@ SIGNATURES: dict[str, list] = {
     "klc_struct_size": [c_int, POINTER(c_size_t)],
     "klc_set_pdl": [c_int],
     "klc_set_pair_tiles": [c_int],
+    "klc_set_fused_quantize": [c_int],
     "klc_selftest_wait_timeout": [c_int64, POINTER(c_int), POINTER(c_int), c_void_p],
     "klc_capabilities": [POINTER(c_int)],
     "klc_mxfp4_dequant": [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int, c_void_p],

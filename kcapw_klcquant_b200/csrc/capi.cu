@@ -73,13 +73,20 @@ namespace klc {
 namespace {
 std::atomic<bool> g_pdl{true};
 std::atomic<int> g_pair_tiles{1};
+std::atomic<bool> g_fused_quantize{true};
 }  // namespace
 bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+bool fused_quantize_enabled() { return g_fused_quantize.load(std::memory_order_relaxed); }
 int pair_tiles_mode() { return g_pair_tiles.load(std::memory_order_relaxed); }
 }  // namespace klc
 
 extern "C" int klc_set_pdl(int enable) {
   klc::g_pdl.store(enable != 0, std::memory_order_relaxed);
+  return KLC_OK;
+}
+
+extern "C" int klc_set_fused_quantize(int enable) {
+  klc::g_fused_quantize.store(enable != 0, std::memory_order_relaxed);
   return KLC_OK;
 }
 

@@ -60,6 +60,7 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 bool pdl_enabled();  // klc_set_pdl, default on
 int pair_tiles_mode();  // klc_set_pair_tiles: 0 never, 1 by rows per expert (default), 2 always
+bool fused_quantize_enabled();  // klc_set_fused_quantize, default on
 
 // cudaLaunchKernelEx with the programmatic-serialization attribute (when enabled)
 // plus, for cluster_x >= 1, a cluster of cluster_x CTAs (0: no cluster launch)
