@@ -61,8 +61,8 @@ FLOPS_PER_TOKEN = 2 * TOP_K * (GPT_OSS_H * 2 * GPT_OSS_I + GPT_OSS_I * GPT_OSS_H
 GATE_UP_FLOPS_PER_PAIR = 2 * GPT_OSS_H * 2 * GPT_OSS_I  # 33,177,600
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate_up launch from ncu captures
 # (profiles/): decode T=256, prefill T=4096 Zipf.  None where no capture was taken.
-PROFILED_GATE_UP_TRAFFIC = {"decode": 1_191_247_000 + 8_817_664, "prefill": 1_071_562_000 + 97_615_616,
-                           "config3": 1_574_400_768 + 366_997_248}
+PROFILED_GATE_UP_TRAFFIC = {"decode": 1_191_247_000 + 8_817_664, "prefill": 1_068_494_336 + 100_976_128,
+                           "config3": 1_583_132_416 + 379_182_848}
 
 
 def peaks() -> dict:
